@@ -1,0 +1,333 @@
+"""Benchmark of the int8 decode GEMV hot path (BASELINE metric, config 1).
+
+Workload (N=1): config 1 — y = x . W^T with x fp32 [1, 2048] and W [6144, 2048]
+quantized by QuickLM's int8 scheme (per-32-block fp32 scales), computed by the
+bit-exact sm_100a GEMV. One "step" streams a stack of G distinct quantized
+copies of W (G * 14.16 MB > the 126 MB L2, so every launch reads HBM) through
+one GEMV each; the step is captured once as a CUDA graph and replayed.
+
+* value  = weight bytes (int8 + scales) of all launches / device time (GB/s)
+* e2e    = the same metric through the C ABI with HOST buffers
+           (qlm_linear_int8 + QLM_LINEAR_HOST_IO: pinned x in, y out, synchronous
+           per call — math::matmul's contract), host wall time
+* roofline: algorithmic bytes per launch (weights + x + y) / mean launch time,
+           against the measured HBM copy bandwidth
+* cpu_baseline: QuickLM's own AVX2 int8 path (compiled from its sources) on
+           this host's cores, same shapes, bounded sample
+
+With --gpus N > 1 (launched by torchrun) every rank holds its own 6144-row
+shard of a [6144*N, 2048] weight per stack entry and the outputs are
+all-gathered over NCCL after every GEMV (row-sharded, column-parallel
+linear); value aggregates all ranks' weight bytes ("weak" scaling).
+
+``--impl reference`` times the reference's CPU implementation instead and
+prints the same line with "impl": "reference".
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+N_ROWS, K_DIM = 6144, 2048
+STACK = 16  # weight copies per step: 16 * 14.16 MB = 226 MB > L2
+METRIC = "int8 GEMV weight GB/s (% HBM peak) at M=1; prefill GEMM TOPS; decode tok/s"
+
+
+def weight_bytes(n=N_ROWS, k=K_DIM):
+    return n * k + 4 * n * ((k + 31) // 32)
+
+
+def algo_bytes(m=1, n=N_ROWS, k=K_DIM):
+    return weight_bytes(n, k) + 4 * m * k + 4 * m * n
+
+
+def measured_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def profile_traffic(name="gemv_exact_cfg1.txt"):
+    """DRAM bytes per launch from the committed ncu summary, if present."""
+    p = os.path.join(ROOT, "profiles", name)
+    if not os.path.exists(p):
+        return None
+    with open(p) as f:
+        for line in f:
+            if line.startswith("traffic_bytes_per_launch:"):
+                try:
+                    return int(line.split(":", 1)[1].strip())
+                except ValueError:
+                    return None
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi clocks/throttle reasons sampled during the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=10)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        sm, smax, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in out.strip().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax.append(float(parts[2]))
+            except ValueError:
+                continue
+            for nm, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(smax) if smax else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def cpu_baseline(x, q, s, seconds=10.0):
+    """QuickLM's own int8 math::matmul (oracle/_ref, strict build) on this
+    host's cores: M=1 GEMVs rotating over STACK copies (larger than the LLC)."""
+    from oracle.oracle import RefCPU
+    cores = len(os.sched_getaffinity(0))
+    ref = RefCPU()
+    ref.init_threads(cores)
+    qs = [q.copy() for _ in range(STACK)]
+    ss = [s.copy() for _ in range(STACK)]
+    ref.matmul_stack_ms(x, qs, ss, rounds=1)  # warm-up
+    rounds, total_ms = 0, 0.0
+    while total_ms < seconds * 1000.0:
+        total_ms += ref.matmul_stack_ms(x, qs, ss, rounds=1)
+        rounds += 1
+    gemvs = rounds * STACK
+    gbs = gemvs * weight_bytes() / (total_ms / 1000.0) / 1e9
+    return {"value": round(gbs, 3), "unit": "GB/s", "cores": cores, "kind": "reference",
+            "sample": f"{gemvs} M=1 GEMVs [6144,2048] over {STACK} rotating weight copies "
+                      f"({total_ms / 1000.0:.1f} s), math::init_thread_pool({cores})"}
+
+
+def run_reference(args):
+    """--impl reference: the reference's own CPU path, all host threads."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    from oracle.oracle import RefCPU, synth_case
+    cores = len(os.sched_getaffinity(0))
+    x, w = synth_case(1, N_ROWS, K_DIM, 0)
+    ref = RefCPU()
+    ref.init_threads(cores)
+    q, s = ref.quantize(w)
+    del w
+    qs = [q.copy() for _ in range(STACK)]
+    ss = [s.copy() for _ in range(STACK)]
+    # one step = one GEMV of the rotating stack (a bounded sample of a pass)
+    for i in range(args.warmup):
+        ref.matmul_stack_ms(x, qs[i % STACK:i % STACK + 1], ss[i % STACK:i % STACK + 1])
+    total = 0.0
+    for i in range(args.steps):
+        total += ref.matmul_stack_ms(x, qs[i % STACK:i % STACK + 1], ss[i % STACK:i % STACK + 1])
+    gbs = args.steps * weight_bytes() / (total / 1000.0) / 1e9
+    line = {"impl": "reference", "metric": METRIC, "value": round(gbs, 3), "unit": "GB/s", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": total / args.steps,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp32 x int8",
+            "data": "synthetic (seed 0, W~N(0,0.02^2), x~N(0,1))",
+            "config": {"workload": "cfg1 int8 GEMV M=1 [6144,2048], reference CPU path", "l2": "n/a (CPU)"},
+            "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": cores, "kind": "reference",
+                             "sample": f"{args.steps} M=1 GEMVs over {STACK} rotating weight copies"},
+            "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=4000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", default="qlm", choices=["qlm", "reference"])
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--e2e-calls", type=int, default=2000)
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    if args.impl == "reference":
+        return run_reference(args)
+
+    import torch
+    import quicklm_b200 as qlm
+    from oracle.oracle import synth_case
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
+
+    # Inputs: the rank's shard rows of config 1's generator (rank 0 = config 1 itself).
+    x_np, w_np = synth_case(1, N_ROWS, K_DIM, 0 + rank)
+    w_dev = torch.from_numpy(w_np).cuda()
+    weights = [qlm.Int8Weight.quantize(w_dev, device=local) for _ in range(STACK)]
+    del w_dev
+    x = torch.from_numpy(x_np).cuda()
+    ys = [torch.empty((1, N_ROWS), device="cuda") for _ in range(STACK)]
+    gathered = [torch.empty((world, N_ROWS), device="cuda") for _ in range(STACK)] if world > 1 else None
+    stream = torch.cuda.Stream()
+
+    def step():
+        for i in range(STACK):
+            qlm.matmul(x, weights[i], ys[i], stream=stream)
+            if world > 1:
+                dist.all_gather_into_tensor(gathered[i], ys[i])
+
+    with torch.cuda.stream(stream):
+        for _ in range(3):
+            step()
+    torch.cuda.synchronize()
+    graph = None
+    if world == 1:
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            step()
+        torch.cuda.synchronize()
+
+    def run(n):
+        with torch.cuda.stream(stream):
+            for _ in range(n):
+                if graph is not None:
+                    graph.replay()
+                else:
+                    step()
+
+    run(args.warmup)
+    torch.cuda.synchronize()
+    clocks = ClockSampler(local)
+    clocks.start()
+    time.sleep(0.3)
+    if dist is not None:
+        dist.barrier()
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record(stream)
+    run(args.steps)
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    if dist is not None:
+        dist.barrier()
+    ms = ev0.elapsed_time(ev1)
+    clk = clocks.stop()
+    if dist is not None:
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+
+    launches = args.steps * STACK
+    total_weight = launches * weight_bytes() * world
+    value = total_weight / (ms / 1000.0) / 1e9
+    mean_launch_s = (ms / 1000.0) / launches
+    peak, peak_kind = measured_peaks()
+    achieved = algo_bytes() / mean_launch_s / 1e9
+
+    # e2e: through the C ABI with host buffers (pinned), synchronous per call.
+    x_pin = torch.empty((1, K_DIM), dtype=torch.float32, pin_memory=True)
+    x_pin.copy_(torch.from_numpy(x_np))
+    y_pin = torch.empty((1, N_ROWS), dtype=torch.float32, pin_memory=True)
+    xh, yh = x_pin.numpy(), y_pin.numpy()
+    for i in range(20):
+        qlm.matmul(xh, weights[i % STACK], yh)
+    if dist is not None:
+        dist.barrier()
+    t0 = time.perf_counter()
+    for i in range(args.e2e_calls):
+        qlm.matmul(xh, weights[i % STACK], yh)
+    e2e_s = time.perf_counter() - t0
+    if dist is not None:
+        t = torch.tensor([e2e_s], device="cuda", dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_s = float(t.item())
+    e2e = args.e2e_calls * weight_bytes() * world / e2e_s / 1e9
+
+    base = None
+    if rank == 0 and not args.no_cpu_baseline:
+        q_ref, s_ref = weights[0].to_int8()
+        base = cpu_baseline(x_np, q_ref, s_ref, args.cpu_seconds)
+
+    if graph is not None:
+        del graph
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "fp32 x int8 (fp32 math, bit-exact)",
+            "data": "synthetic (seed 0, W~N(0,0.02^2), x~N(0,1); QuickLM per-32-block int8 scales)",
+            "config": {"workload": "cfg1 int8 decode GEMV M=1, W [6144,2048] per rank, "
+                                   f"{STACK} distinct weight copies per step",
+                       "l2": f"inputs larger than L2 ({STACK}x{weight_bytes() / 1e6:.2f} MB weights per step)",
+                       "parallelism": "single GPU" if world == 1 else f"row-sharded x{world} + NCCL all-gather",
+                       "kernel": "gemv_exact_kernel<1> (CUDA cores, bit-exact)", "cuda_graph": graph is not None,
+                       "pdl": os.environ.get("QLM_PDL", "1") != "0"},
+            "pct_hbm_peak": round(100.0 * value / world / peak, 2),
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": peak, "unit": "GB/s",
+                         "frac": round(achieved / peak, 4), "traffic": profile_traffic(),
+                         "peak_source": f"MEASURED_PEAKS.json hbm_gbs ({peak_kind})",
+                         "algorithmic_bytes_per_launch": algo_bytes(), "mean_launch_us": mean_launch_s * 1e6},
+            "e2e": {"value": round(e2e, 2), "unit": "GB/s", "h2d_bytes_per_step": STACK * 4 * K_DIM,
+                    "d2h_bytes_per_step": STACK * 4 * N_ROWS,
+                    "how": "qlm_linear_int8(QLM_LINEAR_HOST_IO) per GEMV, pinned host x/y, wall clock"},
+            "gpu_launches": launches,
+            "clocks": clk,
+            "cpu_baseline": base,
+        }
+        print(json.dumps(line), flush=True)
+    for w in weights:
+        w.free()
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,126 @@
+/*
+ * qlm_b200.h — C ABI of the B200 (sm_100a) int8 quantized-matmul path for
+ * QuickLM. Plain pointers and sizes only; every entry point returns a
+ * qlm_status and never throws. qlm_last_error() gives the message of the most
+ * recent failure on the calling thread.
+ *
+ * The path this replaces in QuickLM (paths inside its source tree):
+ *   - load-time quantization: SafetensorsLoader::get_tensor_keep_int8
+ *     (src/io/safetensors.cpp:517-585) with st_quantize_row_f32/_bf16
+ *     (src/io/safetensors.cpp:296-391);
+ *   - the int8 weight storage in Tensor (src/tensor/tensor.hpp:30-43);
+ *   - the int8 branch of math::matmul (src/ops/math_ops.hpp:92,
+ *     src/ops/math_ops.cpp:820-900) and its kernels int8_gemv_range /
+ *     dot8/dot4/dot_avx2_int8 (src/ops/math_ops.cpp:403-579).
+ *
+ * Numerics: the default (exact) linear path reproduces the reference's
+ * per-element arithmetic bit for bit, for any M. QLM_LINEAR_TENSOR selects the
+ * tcgen05 tensor-core GEMM for prefill, which is within relative L2 2e-3.
+ *
+ * Threading: like math::matmul, calls for one device are expected from one
+ * host thread at a time (the library keeps per-device scratch buffers).
+ */
+#ifndef QLM_B200_H
+#define QLM_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define QLM_ABI_VERSION 1
+
+/* Scale granularity: one fp32 scale per 32 consecutive elements of a row
+ * (Tensor::INT8_BLOCK_SIZE, src/tensor/tensor.hpp:32). */
+#define QLM_BLOCK 32
+
+typedef enum qlm_status {
+    QLM_OK = 0,
+    QLM_ERR_INVALID_ARG = 1, /* bad shape, null pointer, stride, range       */
+    QLM_ERR_CUDA = 2,        /* a CUDA runtime call failed                    */
+    QLM_ERR_OUT_OF_MEMORY = 3,
+    QLM_ERR_UNSUPPORTED = 4, /* valid request this build/device cannot serve  */
+    QLM_ERR_TIMEOUT = 5,     /* a bounded device-side wait gave up            */
+    QLM_ERR_NCCL = 6,        /* a NCCL call failed                            */
+    QLM_ERR_INTERNAL = 7
+} qlm_status;
+
+/* Source element type of the weights handed to qlm_weight_quantize_upload,
+ * the two dtypes get_tensor_keep_int8 accepts (src/io/safetensors.cpp:524-527). */
+typedef enum qlm_src_dtype { QLM_SRC_F32 = 0, QLM_SRC_BF16 = 1 } qlm_src_dtype;
+
+/* Flags for qlm_linear_int8. */
+#define QLM_LINEAR_EXACT 0x0   /* bit-exact CUDA-core path (default)            */
+#define QLM_LINEAR_TENSOR 0x1  /* tcgen05 tensor-core GEMM (prefill, M >= 64)   */
+#define QLM_LINEAR_HOST_IO 0x2 /* x and y are HOST pointers; the call copies x  */
+                               /* in, runs, copies y out and returns with y     */
+                               /* complete (math::matmul's synchronous contract) */
+#define QLM_LINEAR_SYNC 0x4    /* device pointers, but synchronize before return */
+
+/* A device-resident int8 weight: rows [row_begin, row_end) of an [n_total, k]
+ * matrix, packed for the decode GEMV, with its per-32-block fp32 scales.
+ * Owns its device memory; release with qlm_weight_free. */
+typedef struct qlm_w8 qlm_w8;
+
+/* ABI version of the loaded library (QLM_ABI_VERSION). */
+int qlm_abi_version(void);
+
+/* Message for the most recent failing call on this thread ("" if none). */
+const char* qlm_last_error(void);
+
+/* Quantize + pack + upload. Replaces get_tensor_keep_int8
+ * (src/io/safetensors.cpp:517-585): per 32-block absmax/127 scale, RN-even
+ * rounding, clamp to [-127, 127], bit-identical to st_quantize_row_f32/_bf16
+ * (src/io/safetensors.cpp:296-391), computed on the device.
+ *   src:            [n_total, k] row-major F32 or BF16 values, row stride
+ *                   src_row_stride elements (>= k); host memory (e.g. the
+ *                   safetensors mmap) or device memory (detected).
+ *   row_begin/end:  the output-row shard this device keeps (0, n_total for all).
+ *   device:         CUDA ordinal that will hold the weight.
+ *   stream:         cudaStream_t (NULL = the legacy default stream).
+ * On success *out holds a new handle; the call returns after the upload. */
+int qlm_weight_quantize_upload(const void* src, int src_dtype, int64_t src_row_stride, int n_total, int k,
+                               int row_begin, int row_end, int device, void* stream, qlm_w8** out);
+
+/* Upload an already-quantized weight given in the reference Tensor's int8
+ * layout (src/tensor/tensor.hpp:34-41): q [n_total, k] int8 row-major and
+ * scales [n_total, ceil(k/32)] fp32; host pointers. Keeps rows
+ * [row_begin, row_end). */
+int qlm_weight_import_int8(const int8_t* q, const float* scales, int n_total, int k, int row_begin,
+                           int row_end, int device, void* stream, qlm_w8** out);
+
+/* Copy a handle's rows back into the reference layout (host pointers):
+ * q [rows, k] int8 and scales [rows, ceil(k/32)] fp32, rows = row_end - row_begin. */
+int qlm_weight_export_int8(const qlm_w8* w, int8_t* q, float* scales);
+
+/* Shape of a handle. Any output pointer may be NULL. */
+int qlm_weight_shape(const qlm_w8* w, int* rows, int* k, int* row_begin, int* row_end, int* n_total);
+
+/* Device bytes read by one M=1 product with this weight: packed int8 plus
+ * scales, the "weight bytes" of the decode roofline. */
+int64_t qlm_weight_bytes(const qlm_w8* w);
+
+/* Release a handle and its device memory (NULL is a no-op). */
+void qlm_weight_free(qlm_w8* w);
+
+/* y[m, 0:rows] = x[m, 0:k] . W^T, for m in [0, M). Replaces the int8 branch of
+ * math::matmul(A, B, C, transpose_B=true) (src/ops/math_ops.cpp:820-900):
+ *   x:    [M, k] fp32, row stride ldx (>= k)
+ *   y:    [M, rows] fp32, row stride ldy (>= rows); overwritten, not accumulated
+ *   flags QLM_LINEAR_*; device pointers unless QLM_LINEAR_HOST_IO.
+ * The exact path accepts any M >= 1; QLM_LINEAR_TENSOR needs M >= 1 and k a
+ * multiple of 64 and falls back to nothing: it returns QLM_ERR_UNSUPPORTED if
+ * the shape does not qualify. Asynchronous on `stream` unless HOST_IO/SYNC. */
+int qlm_linear_int8(const float* x, int M, int k, int64_t ldx, const qlm_w8* w, float* y, int64_t ldy, int flags,
+                    void* stream);
+
+/* Block until all work queued on `stream` is done (reports async errors). */
+int qlm_stream_sync(void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* QLM_B200_H */

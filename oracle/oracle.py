@@ -1,0 +1,167 @@
+"""TEST INFRASTRUCTURE ONLY — ctypes access to the two CPU parity checkers.
+
+* ``RefCPU``: QuickLM's own int8 path compiled from the reference sources
+  (``oracle/_ref/libqlm_refcpu.so``; see ``oracle/ref_shim.cpp``).
+* ``COracle``: the plain-C restatement (``oracle/_build/libqlm_oracle.so``;
+  see ``oracle/qlm_oracle.c``).
+
+Only ``tests/``, ``__graft_entry__.smoke()`` and ``bench.py``'s CPU-baseline /
+reference arm import this module, always as the checker. The product package
+``quicklm_b200`` never imports it.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import subprocess
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+REF_LIB = os.path.join(HERE, "_ref", "libqlm_refcpu.so")
+ORACLE_LIB = os.path.join(HERE, "_build", "libqlm_oracle.so")
+BLOCK = 32  # Tensor::INT8_BLOCK_SIZE (tensor/tensor.hpp:32)
+
+_P = ctypes.c_void_p
+_I = ctypes.c_int
+
+
+def num_blocks(k: int) -> int:
+    return (k + BLOCK - 1) // BLOCK
+
+
+def build(ref_root: str | None = None) -> None:
+    """Compile both checkers with oracle/Makefile (the _ref part only when the
+    reference tree is present)."""
+    cmd = ["make", "-C", HERE, "--no-print-directory", "all"]
+    if ref_root:
+        cmd.append(f"REF={ref_root}")
+    subprocess.run(cmd, check=True, stdout=subprocess.DEVNULL)
+
+
+def _ptr(a: np.ndarray) -> int:
+    return a.ctypes.data
+
+
+def _check_w(w: np.ndarray) -> int:
+    if w.dtype == np.float32:
+        return 0
+    if w.dtype == np.uint16:  # raw bf16 bits
+        return 1
+    raise TypeError("weights must be float32 or uint16 (bf16 bits)")
+
+
+class RefCPU:
+    """QuickLM's own math::matmul / get_tensor_keep_int8, compiled from source."""
+
+    def __init__(self, path: str = REF_LIB):
+        if not os.path.exists(path):
+            raise FileNotFoundError(f"{path} missing: run `make -C oracle ref` where the reference tree exists")
+        lib = ctypes.CDLL(path)
+        lib.qlmref_last_error.restype = ctypes.c_char_p
+        lib.qlmref_init_threads.argtypes = [_I]
+        lib.qlmref_quantize.argtypes = [_P, _I, _I, _I, _P, _P]
+        lib.qlmref_matmul_int8.argtypes = [_P, _I, _I, _P, _P, _I, _P, _I, _I, ctypes.POINTER(ctypes.c_double)]
+        lib.qlmref_matmul_int8_stack.argtypes = [_P, _I, _I, _P, _P, _I, _I, _P, _I,
+                                                 ctypes.POINTER(ctypes.c_double)]
+        self.lib = lib
+        self.threads = 1
+
+    def _rc(self, rc: int) -> None:
+        if rc != 0:
+            raise RuntimeError(self.lib.qlmref_last_error().decode())
+
+    def init_threads(self, n: int) -> None:
+        """math::init_thread_pool(n) (ops/math_ops.cpp:161-171)."""
+        self._rc(self.lib.qlmref_init_threads(int(n)))
+        self.threads = int(n)
+
+    def quantize(self, w: np.ndarray):
+        """get_tensor_keep_int8 on a [n, k] float32 or bf16-bits matrix ->
+        (q int8 [n, k], scales float32 [n, ceil(k/32)])."""
+        w = np.ascontiguousarray(w)
+        dt = _check_w(w)
+        n, k = w.shape
+        q = np.empty((n, k), np.int8)
+        s = np.empty((n, num_blocks(k)), np.float32)
+        self._rc(self.lib.qlmref_quantize(_ptr(w), dt, n, k, _ptr(q), _ptr(s)))
+        return q, s
+
+    def matmul(self, x: np.ndarray, q: np.ndarray, s: np.ndarray, reps: int = 1):
+        """math::matmul(A=x [m, k], B=int8 [n, k]) -> (y [m, n], best_ms)."""
+        x = np.ascontiguousarray(x, np.float32)
+        if x.ndim == 1:
+            x = x[None, :]
+        q = np.ascontiguousarray(q, np.int8)
+        s = np.ascontiguousarray(s, np.float32)
+        m, k = x.shape
+        n = q.shape[0]
+        y = np.empty((m, n), np.float32)
+        best = ctypes.c_double(0.0)
+        self._rc(self.lib.qlmref_matmul_int8(_ptr(x), m, k, _ptr(q), _ptr(s), n, _ptr(y), n, int(reps),
+                                             ctypes.byref(best)))
+        return y, best.value
+
+    def matmul_stack_ms(self, x: np.ndarray, qs, ss, rounds: int = 1) -> float:
+        """Wall ms to stream every weight in (qs, ss) through math::matmul once
+        per round (rounds in a row)."""
+        x = np.ascontiguousarray(x, np.float32)
+        if x.ndim == 1:
+            x = x[None, :]
+        m, k = x.shape
+        n = qs[0].shape[0]
+        g = len(qs)
+        qp = (ctypes.c_void_p * g)(*[_ptr(a) for a in qs])
+        sp = (ctypes.c_void_p * g)(*[_ptr(a) for a in ss])
+        y = np.empty((m, n), np.float32)
+        tot = ctypes.c_double(0.0)
+        self._rc(self.lib.qlmref_matmul_int8_stack(_ptr(x), m, k, qp, sp, g, n, _ptr(y), int(rounds),
+                                                   ctypes.byref(tot)))
+        return tot.value
+
+
+class COracle:
+    """The plain-C restatement of the same arithmetic (oracle/qlm_oracle.c)."""
+
+    def __init__(self, path: str = ORACLE_LIB):
+        if not os.path.exists(path):
+            raise FileNotFoundError(f"{path} missing: run `make -C oracle oracle`")
+        lib = ctypes.CDLL(path)
+        lib.qlmo_quantize.argtypes = [_P, _I, _I, _I, _P, _P]
+        lib.qlmo_matmul_int8.argtypes = [_P, _I, _I, _P, _P, _I, _P, _I]
+        self.lib = lib
+
+    def quantize(self, w: np.ndarray):
+        w = np.ascontiguousarray(w)
+        dt = _check_w(w)
+        n, k = w.shape
+        q = np.empty((n, k), np.int8)
+        s = np.empty((n, num_blocks(k)), np.float32)
+        self.lib.qlmo_quantize(_ptr(w), dt, n, k, _ptr(q), _ptr(s))
+        return q, s
+
+    def matmul(self, x: np.ndarray, q: np.ndarray, s: np.ndarray) -> np.ndarray:
+        x = np.ascontiguousarray(x, np.float32)
+        if x.ndim == 1:
+            x = x[None, :]
+        q = np.ascontiguousarray(q, np.int8)
+        s = np.ascontiguousarray(s, np.float32)
+        m, k = x.shape
+        n = q.shape[0]
+        y = np.empty((m, n), np.float32)
+        self.lib.qlmo_matmul_int8(_ptr(x), m, k, _ptr(q), _ptr(s), n, _ptr(y), n)
+        return y
+
+
+def synth_weights(n: int, k: int, seed: int, std: float = 0.02) -> np.ndarray:
+    """W ~ N(0, std^2) as float64 cast to float32, drawn first from
+    default_rng(seed) (the benchmark's synthetic-input convention)."""
+    rng = np.random.default_rng(seed)
+    return (rng.standard_normal((n, k)) * std).astype(np.float32), rng
+
+
+def synth_case(m: int, n: int, k: int, seed: int):
+    """(x [m, k] ~ N(0,1), W [n, k] ~ N(0, 0.02^2)) — W drawn first, then x."""
+    w, rng = synth_weights(n, k, seed)
+    x = rng.standard_normal((m, k)).astype(np.float32)
+    return x, w

@@ -1,0 +1,247 @@
+"""quicklm_b200 — B200 (sm_100a) int8 quantized-matmul path for QuickLM.
+
+Python binding over the C ABI in ``include/qlm_b200.h`` (library
+``quicklm_b200/lib/libqlm_b200.so``, built by ``quicklm_b200.build``). The
+names mirror QuickLM's operator interface for this path:
+
+* ``Int8Weight.quantize(...)`` — ``SafetensorsLoader::get_tensor_keep_int8``
+  (src/io/safetensors.cpp:517-585) done on the device: the result is an int8
+  weight resident in HBM instead of ``Tensor::int8_data``/``int8_scales``
+  (src/tensor/tensor.hpp:30-43).
+* ``matmul(A, B, C)`` — ``math::matmul(A, B, C, transpose_B=true)``
+  (src/ops/math_ops.hpp:92, src/ops/math_ops.cpp:820-900) for an int8 B:
+  C[m, n] = A[m, :] . B[n, :], C overwritten. Bit-identical to the reference
+  by default.
+
+There is no CPU fallback: if the CUDA library is missing or fails to load,
+``load()`` raises.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+import numpy as np
+
+__all__ = ["QlmError", "Int8Weight", "matmul", "load", "LIB_PATH", "EXACT", "TENSOR", "HOST_IO", "SYNC",
+           "BLOCK"]
+
+LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "lib", "libqlm_b200.so")
+BLOCK = 32
+EXACT, TENSOR, HOST_IO, SYNC = 0x0, 0x1, 0x2, 0x4
+SRC_F32, SRC_BF16 = 0, 1
+
+# Every symbol the header declares; tests check the library exports all of them.
+ABI_SYMBOLS = (
+    "qlm_abi_version", "qlm_last_error", "qlm_weight_quantize_upload", "qlm_weight_import_int8",
+    "qlm_weight_export_int8", "qlm_weight_shape", "qlm_weight_bytes", "qlm_weight_free", "qlm_linear_int8",
+    "qlm_stream_sync",
+)
+
+_STATUS = {0: "OK", 1: "INVALID_ARG", 2: "CUDA", 3: "OUT_OF_MEMORY", 4: "UNSUPPORTED", 5: "TIMEOUT", 6: "NCCL",
+           7: "INTERNAL"}
+
+
+class QlmError(RuntimeError):
+    """A failing qlm_* call; ``status`` is the qlm_status code."""
+
+    def __init__(self, status: int, msg: str):
+        super().__init__(f"{_STATUS.get(status, status)}: {msg}")
+        self.status = status
+
+
+_lib = None
+
+
+def load(path: str = LIB_PATH):
+    """Load the CUDA library (once). Raises if it is missing — no fallback."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(path):
+        raise QlmError(4, f"{path} is missing; build it with `python -m quicklm_b200.build`")
+    lib = ctypes.CDLL(path)
+    P, I, L = ctypes.c_void_p, ctypes.c_int, ctypes.c_int64
+    lib.qlm_abi_version.restype = I
+    lib.qlm_last_error.restype = ctypes.c_char_p
+    lib.qlm_weight_quantize_upload.argtypes = [P, I, L, I, I, I, I, I, P, ctypes.POINTER(P)]
+    lib.qlm_weight_import_int8.argtypes = [P, P, I, I, I, I, I, P, ctypes.POINTER(P)]
+    lib.qlm_weight_export_int8.argtypes = [P, P, P]
+    lib.qlm_weight_shape.argtypes = [P] + [ctypes.POINTER(I)] * 5
+    lib.qlm_weight_bytes.argtypes = [P]
+    lib.qlm_weight_bytes.restype = L
+    lib.qlm_weight_free.argtypes = [P]
+    lib.qlm_weight_free.restype = None
+    lib.qlm_linear_int8.argtypes = [P, I, I, L, P, P, L, I, P]
+    lib.qlm_stream_sync.argtypes = [P]
+    if lib.qlm_abi_version() != 1:
+        raise QlmError(7, "ABI version mismatch")
+    _lib = lib
+    return lib
+
+
+def _check(rc: int) -> None:
+    if rc != 0:
+        raise QlmError(rc, load().qlm_last_error().decode())
+
+
+def _is_torch(t) -> bool:
+    return type(t).__module__.startswith("torch")
+
+
+def _stream_ptr(stream) -> int | None:
+    if stream is None:
+        return None
+    if isinstance(stream, int):
+        return stream
+    return int(stream.cuda_stream)  # torch.cuda.Stream
+
+
+class Int8Weight:
+    """A device-resident int8 weight (rows [row_begin, row_end) of [n_total, k])
+    with per-32-block fp32 scales, owned by a ``qlm_w8`` handle."""
+
+    def __init__(self, handle: int):
+        self._h = ctypes.c_void_p(handle)
+        lib = load()
+        vals = [ctypes.c_int() for _ in range(5)]
+        _check(lib.qlm_weight_shape(self._h, *[ctypes.byref(v) for v in vals]))
+        self.rows, self.k, self.row_begin, self.row_end, self.n_total = (v.value for v in vals)
+        self.device = None
+
+    @property
+    def handle(self) -> ctypes.c_void_p:
+        if not self._h:
+            raise QlmError(1, "weight already freed")
+        return self._h
+
+    @property
+    def shape(self):
+        return (self.rows, self.k)
+
+    @property
+    def nbytes(self) -> int:
+        """Device bytes one M=1 product reads (packed int8 + scales)."""
+        return int(load().qlm_weight_bytes(self.handle))
+
+    @classmethod
+    def quantize(cls, w, device: int = 0, row_begin: int = 0, row_end: int | None = None, stream=None):
+        """Quantize an [n, k] float32 (or bf16-bits uint16 / torch bf16)
+        matrix on the device. ``w`` is a numpy array (host, e.g. an mmap) or a
+        torch tensor (host or CUDA)."""
+        lib = load()
+        if _is_torch(w):
+            import torch
+            if w.dim() != 2 or w.stride(1) != 1:
+                raise QlmError(1, "weight must be a 2-D tensor with unit column stride")
+            dt = {torch.float32: SRC_F32, torch.bfloat16: SRC_BF16}.get(w.dtype)
+            if dt is None:
+                raise QlmError(1, f"unsupported weight dtype {w.dtype}")
+            ptr, stride = w.data_ptr(), w.stride(0)
+            n, k = w.shape
+            keep = w
+        else:
+            arr = np.asarray(w)
+            if arr.ndim != 2:
+                raise QlmError(1, "weight must be 2-D")
+            if arr.dtype == np.float32:
+                dt = SRC_F32
+            elif arr.dtype == np.uint16:
+                dt = SRC_BF16
+            else:
+                raise QlmError(1, f"unsupported weight dtype {arr.dtype}")
+            if arr.strides[1] != arr.itemsize:
+                arr = np.ascontiguousarray(arr)
+            ptr, stride = arr.ctypes.data, arr.strides[0] // arr.itemsize
+            n, k = arr.shape
+            keep = arr
+        if row_end is None:
+            row_end = n
+        h = ctypes.c_void_p()
+        _check(lib.qlm_weight_quantize_upload(ptr, dt, stride, n, k, row_begin, row_end, device,
+                                              _stream_ptr(stream), ctypes.byref(h)))
+        del keep
+        out = cls(h.value)
+        out.device = device
+        return out
+
+    @classmethod
+    def from_int8(cls, q: np.ndarray, scales: np.ndarray, device: int = 0, row_begin: int = 0,
+                  row_end: int | None = None, stream=None):
+        """Upload a weight already in the reference Tensor's int8 layout."""
+        q = np.ascontiguousarray(q, np.int8)
+        scales = np.ascontiguousarray(scales, np.float32)
+        n, k = q.shape
+        if scales.shape != (n, (k + BLOCK - 1) // BLOCK):
+            raise QlmError(1, f"scales shape {scales.shape} != {(n, (k + BLOCK - 1) // BLOCK)}")
+        if row_end is None:
+            row_end = n
+        h = ctypes.c_void_p()
+        _check(load().qlm_weight_import_int8(q.ctypes.data, scales.ctypes.data, n, k, row_begin, row_end, device,
+                                             _stream_ptr(stream), ctypes.byref(h)))
+        out = cls(h.value)
+        out.device = device
+        return out
+
+    def to_int8(self):
+        """(q int8 [rows, k], scales float32 [rows, ceil(k/32)]) in the reference layout."""
+        q = np.empty((self.rows, self.k), np.int8)
+        s = np.empty((self.rows, (self.k + BLOCK - 1) // BLOCK), np.float32)
+        _check(load().qlm_weight_export_int8(self.handle, q.ctypes.data, s.ctypes.data))
+        return q, s
+
+    def free(self) -> None:
+        if self._h:
+            load().qlm_weight_free(self._h)
+            self._h = ctypes.c_void_p()
+
+    def __del__(self):
+        try:
+            self.free()
+        except Exception:
+            pass
+
+
+def matmul(A, B: Int8Weight, C=None, transpose_B: bool = True, flags: int = EXACT, stream=None):
+    """C = A . B^T for an int8 B (``math::matmul`` with transpose_B=true).
+
+    * numpy A/C: host buffers; the call copies in, runs, copies out and
+      returns with C complete (the reference's synchronous contract).
+    * torch CUDA A/C: device buffers on B's device; asynchronous on
+      ``stream`` (default: torch's current stream) unless ``flags`` has SYNC.
+    A is [M, K] or [K]; C (allocated when None) is [M, N] with any row stride.
+    """
+    if not transpose_B:
+        raise QlmError(1, "int8 weights are only supported with transpose_B=true, as in the reference")
+    lib = load()
+    if _is_torch(A):
+        import torch
+        if not A.is_cuda:
+            A = A.numpy()
+        else:
+            a2 = A if A.dim() == 2 else A.view(1, -1)
+            if a2.dtype != torch.float32 or a2.stride(1) != 1:
+                raise QlmError(1, "A must be float32 with unit column stride")
+            M, K = a2.shape
+            if C is None:
+                C = torch.empty((M, B.rows), dtype=torch.float32, device=A.device)
+            c2 = C if C.dim() == 2 else C.view(1, -1)
+            if c2.dtype != torch.float32 or c2.stride(1) != 1 or tuple(c2.shape) != (M, B.rows):
+                raise QlmError(1, "C must be float32 [M, N] with unit column stride")
+            st = _stream_ptr(stream) if stream is not None else torch.cuda.current_stream(A.device).cuda_stream
+            _check(lib.qlm_linear_int8(a2.data_ptr(), M, K, a2.stride(0), B.handle, c2.data_ptr(), c2.stride(0),
+                                       flags & ~HOST_IO, st))
+            return C
+    a = np.asarray(A, dtype=np.float32)
+    a2 = a if a.ndim == 2 else a.reshape(1, -1)
+    if a2.strides[1] != 4:
+        a2 = np.ascontiguousarray(a2)
+    M, K = a2.shape
+    if C is None:
+        C = np.empty((M, B.rows), np.float32)
+    c2 = C if C.ndim == 2 else C.reshape(1, -1)
+    if c2.dtype != np.float32 or c2.strides[1] != 4 or c2.shape != (M, B.rows):
+        raise QlmError(1, "C must be float32 [M, N] with unit column stride")
+    _check(lib.qlm_linear_int8(a2.ctypes.data, M, K, a2.strides[0] // 4, B.handle, c2.ctypes.data,
+                               c2.strides[0] // 4, flags | HOST_IO, _stream_ptr(stream)))
+    return C

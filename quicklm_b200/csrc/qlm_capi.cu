@@ -1,0 +1,359 @@
+// qlm_capi.cu — the C ABI declared in include/qlm_b200.h.
+//
+// Host-side responsibilities: argument validation (the reference's
+// math::matmul validates nothing; here a bad shape is an error code, never
+// undefined behaviour), device selection, weight handles, host<->device
+// staging for QLM_LINEAR_HOST_IO, and dispatch to the kernels. No call throws
+// across the ABI; every failure leaves a message for qlm_last_error().
+#include "../../include/qlm_b200.h"
+#include "qlm_device.cuh"
+#include "qlm_kernels.h"
+
+#include <cstdarg>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <mutex>
+#include <new>
+#include <string>
+#include <vector>
+
+struct qlm_w8 {
+    int device = -1;
+    int rows = 0, k = 0, k_pad = 0, nb_pad = 0;
+    int row_begin = 0, row_end = 0, n_total = 0;
+    uint8_t* q = nullptr;  // packed [rows][k_pad]
+    float* s = nullptr;    // [rows][nb_pad]
+};
+
+namespace {
+
+thread_local std::string g_err;
+
+int set_err(int code, const char* fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof(buf), fmt, ap);
+    va_end(ap);
+    g_err = buf;
+    return code;
+}
+
+int cuda_err(cudaError_t e, const char* what) {
+    if (e == cudaErrorMemoryAllocation)
+        return set_err(QLM_ERR_OUT_OF_MEMORY, "%s: %s", what, cudaGetErrorString(e));
+    return set_err(QLM_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+#define QLM_CUDA(call, what)                         \
+    do {                                             \
+        cudaError_t _e = (call);                     \
+        if (_e != cudaSuccess) return cuda_err(_e, what); \
+    } while (0)
+
+// Restores the caller's current device on scope exit.
+struct DeviceGuard {
+    int prev = -1;
+    bool ok = false;
+    explicit DeviceGuard(int dev) {
+        if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+        ok = cudaSetDevice(dev) == cudaSuccess;
+    }
+    ~DeviceGuard() {
+        if (prev >= 0) cudaSetDevice(prev);
+    }
+};
+
+constexpr int kMaxDevices = 64;
+
+struct DeviceState {
+    int sm_count = 0;
+    float* x_buf = nullptr;  // HOST_IO staging
+    size_t x_cap = 0;
+    float* y_buf = nullptr;
+    size_t y_cap = 0;
+};
+DeviceState g_dev[kMaxDevices];
+std::mutex g_dev_mu;
+
+int device_state(int dev, DeviceState** out) {
+    if (dev < 0 || dev >= kMaxDevices) return set_err(QLM_ERR_INVALID_ARG, "device %d out of range", dev);
+    std::lock_guard<std::mutex> lk(g_dev_mu);
+    DeviceState& st = g_dev[dev];
+    if (st.sm_count == 0) {
+        int sms = 0;
+        QLM_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev), "cudaDeviceGetAttribute");
+        st.sm_count = sms;
+    }
+    *out = &st;
+    return QLM_OK;
+}
+
+int ensure_buf(float** buf, size_t* cap, size_t bytes) {
+    if (*cap >= bytes) return QLM_OK;
+    if (*buf) cudaFree(*buf);
+    *buf = nullptr;
+    *cap = 0;
+    QLM_CUDA(cudaMalloc(buf, bytes), "cudaMalloc(staging)");
+    *cap = bytes;
+    return QLM_OK;
+}
+
+bool pdl_enabled() {
+    static const bool on = [] {
+        const char* e = std::getenv("QLM_PDL");
+        return !(e && e[0] == '0');
+    }();
+    return on;
+}
+
+int alloc_weight(int device, int n_total, int k, int row_begin, int row_end, qlm_w8** out) {
+    qlm_w8* w = new (std::nothrow) qlm_w8();
+    if (!w) return set_err(QLM_ERR_OUT_OF_MEMORY, "host allocation failed");
+    w->device = device;
+    w->n_total = n_total;
+    w->k = k;
+    w->k_pad = qlm::packed_k(k);
+    w->nb_pad = w->k_pad / QLM_BLOCK;
+    w->row_begin = row_begin;
+    w->row_end = row_end;
+    w->rows = row_end - row_begin;
+    cudaError_t e = cudaMalloc(&w->q, (size_t)w->rows * w->k_pad);
+    if (e == cudaSuccess) e = cudaMalloc(&w->s, (size_t)w->rows * w->nb_pad * sizeof(float));
+    if (e != cudaSuccess) {
+        if (w->q) cudaFree(w->q);
+        delete w;
+        return cuda_err(e, "cudaMalloc(weight)");
+    }
+    *out = w;
+    return QLM_OK;
+}
+
+int check_shard(int n_total, int k, int row_begin, int row_end) {
+    if (n_total <= 0 || k <= 0) return set_err(QLM_ERR_INVALID_ARG, "shape [%d, %d] must be positive", n_total, k);
+    if (row_begin < 0 || row_end > n_total || row_begin >= row_end)
+        return set_err(QLM_ERR_INVALID_ARG, "row range [%d, %d) invalid for %d rows", row_begin, row_end, n_total);
+    if (qlm::packed_k(k) < k) return set_err(QLM_ERR_INVALID_ARG, "k=%d too large", k);
+    return QLM_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int qlm_abi_version(void) { return QLM_ABI_VERSION; }
+
+const char* qlm_last_error(void) { return g_err.c_str(); }
+
+int qlm_weight_quantize_upload(const void* src, int src_dtype, int64_t src_row_stride, int n_total, int k,
+                               int row_begin, int row_end, int device, void* stream, qlm_w8** out) {
+    if (!out) return set_err(QLM_ERR_INVALID_ARG, "out is NULL");
+    *out = nullptr;
+    if (!src) return set_err(QLM_ERR_INVALID_ARG, "src is NULL");
+    if (src_dtype != QLM_SRC_F32 && src_dtype != QLM_SRC_BF16)
+        return set_err(QLM_ERR_INVALID_ARG, "unsupported source dtype %d (F32=0, BF16=1 only)", src_dtype);
+    int rc = check_shard(n_total, k, row_begin, row_end);
+    if (rc) return rc;
+    if (src_row_stride < k) return set_err(QLM_ERR_INVALID_ARG, "row stride %lld < k %d", (long long)src_row_stride, k);
+    DeviceState* st;
+    if ((rc = device_state(device, &st))) return rc;
+    DeviceGuard g(device);
+    if (!g.ok) return set_err(QLM_ERR_CUDA, "cudaSetDevice(%d) failed", device);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+
+    const size_t elem = src_dtype == QLM_SRC_BF16 ? 2 : 4;
+    cudaPointerAttributes attr;
+    bool on_device = false;
+    if (cudaPointerGetAttributes(&attr, src) == cudaSuccess)
+        on_device = attr.type == cudaMemoryTypeDevice || attr.type == cudaMemoryTypeManaged;
+    else
+        cudaGetLastError();  // clear: plain host pointers may report an error on old drivers
+
+    qlm_w8* w = nullptr;
+    if ((rc = alloc_weight(device, n_total, k, row_begin, row_end, &w))) return rc;
+
+    cudaError_t e = cudaSuccess;
+    if (on_device) {
+        const char* base = static_cast<const char*>(src) + (size_t)row_begin * src_row_stride * elem;
+        e = qlm::launch_quantize_pack(base, src_dtype, src_row_stride, w->rows, k, w->q, w->s, s);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+    } else {
+        // Stage host rows through a bounded device buffer (<= 64 MB per pass).
+        const size_t row_bytes = (size_t)k * elem;
+        int chunk = (int)((64u << 20) / row_bytes);
+        if (chunk < 1) chunk = 1;
+        if (chunk > w->rows) chunk = w->rows;
+        void* stage = nullptr;
+        e = cudaMalloc(&stage, (size_t)chunk * row_bytes);
+        for (int r = 0; e == cudaSuccess && r < w->rows; r += chunk) {
+            const int nr = (w->rows - r) < chunk ? (w->rows - r) : chunk;
+            const char* hsrc = static_cast<const char*>(src) + ((size_t)(row_begin + r) * src_row_stride) * elem;
+            e = cudaMemcpy2DAsync(stage, row_bytes, hsrc, (size_t)src_row_stride * elem, row_bytes, nr,
+                                  cudaMemcpyHostToDevice, s);
+            if (e == cudaSuccess)
+                e = qlm::launch_quantize_pack(stage, src_dtype, k, nr, k, w->q + (size_t)r * w->k_pad,
+                                              w->s + (size_t)r * w->nb_pad, s);
+        }
+        if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+        if (stage) cudaFree(stage);
+    }
+    if (e != cudaSuccess) {
+        qlm_weight_free(w);
+        return cuda_err(e, "quantize/upload");
+    }
+    *out = w;
+    return QLM_OK;
+}
+
+int qlm_weight_import_int8(const int8_t* q, const float* scales, int n_total, int k, int row_begin, int row_end,
+                           int device, void* stream, qlm_w8** out) {
+    if (!out) return set_err(QLM_ERR_INVALID_ARG, "out is NULL");
+    *out = nullptr;
+    if (!q || !scales) return set_err(QLM_ERR_INVALID_ARG, "q/scales is NULL");
+    int rc = check_shard(n_total, k, row_begin, row_end);
+    if (rc) return rc;
+    DeviceState* st;
+    if ((rc = device_state(device, &st))) return rc;
+    DeviceGuard g(device);
+    if (!g.ok) return set_err(QLM_ERR_CUDA, "cudaSetDevice(%d) failed", device);
+
+    const int k_pad = qlm::packed_k(k), nb_pad = k_pad / QLM_BLOCK, nb = (k + QLM_BLOCK - 1) / QLM_BLOCK;
+    const int rows = row_end - row_begin;
+    std::vector<uint8_t> hq;
+    std::vector<float> hs;
+    try {
+        hq.assign((size_t)rows * k_pad, 0);
+        hs.assign((size_t)rows * nb_pad, 0.0f);
+    } catch (...) {
+        return set_err(QLM_ERR_OUT_OF_MEMORY, "host staging allocation failed");
+    }
+    for (int r = 0; r < rows; ++r) {
+        const int8_t* src = q + (size_t)(row_begin + r) * k;
+        uint8_t* dst = hq.data() + (size_t)r * k_pad;
+        for (int kk = 0; kk < k; ++kk) dst[qlm::packed_offset(kk)] = (uint8_t)src[kk];
+        std::memcpy(hs.data() + (size_t)r * nb_pad, scales + (size_t)(row_begin + r) * nb, nb * sizeof(float));
+    }
+    qlm_w8* w = nullptr;
+    if ((rc = alloc_weight(device, n_total, k, row_begin, row_end, &w))) return rc;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    cudaError_t e = cudaMemcpyAsync(w->q, hq.data(), hq.size(), cudaMemcpyHostToDevice, s);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(w->s, hs.data(), hs.size() * sizeof(float), cudaMemcpyHostToDevice, s);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+    if (e != cudaSuccess) {
+        qlm_weight_free(w);
+        return cuda_err(e, "import upload");
+    }
+    *out = w;
+    return QLM_OK;
+}
+
+int qlm_weight_export_int8(const qlm_w8* w, int8_t* q, float* scales) {
+    if (!w || !q || !scales) return set_err(QLM_ERR_INVALID_ARG, "NULL argument");
+    DeviceGuard g(w->device);
+    if (!g.ok) return set_err(QLM_ERR_CUDA, "cudaSetDevice(%d) failed", w->device);
+    const int nb = (w->k + QLM_BLOCK - 1) / QLM_BLOCK;
+    std::vector<uint8_t> hq;
+    std::vector<float> hs;
+    try {
+        hq.resize((size_t)w->rows * w->k_pad);
+        hs.resize((size_t)w->rows * w->nb_pad);
+    } catch (...) {
+        return set_err(QLM_ERR_OUT_OF_MEMORY, "host staging allocation failed");
+    }
+    QLM_CUDA(cudaMemcpy(hq.data(), w->q, hq.size(), cudaMemcpyDeviceToHost), "export q");
+    QLM_CUDA(cudaMemcpy(hs.data(), w->s, hs.size() * sizeof(float), cudaMemcpyDeviceToHost), "export scales");
+    for (int r = 0; r < w->rows; ++r) {
+        const uint8_t* src = hq.data() + (size_t)r * w->k_pad;
+        int8_t* dst = q + (size_t)r * w->k;
+        for (int kk = 0; kk < w->k; ++kk) dst[kk] = (int8_t)src[qlm::packed_offset(kk)];
+        std::memcpy(scales + (size_t)r * nb, hs.data() + (size_t)r * w->nb_pad, nb * sizeof(float));
+    }
+    return QLM_OK;
+}
+
+int qlm_weight_shape(const qlm_w8* w, int* rows, int* k, int* row_begin, int* row_end, int* n_total) {
+    if (!w) return set_err(QLM_ERR_INVALID_ARG, "NULL handle");
+    if (rows) *rows = w->rows;
+    if (k) *k = w->k;
+    if (row_begin) *row_begin = w->row_begin;
+    if (row_end) *row_end = w->row_end;
+    if (n_total) *n_total = w->n_total;
+    return QLM_OK;
+}
+
+int64_t qlm_weight_bytes(const qlm_w8* w) {
+    if (!w) return 0;
+    return (int64_t)w->rows * w->k_pad + (int64_t)w->rows * w->nb_pad * (int64_t)sizeof(float);
+}
+
+void qlm_weight_free(qlm_w8* w) {
+    if (!w) return;
+    DeviceGuard g(w->device);
+    if (w->q) cudaFree(w->q);
+    if (w->s) cudaFree(w->s);
+    delete w;
+}
+
+int qlm_linear_int8(const float* x, int M, int k, int64_t ldx, const qlm_w8* w, float* y, int64_t ldy, int flags,
+                    void* stream) {
+    if (!x || !y || !w) return set_err(QLM_ERR_INVALID_ARG, "NULL argument");
+    if (M <= 0) return set_err(QLM_ERR_INVALID_ARG, "M=%d must be >= 1", M);
+    if (k != w->k) return set_err(QLM_ERR_INVALID_ARG, "k=%d does not match the weight's k=%d", k, w->k);
+    if (ldx < k) return set_err(QLM_ERR_INVALID_ARG, "ldx %lld < k %d", (long long)ldx, k);
+    if (ldy < w->rows) return set_err(QLM_ERR_INVALID_ARG, "ldy %lld < rows %d", (long long)ldy, w->rows);
+    if (flags & ~(QLM_LINEAR_TENSOR | QLM_LINEAR_HOST_IO | QLM_LINEAR_SYNC))
+        return set_err(QLM_ERR_INVALID_ARG, "unknown flags 0x%x", flags);
+    if (flags & QLM_LINEAR_TENSOR)
+        return set_err(QLM_ERR_UNSUPPORTED, "tensor-core path not available in this build");
+    DeviceState* st;
+    int rc = device_state(w->device, &st);
+    if (rc) return rc;
+    DeviceGuard g(w->device);
+    if (!g.ok) return set_err(QLM_ERR_CUDA, "cudaSetDevice(%d) failed", w->device);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+
+    // Rows of x per launch: all activations of a launch live in shared memory.
+    const size_t budget = 96 * 1024, hard = 200 * 1024;
+    int mm = 8;
+    while (mm > 1 && qlm::gemv_smem_bytes(mm, k) > budget) --mm;
+    if (qlm::gemv_smem_bytes(mm, k) > hard)
+        return set_err(QLM_ERR_UNSUPPORTED, "k=%d exceeds the exact path's shared-memory staging limit", k);
+
+    const float* dx = x;
+    float* dy = y;
+    int64_t dldx = ldx, dldy = ldy;
+    const bool host_io = (flags & QLM_LINEAR_HOST_IO) != 0;
+    if (host_io) {
+        std::lock_guard<std::mutex> lk(g_dev_mu);
+        if ((rc = ensure_buf(&st->x_buf, &st->x_cap, (size_t)M * k * sizeof(float)))) return rc;
+        if ((rc = ensure_buf(&st->y_buf, &st->y_cap, (size_t)M * w->rows * sizeof(float)))) return rc;
+        QLM_CUDA(cudaMemcpy2DAsync(st->x_buf, (size_t)k * sizeof(float), x, (size_t)ldx * sizeof(float),
+                                   (size_t)k * sizeof(float), M, cudaMemcpyHostToDevice, s),
+                 "copy x to device");
+        dx = st->x_buf;
+        dy = st->y_buf;
+        dldx = k;
+        dldy = w->rows;
+    }
+    for (int m0 = 0; m0 < M; m0 += mm) {
+        const int g_rows = (M - m0) < mm ? (M - m0) : mm;
+        QLM_CUDA(qlm::launch_gemv_exact(dx + (int64_t)m0 * dldx, dldx, g_rows, w->q, w->s, w->rows, k,
+                                        dy + (int64_t)m0 * dldy, dldy, st->sm_count, s, pdl_enabled()),
+                 "gemv launch");
+    }
+    if (host_io) {
+        QLM_CUDA(cudaMemcpy2DAsync(y, (size_t)ldy * sizeof(float), dy, (size_t)w->rows * sizeof(float),
+                                   (size_t)w->rows * sizeof(float), M, cudaMemcpyDeviceToHost, s),
+                 "copy y to host");
+    }
+    if (host_io || (flags & QLM_LINEAR_SYNC)) QLM_CUDA(cudaStreamSynchronize(s), "stream synchronize");
+    return QLM_OK;
+}
+
+int qlm_stream_sync(void* stream) {
+    QLM_CUDA(cudaStreamSynchronize(static_cast<cudaStream_t>(stream)), "cudaStreamSynchronize");
+    return QLM_OK;
+}
+
+}  // extern "C"

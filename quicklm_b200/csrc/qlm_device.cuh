@@ -1,0 +1,73 @@
+// qlm_device.cuh — device-side helpers shared by the sm_100a kernels.
+//
+// Packed int8 weight layout in HBM ("P128"), chosen for the decode GEMV:
+//   k_pad  = round_up(k, 128), nb_pad = k_pad / 32
+//   q      : uint8 [rows][k_pad]; element k of row r lives at byte
+//            r*k_pad + (k/128)*128 + (k%8)*16 + ((k/32)%4)*4 + (k%32)/8
+//   scales : fp32  [rows][nb_pad]; scale of block b of row r at r*nb_pad + b
+// Inside one 128-element chunk, the 16 bytes at offset l*16 are exactly the
+// elements "lane" l of the reference kernel consumes from the chunk's four
+// 32-blocks (k = 32*bb + 8*j + l, byte bb*4 + j): one 128-bit load per lane per
+// chunk, and the 8 lanes of a row read one contiguous 128-byte line.
+// Padding bytes are 0 and padding scales are 0; kernels never fold them in.
+#pragma once
+
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace qlm {
+
+constexpr int kBlock = 32;   // Tensor::INT8_BLOCK_SIZE
+constexpr int kChunk = 128;  // elements per packed chunk (4 blocks)
+
+__host__ __device__ inline int round_up(int v, int m) { return (v + m - 1) / m * m; }
+__host__ __device__ inline int packed_k(int k) { return round_up(k, kChunk); }
+
+// Byte offset of element k within a packed row.
+__host__ __device__ inline int packed_offset(int k) {
+    return (k & ~(kChunk - 1)) + (k & 7) * 16 + ((k >> 5) & 3) * 4 + ((k >> 3) & 3);
+}
+
+// Position of x[k] in the permuted activation staging used by the GEMV:
+// chunk c, block bb, lane l, j -> c*128 + bb*32 + l*4 + j, so lane l reads
+// the four x values of block bb as one float4 (conflict-free across lanes).
+__host__ __device__ inline int xperm_offset(int k) {
+    return (k & ~(kChunk - 1)) + ((k >> 5) & 3) * 32 + (k & 7) * 4 + ((k >> 3) & 3);
+}
+
+// Exact int8 -> fp32 for the 4 signed bytes of w: byte j (0..3) is biased to
+// u = q + 128 and placed in the low mantissa of 2^23, so the float is exactly
+// 2^23 + u; subtracting 2^23 + 128 is exact. Returns q_j as fp32 in f[j].
+__device__ __forceinline__ void s8x4_to_f32(uint32_t w, float f[4]) {
+    const uint32_t u = w ^ 0x80808080u;
+    const float bias = 8388736.0f;  // 2^23 + 128
+    f[0] = __fsub_rn(__uint_as_float(__byte_perm(u, 0x4B000000u, 0x7540)), bias);
+    f[1] = __fsub_rn(__uint_as_float(__byte_perm(u, 0x4B000000u, 0x7541)), bias);
+    f[2] = __fsub_rn(__uint_as_float(__byte_perm(u, 0x4B000000u, 0x7542)), bias);
+    f[3] = __fsub_rn(__uint_as_float(__byte_perm(u, 0x4B000000u, 0x7543)), bias);
+}
+
+// Streaming 128-bit load that does not allocate in L1 (weights are read once).
+__device__ __forceinline__ uint4 ldg_stream_u4(const void* p) {
+    uint4 r;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+                 : "l"(p));
+    return r;
+}
+
+__device__ __forceinline__ float4 ldg_f4(const void* p) {
+    float4 r;
+    asm volatile("ld.global.nc.v4.f32 {%0,%1,%2,%3}, [%4];"
+                 : "=f"(r.x), "=f"(r.y), "=f"(r.z), "=f"(r.w)
+                 : "l"(p));
+    return r;
+}
+
+// Programmatic dependent launch (sm_90+): let the next kernel in the stream
+// start launching, and wait until the previous kernel's results are visible.
+// Both are no-ops when the launch did not opt in.
+__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+}  // namespace qlm

@@ -1,0 +1,155 @@
+// qlm_quant.cu — load-time int8 quantize-and-pack on the device.
+//
+// Replaces st_quantize_row_f32 / st_quantize_row_bf16 (QuickLM
+// src/io/safetensors.cpp:348-391 / 296-345) as driven by
+// get_tensor_keep_int8 (src/io/safetensors.cpp:517-585). Per 32-element block:
+//   max_abs = max |v| (8 strided lanes, then the fixed 8->1 tree, then a
+//             scalar pass over the < 8 elements left in a ragged block)
+//   scale   = max_abs > 0 ? max_abs / 127 : 1          (IEEE division)
+//   inv     = 1 / scale                                (IEEE division)
+//   q       = clamp(round(v * inv), -127, 127)
+// with round-half-even for elements covered by an 8-wide step and
+// round-half-away (lround) for the scalar remainder, exactly as the reference.
+// NaN/Inf follow the x86 semantics the reference inherits (MAXPS returns its
+// second operand when unordered; cvtps2dq returns 0x80000000; (int)lround of
+// NaN/Inf is 0), so the bytes and scales are identical for every input.
+//
+// Work mapping: one warp per (row, 32 consecutive blocks). The warp stages the
+// 1024 source values through shared memory with coalesced loads, each lane
+// quantizes one block, and the packed bytes go back out through shared memory
+// as one contiguous 1 KB store (the P128 layout keeps 8 chunks contiguous).
+#include "qlm_device.cuh"
+#include "qlm_kernels.h"
+
+namespace qlm {
+namespace {
+
+constexpr int kWarpsPerCta = 8;
+
+__device__ __forceinline__ float maxps(float a, float b) { return (a > b) ? a : b; }
+__device__ __forceinline__ float stdmax(float a, float b) { return (a < b) ? b : a; }
+
+__device__ __forceinline__ int32_t cvt_rne_indefinite(float v) {
+    const float r = rintf(v);  // cvt.rni: round to nearest, ties to even
+    if (!(fabsf(r) < 2147483648.0f)) return INT32_MIN;
+    return (int32_t)r;
+}
+
+// (int)std::lround(v): ties away from zero; NaN/Inf/|v| >= 2^63 give
+// (int)LONG_MIN == 0; otherwise the low 32 bits of the long.
+__device__ __forceinline__ int32_t cvt_lround_int(float v) {
+    if (!(fabsf(v) < 9.2233720368547758e18f)) return 0;
+    float t = truncf(v);
+    if (fabsf(__fsub_rn(v, t)) >= 0.5f) t = __fadd_rn(t, copysignf(1.0f, v));
+    const long long l = (long long)t;
+    return (int32_t)(uint32_t)(unsigned long long)l;
+}
+
+__device__ __forceinline__ uint32_t clamp127_byte(int32_t q) {
+    q = q < -127 ? -127 : (q > 127 ? 127 : q);
+    return (uint32_t)(q & 0xFF);
+}
+
+__device__ __forceinline__ float load_src(const void* src, int dtype, int64_t idx) {
+    if (dtype == 1) {
+        const uint16_t h = static_cast<const uint16_t*>(src)[idx];
+        return __uint_as_float((uint32_t)h << 16);
+    }
+    return static_cast<const float*>(src)[idx];
+}
+
+__global__ void __launch_bounds__(kWarpsPerCta * 32)
+quantize_pack_kernel(const void* __restrict__ src, int dtype, int64_t src_stride, int rows, int k,
+                     int k_pad, uint8_t* __restrict__ q, float* __restrict__ scales) {
+    __shared__ float vals[kWarpsPerCta][32][33];
+    __shared__ __align__(16) uint8_t packed[kWarpsPerCta][1024];
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int nb_pad = k_pad / kBlock;
+    const int nseg = (nb_pad + 31) / 32;
+    const int64_t gw = (int64_t)blockIdx.x * kWarpsPerCta + warp;
+    if (gw >= (int64_t)rows * nseg) return;  // whole warp exits together
+    const int row = (int)(gw / nseg), seg = (int)(gw % nseg);
+    const int64_t base = (int64_t)row * src_stride;
+    const int e0 = seg * 1024;
+
+    // Coalesced staging: element e0 + 32*i + lane -> vals[i][lane].
+#pragma unroll 4
+    for (int i = 0; i < 32; ++i) {
+        const int e = e0 + 32 * i + lane;
+        vals[warp][i][lane] = (e < k) ? load_src(src, dtype, base + e) : 0.0f;
+    }
+    __syncwarp();
+
+    const int blk = seg * 32 + lane;  // this lane's block
+    const int k0 = blk * kBlock;
+    uint32_t words[8];  // word l holds bytes j=0..3 of lane l for this block
+    float scale = 0.0f;
+    if (blk < nb_pad && k0 < k) {
+        const int k1 = min(k0 + kBlock, k);
+        const float* v = vals[warp][lane];  // v[i] = element k0 + i
+        const int len = k1 - k0;
+        float lanemax[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        int i = 0;
+        for (; i + 8 <= len; i += 8)
+#pragma unroll
+            for (int t = 0; t < 8; ++t) lanemax[t] = maxps(lanemax[t], fabsf(v[i + t]));
+        float m0 = maxps(lanemax[0], lanemax[4]), m1 = maxps(lanemax[1], lanemax[5]);
+        const float m2 = maxps(lanemax[2], lanemax[6]), m3 = maxps(lanemax[3], lanemax[7]);
+        m0 = maxps(m0, m2);
+        m1 = maxps(m1, m3);
+        float max_abs = maxps(m0, m1);
+        for (; i < len; ++i) max_abs = stdmax(max_abs, fabsf(v[i]));
+        scale = (max_abs > 0.0f) ? __fdiv_rn(max_abs, 127.0f) : 1.0f;
+        const float inv = __fdiv_rn(1.0f, scale);
+        const int vec_end = len & ~7;  // elements handled by 8-wide steps
+#pragma unroll
+        for (int l = 0; l < 8; ++l) {
+            uint32_t w = 0;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const int e = 8 * j + l;
+                uint32_t b = 0;
+                if (e < len) {
+                    const float p = __fmul_rn(v[e], inv);
+                    b = clamp127_byte(e < vec_end ? cvt_rne_indefinite(p) : cvt_lround_int(p));
+                }
+                w |= b << (8 * j);
+            }
+            words[l] = w;
+        }
+    } else {
+#pragma unroll
+        for (int l = 0; l < 8; ++l) words[l] = 0u;
+    }
+    if (blk < nb_pad) scales[(int64_t)row * nb_pad + blk] = scale;
+
+    // Packed position inside this segment's 1 KB: chunk (lane/4), lane l, block lane%4.
+    uint32_t* pw = reinterpret_cast<uint32_t*>(packed[warp]);
+#pragma unroll
+    for (int l = 0; l < 8; ++l) pw[(lane >> 2) * 32 + l * 4 + (lane & 3)] = words[l];
+    __syncwarp();
+
+    // 1 KB = 64 uint4; the segment may stop short of 8 chunks at the row end.
+    const int chunks = min(8, nb_pad / 4 - seg * 8);
+    uint4* dst = reinterpret_cast<uint4*>(q + (int64_t)row * k_pad + (int64_t)seg * 1024);
+    const uint4* s4 = reinterpret_cast<const uint4*>(packed[warp]);
+    for (int i = lane; i < chunks * 8; i += 32) dst[i] = s4[i];
+}
+
+}  // namespace
+
+cudaError_t launch_quantize_pack(const void* src, int dtype, int64_t src_stride, int rows, int k, uint8_t* q,
+                                 float* scales, cudaStream_t stream) {
+    if (rows <= 0) return cudaSuccess;
+    const int k_pad = packed_k(k);
+    const int nseg = (k_pad / kBlock + 31) / 32;
+    const int64_t warps = (int64_t)rows * nseg;
+    const int64_t ctas = (warps + kWarpsPerCta - 1) / kWarpsPerCta;
+    if (ctas > 0x7fffffffLL) return cudaErrorInvalidValue;
+    quantize_pack_kernel<<<(unsigned)ctas, kWarpsPerCta * 32, 0, stream>>>(src, dtype, src_stride, rows, k, k_pad,
+                                                                            q, scales);
+    return cudaGetLastError();
+}
+
+}  // namespace qlm

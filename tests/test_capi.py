@@ -1,0 +1,65 @@
+"""CPU-only checks of the C ABI library: it loads without a GPU, exports every
+symbol include/qlm_b200.h declares, and rejects bad arguments on the host
+before touching a device."""
+from __future__ import annotations
+
+import ctypes
+import os
+import re
+
+import numpy as np
+import pytest
+
+from tests.conftest import ROOT
+
+
+def header_functions():
+    with open(os.path.join(ROOT, "include", "qlm_b200.h")) as f:
+        text = f.read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(qlm_[a-z0-9_]+)\s*\(", text)))
+
+
+def test_header_symbols_exported(qlm_lib):
+    import quicklm_b200 as q
+    names = header_functions()
+    assert set(names) == set(q.ABI_SYMBOLS), "binding list out of sync with the header"
+    for name in names:
+        assert hasattr(qlm_lib, name), f"{name} not exported"
+
+
+def test_abi_version(qlm_lib):
+    assert qlm_lib.qlm_abi_version() == 1
+
+
+def test_null_args_rejected_on_host(qlm_lib):
+    import quicklm_b200 as q
+    rc = qlm_lib.qlm_linear_int8(None, 1, 16, 16, None, None, 16, 0, None)
+    assert rc == 1
+    assert b"NULL" in qlm_lib.qlm_last_error()
+    out = ctypes.c_void_p()
+    w = np.zeros((4, 8), np.float32)
+    rc = qlm_lib.qlm_weight_quantize_upload(w.ctypes.data, 7, 8, 4, 8, 0, 4, 0, None, ctypes.byref(out))
+    assert rc == 1 and b"dtype" in qlm_lib.qlm_last_error()
+    rc = qlm_lib.qlm_weight_quantize_upload(w.ctypes.data, 0, 8, 4, 8, 2, 1, 0, None, ctypes.byref(out))
+    assert rc == 1 and b"row range" in qlm_lib.qlm_last_error()
+    rc = qlm_lib.qlm_weight_quantize_upload(w.ctypes.data, 0, 4, 4, 8, 0, 4, 0, None, ctypes.byref(out))
+    assert rc == 1 and b"stride" in qlm_lib.qlm_last_error()
+    with pytest.raises(q.QlmError):
+        q._check(1)
+
+
+def test_weight_free_null_is_noop(qlm_lib):
+    qlm_lib.qlm_weight_free(None)
+    assert qlm_lib.qlm_weight_bytes(None) == 0
+
+
+def test_no_oracle_in_product():
+    """The product package never imports or links the checkers."""
+    pkg = os.path.join(ROOT, "quicklm_b200")
+    for dirpath, _, files in os.walk(pkg):
+        for fn in files:
+            if fn.endswith((".py", ".cu", ".cuh", ".h", ".cpp")):
+                with open(os.path.join(dirpath, fn), errors="ignore") as f:
+                    text = f.read()
+                assert "oracle" not in re.sub(r"(#|//).*", "", text).lower().replace("oracle/", ""), fn

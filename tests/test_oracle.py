@@ -1,0 +1,96 @@
+"""Pins the CPU restatement (oracle/qlm_oracle.c) to QuickLM's own code.
+
+The reference ships no tests or golden vectors for this path, so the pin is
+the reference itself, compiled from its sources (oracle/_ref), and the
+fixtures generated from it (tests/golden/make_golden.py).
+"""
+from __future__ import annotations
+
+import hashlib
+import os
+
+import numpy as np
+import pytest
+
+from tests.conftest import GOLDEN, bits_equal
+from tests.golden.cases import CFG1, CFG4, make_small_case
+
+
+def sha(a):
+    return hashlib.sha256(np.ascontiguousarray(a).tobytes()).hexdigest()
+
+
+def test_small_cases_regenerate(small_cases):
+    """The stored inputs are exactly what the seeded generator makes."""
+    for spec, arr in small_cases:
+        x, w = make_small_case(spec)
+        assert bits_equal(x, arr["x"]), spec
+        assert np.array_equal(w.view(np.uint8), arr["w"].view(np.uint8)), spec
+
+
+def test_c_oracle_quantize_matches_golden(coracle, small_cases):
+    for spec, arr in small_cases:
+        q, s = coracle.quantize(arr["w"])
+        assert np.array_equal(q, arr["q"]), spec
+        assert np.array_equal(s.view(np.uint32), arr["s"].view(np.uint32)), spec
+
+
+def test_c_oracle_matmul_matches_golden(coracle, small_cases):
+    for spec, arr in small_cases:
+        y = coracle.matmul(arr["x"], arr["q"], arr["s"])
+        assert bits_equal(y, arr["y"]), spec
+
+
+def test_reference_build_matches_golden(refcpu, small_cases):
+    """The prebuilt reference library reproduces the fixtures it generated."""
+    for spec, arr in small_cases:
+        q, s = refcpu.quantize(arr["w"])
+        assert np.array_equal(q, arr["q"]), spec
+        y, _ = refcpu.matmul(arr["x"], arr["q"], arr["s"])
+        assert bits_equal(y, arr["y"]), spec
+
+
+def test_cfg1_pinned(coracle, config_hashes):
+    """Config 1 end to end through the C restatement equals the reference's bytes."""
+    m, n, k, seed = CFG1
+    from oracle.oracle import synth_case
+    x, w = synth_case(m, n, k, seed)
+    h = config_hashes["cfg1"]
+    assert sha(w) == h["w"] and sha(x) == h["x"], "seeded generator drifted"
+    q, s = coracle.quantize(w)
+    assert sha(q) == h["q"] and sha(s) == h["s"]
+    y = coracle.matmul(x, q, s)
+    assert sha(y) == h["y"]
+    assert bits_equal(y, np.load(os.path.join(GOLDEN, "cfg1_y.npy")))
+
+
+@pytest.mark.parametrize("m,n,k,seed", [c for c in CFG4 if c[1] <= 2560 and c[0] <= 8][:6])
+def test_cfg4_small_m_pinned(coracle, config_hashes, m, n, k, seed):
+    from oracle.oracle import synth_case
+    x, w = synth_case(m, n, k, seed)
+    h = config_hashes[f"cfg4_m{m}_n{n}_k{k}"]
+    q, s = coracle.quantize(w)
+    assert sha(q) == h["q"] and sha(s) == h["s"]
+    assert sha(coracle.matmul(x, q, s)) == h["y"]
+
+
+def test_fuzz_c_oracle_vs_reference(coracle, refcpu):
+    """Random shapes and special values: restatement == reference, bit for bit."""
+    rng = np.random.default_rng(1234)
+    for trial in range(120):
+        n = int(rng.integers(1, 12))
+        k = int(rng.integers(1, 260))
+        m = int(rng.integers(1, 4))
+        w = (rng.standard_normal((n, k)) * 10.0 ** rng.integers(-42, 8)).astype(np.float32)
+        u = rng.random((n, k))
+        w[u < 0.02] = np.nan
+        w[(u >= 0.02) & (u < 0.04)] = np.inf
+        w[(u >= 0.04) & (u < 0.1)] = 0.0
+        if trial % 2:
+            w = (w.view(np.uint32) >> 16).astype(np.uint16)
+        q1, s1 = refcpu.quantize(w)
+        q2, s2 = coracle.quantize(w)
+        assert np.array_equal(q1, q2) and np.array_equal(s1.view(np.uint32), s2.view(np.uint32))
+        x = (rng.standard_normal((m, k)) * 10.0 ** rng.integers(-30, 20)).astype(np.float32)
+        y1, _ = refcpu.matmul(x, q1, s1)
+        assert bits_equal(y1, coracle.matmul(x, q1, s1))
