@@ -294,8 +294,8 @@ def main():
         q_ref, s_ref = weights[0].to_int8()
         base = cpu_baseline(x_np, q_ref, s_ref, args.cpu_seconds)
 
-    if graph is not None:
-        del graph
+    used_graph = graph is not None
+    graph = None
     if rank == 0:
         line = {
             "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
@@ -306,7 +306,7 @@ def main():
                                    f"{STACK} distinct weight copies per step",
                        "l2": f"inputs larger than L2 ({STACK}x{weight_bytes() / 1e6:.2f} MB weights per step)",
                        "parallelism": "single GPU" if world == 1 else f"row-sharded x{world} + NCCL all-gather",
-                       "kernel": "gemv_exact_kernel<1> (CUDA cores, bit-exact)", "cuda_graph": graph is not None,
+                       "kernel": "gemv_exact_kernel<1> (CUDA cores, bit-exact)", "cuda_graph": used_graph,
                        "pdl": os.environ.get("QLM_PDL", "1") != "0"},
             "pct_hbm_peak": round(100.0 * value / world / peak, 2),
             "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": peak, "unit": "GB/s",
