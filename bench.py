@@ -122,6 +122,59 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
+def measured_tflops():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return float(d["bf16_tflops"]), "measured bf16 burst"
+    return 1590.0, "fallback bf16 burst"
+
+
+def prefill_leg(qlm, torch, steps=50, warmup=5):
+    """Tensor-core prefill GEMM at config 2, M=512: x [512, 2048] . W^T with W
+    [6144, 2048] int8, over 16 rotating weight copies (> L2). Device time with
+    CUDA events; FLOPs = 2*M*N*K per launch."""
+    from oracle.oracle import synth_case
+    m, n, k = 512, 6144, 2048
+    x_np, w_np = synth_case(m, n, k, 2)
+    wd = torch.from_numpy(w_np).cuda()
+    ws = [qlm.Int8Weight.quantize(wd) for _ in range(STACK)]
+    del wd
+    x = torch.from_numpy(x_np).cuda()
+    y = torch.empty((m, n), device="cuda")
+    stream = torch.cuda.Stream()
+    with torch.cuda.stream(stream):
+        for i in range(warmup * STACK):
+            qlm.matmul(x, ws[i % STACK], y, flags=qlm.TENSOR, stream=stream)
+    torch.cuda.synchronize()
+    y_ex = qlm.matmul(x, ws[0], flags=qlm.SYNC)
+    y_tc = qlm.matmul(x, ws[0], flags=qlm.TENSOR | qlm.SYNC)
+    err = float(torch.linalg.norm((y_tc - y_ex).double()) / torch.linalg.norm(y_ex.double()))
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record(stream)
+    with torch.cuda.stream(stream):
+        for i in range(steps * STACK):
+            qlm.matmul(x, ws[i % STACK], y, flags=qlm.TENSOR, stream=stream)
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    ms = ev0.elapsed_time(ev1)
+    launches = steps * STACK
+    per_launch_s = ms / 1000.0 / launches
+    tflops = 2.0 * m * n * k / per_launch_s / 1e12
+    peak, kind = measured_tflops()
+    st = qlm.load().qlm_device_status(0, 1)
+    for w in ws:
+        w.free()
+    return {"metric": "prefill GEMM TFLOP/s (cfg2 M=512, [6144,2048])", "value": round(tflops, 2),
+            "unit": "TFLOP/s", "mean_launch_us": per_launch_s * 1e6,
+            "kernels": "act_to_f16_kernel + gemm_tc_kernel<256> (tcgen05 kind::f16, fp32 accumulate)",
+            "rel_l2_vs_exact": err, "device_status": st,
+            "roofline": {"bound": "tensor", "achieved": round(tflops, 2), "peak": peak, "unit": "TFLOP/s",
+                         "frac": round(tflops / peak, 4), "peak_source": f"MEASURED_PEAKS.json ({kind})"},
+            "gpu_launches": 2 * launches}
+
+
 def cpu_baseline(x, q, s, seconds=10.0):
     """QuickLM's own int8 math::matmul (oracle/_ref, strict build) on this
     host's cores: M=1 GEMVs rotating over STACK copies (larger than the LLC)."""
@@ -185,6 +238,8 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--e2e-calls", type=int, default=2000)
+    ap.add_argument("--no-prefill", action="store_true")
+    ap.add_argument("--prefill-steps", type=int, default=50)
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.impl == "reference":
@@ -289,6 +344,13 @@ def main():
         e2e_s = float(t.item())
     e2e = args.e2e_calls * weight_bytes() * world / e2e_s / 1e9
 
+    prefill = None
+    if world == 1 and not args.no_prefill:
+        try:
+            prefill = prefill_leg(qlm, torch, steps=args.prefill_steps)
+        except Exception as exc:  # reported, never hidden
+            prefill = {"error": f"{type(exc).__name__}: {exc}"}
+
     base = None
     if rank == 0 and not args.no_cpu_baseline:
         q_ref, s_ref = weights[0].to_int8()
@@ -319,6 +381,7 @@ def main():
             "gpu_launches": launches,
             "clocks": clk,
             "cpu_baseline": base,
+            "prefill": prefill,
         }
         print(json.dumps(line), flush=True)
     for w in weights:

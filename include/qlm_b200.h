@@ -110,11 +110,16 @@ void qlm_weight_free(qlm_w8* w);
  *   x:    [M, k] fp32, row stride ldx (>= k)
  *   y:    [M, rows] fp32, row stride ldy (>= rows); overwritten, not accumulated
  *   flags QLM_LINEAR_*; device pointers unless QLM_LINEAR_HOST_IO.
- * The exact path accepts any M >= 1; QLM_LINEAR_TENSOR needs M >= 1 and k a
- * multiple of 64 and falls back to nothing: it returns QLM_ERR_UNSUPPORTED if
- * the shape does not qualify. Asynchronous on `stream` unless HOST_IO/SYNC. */
+ * Both paths accept any M >= 1 and any k (the exact path up to k = 51200).
+ * QLM_LINEAR_TENSOR is never substituted silently: the caller chooses it.
+ * Asynchronous on `stream` unless HOST_IO/SYNC. */
 int qlm_linear_int8(const float* x, int M, int k, int64_t ldx, const qlm_w8* w, float* y, int64_t ldy, int flags,
                     void* stream);
+
+/* Status of bounded device-side waits on `device`: QLM_OK, or QLM_ERR_TIMEOUT
+ * if a kernel gave up waiting since the last reset (reset != 0 clears it).
+ * Synchronous tensor-core calls check this themselves. */
+int qlm_device_status(int device, int reset);
 
 /* Block until all work queued on `stream` is done (reports async errors). */
 int qlm_stream_sync(void* stream);

@@ -24,6 +24,8 @@ struct qlm_w8 {
     int row_begin = 0, row_end = 0, n_total = 0;
     uint8_t* q = nullptr;  // packed [rows][k_pad]
     float* s = nullptr;    // [rows][nb_pad]
+    int* ew = nullptr;     // [rows] range exponents for the tensor-core path
+    qlm::TcMaps* maps = nullptr;  // TMA descriptors, built on first tensor-core use
 };
 
 namespace {
@@ -73,6 +75,11 @@ struct DeviceState {
     size_t x_cap = 0;
     float* y_buf = nullptr;
     size_t y_cap = 0;
+    void* x16 = nullptr;     // tensor-core path: fp16 activations
+    size_t x16_cap = 0;
+    int* ea = nullptr;       // tensor-core path: activation row exponents
+    size_t ea_cap = 0;
+    int* status = nullptr;   // device status word written by kernels on a timeout
 };
 DeviceState g_dev[kMaxDevices];
 std::mutex g_dev_mu;
@@ -84,18 +91,26 @@ int device_state(int dev, DeviceState** out) {
     if (st.sm_count == 0) {
         int sms = 0;
         QLM_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev), "cudaDeviceGetAttribute");
+        int prev = -1;
+        QLM_CUDA(cudaGetDevice(&prev), "cudaGetDevice");
+        QLM_CUDA(cudaSetDevice(dev), "cudaSetDevice");
+        cudaError_t e = cudaMalloc(&st.status, sizeof(int));
+        if (e == cudaSuccess) e = cudaMemset(st.status, 0, sizeof(int));
+        cudaSetDevice(prev);
+        if (e != cudaSuccess) return cuda_err(e, "device status word");
         st.sm_count = sms;
     }
     *out = &st;
     return QLM_OK;
 }
 
-int ensure_buf(float** buf, size_t* cap, size_t bytes) {
+template <typename T>
+int ensure_buf(T** buf, size_t* cap, size_t bytes) {
     if (*cap >= bytes) return QLM_OK;
     if (*buf) cudaFree(*buf);
     *buf = nullptr;
     *cap = 0;
-    QLM_CUDA(cudaMalloc(buf, bytes), "cudaMalloc(staging)");
+    QLM_CUDA(cudaMalloc(reinterpret_cast<void**>(buf), bytes), "cudaMalloc(scratch)");
     *cap = bytes;
     return QLM_OK;
 }
@@ -121,8 +136,10 @@ int alloc_weight(int device, int n_total, int k, int row_begin, int row_end, qlm
     w->rows = row_end - row_begin;
     cudaError_t e = cudaMalloc(&w->q, (size_t)w->rows * w->k_pad);
     if (e == cudaSuccess) e = cudaMalloc(&w->s, (size_t)w->rows * w->nb_pad * sizeof(float));
+    if (e == cudaSuccess) e = cudaMalloc(&w->ew, (size_t)w->rows * sizeof(int));
     if (e != cudaSuccess) {
         if (w->q) cudaFree(w->q);
+        if (w->s) cudaFree(w->s);
         delete w;
         return cuda_err(e, "cudaMalloc(weight)");
     }
@@ -198,6 +215,8 @@ int qlm_weight_quantize_upload(const void* src, int src_dtype, int64_t src_row_s
         if (e == cudaSuccess) e = cudaStreamSynchronize(s);
         if (stage) cudaFree(stage);
     }
+    if (e == cudaSuccess) e = qlm::launch_weight_exponents(w->s, w->rows, k, w->ew, s);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s);
     if (e != cudaSuccess) {
         qlm_weight_free(w);
         return cuda_err(e, "quantize/upload");
@@ -239,6 +258,7 @@ int qlm_weight_import_int8(const int8_t* q, const float* scales, int n_total, in
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     cudaError_t e = cudaMemcpyAsync(w->q, hq.data(), hq.size(), cudaMemcpyHostToDevice, s);
     if (e == cudaSuccess) e = cudaMemcpyAsync(w->s, hs.data(), hs.size() * sizeof(float), cudaMemcpyHostToDevice, s);
+    if (e == cudaSuccess) e = qlm::launch_weight_exponents(w->s, w->rows, k, w->ew, s);
     if (e == cudaSuccess) e = cudaStreamSynchronize(s);
     if (e != cudaSuccess) {
         qlm_weight_free(w);
@@ -292,6 +312,8 @@ void qlm_weight_free(qlm_w8* w) {
     DeviceGuard g(w->device);
     if (w->q) cudaFree(w->q);
     if (w->s) cudaFree(w->s);
+    if (w->ew) cudaFree(w->ew);
+    delete w->maps;
     delete w;
 }
 
@@ -304,8 +326,7 @@ int qlm_linear_int8(const float* x, int M, int k, int64_t ldx, const qlm_w8* w, 
     if (ldy < w->rows) return set_err(QLM_ERR_INVALID_ARG, "ldy %lld < rows %d", (long long)ldy, w->rows);
     if (flags & ~(QLM_LINEAR_TENSOR | QLM_LINEAR_HOST_IO | QLM_LINEAR_SYNC))
         return set_err(QLM_ERR_INVALID_ARG, "unknown flags 0x%x", flags);
-    if (flags & QLM_LINEAR_TENSOR)
-        return set_err(QLM_ERR_UNSUPPORTED, "tensor-core path not available in this build");
+    const bool tensor = (flags & QLM_LINEAR_TENSOR) != 0;
     DeviceState* st;
     int rc = device_state(w->device, &st);
     if (rc) return rc;
@@ -313,12 +334,27 @@ int qlm_linear_int8(const float* x, int M, int k, int64_t ldx, const qlm_w8* w, 
     if (!g.ok) return set_err(QLM_ERR_CUDA, "cudaSetDevice(%d) failed", w->device);
     cudaStream_t s = static_cast<cudaStream_t>(stream);
 
-    // Rows of x per launch: all activations of a launch live in shared memory.
-    const size_t budget = 96 * 1024, hard = 200 * 1024;
+    // Exact path: rows of x per launch (all activations of a launch live in
+    // shared memory next to the weight slots).
     int mm = 8;
-    while (mm > 1 && qlm::gemv_smem_bytes(mm, k) > budget) --mm;
-    if (qlm::gemv_smem_bytes(mm, k) > hard)
+    while (mm > 1 && !qlm::gemv_supported(mm, w->rows, k, st->sm_count)) --mm;
+    if (!tensor && !qlm::gemv_supported(mm, w->rows, k, st->sm_count))
         return set_err(QLM_ERR_UNSUPPORTED, "k=%d exceeds the exact path's shared-memory staging limit", k);
+    if (tensor) {
+        std::lock_guard<std::mutex> lk(g_dev_mu);
+        if (!w->maps) {
+            qlm::TcMaps* maps = new (std::nothrow) qlm::TcMaps();
+            if (!maps) return set_err(QLM_ERR_OUT_OF_MEMORY, "host allocation failed");
+            cudaError_t e = qlm::tc_make_weight_maps(w->q, w->s, w->rows, w->k_pad, maps);
+            if (e != cudaSuccess) {
+                delete maps;
+                return cuda_err(e, "tensor map encode (weights)");
+            }
+            const_cast<qlm_w8*>(w)->maps = maps;
+        }
+        if ((rc = ensure_buf(&st->x16, &st->x16_cap, (size_t)M * w->k_pad * 2))) return rc;
+        if ((rc = ensure_buf(&st->ea, &st->ea_cap, (size_t)M * sizeof(int)))) return rc;
+    }
 
     const float* dx = x;
     float* dy = y;
@@ -336,19 +372,43 @@ int qlm_linear_int8(const float* x, int M, int k, int64_t ldx, const qlm_w8* w, 
         dldx = k;
         dldy = w->rows;
     }
-    for (int m0 = 0; m0 < M; m0 += mm) {
-        const int g_rows = (M - m0) < mm ? (M - m0) : mm;
-        QLM_CUDA(qlm::launch_gemv_exact(dx + (int64_t)m0 * dldx, dldx, g_rows, w->q, w->s, w->rows, k,
-                                        dy + (int64_t)m0 * dldy, dldy, st->sm_count, s, pdl_enabled()),
-                 "gemv launch");
+    if (tensor) {
+        QLM_CUDA(qlm::launch_gemm_tc(*w->maps, w->ew, w->rows, k, dx, dldx, M, st->x16, st->ea, dy, dldy, st->status,
+                                     s, pdl_enabled()),
+                 "tensor-core GEMM launch");
+    } else {
+        for (int m0 = 0; m0 < M; m0 += mm) {
+            const int g_rows = (M - m0) < mm ? (M - m0) : mm;
+            QLM_CUDA(qlm::launch_gemv_exact(dx + (int64_t)m0 * dldx, dldx, g_rows, w->q, w->s, w->rows, k,
+                                            dy + (int64_t)m0 * dldy, dldy, st->status, st->sm_count, s,
+                                            pdl_enabled()),
+                     "gemv launch");
+        }
     }
     if (host_io) {
         QLM_CUDA(cudaMemcpy2DAsync(y, (size_t)ldy * sizeof(float), dy, (size_t)w->rows * sizeof(float),
                                    (size_t)w->rows * sizeof(float), M, cudaMemcpyDeviceToHost, s),
                  "copy y to host");
     }
-    if (host_io || (flags & QLM_LINEAR_SYNC)) QLM_CUDA(cudaStreamSynchronize(s), "stream synchronize");
+    if (host_io || (flags & QLM_LINEAR_SYNC)) {
+        QLM_CUDA(cudaStreamSynchronize(s), "stream synchronize");
+        if (tensor || (flags & QLM_LINEAR_SYNC)) return qlm_device_status(w->device, 1);
+    }
     return QLM_OK;
+}
+
+int qlm_device_status(int device, int reset) {
+    DeviceState* st;
+    int rc = device_state(device, &st);
+    if (rc) return rc;
+    if (!st->status) return QLM_OK;
+    DeviceGuard g(device);
+    if (!g.ok) return set_err(QLM_ERR_CUDA, "cudaSetDevice(%d) failed", device);
+    int code = 0;
+    QLM_CUDA(cudaMemcpy(&code, st->status, sizeof(int), cudaMemcpyDeviceToHost), "read status");
+    if (code == 0) return QLM_OK;
+    if (reset) QLM_CUDA(cudaMemset(st->status, 0, sizeof(int)), "reset status");
+    return set_err(QLM_ERR_TIMEOUT, "a device-side wait gave up (code 0x%x); results of that call are invalid", code);
 }
 
 int qlm_stream_sync(void* stream) {

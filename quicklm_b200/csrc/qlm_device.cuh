@@ -64,6 +64,54 @@ __device__ __forceinline__ float4 ldg_f4(const void* p) {
     return r;
 }
 
+// 1-D bulk copy global -> shared (no multicast), completing on an mbarrier.
+// Both addresses 16-byte aligned, size a multiple of 16.
+__device__ __forceinline__ void bulk_copy_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+                 "l"(src), "r"(bytes), "r"(bar)
+                 : "memory");
+}
+// Order this thread's earlier generic-proxy shared-memory accesses before
+// later async-proxy (bulk copy) writes to the same memory.
+__device__ __forceinline__ void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+// Paired fp32 arithmetic (sm_100): two IEEE binary32 ops, each rounded to
+// nearest-even, in one instruction.
+__device__ __forceinline__ unsigned long long f2pack(float a, float b) {
+    unsigned long long r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+    return r;
+}
+__device__ __forceinline__ void f2unpack(unsigned long long v, float& a, float& b) {
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(v));
+}
+__device__ __forceinline__ unsigned long long f2mul(unsigned long long a, unsigned long long b) {
+    unsigned long long r;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+__device__ __forceinline__ unsigned long long f2add(unsigned long long a, unsigned long long b) {
+    unsigned long long r;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+__device__ __forceinline__ unsigned long long f2sub(unsigned long long a, unsigned long long b) {
+    unsigned long long r;
+    asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+
+// Exact int8 -> fp32 for the 4 signed bytes of w, as two float pairs:
+// lo = (q0, q1), hi = (q2, q3). Same bias construction as s8x4_to_f32.
+__device__ __forceinline__ void s8x4_to_f32x2(uint32_t w, unsigned long long& lo, unsigned long long& hi) {
+    const uint32_t u = w ^ 0x80808080u;
+    const unsigned long long bias = 0x4B0000804B000080ull;  // (2^23 + 128, 2^23 + 128)
+    const uint32_t b0 = __byte_perm(u, 0x4B000000u, 0x7540), b1 = __byte_perm(u, 0x4B000000u, 0x7541);
+    const uint32_t b2 = __byte_perm(u, 0x4B000000u, 0x7542), b3 = __byte_perm(u, 0x4B000000u, 0x7543);
+    lo = f2sub(((unsigned long long)b1 << 32) | b0, bias);
+    hi = f2sub(((unsigned long long)b3 << 32) | b2, bias);
+}
+
 // Programmatic dependent launch (sm_90+): let the next kernel in the stream
 // start launching, and wait until the previous kernel's results are visible.
 // Both are no-ops when the launch did not opt in.

@@ -3,6 +3,7 @@
 
 #include <cstddef>
 #include <cstdint>
+#include <cuda.h>
 #include <cuda_runtime.h>
 
 namespace qlm {
@@ -14,10 +15,32 @@ cudaError_t launch_quantize_pack(const void* src, int dtype, int64_t src_stride,
                                  float* scales, cudaStream_t stream);
 
 // Bit-exact y[m][0:rows] = x[m][0:k] . W^T for m < mm (1..8), W packed.
+// status: device int set non-zero if a bounded wait gave up.
 cudaError_t launch_gemv_exact(const float* x, int64_t ldx, int mm, const uint8_t* q, const float* s, int rows,
-                              int k, float* y, int64_t ldy, int sm_count, cudaStream_t stream, bool pdl);
+                              int k, float* y, int64_t ldy, int* status, int sm_count, cudaStream_t stream, bool pdl);
 
-// Dynamic shared memory the exact GEMV needs for mm activation rows.
-size_t gemv_smem_bytes(int mm, int k);
+// Whether the exact GEMV can stage mm activation rows of length k.
+bool gemv_supported(int mm, int rows, int k, int sm_count);
+
+// ---- tensor-core prefill GEMM (qlm_gemm_tc.cu) ----
+struct TcMaps {
+    alignas(64) CUtensorMap w;  // packed int8, 4-D lane-major view
+    alignas(64) CUtensorMap s;  // fp32 scales
+};
+
+// TMA descriptors for a packed weight (built once per weight).
+cudaError_t tc_make_weight_maps(const uint8_t* q, const float* s, int rows, int k_pad, TcMaps* out);
+
+// Per-row weight exponents ew[rows] used to range-scale the fp16 weight tile.
+cudaError_t launch_weight_exponents(const float* s, int rows, int k, int* ew, cudaStream_t stream);
+
+// Token-tile width the GEMM uses for M activation rows.
+int tc_pick_bn(int M);
+
+// y[M][rows] = x[M][k] . W^T on tensor cores. Scratch: x16 >= M*packed_k(k)
+// fp16 and ea >= M ints; status: device int set non-zero on a timeout.
+cudaError_t launch_gemm_tc(const TcMaps& maps, const int* ew, int rows, int k, const float* x, int64_t ldx, int M,
+                           void* x16_scratch, int* ea_scratch, float* y, int64_t ldy, int* status,
+                           cudaStream_t stream, bool pdl);
 
 }  // namespace qlm
