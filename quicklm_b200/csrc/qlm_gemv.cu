@@ -15,10 +15,9 @@
 //
 // Mapping: one thread per (output row, lane l), 8 consecutive threads per row,
 // 4 rows ("a unit") per warp. The chain t_l is the thread's register; the
-// 8->1 tree is three xor-shuffles inside the row's 8 threads. Products and
-// block sums use paired fp32 instructions (mul/add/sub .rn.f32x2), pairing
-// two *different blocks* of the same lane so every pair member is still one
-// IEEE operation of the reference's sequence; the FMA chain stays scalar.
+// 8->1 tree is three xor-shuffles inside the row's 8 threads. The exact
+// int8 -> fp32 conversion runs on paired fp32 subtracts; every product, sum
+// and FMA of the reference's sequence is a scalar round-to-nearest op.
 //
 // Memory: each warp streams its units' packed rows (and their scales) into
 // private shared-memory slots with 1-D cp.async.bulk copies completing on an
@@ -65,42 +64,49 @@ __device__ __forceinline__ int xperm(int k) {
 }
 
 // One 128-element chunk for this lane: 4 blocks x 4 steps, scales sv[0..3].
+// int8 -> fp32 uses paired subtracts (no multiply feeds them). Products and
+// their sums stay scalar mul.rn / add.rn: ptxas (CUDA 12.9, sm_100a) was seen
+// to contract a paired mul.rn.f32x2 into the add.rn.f32x2 consuming it, which
+// changes the reference's rounding; the scalar .rn forms are never contracted.
 template <int MM>
 __device__ __forceinline__ void chunk_update(const float* __restrict__ xs_chunk, int k_pad, int lane, uint4 qv,
                                              float4 sv, float (&t)[MM], int nblocks) {
-    // q pairs across blocks: qa[j] = (q[bb0][j], q[bb1][j]), qb[j] = (q[bb2][j], q[bb3][j])
     const uint32_t u0 = qv.x ^ 0x80808080u, u1 = qv.y ^ 0x80808080u;
     const uint32_t u2 = qv.z ^ 0x80808080u, u3 = qv.w ^ 0x80808080u;
     const unsigned long long bias = 0x4B0000804B000080ull;  // (2^23 + 128) x 2
-    unsigned long long qa[4], qb[4];
+    float qf[4][4];  // [block][step]
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
         const uint32_t sel = 0x7540u | (uint32_t)j;
         const uint32_t f0 = __byte_perm(u0, 0x4B000000u, sel), f1 = __byte_perm(u1, 0x4B000000u, sel);
         const uint32_t f2 = __byte_perm(u2, 0x4B000000u, sel), f3 = __byte_perm(u3, 0x4B000000u, sel);
-        qa[j] = f2sub(((unsigned long long)f1 << 32) | f0, bias);
-        qb[j] = f2sub(((unsigned long long)f3 << 32) | f2, bias);
+        f2unpack(f2sub(((unsigned long long)f1 << 32) | f0, bias), qf[0][j], qf[1][j]);
+        f2unpack(f2sub(((unsigned long long)f3 << 32) | f2, bias), qf[2][j], qf[3][j]);
     }
+    const float sc[4] = {sv.x, sv.y, sv.z, sv.w};
 #pragma unroll
     for (int m = 0; m < MM; ++m) {
         const float* xm = xs_chunk + (size_t)m * k_pad + lane * 4;
-        unsigned long long pa[4], pb[4];
+        float xv[4][4];  // [step][block]
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
-            const float4 xv = *reinterpret_cast<const float4*>(xm + j * 32);
-            pa[j] = f2mul(f2pack(xv.x, xv.y), qa[j]);
-            pb[j] = f2mul(f2pack(xv.z, xv.w), qb[j]);
+            const float4 v = *reinterpret_cast<const float4*>(xm + j * 32);
+            xv[j][0] = v.x;
+            xv[j][1] = v.y;
+            xv[j][2] = v.z;
+            xv[j][3] = v.w;
         }
-        const unsigned long long bsa = f2add(f2add(pa[0], pa[1]), f2add(pa[2], pa[3]));
-        const unsigned long long bsb = f2add(f2add(pb[0], pb[1]), f2add(pb[2], pb[3]));
-        float bs0, bs1, bs2, bs3;
-        f2unpack(bsa, bs0, bs1);
-        f2unpack(bsb, bs2, bs3);
         float tt = t[m];
-        tt = __fmaf_rn(bs0, sv.x, tt);
-        if (nblocks > 1) tt = __fmaf_rn(bs1, sv.y, tt);
-        if (nblocks > 2) tt = __fmaf_rn(bs2, sv.z, tt);
-        if (nblocks > 3) tt = __fmaf_rn(bs3, sv.w, tt);
+#pragma unroll
+        for (int bb = 0; bb < 4; ++bb) {
+            if (bb < nblocks) {
+                const float p0 = __fmul_rn(xv[0][bb], qf[bb][0]);
+                const float p1 = __fmul_rn(xv[1][bb], qf[bb][1]);
+                const float p2 = __fmul_rn(xv[2][bb], qf[bb][2]);
+                const float p3 = __fmul_rn(xv[3][bb], qf[bb][3]);
+                tt = __fmaf_rn(__fadd_rn(__fadd_rn(p0, p1), __fadd_rn(p2, p3)), sc[bb], tt);
+            }
+        }
         t[m] = tt;
     }
 }
