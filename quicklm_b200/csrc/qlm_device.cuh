@@ -82,6 +82,12 @@ __device__ __forceinline__ unsigned long long f2pack(float a, float b) {
     asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
     return r;
 }
+// Pair two 32-bit registers (lo, hi) without arithmetic.
+__device__ __forceinline__ unsigned long long u2pack(uint32_t lo, uint32_t hi) {
+    unsigned long long r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "r"(lo), "r"(hi));
+    return r;
+}
 __device__ __forceinline__ void f2unpack(unsigned long long v, float& a, float& b) {
     asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(v));
 }

@@ -15,11 +15,12 @@
 // reference (the bar for a reduced-precision prefill MMA is 2e-3).
 //
 // Data flow per CTA (one 128-row weight tile x BN tokens, all of K):
-//   warp 0 lane 0  TMA producer: int8 weight chunks (128 K elements, read
-//                  through a 4-D tensor map so the tile lands lane-major:
-//                  [lane 8][row 128][16 B], conflict-free for a thread per
-//                  row), their scales, and 64-wide fp16 activation tiles
-//                  (128-byte swizzle, the MMA's K-major B operand).
+//   warp 0 lane 0  TMA producer: int8 weight chunks (128 rows x 128 B, one
+//                  packed chunk per row, 128-byte swizzle so a thread per
+//                  row reads its 16-byte lane slices without bank
+//                  conflicts), their scales 8 chunks at a time (also
+//                  swizzled), and 64-wide fp16 activation tiles (128-byte
+//                  swizzle, the MMA's K-major B operand).
 //   warps 4-7      converters, one thread per weight row: int8 -> fp16 with
 //                  two integer ops and two fp16x2 ops per pair, written with
 //                  tcgen05.st straight into tensor memory as the MMA's A
@@ -46,10 +47,12 @@ using namespace sm100;
 constexpr int BM = 128;  // weight rows per tile (MMA M)
 constexpr int BK = 64;   // fp16 K elements per activation stage (one 128-B swizzle row)
 constexpr int SW = 3;    // int8 weight stages (one 128-element chunk each)
+constexpr int SS = 2;    // scale stages (8 chunks each)
+constexpr int S_CHUNKS = 8;
 constexpr int SX = 4;    // activation stages
 constexpr int SA = 4;    // tensor-memory A stages (one BK step = 32 columns each)
-constexpr int W_STAGE_BYTES = BM * 128;  // [lane 8][row 128][16 B]
-constexpr int S_STAGE_BYTES = BM * 16;   // [row 128][4 scales]
+constexpr int W_STAGE_BYTES = BM * 128;  // [row 128][128 B], 128-byte swizzle
+constexpr int S_STAGE_BYTES = BM * 128;  // [row 128][8 chunks x 4 scales], 128-byte swizzle
 constexpr long long WAIT_BUDGET = 4000000000LL;  // ~2 s of SM clock per wait
 
 enum : int { ST_OK = 0, ST_TIMEOUT_PRODUCER = 0x101, ST_TIMEOUT_MMA = 0x102, ST_TIMEOUT_CONVERT = 0x103 };
@@ -71,8 +74,8 @@ struct TcCfg {
     static constexpr int OFF_X = 0;
     static constexpr int OFF_W = OFF_X + SX * X_STAGE_BYTES;
     static constexpr int OFF_S = OFF_W + SW * W_STAGE_BYTES;
-    static constexpr int OFF_BAR = OFF_S + SW * S_STAGE_BYTES;
-    static constexpr int NBAR = 2 * SW + 2 * SX + 2 * SA + 1;
+    static constexpr int OFF_BAR = OFF_S + SS * S_STAGE_BYTES;
+    static constexpr int NBAR = 2 * SW + 2 * SX + 2 * SA + 2 * SS + 1;
     static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
     static constexpr int SMEM = OFF_MISC + 16 + 1024;  // + slack to align the base to 1024 B
 };
@@ -113,6 +116,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__
     const uint32_t XFULL = bar0 + 8 * (2 * SW), XEMPTY = XFULL + 8 * SX;
     const uint32_t AFULL = bar0 + 8 * (2 * SW + 2 * SX), AEMPTY = AFULL + 8 * SA;
     const uint32_t ACCFULL = bar0 + 8 * (2 * SW + 2 * SX + 2 * SA);
+    const uint32_t SFULL = ACCFULL + 8, SEMPTY = SFULL + 8 * SS;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::OFF_MISC);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::OFF_MISC + 4);
 
@@ -134,6 +138,10 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__
             mbar_init(AEMPTY + 8 * i, 1);
         }
         mbar_init(ACCFULL, 1);
+        for (int i = 0; i < SS; ++i) {
+            mbar_init(SFULL + 8 * i, 1);
+            mbar_init(SEMPTY + 8 * i, 4);
+        }
         *abort_flag = 0;
         mbar_fence_init();
     }
@@ -153,16 +161,25 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__
             tma_prefetch_desc(&tm_s);
             tma_prefetch_desc(&tm_x);
             bool ok = true;
-            int w_issued = 0, x_issued = 0;
+            int w_issued = 0, x_issued = 0, s_issued = 0;
             for (int c = 0; c < p.nchunks && ok; ++c) {
+                if (c % S_CHUNKS == 0) {
+                    const int g = c / S_CHUNKS, ss = g % SS;
+                    if (!mbar_wait(SEMPTY + 8 * ss, ((g / SS) & 1) ^ 1, abort_flag, WAIT_BUDGET)) {
+                        ok = false;
+                        break;
+                    }
+                    mbar_arrive_expect_tx(SFULL + 8 * ss, S_STAGE_BYTES);
+                    tma_load_2d(sbase + C::OFF_S + ss * S_STAGE_BYTES, &tm_s, 4 * c, n0, SFULL + 8 * ss);
+                    ++s_issued;
+                }
                 const int ws = c % SW;
                 if (!mbar_wait(WEMPTY + 8 * ws, ((c / SW) & 1) ^ 1, abort_flag, WAIT_BUDGET)) {
                     ok = false;
                     break;
                 }
-                mbar_arrive_expect_tx(WFULL + 8 * ws, W_STAGE_BYTES + S_STAGE_BYTES);
-                tma_load_4d(sbase + C::OFF_W + ws * W_STAGE_BYTES, &tm_w, 0, n0, 0, c, WFULL + 8 * ws);
-                tma_load_2d(sbase + C::OFF_S + ws * S_STAGE_BYTES, &tm_s, 4 * c, n0, WFULL + 8 * ws);
+                mbar_arrive_expect_tx(WFULL + 8 * ws, W_STAGE_BYTES);
+                tma_load_2d(sbase + C::OFF_W + ws * W_STAGE_BYTES, &tm_w, c * 128, n0, WFULL + 8 * ws);
                 ++w_issued;
                 if (c == 0) pdl_wait();  // activations are produced by the previous kernel
                 for (int h = 0; h < 2; ++h) {
@@ -188,6 +205,8 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__
                 mbar_wait(WFULL + 8 * (i % SW), (i / SW) & 1, nullptr, WAIT_BUDGET);
             for (int i = (x_issued > SX ? x_issued - SX : 0); i < x_issued; ++i)
                 mbar_wait(XFULL + 8 * (i % SX), (i / SX) & 1, nullptr, WAIT_BUDGET);
+            for (int i = (s_issued > SS ? s_issued - SS : 0); i < s_issued; ++i)
+                mbar_wait(SFULL + 8 * (i % SS), (i / SS) & 1, nullptr, WAIT_BUDGET);
         }
     } else if (warp == 1) {
         if (lane == 0) {
@@ -226,19 +245,29 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__
         const int ewr = row < p.rows ? p.ew[row] : 0;
         const uint32_t lane_addr = (uint32_t)(32 * qw) << 16;
         bool ok = true;
+        const int sw = r & 7;  // this row's 128-byte swizzle phase
         for (int c = 0; c < p.nchunks && ok; ++c) {
+            const int g = c / S_CHUNKS, ss = g % SS, cc = c % S_CHUNKS;
+            if (cc == 0 && !mbar_wait(SFULL + 8 * ss, (g / SS) & 1, abort_flag, WAIT_BUDGET)) {
+                ok = false;
+                break;
+            }
             const int ws = c % SW;
             if (!mbar_wait(WFULL + 8 * ws, (c / SW) & 1, abort_flag, WAIT_BUDGET)) {
                 ok = false;
                 break;
             }
-            const uint8_t* wst = smem + C::OFF_W + ws * W_STAGE_BYTES;
+            const uint8_t* wst = smem + C::OFF_W + ws * W_STAGE_BYTES + r * 128;
             uint4 v[8];
 #pragma unroll
-            for (int l = 0; l < 8; ++l) v[l] = *reinterpret_cast<const uint4*>(wst + l * (BM * 16) + r * 16);
-            const float4 s4 = *reinterpret_cast<const float4*>(smem + C::OFF_S + ws * S_STAGE_BYTES + r * 16);
+            for (int l = 0; l < 8; ++l) v[l] = *reinterpret_cast<const uint4*>(wst + ((l ^ sw) << 4));
+            const float4 s4 = *reinterpret_cast<const float4*>(smem + C::OFF_S + ss * S_STAGE_BYTES + r * 128 +
+                                                               ((cc ^ sw) << 4));
             __syncwarp();
-            if (lane == 0) mbar_arrive(WEMPTY + 8 * ws);
+            if (lane == 0) {
+                mbar_arrive(WEMPTY + 8 * ws);
+                if (cc == S_CHUNKS - 1 || c == p.nchunks - 1) mbar_arrive(SEMPTY + 8 * ss);
+            }
             const float sv[4] = {s4.x, s4.y, s4.z, s4.w};
             __half2 s16[4];
 #pragma unroll
@@ -407,12 +436,12 @@ cudaError_t tc_make_weight_maps(const uint8_t* q, const float* s, int rows, int 
     auto enc = encode_fn();
     if (!enc) return cudaErrorNotSupported;
     {
-        const cuuint64_t dims[4] = {16, (cuuint64_t)rows, 8, (cuuint64_t)(k_pad / 128)};
-        const cuuint64_t strides[3] = {(cuuint64_t)k_pad, 16, 128};
-        const cuuint32_t box[4] = {16, (cuuint32_t)BM, 8, 1};
-        const cuuint32_t estr[4] = {1, 1, 1, 1};
-        CUresult r = enc(&out->w, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, const_cast<uint8_t*>(q), dims, strides, box, estr,
-                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+        const cuuint64_t dims[2] = {(cuuint64_t)k_pad, (cuuint64_t)rows};
+        const cuuint64_t strides[1] = {(cuuint64_t)k_pad};
+        const cuuint32_t box[2] = {128, (cuuint32_t)BM};
+        const cuuint32_t estr[2] = {1, 1};
+        CUresult r = enc(&out->w, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint8_t*>(q), dims, strides, box, estr,
+                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
         if (r != CUDA_SUCCESS) return cudaErrorInvalidValue;
     }
@@ -420,10 +449,10 @@ cudaError_t tc_make_weight_maps(const uint8_t* q, const float* s, int rows, int 
         const int nb_pad = k_pad / kBlock;
         const cuuint64_t dims[2] = {(cuuint64_t)nb_pad, (cuuint64_t)rows};
         const cuuint64_t strides[1] = {(cuuint64_t)nb_pad * 4};
-        const cuuint32_t box[2] = {4, (cuuint32_t)BM};
+        const cuuint32_t box[2] = {4 * S_CHUNKS, (cuuint32_t)BM};
         const cuuint32_t estr[2] = {1, 1};
         CUresult r = enc(&out->s, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(s), dims, strides, box, estr,
-                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
         if (r != CUDA_SUCCESS) return cudaErrorInvalidValue;
     }

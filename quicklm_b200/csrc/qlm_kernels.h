@@ -24,7 +24,7 @@ bool gemv_supported(int mm, int rows, int k, int sm_count);
 
 // ---- tensor-core prefill GEMM (qlm_gemm_tc.cu) ----
 struct TcMaps {
-    alignas(64) CUtensorMap w;  // packed int8, 4-D lane-major view
+    alignas(64) CUtensorMap w;  // packed int8 rows, 128 x 128-byte boxes
     alignas(64) CUtensorMap s;  // fp32 scales
 };
 

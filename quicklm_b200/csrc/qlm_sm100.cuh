@@ -37,18 +37,31 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
     return ok != 0;
 }
 
+// try_wait with a suspend-time hint: the thread sleeps in hardware (issuing
+// nothing) until the phase completes or ~hint_ns pass.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint32_t bar, uint32_t parity, uint32_t hint_ns) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity), "r"(hint_ns)
+        : "memory");
+    return ok != 0;
+}
+
 // Bounded wait: gives up after ~`budget` clock cycles, or early once another
 // thread of the CTA has raised *abort (abort may be null). Returns false on
-// give-up.
+// give-up. Waiting threads sleep in the try_wait instead of spinning, so they
+// do not take issue slots from the warps that compute.
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort, long long budget) {
     if (mbar_try_wait(bar, parity)) return true;
     const long long t0 = clock64();
-    for (uint32_t it = 1;; ++it) {
-        if (mbar_try_wait(bar, parity)) return true;
-        if ((it & 63u) == 0u) {
-            if (abort && *abort) return false;
-            if (clock64() - t0 > budget) return false;
-        }
+    for (;;) {
+        if (mbar_try_wait_sleep(bar, parity, 20000u)) return true;
+        if (abort && *abort) return false;
+        if (clock64() - t0 > budget) return false;
     }
 }
 
