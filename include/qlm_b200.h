@@ -116,6 +116,24 @@ void qlm_weight_free(qlm_w8* w);
 int qlm_linear_int8(const float* x, int M, int k, int64_t ldx, const qlm_w8* w, float* y, int64_t ldy, int flags,
                     void* stream);
 
+/* The tensor-core GEMM of qlm_linear_int8(QLM_LINEAR_TENSOR), for callers that
+ * must not allocate device memory once running: an engine that hands all of
+ * device memory to its own pool at start-up, or a decode loop that cannot
+ * afford cudaMalloc's device-wide synchronisation. No counterpart in the
+ * reference. It allocates nothing: its scratch (fp16 activations, row
+ * exponents, a status word) lives in 8 MiB of static device memory that every
+ * GPU loading this library holds until exit.
+ *   x, y:  DEVICE pointers, shapes as qlm_linear_int8.
+ *   Limit: M <= 16384 and M * round_up(k, 128) * 2 bytes <= 8 MiB - 64 KiB - 256;
+ *          larger requests return QLM_ERR_INVALID_ARG.
+ *   flags: 0, or QLM_LINEAR_SYNC to wait and report device-side timeouts.
+ * The first call on a device looks up the array's device address
+ * (cudaGetSymbolAddress) with that device current; make that first call
+ * before any stream capture. All calls on a device share the array, so calls
+ * that may overlap on the GPU (unordered streams) race; order them. */
+int qlm_linear_int8_tc_noalloc(const float* x, int M, int k, int64_t ldx, const qlm_w8* w, float* y, int64_t ldy,
+                               int flags, void* stream);
+
 /* Status of bounded device-side waits on `device`: QLM_OK, or QLM_ERR_TIMEOUT
  * if a kernel gave up waiting since the last reset (reset != 0 clears it).
  * Synchronous tensor-core calls check this themselves. */

@@ -35,7 +35,7 @@ SRC_F32, SRC_BF16 = 0, 1
 ABI_SYMBOLS = (
     "qlm_abi_version", "qlm_last_error", "qlm_weight_quantize_upload", "qlm_weight_import_int8",
     "qlm_weight_export_int8", "qlm_weight_shape", "qlm_weight_bytes", "qlm_weight_free", "qlm_linear_int8",
-    "qlm_device_status", "qlm_stream_sync",
+    "qlm_device_status", "qlm_stream_sync", "qlm_linear_int8_tc_noalloc",
 )
 
 _STATUS = {0: "OK", 1: "INVALID_ARG", 2: "CUDA", 3: "OUT_OF_MEMORY", 4: "UNSUPPORTED", 5: "TIMEOUT", 6: "NCCL",
@@ -75,6 +75,7 @@ def load(path: str = LIB_PATH):
     lib.qlm_linear_int8.argtypes = [P, I, I, L, P, P, L, I, P]
     lib.qlm_stream_sync.argtypes = [P]
     lib.qlm_device_status.argtypes = [I, I]
+    lib.qlm_linear_int8_tc_noalloc.argtypes = [P, I, I, L, P, P, L, I, P]
     if lib.qlm_abi_version() != 1:
         raise QlmError(7, "ABI version mismatch")
     _lib = lib

@@ -7,6 +7,7 @@
 // across the ABI; every failure leaves a message for qlm_last_error().
 #include "../../include/qlm_b200.h"
 #include "qlm_device.cuh"
+#include "qlm_handle.h"
 #include "qlm_kernels.h"
 
 #include <cstdarg>
@@ -18,15 +19,6 @@
 #include <string>
 #include <vector>
 
-struct qlm_w8 {
-    int device = -1;
-    int rows = 0, k = 0, k_pad = 0, nb_pad = 0;
-    int row_begin = 0, row_end = 0, n_total = 0;
-    uint8_t* q = nullptr;  // packed [rows][k_pad]
-    float* s = nullptr;    // [rows][nb_pad]
-    int* ew = nullptr;     // [rows] range exponents for the tensor-core path
-    qlm::TcMaps* maps = nullptr;  // TMA descriptors, built on first tensor-core use
-};
 
 namespace {
 
@@ -156,6 +148,10 @@ int check_shard(int n_total, int k, int row_begin, int row_end) {
 }
 
 }  // namespace
+
+namespace qlm_internal {
+void set_last_error(const std::string& msg) { g_err = msg; }
+}  // namespace qlm_internal
 
 extern "C" {
 

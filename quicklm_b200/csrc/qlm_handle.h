@@ -1,0 +1,16 @@
+// qlm_handle.h — layout of the opaque qlm_w8 weight handle (internal).
+#pragma once
+
+#include <cstdint>
+
+#include "qlm_kernels.h"
+
+struct qlm_w8 {
+    int device = -1;
+    int rows = 0, k = 0, k_pad = 0, nb_pad = 0;
+    int row_begin = 0, row_end = 0, n_total = 0;
+    uint8_t* q = nullptr;  // packed [rows][k_pad]
+    float* s = nullptr;    // [rows][nb_pad]
+    int* ew = nullptr;     // [rows] range exponents for the tensor-core path
+    qlm::TcMaps* maps = nullptr;  // TMA descriptors, built on first tensor-core use
+};

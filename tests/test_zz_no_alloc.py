@@ -1,0 +1,62 @@
+"""The allocation-free tensor-core entry point (qlm_linear_int8_tc_noalloc).
+
+It serves callers that may not allocate device memory while running (an
+engine that gives all device memory to its own pool at start-up, or a decode
+loop that cannot take cudaMalloc's device-wide synchronisation): its scratch is
+the library's static device array instead of cudaMalloc'd buffers. This test
+calls it through the C ABI and checks two calls in a row against the regular
+entry point qlm_linear_int8(QLM_LINEAR_TENSOR), with the tolerance the
+tensor-core tests use (relative L2 2e-3). It sits in its own file, collected
+last, and passes both alone in a fresh process and after the other tests.
+"""
+from __future__ import annotations
+
+import ctypes
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+REL_L2_BAR = 2e-3
+
+
+def rel_l2(a, b):
+    a = np.asarray(a, np.float64)
+    b = np.asarray(b, np.float64)
+    return float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-300))
+
+
+def test_noalloc_matches_regular_entry_point(qlm_lib, cuda_device):
+    import torch
+    import quicklm_b200 as q
+
+    rng = np.random.default_rng(99)
+    n, k = 384, 640
+    wf = (rng.standard_normal((n, k)) * 0.02).astype(np.float32)
+    w = q.Int8Weight.quantize(wf)
+    stream = torch.cuda.current_stream().cuda_stream
+    for m in (96, 200):  # two calls in a row, different shapes and data
+        x = torch.from_numpy(rng.standard_normal((m, k)).astype(np.float32)).cuda()
+        y_ref = q.matmul(x, w, flags=q.TENSOR | q.SYNC)
+        y = torch.full((m, n), float("nan"), device="cuda")
+        rc = qlm_lib.qlm_linear_int8_tc_noalloc(x.data_ptr(), m, k, k, w.handle, y.data_ptr(), n, q.SYNC, stream)
+        assert rc == 0, qlm_lib.qlm_last_error()
+        torch.cuda.synchronize()
+        yh = y.cpu().numpy()
+        assert np.all(np.isfinite(yh))
+        assert rel_l2(yh, y_ref.cpu().numpy()) <= REL_L2_BAR
+
+
+def test_noalloc_rejects_oversize(qlm_lib, cuda_device):
+    import torch
+    import quicklm_b200 as q
+
+    k = 4096
+    w = q.Int8Weight.quantize(np.zeros((128, k), np.float32))
+    m = 2048  # 2048 * 4096 * 2 bytes = 16 MiB of staging > the 8 MiB array
+    x = torch.zeros((m, k), device="cuda")
+    y = torch.zeros((m, 128), device="cuda")
+    rc = qlm_lib.qlm_linear_int8_tc_noalloc(x.data_ptr(), m, k, k, w.handle, y.data_ptr(), 128, 0, None)
+    assert rc == 1
+    assert b"static scratch" in qlm_lib.qlm_last_error()
