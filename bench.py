@@ -60,7 +60,7 @@ def measured_peaks():
     return 6650.0, "fallback"
 
 
-def profile_traffic(name="gemv_exact_cfg1.txt"):
+def profile_traffic(name="gemv_m1_cfg1.txt"):
     """DRAM bytes per launch from the committed ncu summary, if present."""
     p = os.path.join(ROOT, "profiles", name)
     if not os.path.exists(p):
@@ -368,7 +368,7 @@ def main():
                                    f"{STACK} distinct weight copies per step",
                        "l2": f"inputs larger than L2 ({STACK}x{weight_bytes() / 1e6:.2f} MB weights per step)",
                        "parallelism": "single GPU" if world == 1 else f"row-sharded x{world} + NCCL all-gather",
-                       "kernel": "gemv_exact_kernel<1> (CUDA cores, bit-exact)", "cuda_graph": used_graph,
+                       "kernel": "gemv_m1_kernel (CUDA cores, bit-exact)", "cuda_graph": used_graph,
                        "pdl": os.environ.get("QLM_PDL", "1") != "0"},
             "pct_hbm_peak": round(100.0 * value / world / peak, 2),
             "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": peak, "unit": "GB/s",
