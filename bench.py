@@ -261,32 +261,69 @@ def main():
         import torch.distributed as dist
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
 
-    # Inputs: the rank's shard rows of config 1's generator (rank 0 = config 1 itself).
+    # Inputs: rank r holds rows [6144 r, 6144 (r+1)) of a [6144 N, 2048] weight
+    # (rank 0's rows are config 1's W); x is config 1's x on every rank.
     x_np, w_np = synth_case(1, N_ROWS, K_DIM, 0 + rank)
-    w_dev = torch.from_numpy(w_np).cuda()
-    weights = [qlm.Int8Weight.quantize(w_dev, device=local) for _ in range(STACK)]
-    del w_dev
+    n_total = N_ROWS * world
+    w_glob = torch.empty((n_total, K_DIM), device="cuda")
+    w_glob[rank * N_ROWS:(rank + 1) * N_ROWS] = torch.from_numpy(w_np).cuda()
+    weights = [qlm.Int8Weight.quantize(w_glob, device=local, row_begin=rank * N_ROWS, row_end=(rank + 1) * N_ROWS)
+               for _ in range(STACK)]
+    del w_glob
     x = torch.from_numpy(x_np).cuda()
-    ys = [torch.empty((1, N_ROWS), device="cuda") for _ in range(STACK)]
-    gathered = [torch.empty((world, N_ROWS), device="cuda") for _ in range(STACK)] if world > 1 else None
+    ys = [torch.empty((1, n_total), device="cuda") for _ in range(STACK)]
     stream = torch.cuda.Stream()
+    comm = None
+    if world > 1:
+        def exchange(h):
+            out = [None] * world
+            dist.all_gather_object(out, h)
+            return out
+        comm = qlm.Comm(local, rank, world, n_total, exchange)
 
     def step():
         for i in range(STACK):
-            qlm.matmul(x, weights[i], ys[i], stream=stream)
-            if world > 1:
-                dist.all_gather_into_tensor(gathered[i], ys[i])
+            if comm is None:
+                qlm.matmul(x, weights[i], ys[i], stream=stream)
+            else:
+                qlm.matmul_allgather(x, weights[i], comm, ys[i], stream=stream)
 
     with torch.cuda.stream(stream):
         for _ in range(3):
             step()
     torch.cuda.synchronize()
-    graph = None
-    if world == 1:
-        graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(graph, stream=stream):
-            step()
+    nccl_gbs = None
+    if world > 1:
+        # Reference point: the same shards gathered with NCCL after every GEMV (eager).
+        yl = [torch.empty((1, N_ROWS), device="cuda") for _ in range(STACK)]
+        gl = [torch.empty((world, N_ROWS), device="cuda") for _ in range(STACK)]
+
+        def nccl_step():
+            for i in range(STACK):
+                qlm.matmul(x, weights[i], yl[i], stream=stream)
+                dist.all_gather_into_tensor(gl[i], yl[i])
+        with torch.cuda.stream(stream):
+            for _ in range(3):
+                nccl_step()
         torch.cuda.synchronize()
+        dist.barrier()
+        n0, n1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        n0.record(stream)
+        with torch.cuda.stream(stream):
+            for _ in range(50):
+                nccl_step()
+        n1.record(stream)
+        torch.cuda.synchronize()
+        t = torch.tensor([n0.elapsed_time(n1)], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        nccl_gbs = 50 * STACK * weight_bytes() * world / (float(t.item()) / 1000.0) / 1e9
+        dist.barrier()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        step()
+    torch.cuda.synchronize()
+    if dist is not None:
+        dist.barrier()
 
     def run(n):
         with torch.cuda.stream(stream):
@@ -320,23 +357,36 @@ def main():
 
     launches = args.steps * STACK
     total_weight = launches * weight_bytes() * world
+    kernels_per_gemv = 1 if world == 1 else 2
     value = total_weight / (ms / 1000.0) / 1e9
     mean_launch_s = (ms / 1000.0) / launches
     peak, peak_kind = measured_peaks()
     achieved = algo_bytes() / mean_launch_s / 1e9
 
-    # e2e: through the C ABI with host buffers (pinned), synchronous per call.
+    # e2e: through the public API with host buffers (pinned): x copied in, the
+    # (gathered) result copied out, every call synchronous.
     x_pin = torch.empty((1, K_DIM), dtype=torch.float32, pin_memory=True)
     x_pin.copy_(torch.from_numpy(x_np))
-    y_pin = torch.empty((1, N_ROWS), dtype=torch.float32, pin_memory=True)
+    y_pin = torch.empty((1, n_total), dtype=torch.float32, pin_memory=True)
     xh, yh = x_pin.numpy(), y_pin.numpy()
+    xd, yd = torch.empty((1, K_DIM), device="cuda"), torch.empty((1, n_total), device="cuda")
+
+    def e2e_call(i):
+        if comm is None:
+            qlm.matmul(xh, weights[i % STACK], yh)
+        else:
+            xd.copy_(x_pin, non_blocking=True)
+            qlm.matmul_allgather(xd, weights[i % STACK], comm, yd)
+            y_pin.copy_(yd, non_blocking=True)
+            torch.cuda.current_stream().synchronize()
+
     for i in range(20):
-        qlm.matmul(xh, weights[i % STACK], yh)
+        e2e_call(i)
     if dist is not None:
         dist.barrier()
     t0 = time.perf_counter()
     for i in range(args.e2e_calls):
-        qlm.matmul(xh, weights[i % STACK], yh)
+        e2e_call(i)
     e2e_s = time.perf_counter() - t0
     if dist is not None:
         t = torch.tensor([e2e_s], device="cuda", dtype=torch.float64)
@@ -367,18 +417,21 @@ def main():
             "config": {"workload": "cfg1 int8 decode GEMV M=1, W [6144,2048] per rank, "
                                    f"{STACK} distinct weight copies per step",
                        "l2": f"inputs larger than L2 ({STACK}x{weight_bytes() / 1e6:.2f} MB weights per step)",
-                       "parallelism": "single GPU" if world == 1 else f"row-sharded x{world} + NCCL all-gather",
-                       "kernel": "gemv_m1_kernel (CUDA cores, bit-exact)", "cuda_graph": used_graph,
+                       "parallelism": "single GPU" if world == 1 else
+                       f"row-sharded x{world}, all-gather fused into the GEMV (NVLink peer stores)",
+                       "kernel": "gemv_m1_kernel (CUDA cores, bit-exact)" if world == 1 else
+                       "gemv_m1_kernel<gather> + gather_wait_copy_kernel", "cuda_graph": used_graph,
                        "pdl": os.environ.get("QLM_PDL", "1") != "0"},
             "pct_hbm_peak": round(100.0 * value / world / peak, 2),
             "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "traffic": profile_traffic(),
                          "peak_source": f"MEASURED_PEAKS.json hbm_gbs ({peak_kind})",
                          "algorithmic_bytes_per_launch": algo_bytes(), "mean_launch_us": mean_launch_s * 1e6},
+            "nccl_allgather_value": None if nccl_gbs is None else round(nccl_gbs, 2),
             "e2e": {"value": round(e2e, 2), "unit": "GB/s", "h2d_bytes_per_step": STACK * 4 * K_DIM,
-                    "d2h_bytes_per_step": STACK * 4 * N_ROWS,
+                    "d2h_bytes_per_step": STACK * 4 * n_total,
                     "how": "qlm_linear_int8(QLM_LINEAR_HOST_IO) per GEMV, pinned host x/y, wall clock"},
-            "gpu_launches": launches,
+            "gpu_launches": launches * kernels_per_gemv,
             "clocks": clk,
             "cpu_baseline": base,
             "prefill": prefill,
@@ -386,6 +439,10 @@ def main():
         print(json.dumps(line), flush=True)
     for w in weights:
         w.free()
+    if comm is not None:
+        torch.cuda.synchronize()
+        dist.barrier()
+        comm.free()
     if dist is not None:
         dist.barrier()
         dist.destroy_process_group()

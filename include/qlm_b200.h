@@ -134,6 +134,32 @@ int qlm_linear_int8(const float* x, int M, int k, int64_t ldx, const qlm_w8* w, 
 int qlm_linear_int8_tc_noalloc(const float* x, int M, int k, int64_t ldx, const qlm_w8* w, float* y, int64_t ldy,
                                int flags, void* stream);
 
+/* ---- Row-sharded weights across the GPUs of one box (NVLink) ----------------
+ * No counterpart in the reference (QuickLM is single-process); the sharded
+ * product keeps the reference's bits, since each output element is still
+ * computed by exactly one thread with the reference's sequence
+ * (src/ops/math_ops.cpp:874-894), on the GPU that owns its row. */
+typedef struct qlm_comm qlm_comm;
+
+/* Bytes of one rank's exchange handle (a CUDA IPC handle). */
+int qlm_comm_handle_bytes(void);
+
+/* This rank's exchange buffer on `device` for gathered outputs of up to
+ * max_out floats; writes its handle (qlm_comm_handle_bytes() bytes) to
+ * handle_out. The caller exchanges the handles between ranks (any transport)
+ * and passes all of them, in rank order, to qlm_comm_connect. */
+int qlm_comm_create(int device, int rank, int nranks, int64_t max_out, qlm_comm** out, void* handle_out);
+int qlm_comm_connect(qlm_comm* c, const void* all_handles);
+void qlm_comm_free(qlm_comm* c);
+
+/* y[0, 0:n_total] = x[0, 0:k] . W^T for a row-sharded W: this rank's shard w
+ * (rows [row_begin, row_end) of n_total) is computed and stored into every
+ * rank's exchange buffer over NVLink by the GEMV kernel itself; a bounded wait
+ * then copies the gathered row into y (device pointer, n_total floats).
+ * M must be 1 (decode). All ranks must make the same sequence of calls. */
+int qlm_linear_int8_allgather(const float* x, int M, int k, int64_t ldx, const qlm_w8* w, qlm_comm* c, float* y,
+                              int64_t ldy, int flags, void* stream);
+
 /* Status of bounded device-side waits on `device`: QLM_OK, or QLM_ERR_TIMEOUT
  * if a kernel gave up waiting since the last reset (reset != 0 clears it).
  * Synchronous tensor-core calls check this themselves. */

@@ -24,7 +24,7 @@ import os
 import numpy as np
 
 __all__ = ["QlmError", "Int8Weight", "matmul", "load", "LIB_PATH", "EXACT", "TENSOR", "HOST_IO", "SYNC",
-           "BLOCK"]
+           "BLOCK", "Comm", "shard_rows", "matmul_allgather"]
 
 LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "lib", "libqlm_b200.so")
 BLOCK = 32
@@ -35,7 +35,8 @@ SRC_F32, SRC_BF16 = 0, 1
 ABI_SYMBOLS = (
     "qlm_abi_version", "qlm_last_error", "qlm_weight_quantize_upload", "qlm_weight_import_int8",
     "qlm_weight_export_int8", "qlm_weight_shape", "qlm_weight_bytes", "qlm_weight_free", "qlm_linear_int8",
-    "qlm_device_status", "qlm_stream_sync", "qlm_linear_int8_tc_noalloc",
+    "qlm_device_status", "qlm_stream_sync", "qlm_linear_int8_tc_noalloc", "qlm_comm_handle_bytes",
+    "qlm_comm_create", "qlm_comm_connect", "qlm_comm_free", "qlm_linear_int8_allgather",
 )
 
 _STATUS = {0: "OK", 1: "INVALID_ARG", 2: "CUDA", 3: "OUT_OF_MEMORY", 4: "UNSUPPORTED", 5: "TIMEOUT", 6: "NCCL",
@@ -76,6 +77,12 @@ def load(path: str = LIB_PATH):
     lib.qlm_stream_sync.argtypes = [P]
     lib.qlm_device_status.argtypes = [I, I]
     lib.qlm_linear_int8_tc_noalloc.argtypes = [P, I, I, L, P, P, L, I, P]
+    lib.qlm_comm_handle_bytes.restype = I
+    lib.qlm_comm_create.argtypes = [I, I, I, L, ctypes.POINTER(P), P]
+    lib.qlm_comm_connect.argtypes = [P, P]
+    lib.qlm_comm_free.argtypes = [P]
+    lib.qlm_comm_free.restype = None
+    lib.qlm_linear_int8_allgather.argtypes = [P, I, I, L, P, P, P, L, I, P]
     if lib.qlm_abi_version() != 1:
         raise QlmError(7, "ABI version mismatch")
     _lib = lib
@@ -247,3 +254,70 @@ def matmul(A, B: Int8Weight, C=None, transpose_B: bool = True, flags: int = EXAC
     _check(lib.qlm_linear_int8(a2.ctypes.data, M, K, a2.strides[0] // 4, B.handle, c2.ctypes.data,
                                c2.strides[0] // 4, flags | HOST_IO, _stream_ptr(stream)))
     return C
+
+
+def shard_rows(n: int, nranks: int, rank: int):
+    """Output rows [begin, end) that `rank` owns when n rows are split over
+    nranks GPUs as evenly as possible (the first n % nranks ranks get one more)."""
+    if not (0 <= rank < nranks):
+        raise QlmError(1, f"rank {rank} not in [0, {nranks})")
+    q, r = divmod(n, nranks)
+    begin = rank * q + min(rank, r)
+    return begin, begin + q + (1 if rank < r else 0)
+
+
+class Comm:
+    """One rank's NVLink exchange buffer for row-sharded outputs.
+
+    ``exchange`` maps this rank's handle (bytes) to the list of every rank's
+    handle in rank order — e.g. ``lambda h: all_gather_object(h)`` over
+    torch.distributed; the data path itself never touches it."""
+
+    def __init__(self, device: int, rank: int, nranks: int, max_out: int, exchange):
+        lib = load()
+        nb = lib.qlm_comm_handle_bytes()
+        buf = ctypes.create_string_buffer(nb)
+        h = ctypes.c_void_p()
+        _check(lib.qlm_comm_create(device, rank, nranks, max_out, ctypes.byref(h), buf))
+        self._h = h
+        self.device, self.rank, self.nranks, self.max_out = device, rank, nranks, max_out
+        handles = exchange(buf.raw)
+        if len(handles) != nranks or any(len(x) != nb for x in handles):
+            self.free()
+            raise QlmError(1, "handle exchange returned the wrong number or size of handles")
+        allb = ctypes.create_string_buffer(b"".join(handles), nb * nranks)
+        _check(lib.qlm_comm_connect(self._h, allb))
+
+    @property
+    def handle(self):
+        if not self._h:
+            raise QlmError(1, "communicator already freed")
+        return self._h
+
+    def free(self) -> None:
+        if self._h:
+            load().qlm_comm_free(self._h)
+            self._h = ctypes.c_void_p()
+
+    def __del__(self):
+        try:
+            self.free()
+        except Exception:
+            pass
+
+
+def matmul_allgather(x, w: Int8Weight, comm: Comm, y=None, flags: int = 0, stream=None):
+    """y[0:n_total] = x . W^T for a row-sharded W (this rank holds ``w``), the
+    shards gathered over NVLink by the GEMV kernel. x: CUDA float32 [K] or
+    [1, K]; y (allocated when None): CUDA float32 [1, n_total]."""
+    import torch
+    lib = load()
+    a2 = x if x.dim() == 2 else x.view(1, -1)
+    if a2.shape[0] != 1 or a2.dtype != torch.float32 or not a2.is_cuda:
+        raise QlmError(1, "x must be a CUDA float32 row")
+    if y is None:
+        y = torch.empty((1, w.n_total), dtype=torch.float32, device=x.device)
+    st = _stream_ptr(stream) if stream is not None else torch.cuda.current_stream(x.device).cuda_stream
+    _check(lib.qlm_linear_int8_allgather(a2.data_ptr(), 1, a2.shape[1], a2.stride(0), w.handle, comm.handle,
+                                         y.data_ptr(), y.shape[-1], flags, st))
+    return y

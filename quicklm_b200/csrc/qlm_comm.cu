@@ -1,0 +1,183 @@
+// qlm_comm.cu — row-sharded int8 linear with a fused NVLink all-gather.
+//
+// QuickLM runs on one CPU; the B200 build shards weight matrices by output
+// rows across the GPUs of a box (column-parallel lm_head / MLP / projections).
+// Row sharding preserves the reference's bits: each output element is still
+// computed by exactly one thread with the reference's sequence
+// (src/ops/math_ops.cpp:874-894), only on a different GPU.
+//
+// Exchange: every rank owns one exchange buffer (flags + two halves of the
+// gathered output) shared with the other ranks through CUDA IPC. A call is
+// ONE kernel: the GEMV stores each of its output rows straight into every
+// rank's buffer over NVLink (plain peer stores; no multicast); its last CTA
+// publishes the call's epoch to every rank's flags with system-scope release
+// stores, waits (bounded) until all ranks have published, and copies the
+// gathered row into y. The epoch lives on the device, so a sequence of calls
+// can be captured in a CUDA graph and replayed.
+#include "../../include/qlm_b200.h"
+#include "qlm_device.cuh"
+#include "qlm_handle.h"
+#include "qlm_kernels.h"
+
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <new>
+#include <string>
+
+struct qlm_comm {
+    int device = -1, rank = 0, nranks = 0, sm_count = 0;
+    long long max_out = 0;             // floats per output half
+    char* base = nullptr;              // local exchange buffer
+    char* peers[qlm::kMaxRanks] = {};  // every rank's buffer as seen from this device
+    bool opened[qlm::kMaxRanks] = {};
+    int* state = nullptr;              // [0] CTA counter, [1] epoch, [2] status
+};
+
+namespace qlm_internal {
+void set_last_error(const std::string& msg);
+}
+
+namespace {
+
+constexpr size_t kFlagBytes = 256;
+
+int fail(int code, const char* fmt, ...) {
+    char buf[384];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof(buf), fmt, ap);
+    va_end(ap);
+    qlm_internal::set_last_error(buf);
+    return code;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+    return fail(e == cudaErrorMemoryAllocation ? QLM_ERR_OUT_OF_MEMORY : QLM_ERR_CUDA, "%s: %s", what,
+                cudaGetErrorString(e));
+}
+
+struct Dev {
+    int prev = -1;
+    bool ok = false;
+    explicit Dev(int d) {
+        if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+        ok = cudaSetDevice(d) == cudaSuccess;
+    }
+    ~Dev() {
+        if (prev >= 0) cudaSetDevice(prev);
+    }
+};
+
+}  // namespace
+
+extern "C" {
+
+int qlm_comm_create(int device, int rank, int nranks, int64_t max_out, qlm_comm** out, void* handle_out) {
+    if (!out || !handle_out) return fail(QLM_ERR_INVALID_ARG, "NULL argument");
+    *out = nullptr;
+    if (nranks < 1 || nranks > qlm::kMaxRanks) return fail(QLM_ERR_INVALID_ARG, "nranks %d not in [1, %d]", nranks, qlm::kMaxRanks);
+    if (rank < 0 || rank >= nranks) return fail(QLM_ERR_INVALID_ARG, "rank %d not in [0, %d)", rank, nranks);
+    if (max_out <= 0) return fail(QLM_ERR_INVALID_ARG, "max_out must be positive");
+    Dev g(device);
+    if (!g.ok) return fail(QLM_ERR_CUDA, "cudaSetDevice(%d) failed", device);
+    qlm_comm* c = new (std::nothrow) qlm_comm();
+    if (!c) return fail(QLM_ERR_OUT_OF_MEMORY, "host allocation failed");
+    c->device = device;
+    c->rank = rank;
+    c->nranks = nranks;
+    c->max_out = max_out;
+    cudaError_t e = cudaDeviceGetAttribute(&c->sm_count, cudaDevAttrMultiProcessorCount, device);
+    const size_t bytes = kFlagBytes + 2 * (size_t)max_out * sizeof(float);
+    if (e == cudaSuccess) e = cudaMalloc(&c->base, bytes);
+    if (e == cudaSuccess) e = cudaMemset(c->base, 0, bytes);
+    if (e == cudaSuccess) e = cudaMalloc(&c->state, 4 * sizeof(int));
+    if (e == cudaSuccess) e = cudaMemset(c->state, 0, 4 * sizeof(int));
+    cudaIpcMemHandle_t h;
+    if (e == cudaSuccess) e = cudaIpcGetMemHandle(&h, c->base);
+    if (e != cudaSuccess) {
+        if (c->base) cudaFree(c->base);
+        if (c->state) cudaFree(c->state);
+        delete c;
+        return cuda_fail(e, "exchange buffer");
+    }
+    std::memcpy(handle_out, &h, sizeof(h));
+    c->peers[rank] = c->base;
+    *out = c;
+    return QLM_OK;
+}
+
+int qlm_comm_handle_bytes(void) { return (int)sizeof(cudaIpcMemHandle_t); }
+
+int qlm_comm_connect(qlm_comm* c, const void* all_handles) {
+    if (!c || !all_handles) return fail(QLM_ERR_INVALID_ARG, "NULL argument");
+    Dev g(c->device);
+    if (!g.ok) return fail(QLM_ERR_CUDA, "cudaSetDevice(%d) failed", c->device);
+    for (int r = 0; r < c->nranks; ++r) {
+        if (r == c->rank || c->opened[r]) continue;
+        cudaIpcMemHandle_t h;
+        std::memcpy(&h, static_cast<const char*>(all_handles) + (size_t)r * sizeof(h), sizeof(h));
+        void* ptr = nullptr;
+        const cudaError_t e = cudaIpcOpenMemHandle(&ptr, h, cudaIpcMemLazyEnablePeerAccess);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaIpcOpenMemHandle (peer exchange buffer)");
+        c->peers[r] = static_cast<char*>(ptr);
+        c->opened[r] = true;
+    }
+    return QLM_OK;
+}
+
+void qlm_comm_free(qlm_comm* c) {
+    if (!c) return;
+    Dev g(c->device);
+    for (int r = 0; r < c->nranks; ++r)
+        if (c->opened[r]) cudaIpcCloseMemHandle(c->peers[r]);
+    if (c->base) cudaFree(c->base);
+    if (c->state) cudaFree(c->state);
+    delete c;
+}
+
+int qlm_linear_int8_allgather(const float* x, int M, int k, int64_t ldx, const qlm_w8* w, qlm_comm* c, float* y,
+                              int64_t ldy, int flags, void* stream) {
+    if (!x || !w || !c || !y) return fail(QLM_ERR_INVALID_ARG, "NULL argument");
+    if (M != 1) return fail(QLM_ERR_UNSUPPORTED, "the fused all-gather serves decode (M = 1); got M=%d", M);
+    if (k != w->k || ldx < k) return fail(QLM_ERR_INVALID_ARG, "k=%d does not match the weight's k=%d", k, w->k);
+    if (ldy < w->n_total) return fail(QLM_ERR_INVALID_ARG, "ldy %lld < gathered width %d", (long long)ldy, w->n_total);
+    if (w->device != c->device) return fail(QLM_ERR_INVALID_ARG, "weight and communicator on different devices");
+    if (w->n_total > c->max_out) return fail(QLM_ERR_INVALID_ARG, "gathered width %d > exchange capacity %lld", w->n_total, c->max_out);
+    if (flags & ~QLM_LINEAR_SYNC) return fail(QLM_ERR_INVALID_ARG, "only QLM_LINEAR_SYNC is accepted (device pointers)");
+    for (int r = 0; r < c->nranks; ++r)
+        if (!c->peers[r]) return fail(QLM_ERR_INVALID_ARG, "communicator not connected (rank %d)", r);
+    Dev g(c->device);
+    if (!g.ok) return fail(QLM_ERR_CUDA, "cudaSetDevice(%d) failed", c->device);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+
+    qlm::GatherArgs ga{};
+    for (int r = 0; r < c->nranks; ++r) {
+        ga.peer_flags[r] = reinterpret_cast<int*>(c->peers[r]);
+        ga.peer_out[r] = reinterpret_cast<float*>(c->peers[r] + kFlagBytes);
+    }
+    ga.counter = c->state;
+    ga.epoch = c->state + 1;
+    ga.out_stride = c->max_out;
+    ga.nranks = c->nranks;
+    ga.rank = c->rank;
+    ga.col0 = w->row_begin;
+    ga.n_total = w->n_total;
+    cudaError_t e = qlm::launch_gemv_exact(x, ldx, 1, w->q, w->s, w->rows, k, y, ldy, c->state + 2, c->sm_count, s,
+                                           true, &ga);
+    if (e != cudaSuccess) return cuda_fail(e, "fused GEMV + all-gather launch");
+    if (flags & QLM_LINEAR_SYNC) {
+        e = cudaStreamSynchronize(s);
+        if (e != cudaSuccess) return cuda_fail(e, "stream synchronize");
+        int code = 0;
+        e = cudaMemcpy(&code, c->state + 2, sizeof(int), cudaMemcpyDeviceToHost);
+        if (e != cudaSuccess) return cuda_fail(e, "read status");
+        if (code) {
+            cudaMemset(c->state + 2, 0, sizeof(int));
+            return fail(QLM_ERR_TIMEOUT, "a bounded wait for peer ranks gave up (code 0x%x)", code);
+        }
+    }
+    return QLM_OK;
+}
+
+}  // extern "C"

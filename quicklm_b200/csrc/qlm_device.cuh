@@ -118,6 +118,20 @@ __device__ __forceinline__ void s8x4_to_f32x2(uint32_t w, unsigned long long& lo
     hi = f2sub(((unsigned long long)b3 << 32) | b2, bias);
 }
 
+// Release/acquire fence at system scope (orders this thread's, and by
+// cumulativity its CTA's barrier-ordered, memory accesses for peer GPUs).
+__device__ __forceinline__ void fence_acq_rel_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
+
+// System-scope release store / acquire load (flags shared with peer GPUs).
+__device__ __forceinline__ void st_release_sys(int* p, int v) {
+    asm volatile("st.release.sys.global.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ int ld_acquire_sys(const int* p) {
+    int v;
+    asm volatile("ld.acquire.sys.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
 // Programmatic dependent launch (sm_90+): let the next kernel in the stream
 // start launching, and wait until the previous kernel's results are visible.
 // Both are no-ops when the launch did not opt in.

@@ -40,6 +40,7 @@ constexpr long long kWaitBudget = 4000000000LL;  // ~2 s of SM clock
 constexpr int kMaxSegChunks = 16;                // chunks per slot (2048 K elements)
 constexpr int kSlotBytesPerChunk = 4 * (kChunk + 16);  // 4 rows x (128 int8 + 4 fp32 scales)
 constexpr int kStatusTimeout = 0x201;
+constexpr int kStatusGatherTimeout = 0x202;
 
 struct GemvParams {
     const float* x;
@@ -55,6 +56,9 @@ struct GemvParams {
     int d;           // slots per warp
     int xs_bytes;    // activation staging bytes (128-aligned)
     int ucta_q, ucta_r;  // units per CTA: CTA b owns [b*q + min(b, r), +q + (b < r))
+    // Row-sharded all-gather (M = 1): every output row is also stored into each
+    // rank's exchange buffer over NVLink, at column col0 + row.
+    GatherArgs ga;
 };
 
 // Balanced contiguous unit range of this CTA without any integer division.
@@ -312,6 +316,31 @@ __device__ __forceinline__ float4 block_sums(const float* __restrict__ xc, uint4
     return make_float4(bs[0], bs[1], bs[2], bs[3]);
 }
 
+// dst[i] = src[i] for i in [c0, c1) by all threads of the CTA: 16-byte moves
+// for the aligned middle (four loads in flight per thread), scalar edges.
+__device__ __forceinline__ void cta_copy(float* __restrict__ dst, const float* __restrict__ src, int c0, int c1) {
+    const int a0 = min(c1, (c0 + 3) & ~3), a1 = max(a0, c1 & ~3);
+    for (int i = c0 + (int)threadIdx.x; i < a0; i += blockDim.x) dst[i] = src[i];
+    for (int i = a1 + (int)threadIdx.x; i < c1; i += blockDim.x) dst[i] = src[i];
+    const float4* s4 = reinterpret_cast<const float4*>(src + a0);
+    float4* d4 = reinterpret_cast<float4*>(dst + a0);
+    const int n4 = (a1 - a0) / 4, step = (int)blockDim.x;
+    for (int base = 0; base < n4; base += 4 * step) {
+        float4 v[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const int i = base + u * step + (int)threadIdx.x;
+            if (i < n4) v[u] = s4[i];
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const int i = base + u * step + (int)threadIdx.x;
+            if (i < n4) d4[i] = v[u];
+        }
+    }
+}
+
+template <bool GATHER>
 __global__ void __launch_bounds__(704, 2) gemv_m1_kernel(const GemvParams p) {
     extern __shared__ __align__(128) uint8_t smem[];
     using namespace sm100;
@@ -470,7 +499,12 @@ __global__ void __launch_bounds__(704, 2) gemv_m1_kernel(const GemvParams p) {
                     }
                     v = __fadd_rn(v, __fmul_rn(acc, st));
                 }
-                p.y[row] = v;
+                if (GATHER) {
+                    // this rank's own exchange buffer; the last CTA pushes the shard to the peers
+                    p.ga.peer_out[p.ga.rank][((*p.ga.epoch + 1) & 1) * p.ga.out_stride + p.ga.col0 + row] = v;
+                } else {
+                    p.y[row] = v;
+                }
             }
             t = 0.0f;
         }
@@ -478,6 +512,62 @@ __global__ void __launch_bounds__(704, 2) gemv_m1_kernel(const GemvParams p) {
     if (lane32 == 0)
         for (int j = stop; j < stop + p.d && j < items; ++j)
             mbar_wait(bars + (j % p.d) * 8, (uint32_t)((j / p.d) & 1), nullptr, kWaitBudget);  // give-up path only
+    if (GATHER) {
+        // Completion: each CTA's rows are in this rank's own buffer; it counts
+        // itself done with a GPU-scope release. The last CTA acquires them,
+        // pushes the whole shard to every peer with 16-byte stores, releases
+        // them at system scope once, publishes this call's epoch e to every
+        // rank, waits (bounded) until every rank has published e, copies the
+        // gathered row into y and records e.
+        __shared__ int is_last, bad;
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            __threadfence();
+            is_last = atomicAdd(p.ga.counter, 1) == (int)gridDim.x - 1;
+            bad = 0;
+        }
+        __syncthreads();
+        if (is_last) {
+            __threadfence();
+            const int e = *p.ga.epoch + 1;
+            const long long half = (e & 1) * p.ga.out_stride;
+            const float* mine = p.ga.peer_out[p.ga.rank] + half;
+#pragma unroll 1
+            for (int r = 0; r < p.ga.nranks; ++r)
+                if (r != p.ga.rank) cta_copy(p.ga.peer_out[r] + half, mine, p.ga.col0, p.ga.col0 + p.rows);
+            __syncthreads();
+            if (threadIdx.x == 0) {
+                fence_acq_rel_sys();
+#pragma unroll 1
+                for (int r = 0; r < p.ga.nranks; ++r) st_release_sys(p.ga.peer_flags[r] + p.ga.rank, e);
+            }
+            if ((int)threadIdx.x < p.ga.nranks) {
+                const int* flag = p.ga.peer_flags[p.ga.rank] + threadIdx.x;  // this rank's own flag array
+                const long long t0 = clock64();
+                while (ld_acquire_sys(flag) - e < 0) {
+                    if (clock64() - t0 > kWaitBudget) {
+                        bad = 1;
+                        if (p.status) atomicCAS(p.status, 0, kStatusGatherTimeout);
+                        break;
+                    }
+                    __nanosleep(32);
+                }
+            }
+            __syncthreads();
+            if (!bad) {
+                if ((reinterpret_cast<uintptr_t>(p.y) & 15) == 0) {
+                    cta_copy(p.y, mine, 0, p.ga.n_total);
+                } else {
+                    for (int i = threadIdx.x; i < p.ga.n_total; i += blockDim.x) p.y[i] = mine[i];
+                }
+            }
+            __syncthreads();
+            if (threadIdx.x == 0) {
+                *p.ga.counter = 0;
+                *const_cast<int*>(p.ga.epoch) = e;
+            }
+        }
+    }
 }
 
 struct Plan {
@@ -521,16 +611,17 @@ bool make_plan(int mm, int rows, int k, int sm_count, Plan* pl) {
 
 template <int MM>
 cudaError_t launch_mm(const GemvParams& p0, const Plan& pl, cudaStream_t stream, bool pdl) {
-    static bool attr_set[64] = {};
+    static bool attr_set[2][64] = {};
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
     if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
-    auto kern = MM == 1 ? gemv_m1_kernel : gemv_stream_kernel<MM>;
-    if (!attr_set[dev]) {
-        e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+    auto kern = MM == 1 ? (p0.ga.nranks > 0 ? gemv_m1_kernel<true> : gemv_m1_kernel<false>) : gemv_stream_kernel<MM>;
+    const int gi = p0.ga.nranks > 0 ? 1 : 0;
+    if (!attr_set[gi][dev]) {
+        e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 224 * 1024);
         if (e != cudaSuccess) return e;
-        attr_set[dev] = true;
+        attr_set[gi][dev] = true;
     }
     GemvParams p = p0;
     p.units = (p.rows + (MM == 1 ? 1 : 3)) / (MM == 1 ? 2 : 4);
@@ -553,6 +644,7 @@ cudaError_t launch_mm(const GemvParams& p0, const Plan& pl, cudaStream_t stream,
     return cudaLaunchKernelEx(&cfg, kern, p);
 }
 
+
 }  // namespace
 
 bool gemv_supported(int mm, int rows, int k, int sm_count) {
@@ -561,10 +653,13 @@ bool gemv_supported(int mm, int rows, int k, int sm_count) {
 }
 
 cudaError_t launch_gemv_exact(const float* x, int64_t ldx, int mm, const uint8_t* q, const float* s, int rows,
-                              int k, float* y, int64_t ldy, int* status, int sm_count, cudaStream_t stream, bool pdl) {
+                              int k, float* y, int64_t ldy, int* status, int sm_count, cudaStream_t stream, bool pdl,
+                              const GatherArgs* gather) {
     Plan pl;
     if (!make_plan(mm, rows, k, sm_count, &pl)) return cudaErrorInvalidValue;
+    if (gather && mm != 1) return cudaErrorInvalidValue;
     GemvParams p{};
+    if (gather) p.ga = *gather;
     p.x = x;
     p.ldx = ldx;
     p.q = q;

@@ -14,10 +14,33 @@ namespace qlm {
 cudaError_t launch_quantize_pack(const void* src, int dtype, int64_t src_stride, int rows, int k, uint8_t* q,
                                  float* scales, cudaStream_t stream);
 
+constexpr int kMaxRanks = 8;
+
+// Peer pointers for the fused GEMV + all-gather (M = 1). peer_out[r] is
+// rank r's exchange area (two halves of out_stride floats, picked by epoch
+// parity), peer_flags[r] its flag array. Device-resident state of this rank:
+// counter (CTA completions, starts at 0) and epoch (last completed call).
+// A call works on epoch e = *epoch + 1, publishes e to every rank, and its
+// last CTA waits for every rank's e before copying the gathered row to y.
+struct GatherArgs {
+    float* peer_out[kMaxRanks];
+    int* peer_flags[kMaxRanks];
+    int* counter;
+    const int* epoch;
+    long long out_stride;
+    int n_total; // gathered width copied into y by the last CTA
+    int nranks;  // 0 = no gather
+    int rank;
+    int col0;    // this shard's first output column
+};
+
 // Bit-exact y[m][0:rows] = x[m][0:k] . W^T for m < mm (1..8), W packed.
-// status: device int set non-zero if a bounded wait gave up.
+// status: device int set non-zero if a bounded wait gave up. With gather
+// (mm == 1 only) the rows are stored into every rank's exchange buffer
+// instead of y.
 cudaError_t launch_gemv_exact(const float* x, int64_t ldx, int mm, const uint8_t* q, const float* s, int rows,
-                              int k, float* y, int64_t ldy, int* status, int sm_count, cudaStream_t stream, bool pdl);
+                              int k, float* y, int64_t ldy, int* status, int sm_count, cudaStream_t stream, bool pdl,
+                              const GatherArgs* gather = nullptr);
 
 // Whether the exact GEMV can stage mm activation rows of length k.
 bool gemv_supported(int mm, int rows, int k, int sm_count);
