@@ -419,8 +419,8 @@ def main():
                        "l2": f"inputs larger than L2 ({STACK}x{weight_bytes() / 1e6:.2f} MB weights per step)",
                        "parallelism": "single GPU" if world == 1 else
                        f"row-sharded x{world}, all-gather fused into the GEMV (NVLink peer stores)",
-                       "kernel": "gemv_m1_kernel (CUDA cores, bit-exact)" if world == 1 else
-                       "gemv_m1_kernel<gather> + gather_wait_copy_kernel", "cuda_graph": used_graph,
+                       "kernel": "gemv_kernel<1,R> (CUDA cores, bit-exact)" if world == 1 else
+                       "gemv_kernel<1,R,gather> (fused NVLink all-gather)", "cuda_graph": used_graph,
                        "pdl": os.environ.get("QLM_PDL", "1") != "0"},
             "pct_hbm_peak": round(100.0 * value / world / peak, 2),
             "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": peak, "unit": "GB/s",

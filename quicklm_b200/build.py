@@ -56,7 +56,8 @@ def build(force: bool = False, verbose: bool = False) -> str:
     objs = []
     for src in sources():
         obj = os.path.join(OBJ, os.path.basename(src)[:-3] + ".o")
-        cmd = [cc, *ARCH, *NVCC_FLAGS, "-I", os.path.join(ROOT, "include"), "-c", src, "-o", obj]
+        cmd = [cc, *ARCH, *NVCC_FLAGS, "-I", os.path.join(ROOT, "include"),
+               "-c", src, "-o", obj]
         if verbose:
             cmd += ["-Xptxas", "-v"]
             print(" ".join(cmd), flush=True)

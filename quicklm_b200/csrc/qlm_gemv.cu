@@ -14,21 +14,33 @@
 // input (including NaN/Inf propagation).
 //
 // Mapping: one thread per (output row, lane l), 8 consecutive threads per row,
-// 4 rows ("a unit") per warp. The chain t_l is the thread's register; the
-// 8->1 tree is three xor-shuffles inside the row's 8 threads. The exact
-// int8 -> fp32 conversion runs on paired fp32 subtracts; every product, sum
-// and FMA of the reference's sequence is a scalar round-to-nearest op.
+// 4 rows ("a unit") per warp; every thread runs its own chain t_l over all
+// blocks in order, and the 8->1 tree is three xor-shuffles inside the row's 8
+// threads. Within a thread two neighbouring blocks are independent until their
+// FMA, so the int8 -> fp32 conversion, the products and the three sums of
+// blocks b and b+1 run as paired fp32 ops (one f32x2 instruction for both
+// blocks); only the FMA chain is scalar.
+//
+// The products are fma.rn.f32x2(x, q, z) with z = -0.0 read from the kernel
+// parameters: fma(x, q, -0) rounds x*q once and keeps its sign, so it is
+// bit-identical to mul.rn(x, q) for every input, but ptxas cannot see that z
+// is a zero. With mul.rn.f32x2 products, ptxas (CUDA 12.9, sm_100a) contracts
+// the paired add.rn.f32x2 that consumes them into fma(x0, q0, p1) despite the
+// .rn qualifiers, with or without --fmad=false and through an opaque mov
+// (identified bit-for-bit against a CPU emulation of that contraction); a
+// compile-time -0.0 addend is folded and contracted the same way.
 //
 // Memory: each warp streams its units' packed rows (and their scales) into
 // private shared-memory slots with 1-D cp.async.bulk copies completing on an
-// mbarrier. A warp issues its first slots BEFORE the programmatic-dependent-
-// launch wait, so a kernel in a stream or CUDA graph starts pulling weights
-// from HBM while its predecessor is still computing; with one CTA per SM and
-// a balanced contiguous unit range per CTA, a decode-sized matrix is in
-// flight in full within the first microsecond. The activations for all MM
-// rows are staged once per CTA in a lane-permuted shared layout (one
-// conflict-free float4 per lane per step). Waits are bounded: on give-up the
-// kernel records a status code and stops.
+// mbarrier, one slot per (unit, segment of the row), so the chain starts on a
+// row's first segment while the rest is still in flight. A warp issues its
+// first slots BEFORE the programmatic-dependent-launch wait, so a kernel in a
+// stream or CUDA graph starts pulling weights from HBM while its predecessor
+// is still computing; with one CTA per SM and a balanced contiguous unit range
+// per CTA, a decode-sized matrix is in flight in full within the first
+// microsecond. The activations for all MM rows are staged once per CTA in a
+// lane-permuted shared layout (one conflict-free float4 per lane per step).
+// Waits are bounded: on give-up the kernel records a status code and stops.
 #include "qlm_device.cuh"
 #include "qlm_kernels.h"
 #include "qlm_sm100.cuh"
@@ -37,21 +49,22 @@ namespace qlm {
 namespace {
 
 constexpr long long kWaitBudget = 4000000000LL;  // ~2 s of SM clock
-constexpr int kMaxSegChunks = 16;                // chunks per slot (2048 K elements)
-constexpr int kSlotBytesPerChunk = 4 * (kChunk + 16);  // 4 rows x (128 int8 + 4 fp32 scales)
+constexpr int kMaxSegChunks = 8;                 // chunks per slot (1024 K elements)
+constexpr int kRowChunkBytes = kChunk + 16;  // one row x one chunk: 128 int8 + 4 fp32 scales
 constexpr int kStatusTimeout = 0x201;
 constexpr int kStatusGatherTimeout = 0x202;
 
 struct GemvParams {
     const float* x;
     int64_t ldx;
+    float zero_neg;  // -0.0f: the product addend (see the file header)
     const uint8_t* q;
     const float* s;
     float* y;
     int64_t ldy;
     int* status;
     int rows, k, k_pad, nb_pad;
-    int units;       // ceil(rows / 4)
+    int units;       // ceil(rows / (4 R))
     int sc, nseg;    // chunks per segment, segments per row
     int d;           // slots per warp
     int xs_bytes;    // activation staging bytes (128-aligned)
@@ -75,245 +88,62 @@ __device__ __forceinline__ int xperm(int k) {
     return (k & ~(kChunk - 1)) + ((k >> 3) & 3) * 32 + (k & 7) * 4 + ((k >> 5) & 3);
 }
 
-// One 128-element chunk for this lane: 4 blocks x 4 steps, scales sv[0..3].
-// Every product, sum and FMA of the reference's sequence is a scalar
-// round-to-nearest op (the scalar .rn forms are never contracted by ptxas;
-// paired f32x2 mul/add were seen to be contracted into a paired FMA).
-template <int MM>
-__device__ __forceinline__ void chunk_update(const float* __restrict__ xs_chunk, int k_pad, int lane, uint4 qv,
-                                             float4 sv, float (&t)[MM], int nblocks) {
-    const uint32_t w[4] = {qv.x ^ 0x80808080u, qv.y ^ 0x80808080u, qv.z ^ 0x80808080u, qv.w ^ 0x80808080u};
-    const float sc[4] = {sv.x, sv.y, sv.z, sv.w};
-    float qf[4][4];  // [block][step], exact: (2^23 + q + 128) - (2^23 + 128)
+// One 128-element chunk of this lane for the thread's R rows. Row i's 16-byte
+// slice (at sq + i * qstride) holds blocks 0..3 (one word each) x steps 0..3
+// (one byte each); its four scales are at ss + i * sstride. The activations
+// are loaded once per chunk and reused for all R rows. Blocks are processed in
+// pairs (0,1) and (2,3): each f32x2 op below is the reference's scalar op for
+// both blocks of a pair, so every rounding matches, and the FMAs run in block
+// order. nz = (-0, -0) from the kernel parameters. With FULL = false only
+// the first nblocks blocks enter the chain (the last chunk of a row with
+// K % 128 != 0).
+template <int MM, int R, bool FULL>
+__device__ __forceinline__ void chunk_update(const float* __restrict__ xs_chunk, int k_pad, int lane,
+                                             const uint8_t* sq, int qstride, const uint8_t* ss, int sstride,
+                                             unsigned long long nz, float (&t)[MM][R], int nblocks) {
+    uint4 qv[R];
+    float4 sv[R];
 #pragma unroll
-    for (int bb = 0; bb < 4; ++bb)
-#pragma unroll
-        for (int j = 0; j < 4; ++j)
-            qf[bb][j] = __fsub_rn(__uint_as_float(__byte_perm(w[bb], 0x4B000000u, 0x7540u | (uint32_t)j)),
-                                  8388736.0f);
+    for (int i = 0; i < R; ++i) {
+        qv[i] = *reinterpret_cast<const uint4*>(sq + i * qstride);
+        sv[i] = *reinterpret_cast<const float4*>(ss + i * sstride);
+    }
+    const unsigned long long bias = 0x4B0000804B000080ull;  // (2^23 + 128) x 2
 #pragma unroll
     for (int m = 0; m < MM; ++m) {
         const float* xm = xs_chunk + (size_t)m * k_pad + lane * 4;
         float4 xv[4];  // step j: blocks 0..3
 #pragma unroll
         for (int j = 0; j < 4; ++j) xv[j] = *reinterpret_cast<const float4*>(xm + j * 32);
-        float tt = t[m];
 #pragma unroll
-        for (int bb = 0; bb < 4; ++bb) {
-            if (bb < nblocks) {
-                const float x0 = bb == 0 ? xv[0].x : bb == 1 ? xv[0].y : bb == 2 ? xv[0].z : xv[0].w;
-                const float x1 = bb == 0 ? xv[1].x : bb == 1 ? xv[1].y : bb == 2 ? xv[1].z : xv[1].w;
-                const float x2 = bb == 0 ? xv[2].x : bb == 1 ? xv[2].y : bb == 2 ? xv[2].z : xv[2].w;
-                const float x3 = bb == 0 ? xv[3].x : bb == 1 ? xv[3].y : bb == 2 ? xv[3].z : xv[3].w;
-                const float p0 = __fmul_rn(x0, qf[bb][0]);
-                const float p1 = __fmul_rn(x1, qf[bb][1]);
-                const float p2 = __fmul_rn(x2, qf[bb][2]);
-                const float p3 = __fmul_rn(x3, qf[bb][3]);
-                tt = __fmaf_rn(__fadd_rn(__fadd_rn(p0, p1), __fadd_rn(p2, p3)), sc[bb], tt);
-            }
-        }
-        t[m] = tt;
-    }
-}
-
-template <int MM>
-__global__ void __launch_bounds__(512, 1) gemv_stream_kernel(const GemvParams p) {
-    extern __shared__ __align__(128) uint8_t smem[];
-    using namespace sm100;
-    const int warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5, lane32 = threadIdx.x & 31;
-    const int lane = threadIdx.x & 7;         // reference lane l
-    const int rsub = (threadIdx.x >> 3) & 3;  // row within the warp's unit
-
-    const int slot_bytes = p.sc * kSlotBytesPerChunk;
-    float* xs = reinterpret_cast<float*>(smem);
-    uint8_t* my_slots = smem + p.xs_bytes + (size_t)warp * p.d * slot_bytes;
-    const uint32_t bars = smem_u32(smem + p.xs_bytes + (size_t)nwarps * p.d * slot_bytes) + warp * p.d * 8;
-    volatile int* abort_flag = reinterpret_cast<volatile int*>(
-        smem + p.xs_bytes + (size_t)nwarps * p.d * slot_bytes + (size_t)nwarps * p.d * 8);
-
-    // Balanced contiguous unit range for this CTA; warp w takes units w, w+nwarps, ...
-    int u_begin, u_end;
-    cta_units(p, u_begin, u_end);
-    const int my_units = warp < (u_end - u_begin) ? (u_end - u_begin - warp + nwarps - 1) / nwarps : 0;
-    const int items = my_units * p.nseg;
-    const int nck = p.k_pad / kChunk;
-
-    auto issue = [&](int item, int slot) {
-        // lane 0 only: unit's 4 rows, chunks [g*sc, g*sc + n) of segment g
-        const int u = u_begin + warp + (item / p.nseg) * nwarps;
-        const int g = item % p.nseg;
-        const int c0 = g * p.sc;
-        const int n = min(p.sc, nck - c0);
-        const uint32_t bar = bars + slot * 8;
-        const uint32_t dst = smem_u32(my_slots + (size_t)slot * slot_bytes);
-        int valid = min(4, p.rows - 4 * u);
-        mbar_arrive_expect_tx(bar, (uint32_t)(valid * n * (kChunk + 16)));
-        for (int r = 0; r < valid; ++r) {
-            const int row = 4 * u + r;
-            bulk_copy_g2s(dst + r * p.sc * kChunk, p.q + (int64_t)row * p.k_pad + (int64_t)c0 * kChunk,
-                          (uint32_t)(n * kChunk), bar);
-            bulk_copy_g2s(dst + 4 * p.sc * kChunk + r * p.sc * 16, p.s + (int64_t)row * p.nb_pad + c0 * 4,
-                          (uint32_t)(n * 16), bar);
-        }
-    };
-
-    if (lane32 == 0) {
-        for (int i = 0; i < p.d; ++i) mbar_init(bars + i * 8, 1);
-        if (warp == 0) *abort_flag = 0;
-        mbar_fence_init();
-        for (int i = 0; i < p.d && i < items; ++i) issue(i, i);
-    }
-    pdl_launch_dependents();
-    // Activations are produced by the previous kernel in the stream.
-    pdl_wait();
-    // All of a thread's loads are issued before its first store, so staging
-    // costs one L2 round trip per 8 elements per thread, not one per element.
-#pragma unroll 1
-    for (int m = 0; m < MM; ++m) {
-        const float* xr = p.x + (int64_t)m * p.ldx;
-        float* xd = xs + m * p.k_pad;
-        for (int base = 0; base < p.k_pad; base += 8 * (int)blockDim.x) {
-            float v[8];
+        for (int i = 0; i < R; ++i) {
+            const uint32_t w[4] = {qv[i].x ^ 0x80808080u, qv[i].y ^ 0x80808080u, qv[i].z ^ 0x80808080u,
+                                   qv[i].w ^ 0x80808080u};
+            float tt = t[m][i];
 #pragma unroll
-            for (int i = 0; i < 8; ++i) {
-                const int kk = base + (int)threadIdx.x + i * (int)blockDim.x;
-                v[i] = kk < p.k ? __ldg(xr + kk) : 0.0f;
-            }
+            for (int h = 0; h < 2; ++h) {
+                unsigned long long qp[4];  // step j: (q of block 2h, q of block 2h+1), exact
 #pragma unroll
-            for (int i = 0; i < 8; ++i) {
-                const int kk = base + (int)threadIdx.x + i * (int)blockDim.x;
-                if (kk < p.k_pad) xd[xperm(kk)] = v[i];
+                for (int j = 0; j < 4; ++j)
+                    qp[j] = f2sub(u2pack(__byte_perm(w[2 * h], 0x4B000000u, 0x7540u | (uint32_t)j),
+                                         __byte_perm(w[2 * h + 1], 0x4B000000u, 0x7540u | (uint32_t)j)),
+                                  bias);
+                const unsigned long long p0 =
+                    f2fma(h ? f2pack(xv[0].z, xv[0].w) : f2pack(xv[0].x, xv[0].y), qp[0], nz);
+                const unsigned long long p1 =
+                    f2fma(h ? f2pack(xv[1].z, xv[1].w) : f2pack(xv[1].x, xv[1].y), qp[1], nz);
+                const unsigned long long p2 =
+                    f2fma(h ? f2pack(xv[2].z, xv[2].w) : f2pack(xv[2].x, xv[2].y), qp[2], nz);
+                const unsigned long long p3 =
+                    f2fma(h ? f2pack(xv[3].z, xv[3].w) : f2pack(xv[3].x, xv[3].y), qp[3], nz);
+                float b0, b1;  // block sums of blocks 2h and 2h+1
+                f2unpack(f2add(f2add(p0, p1), f2add(p2, p3)), b0, b1);
+                if (FULL || 2 * h < nblocks) tt = __fmaf_rn(b0, h ? sv[i].z : sv[i].x, tt);
+                if (FULL || 2 * h + 1 < nblocks) tt = __fmaf_rn(b1, h ? sv[i].w : sv[i].y, tt);
             }
+            t[m][i] = tt;
         }
     }
-    __syncthreads();
-
-    const int nbf = p.k / kBlock;  // full blocks
-    const int cfull = nbf / 4;     // chunks of 4 full blocks
-    const int rem_blocks = nbf - cfull * 4;
-    const int nchunks = cfull + (rem_blocks ? 1 : 0);
-
-    float t[MM];
-#pragma unroll
-    for (int m = 0; m < MM; ++m) t[m] = 0.0f;
-
-    int stop = items;  // first item not consumed (== items on the normal path)
-    for (int i = 0; i < items; ++i) {
-        const int slot = i % p.d;
-        const int u = u_begin + warp + (i / p.nseg) * nwarps;
-        const int g = i % p.nseg;
-        if (!mbar_wait(bars + slot * 8, (uint32_t)((i / p.d) & 1), abort_flag, kWaitBudget)) {
-            *abort_flag = 1;
-            if (lane32 == 0 && p.status) atomicCAS(p.status, 0, kStatusTimeout);
-            stop = i;
-            break;
-        }
-        const uint8_t* sq = my_slots + (size_t)slot * slot_bytes + rsub * p.sc * kChunk + lane * 16;
-        const uint8_t* ss = my_slots + (size_t)slot * slot_bytes + 4 * p.sc * kChunk + rsub * p.sc * 16;
-        const int c0 = g * p.sc;
-        const int c1 = min(c0 + p.sc, nchunks);
-        const int cf = min(c1, cfull);  // chunks made of four full blocks
-        int c = c0;
-#pragma unroll 2
-        for (; c < cf; ++c) {
-            const uint4 qv = *reinterpret_cast<const uint4*>(sq + (c - c0) * kChunk);
-            const float4 sv = *reinterpret_cast<const float4*>(ss + (c - c0) * 16);
-            chunk_update<MM>(xs + c * kChunk, p.k_pad, lane, qv, sv, t, 4);
-        }
-        if (c < c1) {  // the chunk holding the last (1..3) full blocks
-            const uint4 qv = *reinterpret_cast<const uint4*>(sq + (c - c0) * kChunk);
-            const float4 sv = *reinterpret_cast<const float4*>(ss + (c - c0) * 16);
-            chunk_update<MM>(xs + c * kChunk, p.k_pad, lane, qv, sv, t, rem_blocks);
-        }
-        __syncwarp();
-        if (lane32 == 0 && i + p.d < items) {
-            fence_proxy_async_smem();
-            issue(i + p.d, slot);
-        }
-        if (g == p.nseg - 1) {
-            const int row_raw = 4 * u + rsub;
-            const bool valid = row_raw < p.rows;
-            const int row = valid ? row_raw : p.rows - 1;
-#pragma unroll
-            for (int m = 0; m < MM; ++m) {
-                float v = t[m];
-                v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, 4));
-                v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, 1));
-                v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, 2));
-                t[m] = v;
-            }
-            if (lane == 0 && valid) {
-                if (p.k > nbf * kBlock) {
-                    // Ragged tail: sequential scalar sum times the last block's scale.
-                    const uint8_t* qr = p.q + (int64_t)row * p.k_pad;
-                    const float st = p.s[(int64_t)row * p.nb_pad + nbf];
-#pragma unroll
-                    for (int m = 0; m < MM; ++m) {
-                        float acc = 0.0f;
-                        for (int kk = nbf * kBlock; kk < p.k; ++kk) {
-                            const float qf = (float)(int8_t)qr[packed_offset(kk)];
-                            acc = __fadd_rn(acc, __fmul_rn(xs[m * p.k_pad + xperm(kk)], qf));
-                        }
-                        t[m] = __fadd_rn(t[m], __fmul_rn(acc, st));
-                    }
-                }
-#pragma unroll
-                for (int m = 0; m < MM; ++m) p.y[(int64_t)m * p.ldy + row] = t[m];
-            }
-#pragma unroll
-            for (int m = 0; m < MM; ++m) t[m] = 0.0f;
-        }
-    }
-    // Drain after a give-up: items [stop, stop + d) were issued but not
-    // consumed; their copies must land before this warp's slots are released.
-    if (lane32 == 0)
-        for (int j = stop; j < stop + p.d && j < items; ++j)
-            mbar_wait(bars + (j % p.d) * 8, (uint32_t)((j / p.d) & 1), nullptr, kWaitBudget);
-}
-
-// ---------------------------------------------------------------------------
-// M = 1 (decode) kernel. Same arithmetic, organised for more warps per SM:
-// a warp owns a 2-row unit; phase 1 (all 32 threads, uniform): every thread
-// turns its 16-byte slices into the four block sums bs = (p0+p1)+(p2+p3) of
-// the reference and writes them over the int8 bytes it just consumed (same 16
-// bytes); phase 2: one thread per (row, lane) runs the FMA chain
-// t = fma(bs, s, t) over every block in order from shared memory. The block
-// sums have no ordering constraint, so phase 1 splits each row's chunks
-// between two thread halves; the chain stays sequential per (row, lane).
-// Activations are staged block-major: x of (chunk c, block bb, lane l, step j)
-// at c*128 + bb*32 + l*4 + j, one float4 per lane per block.
-__device__ __forceinline__ int xperm_bm(int k) {
-    return (k & ~(kChunk - 1)) + ((k >> 5) & 3) * 32 + (k & 7) * 4 + ((k >> 3) & 3);
-}
-
-constexpr int kM1SlotBytesPerChunk = 2 * (kChunk + 16);  // 2 rows x (128 int8 + 4 fp32 scales)
-
-// Block sums of one 16-byte lane slice: bs[bb] = (p0 + p1) + (p2 + p3) with
-// p_j = x_j * q_j. The int8 -> fp32 bias subtracts and the products run as
-// paired fp32 ops; the two products of a pair are then added horizontally
-// with scalar .rn adds, a shape ptxas cannot contract into a paired FMA (it
-// did contract paired products feeding a paired add).
-__device__ __forceinline__ float4 block_sums(const float* __restrict__ xc, uint4 qv, int nblocks) {
-    const uint32_t w[4] = {qv.x ^ 0x80808080u, qv.y ^ 0x80808080u, qv.z ^ 0x80808080u, qv.w ^ 0x80808080u};
-    const unsigned long long bias = 0x4B0000804B000080ull;  // (2^23 + 128) x 2
-    float bs[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-    for (int bb = 0; bb < 4; ++bb) {
-        if (bb < nblocks) {
-            const float4 xv = *reinterpret_cast<const float4*>(xc + bb * 32);
-            const uint32_t f0 = __byte_perm(w[bb], 0x4B000000u, 0x7540u);
-            const uint32_t f1 = __byte_perm(w[bb], 0x4B000000u, 0x7541u);
-            const uint32_t f2 = __byte_perm(w[bb], 0x4B000000u, 0x7542u);
-            const uint32_t f3 = __byte_perm(w[bb], 0x4B000000u, 0x7543u);
-            const unsigned long long q01 = f2sub(((unsigned long long)f1 << 32) | f0, bias);
-            const unsigned long long q23 = f2sub(((unsigned long long)f3 << 32) | f2, bias);
-            float p0, p1, p2, p3;
-            f2unpack(f2mul(f2pack(xv.x, xv.y), q01), p0, p1);
-            f2unpack(f2mul(f2pack(xv.z, xv.w), q23), p2, p3);
-            bs[bb] = __fadd_rn(__fadd_rn(p0, p1), __fadd_rn(p2, p3));
-        }
-    }
-    return make_float4(bs[0], bs[1], bs[2], bs[3]);
 }
 
 // dst[i] = src[i] for i in [c0, c1) by all threads of the CTA: 16-byte moves
@@ -340,52 +170,62 @@ __device__ __forceinline__ void cta_copy(float* __restrict__ dst, const float* _
     }
 }
 
-template <bool GATHER>
-__global__ void __launch_bounds__(704, 2) gemv_m1_kernel(const GemvParams p) {
+// R rows per thread (4R per warp unit): the activations a thread loads from
+// shared memory serve R rows, which halves the shared-memory traffic and the
+// load instructions per weight byte at R = 2 (every 128-bit shared load is
+// served per quarter-warp, so rows of one warp cannot share a load). M = 1:
+// up to 12 warps and 80 registers, so two CTAs fit on an SM and the next
+// kernel's CTA can start its weight copies while this one finishes.
+template <int MM, int R, bool GATHER>
+__global__ void __launch_bounds__(MM == 1 ? 384 : 512, MM == 1 ? 2 : 1) gemv_kernel(const GemvParams p) {
     extern __shared__ __align__(128) uint8_t smem[];
     using namespace sm100;
     const int warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5, lane32 = threadIdx.x & 31;
-    const int lane = threadIdx.x & 7;           // reference lane l
-    const int rsub = (threadIdx.x >> 3) & 1;    // row within the warp's 2-row unit
-    const int half = (threadIdx.x >> 4) & 1;    // phase-1 chunk parity
+    const int lane = threadIdx.x & 7;                // reference lane l
+    const int rsub = ((threadIdx.x >> 3) & 3) * R;   // first of the thread's R rows within the unit
+    constexpr int kUnitRows = 4 * R;
 
-    const int slot_bytes = p.sc * kM1SlotBytesPerChunk;
+    const int slot_bytes = p.sc * kUnitRows * kRowChunkBytes;
     float* xs = reinterpret_cast<float*>(smem);
     uint8_t* my_slots = smem + p.xs_bytes + (size_t)warp * p.d * slot_bytes;
     const uint32_t bars = smem_u32(smem + p.xs_bytes + (size_t)nwarps * p.d * slot_bytes) + warp * p.d * 8;
     volatile int* abort_flag = reinterpret_cast<volatile int*>(
         smem + p.xs_bytes + (size_t)nwarps * p.d * slot_bytes + (size_t)nwarps * p.d * 8);
 
+    // Balanced contiguous unit range for this CTA; warp w takes units w,
+    // w + nwarps, ...; its work items are (unit, segment g), g fastest.
     int u_begin, u_end;
     cta_units(p, u_begin, u_end);
-    // Work items of this warp: (unit u_begin + warp + j*nwarps, segment g),
-    // g fastest. Counted without division.
     int my_units = 0;
     for (int u = u_begin + warp; u < u_end; u += nwarps) ++my_units;
     const int items = my_units * p.nseg;
     const int nck = p.k_pad >> 7;
 
-    auto issue = [&](int uu, int g, int slot) {  // lane 0 only: unit index uu of this warp, segment g
+    // Whole warp: lane r < 4R copies row r's int8 slice, lane 16 + r its scales.
+    auto issue = [&](int uu, int g, int slot) {
         const int u = u_begin + warp + uu * nwarps;
         const int c0 = g * p.sc;
         const int n = min(p.sc, nck - c0);
         const uint32_t bar = bars + slot * 8;
         const uint32_t dst = smem_u32(my_slots + (size_t)slot * slot_bytes);
-        const int valid = min(2, p.rows - 2 * u);
-        mbar_arrive_expect_tx(bar, (uint32_t)(valid * n * (kChunk + 16)));
-        for (int r = 0; r < valid; ++r) {
-            const int row = 2 * u + r;
+        const int valid = min(kUnitRows, p.rows - kUnitRows * u);
+        if (lane32 == 0) mbar_arrive_expect_tx(bar, (uint32_t)(valid * n * kRowChunkBytes));
+        const int r = lane32 & 15, row = kUnitRows * u + r;
+        if (lane32 < 16 && r < valid)
             bulk_copy_g2s(dst + r * p.sc * kChunk, p.q + (int64_t)row * p.k_pad + (int64_t)c0 * kChunk,
                           (uint32_t)(n * kChunk), bar);
-            bulk_copy_g2s(dst + 2 * p.sc * kChunk + r * p.sc * 16, p.s + (int64_t)row * p.nb_pad + c0 * 4,
+        else if (lane32 >= 16 && r < valid)
+            bulk_copy_g2s(dst + kUnitRows * p.sc * kChunk + r * p.sc * 16, p.s + (int64_t)row * p.nb_pad + c0 * 4,
                           (uint32_t)(n * 16), bar);
-        }
     };
 
     if (lane32 == 0) {
         for (int i = 0; i < p.d; ++i) mbar_init(bars + i * 8, 1);
         if (warp == 0) *abort_flag = 0;
         mbar_fence_init();
+    }
+    __syncwarp();
+    {
         int uu = 0, g = 0;
         for (int i = 0; i < p.d && i < items; ++i) {
             issue(uu, g, i);
@@ -393,9 +233,14 @@ __global__ void __launch_bounds__(704, 2) gemv_m1_kernel(const GemvParams p) {
         }
     }
     pdl_launch_dependents();
-    pdl_wait();  // activations are produced by the previous kernel in the stream
-    {
-        const float* xr = p.x;
+    // Activations are produced by the previous kernel in the stream. All of a
+    // thread's loads are issued before its first store, so staging costs one
+    // L2 round trip per 8 elements per thread, not one per element.
+    pdl_wait();
+#pragma unroll 1
+    for (int m = 0; m < MM; ++m) {
+        const float* xr = p.x + (int64_t)m * p.ldx;
+        float* xd = xs + m * p.k_pad;
         for (int base = 0; base < p.k_pad; base += 8 * (int)blockDim.x) {
             float v[8];
 #pragma unroll
@@ -406,21 +251,27 @@ __global__ void __launch_bounds__(704, 2) gemv_m1_kernel(const GemvParams p) {
 #pragma unroll
             for (int i = 0; i < 8; ++i) {
                 const int kk = base + (int)threadIdx.x + i * (int)blockDim.x;
-                if (kk < p.k_pad) xs[xperm_bm(kk)] = v[i];
+                if (kk < p.k_pad) xd[xperm(kk)] = v[i];
             }
         }
     }
     __syncthreads();
 
-    const int nbf = p.k / kBlock;
-    const int cfull = nbf / 4;
+    const int nbf = p.k / kBlock;  // full blocks
+    const int cfull = nbf / 4;     // chunks of 4 full blocks
     const int rem_blocks = nbf - cfull * 4;
     const int nchunks = cfull + (rem_blocks ? 1 : 0);
 
-    float t = 0.0f;
-    int stop = items;
-    // item i = (unit index uu, segment g); slot = i mod d with phase parity;
-    // (uu2, g2) tracks item i + d, the next one issued into this slot.
+    const unsigned long long nz = f2pack(p.zero_neg, p.zero_neg);
+    float t[MM][R];
+#pragma unroll
+    for (int m = 0; m < MM; ++m)
+#pragma unroll
+        for (int i = 0; i < R; ++i) t[m][i] = 0.0f;
+
+    int stop = items;  // first item not consumed (== items on the normal path)
+    // item i = (unit index uu, segment g) in slot i mod d with phase parity;
+    // (uu2, g2) tracks item i + d, the next one issued into the same slot.
     int uu = 0, g = 0, slot = 0;
     uint32_t parity = 0;
     int uu2 = 0, g2 = 0;
@@ -434,45 +285,24 @@ __global__ void __launch_bounds__(704, 2) gemv_m1_kernel(const GemvParams p) {
             stop = i;
             break;
         }
-        uint8_t* sq = my_slots + slot * slot_bytes + rsub * p.sc * kChunk + lane * 16;
-        const uint8_t* ss = my_slots + slot * slot_bytes + 2 * p.sc * kChunk + rsub * p.sc * 16;
+        const uint8_t* sq = my_slots + (size_t)slot * slot_bytes + rsub * p.sc * kChunk + lane * 16;
+        const uint8_t* ss = my_slots + (size_t)slot * slot_bytes + kUnitRows * p.sc * kChunk + rsub * p.sc * 16;
+        const int qstride = p.sc * kChunk, sstride = p.sc * 16;
         const int c0 = g * p.sc;
         const int c1 = min(c0 + p.sc, nchunks);
-        const int cf = min(c1, cfull);  // chunks of four full blocks in this segment
-        // phase 1: block sums for chunks c0 + half, c0 + half + 2, ... written in place
-#pragma unroll 2
-        for (int c = c0 + half; c < cf; c += 2) {
-            const uint4 qv = *reinterpret_cast<const uint4*>(sq + (c - c0) * kChunk);
-            const float4 bs = block_sums(xs + c * kChunk + lane * 4, qv, 4);
-            *reinterpret_cast<float4*>(sq + (c - c0) * kChunk) = bs;
+        const int cf = min(c1, cfull);  // chunks made of four full blocks
+        const float* xc = xs + c0 * kChunk;
+#pragma unroll 1
+        for (int c = 0; c < cf - c0; ++c) {
+            chunk_update<MM, R, true>(xc + c * kChunk, p.k_pad, lane, sq + c * kChunk, qstride, ss + c * 16, sstride,
+                                      nz, t, 4);
         }
-        if (cf < c1 && ((cf - c0) & 1) == half) {  // the chunk with the last 1..3 full blocks
-            const uint4 qv = *reinterpret_cast<const uint4*>(sq + (cf - c0) * kChunk);
-            const float4 bs = block_sums(xs + cf * kChunk + lane * 4, qv, rem_blocks);
-            *reinterpret_cast<float4*>(sq + (cf - c0) * kChunk) = bs;
+        if (cf < c1) {  // the chunk holding the last (1..3) full blocks
+            chunk_update<MM, R, false>(xs + cf * kChunk, p.k_pad, lane, sq + (cf - c0) * kChunk, qstride,
+                                       ss + (cf - c0) * 16, sstride, nz, t, rem_blocks);
         }
         __syncwarp();
-        // phase 2: the chain over every block of the segment, in order
-        if (half == 0) {
-#pragma unroll 4
-            for (int c = c0; c < cf; ++c) {
-                const float4 bs = *reinterpret_cast<const float4*>(sq + (c - c0) * kChunk);
-                const float4 sv = *reinterpret_cast<const float4*>(ss + (c - c0) * 16);
-                t = __fmaf_rn(bs.x, sv.x, t);
-                t = __fmaf_rn(bs.y, sv.y, t);
-                t = __fmaf_rn(bs.z, sv.z, t);
-                t = __fmaf_rn(bs.w, sv.w, t);
-            }
-            if (cf < c1) {
-                const float4 bs = *reinterpret_cast<const float4*>(sq + (cf - c0) * kChunk);
-                const float4 sv = *reinterpret_cast<const float4*>(ss + (cf - c0) * 16);
-                t = __fmaf_rn(bs.x, sv.x, t);
-                if (rem_blocks > 1) t = __fmaf_rn(bs.y, sv.y, t);
-                if (rem_blocks > 2) t = __fmaf_rn(bs.z, sv.z, t);
-            }
-        }
-        __syncwarp();
-        if (lane32 == 0 && i + p.d < items) {
+        if (i + p.d < items) {
             fence_proxy_async_smem();
             issue(uu2, g2, slot);
         }
@@ -481,37 +311,56 @@ __global__ void __launch_bounds__(704, 2) gemv_m1_kernel(const GemvParams p) {
         if (++g == p.nseg) { g = 0; ++uu; }
         if (++slot == p.d) { slot = 0; parity ^= 1u; }
         if (unit_done) {
-            const int row_raw = 2 * u + rsub;
-            const bool valid = row_raw < p.rows;
-            const int row = valid ? row_raw : p.rows - 1;
-            float v = t;
-            v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, 4));
-            v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, 1));
-            v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, 2));
-            if (half == 0 && lane == 0 && valid) {
-                if (p.k > nbf * kBlock) {
-                    const uint8_t* qr = p.q + (int64_t)row * p.k_pad;
-                    const float st = p.s[(int64_t)row * p.nb_pad + nbf];
-                    float acc = 0.0f;
-                    for (int kk = nbf * kBlock; kk < p.k; ++kk) {
-                        const float qf = (float)(int8_t)qr[packed_offset(kk)];
-                        acc = __fadd_rn(acc, __fmul_rn(xs[xperm_bm(kk)], qf));
-                    }
-                    v = __fadd_rn(v, __fmul_rn(acc, st));
+#pragma unroll
+            for (int m = 0; m < MM; ++m)
+#pragma unroll
+                for (int i = 0; i < R; ++i) {
+                    float v = t[m][i];
+                    v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, 4));
+                    v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, 1));
+                    v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, 2));
+                    t[m][i] = v;
                 }
-                if (GATHER) {
-                    // this rank's own exchange buffer; the last CTA pushes the shard to the peers
-                    p.ga.peer_out[p.ga.rank][((*p.ga.epoch + 1) & 1) * p.ga.out_stride + p.ga.col0 + row] = v;
-                } else {
-                    p.y[row] = v;
+            if (lane == 0) {
+#pragma unroll
+                for (int i = 0; i < R; ++i) {
+                    const int row = kUnitRows * u + rsub + i;
+                    if (row >= p.rows) break;
+                    if (p.k > nbf * kBlock) {
+                        // Ragged tail: sequential scalar sum times the last block's scale.
+                        const uint8_t* qr = p.q + (int64_t)row * p.k_pad;
+                        const float st = p.s[(int64_t)row * p.nb_pad + nbf];
+#pragma unroll
+                        for (int m = 0; m < MM; ++m) {
+                            float acc = 0.0f;
+                            for (int kk = nbf * kBlock; kk < p.k; ++kk) {
+                                const float qf = (float)(int8_t)qr[packed_offset(kk)];
+                                acc = __fadd_rn(acc, __fmul_rn(xs[m * p.k_pad + xperm(kk)], qf));
+                            }
+                            t[m][i] = __fadd_rn(t[m][i], __fmul_rn(acc, st));
+                        }
+                    }
+                    if (GATHER) {
+                        // this rank's own exchange buffer; the last CTA pushes the shard to the peers
+                        p.ga.peer_out[p.ga.rank][((*p.ga.epoch + 1) & 1) * p.ga.out_stride + p.ga.col0 + row] =
+                            t[0][i];
+                    } else {
+#pragma unroll
+                        for (int m = 0; m < MM; ++m) p.y[(int64_t)m * p.ldy + row] = t[m][i];
+                    }
                 }
             }
-            t = 0.0f;
+#pragma unroll
+            for (int m = 0; m < MM; ++m)
+#pragma unroll
+                for (int i = 0; i < R; ++i) t[m][i] = 0.0f;
         }
     }
+    // Drain after a give-up: items [stop, stop + d) were issued but not
+    // consumed; their copies must land before this warp's slots are released.
     if (lane32 == 0)
         for (int j = stop; j < stop + p.d && j < items; ++j)
-            mbar_wait(bars + (j % p.d) * 8, (uint32_t)((j / p.d) & 1), nullptr, kWaitBudget);  // give-up path only
+            mbar_wait(bars + (j % p.d) * 8, (uint32_t)((j / p.d) & 1), nullptr, kWaitBudget);
     if (GATHER) {
         // Completion: each CTA's rows are in this rank's own buffer; it counts
         // itself done with a GPU-scope release. The last CTA acquires them,
@@ -571,28 +420,42 @@ __global__ void __launch_bounds__(704, 2) gemv_m1_kernel(const GemvParams p) {
 }
 
 struct Plan {
-    int mm, sc, nseg, d, nwarps, ctas, xs_bytes, smem;
+    int mm, r, sc, nseg, d, nwarps, ctas, xs_bytes, smem;
 };
+
+// Rows per thread (measured on B200, M = 1): R = 2 pays from ~48 rows per SM
+// (lm_head 151936 x 2560: 98.5 us vs 115 us at R = 1; 9728 x 2560: 10.3 vs
+// 12.1 us); below that R = 1 keeps enough warps per SM and two CTAs per SM
+// (config 1, 6144 x 2048: 5.5 us vs 8.2 us at R = 2). R = 4 was slower than
+// R = 2 everywhere. M > 1 keeps R = 1.
+int pick_rows_per_thread(int mm, int rows, int sm_count) {
+    if (mm > 1) return 1;
+    return rows / sm_count >= 48 ? 2 : 1;
+}
 
 bool make_plan(int mm, int rows, int k, int sm_count, Plan* pl) {
     const int k_pad = packed_k(k);
     const int nck = k_pad / kChunk;
-    const int rpu = mm == 1 ? 2 : 4;  // rows per warp unit
-    const int max_warps = mm == 1 ? 22 : 16;
+    const int max_warps = mm == 1 ? 12 : 16;
     pl->mm = mm;
-    pl->sc = nck < kMaxSegChunks ? nck : kMaxSegChunks;
+    pl->r = pick_rows_per_thread(mm, rows, sm_count);
+    const int unit_rows = 4 * pl->r;
+    // About four segments per row, so a row's chain starts on its first
+    // quarter while the rest is in flight.
+    int sc = (nck + 3) / 4;
+    sc = sc < 2 ? 2 : sc > kMaxSegChunks ? kMaxSegChunks : sc;
+    pl->sc = sc < nck ? sc : nck;
     pl->nseg = (nck + pl->sc - 1) / pl->sc;
-    const int slot_bytes = pl->sc * (mm == 1 ? kM1SlotBytesPerChunk : kSlotBytesPerChunk);
+    const int slot_bytes = pl->sc * unit_rows * kRowChunkBytes;
     pl->xs_bytes = round_up(mm * k_pad * 4, 128);
-    const int units = (rows + rpu - 1) / rpu;
+    const int units = (rows + unit_rows - 1) / unit_rows;
     pl->ctas = units < sm_count ? units : sm_count;
     const int upc = (units + pl->ctas - 1) / pl->ctas;
-    // Short kernels: everything in flight at once within ~113 KB, leaving room
+    // Short kernels: everything in flight at once within ~110 KB, leaving room
     // for the next kernel's CTA on the same SM. Long ones: up to 200 KB.
-    const int small_budget = 113 * 1024, big_budget = 200 * 1024;
+    const int small_budget = 110 * 1024, big_budget = 200 * 1024;
     int max_slots = (small_budget - pl->xs_bytes - 1024) / slot_bytes;
-    const int upw_all = upc;  // with one warp per unit
-    if (max_slots >= 1 && upc <= max_warps && upw_all * pl->nseg <= max_slots) {
+    if (max_slots >= 1 && upc <= max_warps && upc * pl->nseg <= max_slots) {
         pl->nwarps = upc;
         pl->d = pl->nseg;
     } else {
@@ -609,22 +472,23 @@ bool make_plan(int mm, int rows, int k, int sm_count, Plan* pl) {
     return true;
 }
 
-template <int MM>
+template <int MM, int R>
 cudaError_t launch_mm(const GemvParams& p0, const Plan& pl, cudaStream_t stream, bool pdl) {
     static bool attr_set[2][64] = {};
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
     if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
-    auto kern = MM == 1 ? (p0.ga.nranks > 0 ? gemv_m1_kernel<true> : gemv_m1_kernel<false>) : gemv_stream_kernel<MM>;
-    const int gi = p0.ga.nranks > 0 ? 1 : 0;
+    const bool gather = p0.ga.nranks > 0;
+    auto kern = MM == 1 && gather ? gemv_kernel<1, R, true> : gemv_kernel<MM, R, false>;
+    const int gi = gather ? 1 : 0;
     if (!attr_set[gi][dev]) {
         e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 224 * 1024);
         if (e != cudaSuccess) return e;
         attr_set[gi][dev] = true;
     }
     GemvParams p = p0;
-    p.units = (p.rows + (MM == 1 ? 1 : 3)) / (MM == 1 ? 2 : 4);
+    p.units = (p.rows + 4 * R - 1) / (4 * R);
     p.ucta_q = p.units / pl.ctas;
     p.ucta_r = p.units % pl.ctas;
     p.sc = pl.sc;
@@ -644,7 +508,6 @@ cudaError_t launch_mm(const GemvParams& p0, const Plan& pl, cudaStream_t stream,
     return cudaLaunchKernelEx(&cfg, kern, p);
 }
 
-
 }  // namespace
 
 bool gemv_supported(int mm, int rows, int k, int sm_count) {
@@ -662,6 +525,7 @@ cudaError_t launch_gemv_exact(const float* x, int64_t ldx, int mm, const uint8_t
     if (gather) p.ga = *gather;
     p.x = x;
     p.ldx = ldx;
+    p.zero_neg = -0.0f;
     p.q = q;
     p.s = s;
     p.y = y;
@@ -671,16 +535,15 @@ cudaError_t launch_gemv_exact(const float* x, int64_t ldx, int mm, const uint8_t
     p.k = k;
     p.k_pad = packed_k(k);
     p.nb_pad = p.k_pad / kBlock;
-    p.units = (rows + 3) / 4;
     switch (mm) {
-        case 1: return launch_mm<1>(p, pl, stream, pdl);
-        case 2: return launch_mm<2>(p, pl, stream, pdl);
-        case 3: return launch_mm<3>(p, pl, stream, pdl);
-        case 4: return launch_mm<4>(p, pl, stream, pdl);
-        case 5: return launch_mm<5>(p, pl, stream, pdl);
-        case 6: return launch_mm<6>(p, pl, stream, pdl);
-        case 7: return launch_mm<7>(p, pl, stream, pdl);
-        case 8: return launch_mm<8>(p, pl, stream, pdl);
+        case 1: return pl.r == 2 ? launch_mm<1, 2>(p, pl, stream, pdl) : launch_mm<1, 1>(p, pl, stream, pdl);
+        case 2: return launch_mm<2, 1>(p, pl, stream, pdl);
+        case 3: return launch_mm<3, 1>(p, pl, stream, pdl);
+        case 4: return launch_mm<4, 1>(p, pl, stream, pdl);
+        case 5: return launch_mm<5, 1>(p, pl, stream, pdl);
+        case 6: return launch_mm<6, 1>(p, pl, stream, pdl);
+        case 7: return launch_mm<7, 1>(p, pl, stream, pdl);
+        case 8: return launch_mm<8, 1>(p, pl, stream, pdl);
         default: return cudaErrorInvalidValue;
     }
 }
