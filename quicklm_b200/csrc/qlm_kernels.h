@@ -57,8 +57,9 @@ cudaError_t tc_make_weight_maps(const uint8_t* q, const float* s, int rows, int 
 // Per-row weight exponents ew[rows] used to range-scale the fp16 weight tile.
 cudaError_t launch_weight_exponents(const float* s, int rows, int k, int* ew, cudaStream_t stream);
 
-// Token-tile width the GEMM uses for M activation rows.
-int tc_pick_bn(int M);
+// Token-tile width (multiple of 16, <= 256) the GEMM uses for M activation
+// rows against a weight of `rows` rows on a GPU with sm_count SMs.
+int tc_pick_bn(int M, int rows, int sm_count);
 
 // y[M][rows] = x[M][k] . W^T on tensor cores. Scratch: x16 >= M*packed_k(k)
 // fp16 and ea >= M ints; status: device int set non-zero on a timeout.
