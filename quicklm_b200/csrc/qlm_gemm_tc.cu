@@ -82,6 +82,8 @@ __host__ __device__ constexpr int off_misc(int bn) { return off_bar(bn) + NBAR *
 __host__ __device__ constexpr int off_ea(int bn) { return off_misc(bn) + 16; }
 __host__ __device__ constexpr int smem_bytes(int bn) { return off_ea(bn) + 4 * BN_MAX + 1024; }  // + base alignment
 static_assert(smem_bytes(BN_MAX) <= 232448, "shared memory budget");
+static_assert(BN_MAX % (16 * NG) == 0, "epilogue column blocks");
+static_assert(SW <= S_CHUNKS, "the first weight chunks issued at set-up all use scale stage 0");
 static_assert(BM * 4 <= SX * 2 * 128, "epilogue staging (BM x bn fp32) fits below the barriers for every bn");
 constexpr long long DRAIN_BUDGET = 1LL << 25;  // ~17 ms: bound for copies still in flight after an abort
 
@@ -161,6 +163,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__
 
     if (warp == 0) {
         // ------------------ TMA producer: weights + scales ------------------
+        int w_issued = 0, s_issued = 0;
         if (lane == 0) {
             for (int i = 0; i < SW; ++i) {
                 mbar_init(WFULL + 8 * i, 1);
@@ -169,6 +172,15 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__
             for (int i = 0; i < SS; ++i) {
                 mbar_init(SFULL + 8 * i, 1);
                 mbar_init(SEMPTY + 8 * i, 4 * NG);
+            }
+            mbar_fence_init();
+            // The first scale stage and weight chunks go out before anything
+            // else is set up (the stages are empty: no wait needed).
+            mbar_arrive_expect_tx(SFULL, S_STAGE_BYTES);
+            tma_load_2d(sbase + OFF_S, &tm_s, 0, n0, SFULL);
+            for (int c = 0; c < SW && c < nchunks; ++c) {
+                mbar_arrive_expect_tx(WFULL + 8 * c, W_STAGE_BYTES);
+                tma_load_2d(sbase + OFF_W + c * W_STAGE_BYTES, &tm_w, c * 128, n0, WFULL + 8 * c);
             }
             for (int i = 0; i < SX; ++i) mbar_init(XEMPTY + 8 * i, 1);
             for (int i = 0; i < NSLOT; ++i) {
@@ -179,16 +191,15 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__
             mbar_init(ACCFULL, 1);
             *abort_flag = 0;
             mbar_fence_init();
-            tma_prefetch_desc(&tm_w);
-            tma_prefetch_desc(&tm_s);
         }
         __syncwarp();
         setup_arrive();
         // Weights are not written by the preceding kernel, so these copies
         // start before the programmatic-dependent-launch wait.
         bool ok = true;
-        int w_issued = 0, s_issued = 0;
-        for (int c = 0; c < nchunks && ok; ++c) {
+        s_issued = 1;
+        w_issued = min(SW, nchunks);
+        for (int c = w_issued; c < nchunks && ok; ++c) {
             if (c % S_CHUNKS == 0) {
                 const int g = c / S_CHUNKS, ss = g % SS;
                 if (!mbar_wait_warp(SEMPTY + 8 * ss, ((g / SS) & 1) ^ 1, abort_flag, WAIT_BUDGET)) {
@@ -397,13 +408,22 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__
         float* stage = reinterpret_cast<float*>(smem);
         const int cols = min(bn, p.M - m0);
         if (!*abort_flag) {
-            for (int col0 = 16 * grp; col0 < cols; col0 += 16 * NG) {
-                uint32_t acc[16];
-                tmem_ld_32x32b_x16(tmem + lane_addr + col0, acc);
-                tmem_ld_wait();
+            // All of this warp's column blocks (16 wide, every NG-th) are
+            // loaded before a single wait, so the TMEM load latency is paid
+            // once. Columns past the tile are allocated and simply not stored.
+            constexpr int NCB = BN_MAX / (16 * NG);
+            uint32_t acc[NCB][16];
 #pragma unroll
-                for (int i = 0; i < 16; ++i)
-                    stage[(col0 + i) * BM + r] = scale_pow2(__uint_as_float(acc[i]), -(ewr + ea_s[col0 + i]));
+            for (int j = 0; j < NCB; ++j) tmem_ld_32x32b_x16(tmem + lane_addr + 16 * (grp + NG * j), acc[j]);
+            tmem_ld_wait();
+#pragma unroll
+            for (int j = 0; j < NCB; ++j) {
+                const int col0 = 16 * (grp + NG * j);
+                if (col0 < cols) {
+#pragma unroll
+                    for (int i = 0; i < 16; ++i)
+                        stage[(col0 + i) * BM + r] = scale_pow2(__uint_as_float(acc[j][i]), -(ewr + ea_s[col0 + i]));
+                }
             }
         }
         converters_sync();
