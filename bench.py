@@ -60,7 +60,7 @@ def measured_peaks():
     return 6650.0, "fallback"
 
 
-def profile_traffic(name="gemv_m1_cfg1.txt"):
+def profile_traffic(name="gemv_kernel_m1_cfg1.txt"):
     """DRAM bytes per launch from the committed ncu summary, if present."""
     p = os.path.join(ROOT, "profiles", name)
     if not os.path.exists(p):
