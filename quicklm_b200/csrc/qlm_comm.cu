@@ -6,14 +6,17 @@
 // computed by exactly one thread with the reference's sequence
 // (src/ops/math_ops.cpp:874-894), only on a different GPU.
 //
-// Exchange: every rank owns one exchange buffer (flags + two halves of the
-// gathered output) shared with the other ranks through CUDA IPC. A call is
-// ONE kernel: the GEMV stores each of its output rows straight into every
-// rank's buffer over NVLink (plain peer stores; no multicast); its last CTA
-// publishes the call's epoch to every rank's flags with system-scope release
-// stores, waits (bounded) until all ranks have published, and copies the
-// gathered row into y. The epoch lives on the device, so a sequence of calls
-// can be captured in a CUDA graph and replayed.
+// Exchange: every rank owns one exchange buffer (two halves of the gathered
+// output, as 64-bit words (epoch << 32) | value) shared with the other ranks
+// through CUDA IPC. A call is ONE kernel: the thread that computes an output
+// row stores its word into every rank's buffer (plain 8-byte peer stores over
+// NVLink; no multicast, no fences, no separate flags: the epoch travels with
+// the value), then every CTA waits (bounded) until the words of its slice of
+// the gathered row carry this call's epoch and copies their values into y.
+// The epoch lives on the device, so a sequence of calls can be captured in a
+// CUDA graph and replayed. Halves alternate by epoch parity: a rank can start
+// call e + 1 only after every rank has stored all of call e, which each rank
+// does only after its call e - 1 kernel (the last reader of that half) ended.
 #include "../../include/qlm_b200.h"
 #include "qlm_device.cuh"
 #include "qlm_handle.h"
@@ -27,7 +30,8 @@
 
 struct qlm_comm {
     int device = -1, rank = 0, nranks = 0, sm_count = 0;
-    long long max_out = 0;             // floats per output half
+    long long max_out = 0;             // gathered-width capacity (floats)
+    long long stride = 0;              // 64-bit words per output half
     char* base = nullptr;              // local exchange buffer
     char* peers[qlm::kMaxRanks] = {};  // every rank's buffer as seen from this device
     bool opened[qlm::kMaxRanks] = {};
@@ -40,7 +44,7 @@ void set_last_error(const std::string& msg);
 
 namespace {
 
-constexpr size_t kFlagBytes = 256;
+constexpr size_t kHeaderBytes = 256;  // keeps the word area 256-byte aligned
 
 int fail(int code, const char* fmt, ...) {
     char buf[384];
@@ -87,8 +91,9 @@ int qlm_comm_create(int device, int rank, int nranks, int64_t max_out, qlm_comm*
     c->rank = rank;
     c->nranks = nranks;
     c->max_out = max_out;
+    c->stride = (max_out + 1) & ~1LL;  // both halves start 16-byte aligned
     cudaError_t e = cudaDeviceGetAttribute(&c->sm_count, cudaDevAttrMultiProcessorCount, device);
-    const size_t bytes = kFlagBytes + 2 * (size_t)max_out * sizeof(float);
+    const size_t bytes = kHeaderBytes + 2 * (size_t)c->stride * sizeof(unsigned long long);
     if (e == cudaSuccess) e = cudaMalloc(&c->base, bytes);
     if (e == cudaSuccess) e = cudaMemset(c->base, 0, bytes);
     if (e == cudaSuccess) e = cudaMalloc(&c->state, 4 * sizeof(int));
@@ -153,12 +158,11 @@ int qlm_linear_int8_allgather(const float* x, int M, int k, int64_t ldx, const q
 
     qlm::GatherArgs ga{};
     for (int r = 0; r < c->nranks; ++r) {
-        ga.peer_flags[r] = reinterpret_cast<int*>(c->peers[r]);
-        ga.peer_out[r] = reinterpret_cast<float*>(c->peers[r] + kFlagBytes);
+        ga.peer_slots[r] = reinterpret_cast<unsigned long long*>(c->peers[r] + kHeaderBytes);
     }
     ga.counter = c->state;
     ga.epoch = c->state + 1;
-    ga.out_stride = c->max_out;
+    ga.out_stride = c->stride;
     ga.nranks = c->nranks;
     ga.rank = c->rank;
     ga.col0 = w->row_begin;

@@ -138,6 +138,17 @@ __device__ __forceinline__ int ld_acquire_sys(const int* p) {
     return v;
 }
 
+// 64-bit relaxed accesses at system scope (single-copy atomic: a reader sees
+// a whole word written by a peer GPU or none of it; never served from L1).
+__device__ __forceinline__ void st_relaxed_sys_u64(unsigned long long* p, unsigned long long v) {
+    asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_relaxed_sys_u64(const unsigned long long* p) {
+    unsigned long long v;
+    asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+
 // Programmatic dependent launch (sm_90+): let the next kernel in the stream
 // start launching, and wait until the previous kernel's results are visible.
 // Both are no-ops when the launch did not opt in.

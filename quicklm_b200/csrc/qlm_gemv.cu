@@ -146,30 +146,6 @@ __device__ __forceinline__ void chunk_update(const float* __restrict__ xs_chunk,
     }
 }
 
-// dst[i] = src[i] for i in [c0, c1) by all threads of the CTA: 16-byte moves
-// for the aligned middle (four loads in flight per thread), scalar edges.
-__device__ __forceinline__ void cta_copy(float* __restrict__ dst, const float* __restrict__ src, int c0, int c1) {
-    const int a0 = min(c1, (c0 + 3) & ~3), a1 = max(a0, c1 & ~3);
-    for (int i = c0 + (int)threadIdx.x; i < a0; i += blockDim.x) dst[i] = src[i];
-    for (int i = a1 + (int)threadIdx.x; i < c1; i += blockDim.x) dst[i] = src[i];
-    const float4* s4 = reinterpret_cast<const float4*>(src + a0);
-    float4* d4 = reinterpret_cast<float4*>(dst + a0);
-    const int n4 = (a1 - a0) / 4, step = (int)blockDim.x;
-    for (int base = 0; base < n4; base += 4 * step) {
-        float4 v[4];
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-            const int i = base + u * step + (int)threadIdx.x;
-            if (i < n4) v[u] = s4[i];
-        }
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-            const int i = base + u * step + (int)threadIdx.x;
-            if (i < n4) d4[i] = v[u];
-        }
-    }
-}
-
 // R rows per thread (4R per warp unit): the activations a thread loads from
 // shared memory serve R rows, which halves the shared-memory traffic and the
 // load instructions per weight byte at R = 2 (every 128-bit shared load is
@@ -237,6 +213,14 @@ __global__ void __launch_bounds__(MM == 1 ? 384 : 512, MM == 1 ? 2 : 1) gemv_ker
     // thread's loads are issued before its first store, so staging costs one
     // L2 round trip per 8 elements per thread, not one per element.
     pdl_wait();
+    // Gather: this call's epoch (the previous call's kernel, which advanced
+    // it, has completed) and the exchange half it selects.
+    int g_epoch = 0;
+    long long g_half = 0;
+    if (GATHER) {
+        g_epoch = *reinterpret_cast<volatile const int*>(p.ga.epoch) + 1;
+        g_half = (long long)(g_epoch & 1) * p.ga.out_stride;
+    }
 #pragma unroll 1
     for (int m = 0; m < MM; ++m) {
         const float* xr = p.x + (int64_t)m * p.ldx;
@@ -341,9 +325,12 @@ __global__ void __launch_bounds__(MM == 1 ? 384 : 512, MM == 1 ? 2 : 1) gemv_ker
                         }
                     }
                     if (GATHER) {
-                        // this rank's own exchange buffer; the last CTA pushes the shard to the peers
-                        p.ga.peer_out[p.ga.rank][((*p.ga.epoch + 1) & 1) * p.ga.out_stride + p.ga.col0 + row] =
-                            t[0][i];
+                        // one word per rank: this call's epoch with the value
+                        const unsigned long long word =
+                            ((unsigned long long)(uint32_t)g_epoch << 32) | __float_as_uint(t[0][i]);
+#pragma unroll 1
+                        for (int r = 0; r < p.ga.nranks; ++r)
+                            st_relaxed_sys_u64(p.ga.peer_slots[r] + g_half + p.ga.col0 + row, word);
                     } else {
 #pragma unroll
                         for (int m = 0; m < MM; ++m) p.y[(int64_t)m * p.ldy + row] = t[m][i];
@@ -362,58 +349,33 @@ __global__ void __launch_bounds__(MM == 1 ? 384 : 512, MM == 1 ? 2 : 1) gemv_ker
         for (int j = stop; j < stop + p.d && j < items; ++j)
             mbar_wait(bars + (j % p.d) * 8, (uint32_t)((j / p.d) & 1), nullptr, kWaitBudget);
     if (GATHER) {
-        // Completion: each CTA's rows are in this rank's own buffer; it counts
-        // itself done with a GPU-scope release. The last CTA acquires them,
-        // pushes the whole shard to every peer with 16-byte stores, releases
-        // them at system scope once, publishes this call's epoch e to every
-        // rank, waits (bounded) until every rank has published e, copies the
-        // gathered row into y and records e.
-        __shared__ int is_last, bad;
-        __syncthreads();
-        if (threadIdx.x == 0) {
-            __threadfence();
-            is_last = atomicAdd(p.ga.counter, 1) == (int)gridDim.x - 1;
-            bad = 0;
+        // Completion, by every CTA: wait (bounded) until every word of this
+        // CTA's slice of the gathered row carries this call's epoch, and copy
+        // the values into y. The last CTA to finish resets the counter and
+        // records the epoch (every CTA read it before counting itself).
+        __shared__ int is_last;
+        const int per = (p.ga.n_total + (int)gridDim.x - 1) / (int)gridDim.x;
+        const int c0 = min((int)blockIdx.x * per, p.ga.n_total), c1 = min(c0 + per, p.ga.n_total);
+        const unsigned long long* mine = p.ga.peer_slots[p.ga.rank] + g_half;
+        const long long t0 = clock64();
+        for (int i = c0 + (int)threadIdx.x; i < c1; i += blockDim.x) {
+            unsigned long long v = ld_relaxed_sys_u64(mine + i);
+            while ((int)(v >> 32) != g_epoch) {
+                if (clock64() - t0 > kWaitBudget) {
+                    if (p.status) atomicCAS(p.status, 0, kStatusGatherTimeout);
+                    break;
+                }
+                __nanosleep(32);
+                v = ld_relaxed_sys_u64(mine + i);
+            }
+            if ((int)(v >> 32) == g_epoch) p.y[i] = __uint_as_float((uint32_t)v);
         }
         __syncthreads();
-        if (is_last) {
-            __threadfence();
-            const int e = *p.ga.epoch + 1;
-            const long long half = (e & 1) * p.ga.out_stride;
-            const float* mine = p.ga.peer_out[p.ga.rank] + half;
-#pragma unroll 1
-            for (int r = 0; r < p.ga.nranks; ++r)
-                if (r != p.ga.rank) cta_copy(p.ga.peer_out[r] + half, mine, p.ga.col0, p.ga.col0 + p.rows);
-            __syncthreads();
-            if (threadIdx.x == 0) {
-                fence_acq_rel_sys();
-#pragma unroll 1
-                for (int r = 0; r < p.ga.nranks; ++r) st_release_sys(p.ga.peer_flags[r] + p.ga.rank, e);
-            }
-            if ((int)threadIdx.x < p.ga.nranks) {
-                const int* flag = p.ga.peer_flags[p.ga.rank] + threadIdx.x;  // this rank's own flag array
-                const long long t0 = clock64();
-                while (ld_acquire_sys(flag) - e < 0) {
-                    if (clock64() - t0 > kWaitBudget) {
-                        bad = 1;
-                        if (p.status) atomicCAS(p.status, 0, kStatusGatherTimeout);
-                        break;
-                    }
-                    __nanosleep(32);
-                }
-            }
-            __syncthreads();
-            if (!bad) {
-                if ((reinterpret_cast<uintptr_t>(p.y) & 15) == 0) {
-                    cta_copy(p.y, mine, 0, p.ga.n_total);
-                } else {
-                    for (int i = threadIdx.x; i < p.ga.n_total; i += blockDim.x) p.y[i] = mine[i];
-                }
-            }
-            __syncthreads();
-            if (threadIdx.x == 0) {
+        if (threadIdx.x == 0) {
+            is_last = atomicAdd(p.ga.counter, 1) == (int)gridDim.x - 1;
+            if (is_last) {
                 *p.ga.counter = 0;
-                *const_cast<int*>(p.ga.epoch) = e;
+                *const_cast<volatile int*>(p.ga.epoch) = g_epoch;
             }
         }
     }

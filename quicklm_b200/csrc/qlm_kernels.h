@@ -16,19 +16,18 @@ cudaError_t launch_quantize_pack(const void* src, int dtype, int64_t src_stride,
 
 constexpr int kMaxRanks = 8;
 
-// Peer pointers for the fused GEMV + all-gather (M = 1). peer_out[r] is
-// rank r's exchange area (two halves of out_stride floats, picked by epoch
-// parity), peer_flags[r] its flag array. Device-resident state of this rank:
-// counter (CTA completions, starts at 0) and epoch (last completed call).
-// A call works on epoch e = *epoch + 1, publishes e to every rank, and its
-// last CTA waits for every rank's e before copying the gathered row to y.
+// Peer pointers for the fused GEMV + all-gather (M = 1). peer_slots[r] is
+// rank r's exchange area: two halves of out_stride 64-bit words, picked by
+// the parity of the call's epoch; a word holds (epoch << 32) | float bits of
+// one gathered output, so a reader knows from the word alone whether it
+// belongs to the current call. Device-resident state of this rank: counter
+// (CTA completions, starts at 0) and epoch (last completed call).
 struct GatherArgs {
-    float* peer_out[kMaxRanks];
-    int* peer_flags[kMaxRanks];
+    unsigned long long* peer_slots[kMaxRanks];
     int* counter;
     const int* epoch;
     long long out_stride;
-    int n_total; // gathered width copied into y by the last CTA
+    int n_total; // gathered width copied into y
     int nranks;  // 0 = no gather
     int rank;
     int col0;    // this shard's first output column

@@ -80,6 +80,25 @@ def _worker(rank, world, port, result_dir):
                     msg = f"replay {i}: gathered output differs"
                     break
             del g
+        if msg == "ok":
+            # uneven shards of an odd gathered width with ragged K: the second
+            # exchange half starts at a width that is not a multiple of 4
+            xo, wo = synth_case(1, 1001, 300, 5)
+            wod = torch.from_numpy(wo).cuda()
+            b2, e2 = q.shard_rows(1001, world, rank)
+            shard2 = q.Int8Weight.quantize(wod, device=rank, row_begin=b2, row_end=e2)
+            full2 = q.Int8Weight.quantize(wod, device=rank)
+            comm2 = q.Comm(rank, rank, world, 1001, exchange)
+            xod = torch.from_numpy(xo).cuda()
+            y_ref = q.matmul(xod, full2, flags=q.SYNC)
+            for i in range(3):  # both exchange halves
+                y = q.matmul_allgather(xod, shard2, comm2, flags=q.SYNC)
+                if not torch.equal(y.view(torch.int32), y_ref.view(torch.int32)):
+                    msg = f"odd width, call {i}: gathered output differs"
+                    break
+            torch.cuda.synchronize()
+            dist.barrier()
+            comm2.free()
         if q.load().qlm_device_status(rank, 1) != 0:
             msg = "device status reports a timeout"
         dist.barrier()
