@@ -160,6 +160,19 @@ void qlm_comm_free(qlm_comm* c);
 int qlm_linear_int8_allgather(const float* x, int M, int k, int64_t ldx, const qlm_w8* w, qlm_comm* c, float* y,
                               int64_t ldy, int flags, void* stream);
 
+/* Greedy token choice over device logits, as DecoderModel::sample(logits, 0, 0)
+ * (src/model/model.cpp:259-272): 0 if logit 0 is NaN, else the lowest index of
+ * the largest non-NaN logit. logits: this rank's n logits (device pointer),
+ * the first of which is global logit col0 (0 without sharding). c: NULL on one
+ * GPU (the current device); or the communicator of a row-sharded lm_head, in
+ * which case every rank passes its own shard and all receive the choice over
+ * all shards (one 8-byte word per rank crosses NVLink instead of the logits;
+ * all ranks must make the same sequence of calls on c). out_index / out_value:
+ * device pointers (-1 / NaN when no logit is a number). Global indices must be
+ * below 2^24 - 2. flags: 0 or QLM_LINEAR_SYNC. */
+int qlm_argmax_f32(const float* logits, int n, int64_t col0, qlm_comm* c, int* out_index, float* out_value, int flags,
+                   void* stream);
+
 /* Status of bounded device-side waits on `device`: QLM_OK, or QLM_ERR_TIMEOUT
  * if a kernel gave up waiting since the last reset (reset != 0 clears it).
  * Synchronous tensor-core calls check this themselves. */

@@ -64,12 +64,20 @@ class RefCPU:
         lib.qlmref_matmul_int8.argtypes = [_P, _I, _I, _P, _P, _I, _P, _I, _I, ctypes.POINTER(ctypes.c_double)]
         lib.qlmref_matmul_int8_stack.argtypes = [_P, _I, _I, _P, _P, _I, _I, _P, _I,
                                                  ctypes.POINTER(ctypes.c_double)]
+        lib.qlmref_greedy_sample.argtypes = [_P, _I, ctypes.POINTER(_I)]
         self.lib = lib
         self.threads = 1
 
     def _rc(self, rc: int) -> None:
         if rc != 0:
             raise RuntimeError(self.lib.qlmref_last_error().decode())
+
+    def greedy_sample(self, logits: np.ndarray) -> int:
+        """DecoderModel::sample(logits, 0, 0) (model/model.cpp:259-272)."""
+        v = np.ascontiguousarray(logits, np.float32).ravel()
+        out = _I(0)
+        self._rc(self.lib.qlmref_greedy_sample(v.ctypes.data, v.size, ctypes.byref(out)))
+        return int(out.value)
 
     def init_threads(self, n: int) -> None:
         """math::init_thread_pool(n) (ops/math_ops.cpp:161-171)."""
@@ -165,3 +173,17 @@ def synth_case(m: int, n: int, k: int, seed: int):
     w, rng = synth_weights(n, k, seed)
     x = rng.standard_normal((m, k)).astype(np.float32)
     return x, w
+
+
+def greedy_argmax(logits: np.ndarray) -> int:
+    """Restatement of QuickLM's greedy sampling (model/model.cpp:259-272): a
+    scan from index 0 keeping the first strictly larger value. Equivalently:
+    0 if logits[0] is NaN, else the lowest index holding the maximum of the
+    non-NaN values (NaN never compares larger; ties keep the lower index;
+    +0 and -0 tie)."""
+    v = np.asarray(logits, np.float32).ravel()
+    if np.isnan(v[0]):
+        return 0
+    finite = ~np.isnan(v)
+    m = v[finite].max()
+    return int(np.flatnonzero(finite & (v == m))[0])

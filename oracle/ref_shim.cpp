@@ -14,11 +14,14 @@
 //                          (ops/math_ops.cpp:820-900 -> int8_gemv_range 558-579
 //                          -> dot8/dot4/dot_avx2_int8 414-553)
 //   qlmref_init_threads -> math::init_thread_pool (ops/math_ops.cpp:161-171)
+//   qlmref_greedy_sample -> DecoderModel::sample(logits, 0, 0), the greedy branch
+//                          (model/model.cpp:259-272)
 //
 // The reference quantizer only reads safetensors files, so qlmref_quantize
 // writes the matrix to a private temporary file first.
 
 #include "math_ops.hpp"
+#include "model.hpp"
 #include "safetensors.hpp"
 
 #include <chrono>
@@ -61,6 +64,17 @@ bool write_safetensors(const std::string& path, const void* data, int dtype, int
 extern "C" {
 
 const char* qlmref_last_error(void) { return g_err.c_str(); }
+
+// The reference's greedy sampling over n logits (a view, not a copy).
+int qlmref_greedy_sample(const float* logits, int n, int* out) {
+    if (!logits || n <= 0 || !out) return fail("bad arguments");
+    Tensor t;
+    t.shape = {1, n};
+    t.data = const_cast<float*>(logits);
+    DecoderModel model;
+    *out = model.sample(t, 0.0f, 0);
+    return 0;
+}
 
 int qlmref_init_threads(int n) {
     try {

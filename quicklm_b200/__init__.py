@@ -23,7 +23,7 @@ import os
 
 import numpy as np
 
-__all__ = ["QlmError", "Int8Weight", "matmul", "load", "LIB_PATH", "EXACT", "TENSOR", "HOST_IO", "SYNC",
+__all__ = ["QlmError", "Int8Weight", "matmul", "argmax", "load", "LIB_PATH", "EXACT", "TENSOR", "HOST_IO", "SYNC",
            "BLOCK", "Comm", "shard_rows", "matmul_allgather"]
 
 LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "lib", "libqlm_b200.so")
@@ -36,7 +36,7 @@ ABI_SYMBOLS = (
     "qlm_abi_version", "qlm_last_error", "qlm_weight_quantize_upload", "qlm_weight_import_int8",
     "qlm_weight_export_int8", "qlm_weight_shape", "qlm_weight_bytes", "qlm_weight_free", "qlm_linear_int8",
     "qlm_device_status", "qlm_stream_sync", "qlm_linear_int8_tc_noalloc", "qlm_comm_handle_bytes",
-    "qlm_comm_create", "qlm_comm_connect", "qlm_comm_free", "qlm_linear_int8_allgather",
+    "qlm_comm_create", "qlm_comm_connect", "qlm_comm_free", "qlm_linear_int8_allgather", "qlm_argmax_f32",
 )
 
 _STATUS = {0: "OK", 1: "INVALID_ARG", 2: "CUDA", 3: "OUT_OF_MEMORY", 4: "UNSUPPORTED", 5: "TIMEOUT", 6: "NCCL",
@@ -83,6 +83,7 @@ def load(path: str = LIB_PATH):
     lib.qlm_comm_free.argtypes = [P]
     lib.qlm_comm_free.restype = None
     lib.qlm_linear_int8_allgather.argtypes = [P, I, I, L, P, P, P, L, I, P]
+    lib.qlm_argmax_f32.argtypes = [P, I, L, P, P, P, I, P]
     if lib.qlm_abi_version() != 1:
         raise QlmError(7, "ABI version mismatch")
     _lib = lib
@@ -321,3 +322,25 @@ def matmul_allgather(x, w: Int8Weight, comm: Comm, y=None, flags: int = 0, strea
     _check(lib.qlm_linear_int8_allgather(a2.data_ptr(), 1, a2.shape[1], a2.stride(0), w.handle, comm.handle,
                                          y.data_ptr(), y.shape[-1], flags, st))
     return y
+
+
+def argmax(logits, comm: "Comm" = None, col0: int = 0, stream=None):
+    """Greedy token choice on the device, as QuickLM's
+    DecoderModel::sample(logits, 0, 0) (model/model.cpp:259-272): 0 if logit 0
+    is NaN, else the lowest index of the largest non-NaN logit. logits: CUDA
+    float32 [n] or [1, n] — with ``comm`` (row-sharded lm_head) this rank's
+    shard, whose first logit is global index ``col0``; every rank calls it and
+    all get the choice over all shards. Returns (index, value); index is -1
+    when no logit is a number. Synchronous."""
+    import torch
+    lib = load()
+    v = logits.reshape(-1)
+    if v.dtype != torch.float32 or not v.is_cuda or not v.is_contiguous():
+        raise QlmError(1, "logits must be a contiguous CUDA float32 vector")
+    out_i = torch.empty(1, dtype=torch.int32, device=v.device)
+    out_v = torch.empty(1, dtype=torch.float32, device=v.device)
+    st = _stream_ptr(stream) if stream is not None else torch.cuda.current_stream(v.device).cuda_stream
+    with torch.cuda.device(v.device):
+        _check(lib.qlm_argmax_f32(v.data_ptr(), v.numel(), int(col0), comm.handle if comm is not None else None,
+                                  out_i.data_ptr(), out_v.data_ptr(), SYNC, st))
+    return int(out_i.item()), float(out_v.item())

@@ -44,7 +44,8 @@ void set_last_error(const std::string& msg);
 
 namespace {
 
-constexpr size_t kHeaderBytes = 256;  // keeps the word area 256-byte aligned
+constexpr size_t kHeaderBytes = 256;  // greedy-choice words; keeps the gathered words 256-byte aligned
+static_assert(2 * qlm::kMaxRanks * sizeof(unsigned long long) <= kHeaderBytes, "argmax words fit the header");
 
 int fail(int code, const char* fmt, ...) {
     char buf[384];
@@ -179,6 +180,50 @@ int qlm_linear_int8_allgather(const float* x, int M, int k, int64_t ldx, const q
         if (code) {
             cudaMemset(c->state + 2, 0, sizeof(int));
             return fail(QLM_ERR_TIMEOUT, "a bounded wait for peer ranks gave up (code 0x%x)", code);
+        }
+    }
+    return QLM_OK;
+}
+
+int qlm_argmax_f32(const float* logits, int n, int64_t col0, qlm_comm* c, int* out_index, float* out_value, int flags,
+                   void* stream) {
+    if (!logits || !out_index || !out_value) return fail(QLM_ERR_INVALID_ARG, "NULL argument");
+    if (n <= 0) return fail(QLM_ERR_INVALID_ARG, "n=%d must be >= 1", n);
+    if (col0 < 0 || col0 + n > 0xFFFFFD)
+        return fail(QLM_ERR_INVALID_ARG, "global logit indices [%lld, %lld) exceed 2^24 - 2", (long long)col0,
+                    (long long)(col0 + n));
+    if (flags & ~QLM_LINEAR_SYNC) return fail(QLM_ERR_INVALID_ARG, "only QLM_LINEAR_SYNC is accepted (device pointers)");
+    qlm::ArgmaxArgs a{};
+    int device = -1;
+    if (c) {
+        for (int r = 0; r < c->nranks; ++r)
+            if (!c->peers[r]) return fail(QLM_ERR_INVALID_ARG, "communicator not connected (rank %d)", r);
+        for (int r = 0; r < c->nranks; ++r) a.peer_words[r] = reinterpret_cast<unsigned long long*>(c->peers[r]);
+        a.epoch = c->state + 1;
+        a.status = c->state + 2;
+        a.nranks = c->nranks;
+        a.rank = c->rank;
+        device = c->device;
+    } else {
+        cudaError_t e = cudaGetDevice(&device);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+    }
+    Dev g(device);
+    if (!g.ok) return fail(QLM_ERR_CUDA, "cudaSetDevice(%d) failed", device);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    cudaError_t e = qlm::launch_argmax(logits, n, (int)col0, a, out_index, out_value, s, true);
+    if (e != cudaSuccess) return cuda_fail(e, "argmax launch");
+    if (flags & QLM_LINEAR_SYNC) {
+        e = cudaStreamSynchronize(s);
+        if (e != cudaSuccess) return cuda_fail(e, "stream synchronize");
+        if (c) {
+            int code = 0;
+            e = cudaMemcpy(&code, c->state + 2, sizeof(int), cudaMemcpyDeviceToHost);
+            if (e != cudaSuccess) return cuda_fail(e, "read status");
+            if (code) {
+                cudaMemset(c->state + 2, 0, sizeof(int));
+                return fail(QLM_ERR_TIMEOUT, "a bounded wait for peer ranks gave up (code 0x%x)", code);
+            }
         }
     }
     return QLM_OK;

@@ -33,6 +33,23 @@ struct GatherArgs {
     int col0;    // this shard's first output column
 };
 
+// Greedy selection across ranks: peer_words[r] is rank r's exchange header
+// (two halves of kMaxRanks 64-bit words, by epoch parity). nranks = 0: this
+// launch reduces its logits alone.
+struct ArgmaxArgs {
+    unsigned long long* peer_words[kMaxRanks];
+    const int* epoch;
+    int* status;
+    int nranks;
+    int rank;
+};
+
+// out_idx / out_val (device) = the reference's greedy choice over the logits
+// y[0:n], whose first element is global logit col0; with a.nranks > 0 the
+// choice is over every rank's shard (each rank passes its own).
+cudaError_t launch_argmax(const float* y, int n, int col0, const ArgmaxArgs& a, int* out_idx, float* out_val,
+                          cudaStream_t stream, bool pdl);
+
 // Bit-exact y[m][0:rows] = x[m][0:k] . W^T for m < mm (1..8), W packed.
 // status: device int set non-zero if a bounded wait gave up. With gather
 // (mm == 1 only) the rows are stored into every rank's exchange buffer

@@ -45,6 +45,14 @@ def test_null_args_rejected_on_host(qlm_lib):
     assert rc == 1 and b"row range" in qlm_lib.qlm_last_error()
     rc = qlm_lib.qlm_weight_quantize_upload(w.ctypes.data, 0, 4, 4, 8, 0, 4, 0, None, ctypes.byref(out))
     assert rc == 1 and b"stride" in qlm_lib.qlm_last_error()
+    i32, f32 = ctypes.c_int(0), ctypes.c_float(0)
+    rc = qlm_lib.qlm_argmax_f32(None, 4, 0, None, ctypes.byref(i32), ctypes.byref(f32), 0, None)
+    assert rc == 1 and b"NULL" in qlm_lib.qlm_last_error()
+    v = np.zeros(4, np.float32)
+    rc = qlm_lib.qlm_argmax_f32(v.ctypes.data, 0, 0, None, ctypes.byref(i32), ctypes.byref(f32), 0, None)
+    assert rc == 1 and b"n=0" in qlm_lib.qlm_last_error()
+    rc = qlm_lib.qlm_argmax_f32(v.ctypes.data, 4, 1 << 24, None, ctypes.byref(i32), ctypes.byref(f32), 0, None)
+    assert rc == 1 and b"2^24" in qlm_lib.qlm_last_error()
     with pytest.raises(q.QlmError):
         q._check(1)
 

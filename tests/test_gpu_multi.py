@@ -96,6 +96,28 @@ def _worker(rank, world, port, result_dir):
                 if not torch.equal(y.view(torch.int32), y_ref.view(torch.int32)):
                     msg = f"odd width, call {i}: gathered output differs"
                     break
+            # greedy choice over a row-sharded lm_head: each rank reduces its own
+            # logits, one word per rank crosses NVLink (QuickLM's sample(), model.cpp:259-272)
+            from oracle.oracle import greedy_argmax
+            y_loc = q.matmul(xod, shard2, flags=q.SYNC)  # this rank's shard of the logits
+            full_logits = y_ref.cpu().numpy()[0]
+            got = q.argmax(y_loc, comm2, col0=b2)
+            if msg == "ok" and got[0] != greedy_argmax(full_logits):
+                msg = f"sharded argmax {got} != {greedy_argmax(full_logits)}"
+            cases = []
+            t = np.random.default_rng(3).standard_normal(1001).astype(np.float32)
+            t[[10, 900]] = 7.0  # equal maxima in different shards: the lower index wins
+            cases.append(t.copy())
+            t[0] = np.nan       # NaN at global index 0: the answer is 0
+            cases.append(t.copy())
+            t[:] = -np.inf
+            t[600] = np.nan
+            cases.append(t.copy())
+            for v in cases:
+                loc = torch.from_numpy(v[b2:e2].copy()).cuda()
+                got = q.argmax(loc, comm2, col0=b2)
+                if msg == "ok" and got[0] != greedy_argmax(v):
+                    msg = f"sharded argmax case: {got} != {greedy_argmax(v)}"
             torch.cuda.synchronize()
             dist.barrier()
             comm2.free()

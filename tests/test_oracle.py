@@ -94,3 +94,35 @@ def test_fuzz_c_oracle_vs_reference(coracle, refcpu):
         x = (rng.standard_normal((m, k)) * 10.0 ** rng.integers(-30, 20)).astype(np.float32)
         y1, _ = refcpu.matmul(x, q1, s1)
         assert bits_equal(y1, coracle.matmul(x, q1, s1))
+
+
+def greedy_cases(seed=0, count=200):
+    """Fuzzed logit vectors with the values that decide greedy sampling:
+    ties, NaN (at index 0 and elsewhere), +-inf, +-0, subnormals."""
+    rng = np.random.default_rng(seed)
+    specials = np.array([np.nan, np.inf, -np.inf, 0.0, -0.0, 1e-45, -1e-45, 3.0], np.float32)
+    out = []
+    for t in range(count):
+        n = int(rng.integers(1, 300))
+        v = rng.standard_normal(n).astype(np.float32)
+        if t % 3 == 0:  # repeated maxima
+            v[rng.integers(0, n, size=3)] = v.max() if n else 0
+        if t % 4 == 1:
+            idx = rng.integers(0, n, size=max(1, n // 5))
+            v[idx] = rng.choice(specials, size=idx.size)
+        if t % 10 == 2:
+            v[0] = np.nan
+        if t % 10 == 3:
+            v[:] = -np.inf
+        if t % 10 == 4:
+            v[:] = np.nan
+        out.append(v)
+    return out
+
+
+def test_greedy_argmax_matches_reference(refcpu):
+    """oracle.greedy_argmax == DecoderModel::sample(logits, 0, 0), compiled
+    from the reference (model/model.cpp:259-272)."""
+    from oracle.oracle import greedy_argmax
+    for v in greedy_cases():
+        assert greedy_argmax(v) == refcpu.greedy_sample(v), v
