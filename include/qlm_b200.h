@@ -116,6 +116,17 @@ void qlm_weight_free(qlm_w8* w);
 int qlm_linear_int8(const float* x, int M, int k, int64_t ldx, const qlm_w8* w, float* y, int64_t ldy, int flags,
                     void* stream);
 
+/* y_g[m, 0:rows_g] = x[m, 0:k] . W_g^T for nw (1..8) weights that share the
+ * activations (q/k/v, gate/up, GDN qkv/z/b/a): one exact launch per group of
+ * up to 8 activation rows streams all the weights, instead of one launch per
+ * weight; every output is bit-identical to qlm_linear_int8's exact path. The
+ * int8 counterpart of math::matmul_batched (src/ops/math_ops.cpp:902-954),
+ * which QuickLM runs for bf16 weights only. ws: handles on one device with the
+ * same k; ys / ldys: device outputs [M, rows_g] with row strides >= rows_g.
+ * flags: 0 or QLM_LINEAR_SYNC (device pointers). */
+int qlm_linear_int8_grouped(const float* x, int M, int k, int64_t ldx, const qlm_w8* const* ws, int nw,
+                            float* const* ys, const int64_t* ldys, int flags, void* stream);
+
 /* The tensor-core GEMM of qlm_linear_int8(QLM_LINEAR_TENSOR), for callers that
  * must not allocate device memory once running: an engine that hands all of
  * device memory to its own pool at start-up, or a decode loop that cannot

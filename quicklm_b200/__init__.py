@@ -23,7 +23,7 @@ import os
 
 import numpy as np
 
-__all__ = ["QlmError", "Int8Weight", "matmul", "argmax", "load", "LIB_PATH", "EXACT", "TENSOR", "HOST_IO", "SYNC",
+__all__ = ["QlmError", "Int8Weight", "matmul", "matmul_grouped", "argmax", "load", "LIB_PATH", "EXACT", "TENSOR", "HOST_IO", "SYNC",
            "BLOCK", "Comm", "shard_rows", "matmul_allgather"]
 
 LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "lib", "libqlm_b200.so")
@@ -37,6 +37,7 @@ ABI_SYMBOLS = (
     "qlm_weight_export_int8", "qlm_weight_shape", "qlm_weight_bytes", "qlm_weight_free", "qlm_linear_int8",
     "qlm_device_status", "qlm_stream_sync", "qlm_linear_int8_tc_noalloc", "qlm_comm_handle_bytes",
     "qlm_comm_create", "qlm_comm_connect", "qlm_comm_free", "qlm_linear_int8_allgather", "qlm_argmax_f32",
+    "qlm_linear_int8_grouped",
 )
 
 _STATUS = {0: "OK", 1: "INVALID_ARG", 2: "CUDA", 3: "OUT_OF_MEMORY", 4: "UNSUPPORTED", 5: "TIMEOUT", 6: "NCCL",
@@ -84,6 +85,7 @@ def load(path: str = LIB_PATH):
     lib.qlm_comm_free.restype = None
     lib.qlm_linear_int8_allgather.argtypes = [P, I, I, L, P, P, P, L, I, P]
     lib.qlm_argmax_f32.argtypes = [P, I, L, P, P, P, I, P]
+    lib.qlm_linear_int8_grouped.argtypes = [P, I, I, L, P, I, P, P, I, P]
     if lib.qlm_abi_version() != 1:
         raise QlmError(7, "ABI version mismatch")
     _lib = lib
@@ -344,3 +346,27 @@ def argmax(logits, comm: "Comm" = None, col0: int = 0, stream=None):
         _check(lib.qlm_argmax_f32(v.data_ptr(), v.numel(), int(col0), comm.handle if comm is not None else None,
                                   out_i.data_ptr(), out_v.data_ptr(), SYNC, st))
     return int(out_i.item()), float(out_v.item())
+
+
+def matmul_grouped(x, weights, ys=None, flags: int = 0, stream=None):
+    """[x . W_g^T for W_g in weights] in one exact launch per 8 activation rows
+    (weights that share x: q/k/v, gate/up; the int8 counterpart of QuickLM's
+    bf16-only math::matmul_batched, ops/math_ops.cpp:902-954). x: CUDA float32
+    [M, K]; weights: 1..8 Int8Weight on x's device with the same K; ys:
+    optional list of CUDA float32 [M, rows_g] outputs. Bit-identical to
+    matmul(x, W_g) for every g."""
+    import torch
+    lib = load()
+    a2 = x if x.dim() == 2 else x.view(1, -1)
+    if a2.dtype != torch.float32 or not a2.is_cuda or a2.stride(1) != 1:
+        raise QlmError(1, "x must be a CUDA float32 matrix with unit column stride")
+    if ys is None:
+        ys = [torch.empty((a2.shape[0], w.rows), dtype=torch.float32, device=x.device) for w in weights]
+    n = len(weights)
+    hs = (ctypes.c_void_p * n)(*[w.handle for w in weights])
+    yp = (ctypes.c_void_p * n)(*[y.data_ptr() for y in ys])
+    ld = (ctypes.c_int64 * n)(*[y.stride(0) for y in ys])
+    st = _stream_ptr(stream) if stream is not None else torch.cuda.current_stream(x.device).cuda_stream
+    _check(lib.qlm_linear_int8_grouped(a2.data_ptr(), a2.shape[0], a2.shape[1], a2.stride(0), hs, n, yp, ld, flags,
+                                       st))
+    return ys

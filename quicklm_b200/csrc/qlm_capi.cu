@@ -393,6 +393,52 @@ int qlm_linear_int8(const float* x, int M, int k, int64_t ldx, const qlm_w8* w, 
     return QLM_OK;
 }
 
+int qlm_linear_int8_grouped(const float* x, int M, int k, int64_t ldx, const qlm_w8* const* ws, int nw,
+                            float* const* ys, const int64_t* ldys, int flags, void* stream) {
+    if (!x || !ws || !ys || !ldys) return set_err(QLM_ERR_INVALID_ARG, "NULL argument");
+    if (nw < 1 || nw > qlm::kMaxGroup) return set_err(QLM_ERR_INVALID_ARG, "nw=%d not in [1, %d]", nw, qlm::kMaxGroup);
+    if (M <= 0) return set_err(QLM_ERR_INVALID_ARG, "M=%d must be >= 1", M);
+    if (ldx < k) return set_err(QLM_ERR_INVALID_ARG, "ldx %lld < k %d", (long long)ldx, k);
+    if (flags & ~QLM_LINEAR_SYNC) return set_err(QLM_ERR_INVALID_ARG, "only QLM_LINEAR_SYNC is accepted (device pointers)");
+    qlm::GemvWeight gw[qlm::kMaxGroup];
+    int rows_total = 0;
+    for (int g = 0; g < nw; ++g) {
+        const qlm_w8* w = ws[g];
+        if (!w || !ys[g]) return set_err(QLM_ERR_INVALID_ARG, "NULL weight or output %d", g);
+        if (w->k != k) return set_err(QLM_ERR_INVALID_ARG, "weight %d has k=%d, expected %d", g, w->k, k);
+        if (w->device != ws[0]->device) return set_err(QLM_ERR_INVALID_ARG, "weights on different devices");
+        if (ldys[g] < w->rows) return set_err(QLM_ERR_INVALID_ARG, "ldy %lld < rows %d (weight %d)", (long long)ldys[g], w->rows, g);
+        gw[g] = qlm::GemvWeight{w->q, w->s, w->rows, ys[g], ldys[g]};
+        rows_total += w->rows;
+    }
+    DeviceState* st;
+    int rc = device_state(ws[0]->device, &st);
+    if (rc) return rc;
+    DeviceGuard g(ws[0]->device);
+    if (!g.ok) return set_err(QLM_ERR_CUDA, "cudaSetDevice(%d) failed", ws[0]->device);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    int mm = 8;
+    while (mm > 1 && !qlm::gemv_supported(mm, rows_total, k, st->sm_count)) --mm;
+    if (!qlm::gemv_supported(mm, rows_total, k, st->sm_count))
+        return set_err(QLM_ERR_UNSUPPORTED, "k=%d exceeds the exact path's shared-memory staging limit", k);
+    for (int m0 = 0; m0 < M; m0 += mm) {
+        const int rows_m = (M - m0) < mm ? (M - m0) : mm;
+        qlm::GemvWeight gm[qlm::kMaxGroup];
+        for (int i = 0; i < nw; ++i) {
+            gm[i] = gw[i];
+            gm[i].y = gw[i].y + (int64_t)m0 * gw[i].ldy;
+        }
+        QLM_CUDA(qlm::launch_gemv_grouped(x + (int64_t)m0 * ldx, ldx, rows_m, gm, nw, k, st->status, st->sm_count, s,
+                                          pdl_enabled()),
+                 "grouped gemv launch");
+    }
+    if (flags & QLM_LINEAR_SYNC) {
+        QLM_CUDA(cudaStreamSynchronize(s), "stream synchronize");
+        return qlm_device_status(ws[0]->device, 1);
+    }
+    return QLM_OK;
+}
+
 int qlm_device_status(int device, int reset) {
     DeviceState* st;
     int rc = device_state(device, &st);

@@ -54,17 +54,27 @@ constexpr int kRowChunkBytes = kChunk + 16;  // one row x one chunk: 128 int8 + 
 constexpr int kStatusTimeout = 0x201;
 constexpr int kStatusGatherTimeout = 0x202;
 
-struct GemvParams {
-    const float* x;
-    int64_t ldx;
-    float zero_neg;  // -0.0f: the product addend (see the file header)
+// One weight of a launch. A launch serves up to kMaxGroup weights that share
+// the activations (q/k/v, gate/up): their units are concatenated, weight g
+// owning units [ubase, ubase + ceil(rows / (4 R))).
+struct GemvGroup {
     const uint8_t* q;
     const float* s;
     float* y;
     int64_t ldy;
+    int rows;
+    int ubase;
+};
+
+struct GemvParams {
+    const float* x;
+    int64_t ldx;
+    float zero_neg;  // -0.0f: the product addend (see the file header)
+    GemvGroup grp[kMaxGroup];
+    int ngroup;
     int* status;
-    int rows, k, k_pad, nb_pad;
-    int units;       // ceil(rows / (4 R))
+    int k, k_pad, nb_pad;
+    int units;       // total units over the weights
     int sc, nseg;    // chunks per segment, segments per row
     int d;           // slots per warp
     int xs_bytes;    // activation staging bytes (128-aligned)
@@ -79,6 +89,14 @@ __device__ __forceinline__ void cta_units(const GemvParams& p, int& u_begin, int
     const int b = (int)blockIdx.x;
     u_begin = b * p.ucta_q + min(b, p.ucta_r);
     u_end = u_begin + p.ucta_q + (b < p.ucta_r ? 1 : 0);
+}
+
+// Weight of global unit u (the last one whose first unit is <= u).
+__device__ __forceinline__ int unit_group(const GemvParams& p, int u) {
+    int g = 0;
+    for (int i = 1; i < p.ngroup; ++i)
+        if (u >= p.grp[i].ubase) g = i;
+    return g;
 }
 
 // x element k lives at (k/128)*128 + j*32 + l*4 + bb (block bb = (k/32)%4,
@@ -153,7 +171,8 @@ __device__ __forceinline__ void chunk_update(const float* __restrict__ xs_chunk,
 // up to 12 warps and 80 registers, so two CTAs fit on an SM and the next
 // kernel's CTA can start its weight copies while this one finishes.
 template <int MM, int R, bool GATHER>
-__global__ void __launch_bounds__(MM == 1 ? 384 : 512, MM == 1 ? 2 : 1) gemv_kernel(const GemvParams p) {
+__global__ void __launch_bounds__(MM == 1 ? 384 : 512, MM == 1 ? 2 : 1)
+    gemv_kernel(const __grid_constant__ GemvParams p) {
     extern __shared__ __align__(128) uint8_t smem[];
     using namespace sm100;
     const int warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5, lane32 = threadIdx.x & 31;
@@ -180,18 +199,20 @@ __global__ void __launch_bounds__(MM == 1 ? 384 : 512, MM == 1 ? 2 : 1) gemv_ker
     // Whole warp: lane r < 4R copies row r's int8 slice, lane 16 + r its scales.
     auto issue = [&](int uu, int g, int slot) {
         const int u = u_begin + warp + uu * nwarps;
+        const GemvGroup& W = p.grp[unit_group(p, u)];
+        const int lu = u - W.ubase;  // unit within its weight
         const int c0 = g * p.sc;
         const int n = min(p.sc, nck - c0);
         const uint32_t bar = bars + slot * 8;
         const uint32_t dst = smem_u32(my_slots + (size_t)slot * slot_bytes);
-        const int valid = min(kUnitRows, p.rows - kUnitRows * u);
+        const int valid = min(kUnitRows, W.rows - kUnitRows * lu);
         if (lane32 == 0) mbar_arrive_expect_tx(bar, (uint32_t)(valid * n * kRowChunkBytes));
-        const int r = lane32 & 15, row = kUnitRows * u + r;
+        const int r = lane32 & 15, row = kUnitRows * lu + r;
         if (lane32 < 16 && r < valid)
-            bulk_copy_g2s(dst + r * p.sc * kChunk, p.q + (int64_t)row * p.k_pad + (int64_t)c0 * kChunk,
+            bulk_copy_g2s(dst + r * p.sc * kChunk, W.q + (int64_t)row * p.k_pad + (int64_t)c0 * kChunk,
                           (uint32_t)(n * kChunk), bar);
         else if (lane32 >= 16 && r < valid)
-            bulk_copy_g2s(dst + kUnitRows * p.sc * kChunk + r * p.sc * 16, p.s + (int64_t)row * p.nb_pad + c0 * 4,
+            bulk_copy_g2s(dst + kUnitRows * p.sc * kChunk + r * p.sc * 16, W.s + (int64_t)row * p.nb_pad + c0 * 4,
                           (uint32_t)(n * 16), bar);
     };
 
@@ -306,14 +327,16 @@ __global__ void __launch_bounds__(MM == 1 ? 384 : 512, MM == 1 ? 2 : 1) gemv_ker
                     t[m][i] = v;
                 }
             if (lane == 0) {
+                const GemvGroup& W = p.grp[unit_group(p, u)];
+                const int lu = u - W.ubase;
 #pragma unroll
                 for (int i = 0; i < R; ++i) {
-                    const int row = kUnitRows * u + rsub + i;
-                    if (row >= p.rows) break;
+                    const int row = kUnitRows * lu + rsub + i;
+                    if (row >= W.rows) break;
                     if (p.k > nbf * kBlock) {
                         // Ragged tail: sequential scalar sum times the last block's scale.
-                        const uint8_t* qr = p.q + (int64_t)row * p.k_pad;
-                        const float st = p.s[(int64_t)row * p.nb_pad + nbf];
+                        const uint8_t* qr = W.q + (int64_t)row * p.k_pad;
+                        const float st = W.s[(int64_t)row * p.nb_pad + nbf];
 #pragma unroll
                         for (int m = 0; m < MM; ++m) {
                             float acc = 0.0f;
@@ -333,7 +356,7 @@ __global__ void __launch_bounds__(MM == 1 ? 384 : 512, MM == 1 ? 2 : 1) gemv_ker
                             st_relaxed_sys_u64(p.ga.peer_slots[r] + g_half + p.ga.col0 + row, word);
                     } else {
 #pragma unroll
-                        for (int m = 0; m < MM; ++m) p.y[(int64_t)m * p.ldy + row] = t[m][i];
+                        for (int m = 0; m < MM; ++m) W.y[(int64_t)m * W.ldy + row] = t[m][i];
                     }
                 }
             }
@@ -368,7 +391,7 @@ __global__ void __launch_bounds__(MM == 1 ? 384 : 512, MM == 1 ? 2 : 1) gemv_ker
                 __nanosleep(32);
                 v = ld_relaxed_sys_u64(mine + i);
             }
-            if ((int)(v >> 32) == g_epoch) p.y[i] = __uint_as_float((uint32_t)v);
+            if ((int)(v >> 32) == g_epoch) p.grp[0].y[i] = __uint_as_float((uint32_t)v);
         }
         __syncthreads();
         if (threadIdx.x == 0) {
@@ -395,12 +418,14 @@ int pick_rows_per_thread(int mm, int rows, int sm_count) {
     return rows / sm_count >= 48 ? 2 : 1;
 }
 
-bool make_plan(int mm, int rows, int k, int sm_count, Plan* pl) {
+// rows: the rows the launch covers (for several weights, the sum of their
+// rows each rounded up to whole units of the forced R).
+bool make_plan(int mm, int rows, int k, int sm_count, Plan* pl, int force_r = 0) {
     const int k_pad = packed_k(k);
     const int nck = k_pad / kChunk;
     const int max_warps = mm == 1 ? 12 : 16;
     pl->mm = mm;
-    pl->r = pick_rows_per_thread(mm, rows, sm_count);
+    pl->r = force_r ? force_r : pick_rows_per_thread(mm, rows, sm_count);
     const int unit_rows = 4 * pl->r;
     // About four segments per row, so a row's chain starts on its first
     // quarter while the rest is in flight.
@@ -450,7 +475,12 @@ cudaError_t launch_mm(const GemvParams& p0, const Plan& pl, cudaStream_t stream,
         attr_set[gi][dev] = true;
     }
     GemvParams p = p0;
-    p.units = (p.rows + 4 * R - 1) / (4 * R);
+    int ub = 0;
+    for (int g = 0; g < p.ngroup; ++g) {
+        p.grp[g].ubase = ub;
+        ub += (p.grp[g].rows + 4 * R - 1) / (4 * R);
+    }
+    p.units = ub;
     p.ucta_q = p.units / pl.ctas;
     p.ucta_r = p.units % pl.ctas;
     p.sc = pl.sc;
@@ -477,23 +507,33 @@ bool gemv_supported(int mm, int rows, int k, int sm_count) {
     return make_plan(mm, rows, k, sm_count, &pl);
 }
 
-cudaError_t launch_gemv_exact(const float* x, int64_t ldx, int mm, const uint8_t* q, const float* s, int rows,
-                              int k, float* y, int64_t ldy, int* status, int sm_count, cudaStream_t stream, bool pdl,
-                              const GatherArgs* gather) {
+cudaError_t launch_gemv_grouped(const float* x, int64_t ldx, int mm, const GemvWeight* ws, int nw, int k,
+                                int* status, int sm_count, cudaStream_t stream, bool pdl, const GatherArgs* gather) {
+    if (nw < 1 || nw > kMaxGroup || (gather && (mm != 1 || nw != 1))) return cudaErrorInvalidValue;
+    int rows_total = 0;
+    for (int g = 0; g < nw; ++g) {
+        if (ws[g].rows < 1) return cudaErrorInvalidValue;
+        rows_total += ws[g].rows;
+    }
+    const int r = pick_rows_per_thread(mm, rows_total, sm_count);
+    int rows_eff = 0;  // whole units per weight
+    for (int g = 0; g < nw; ++g) rows_eff += round_up(ws[g].rows, 4 * r);
     Plan pl;
-    if (!make_plan(mm, rows, k, sm_count, &pl)) return cudaErrorInvalidValue;
-    if (gather && mm != 1) return cudaErrorInvalidValue;
+    if (!make_plan(mm, rows_eff, k, sm_count, &pl, r)) return cudaErrorInvalidValue;
     GemvParams p{};
     if (gather) p.ga = *gather;
     p.x = x;
     p.ldx = ldx;
     p.zero_neg = -0.0f;
-    p.q = q;
-    p.s = s;
-    p.y = y;
-    p.ldy = ldy;
+    for (int g = 0; g < nw; ++g) {
+        p.grp[g].q = ws[g].q;
+        p.grp[g].s = ws[g].s;
+        p.grp[g].y = ws[g].y;
+        p.grp[g].ldy = ws[g].ldy;
+        p.grp[g].rows = ws[g].rows;
+    }
+    p.ngroup = nw;
     p.status = status;
-    p.rows = rows;
     p.k = k;
     p.k_pad = packed_k(k);
     p.nb_pad = p.k_pad / kBlock;
@@ -508,6 +548,13 @@ cudaError_t launch_gemv_exact(const float* x, int64_t ldx, int mm, const uint8_t
         case 8: return launch_mm<8, 1>(p, pl, stream, pdl);
         default: return cudaErrorInvalidValue;
     }
+}
+
+cudaError_t launch_gemv_exact(const float* x, int64_t ldx, int mm, const uint8_t* q, const float* s, int rows,
+                              int k, float* y, int64_t ldy, int* status, int sm_count, cudaStream_t stream, bool pdl,
+                              const GatherArgs* gather) {
+    const GemvWeight w{q, s, rows, y, ldy};
+    return launch_gemv_grouped(x, ldx, mm, &w, 1, k, status, sm_count, stream, pdl, gather);
 }
 
 }  // namespace qlm

@@ -58,6 +58,23 @@ cudaError_t launch_gemv_exact(const float* x, int64_t ldx, int mm, const uint8_t
                               int k, float* y, int64_t ldy, int* status, int sm_count, cudaStream_t stream, bool pdl,
                               const GatherArgs* gather = nullptr);
 
+// One weight of a grouped exact launch (packed q, scales, rows, output).
+constexpr int kMaxGroup = 8;
+struct GemvWeight {
+    const uint8_t* q;
+    const float* s;
+    int rows;
+    float* y;
+    int64_t ldy;
+};
+
+// Bit-exact y_g[m][0:rows_g] = x[m][0:k] . W_g^T for nw <= kMaxGroup weights
+// that share x, in one launch (each output identical to a single-weight
+// launch). Gather requires nw == 1 and mm == 1.
+cudaError_t launch_gemv_grouped(const float* x, int64_t ldx, int mm, const GemvWeight* ws, int nw, int k,
+                                int* status, int sm_count, cudaStream_t stream, bool pdl,
+                                const GatherArgs* gather = nullptr);
+
 // Whether the exact GEMV can stage mm activation rows of length k.
 bool gemv_supported(int mm, int rows, int k, int sm_count);
 
