@@ -84,6 +84,17 @@ const char* qlm_last_error(void);
 int qlm_weight_quantize_upload(const void* src, int src_dtype, int64_t src_row_stride, int n_total, int k,
                                int row_begin, int row_end, int device, void* stream, qlm_w8** out);
 
+/* Int4 (Q4_0) variant of qlm_weight_quantize_upload, same arguments.
+ * Replaces get_tensor_keep_int4 (src/io/safetensors.cpp:587-656): per
+ * 32-block scale absmax/8, RN-even rounding, clamp to [-8, 7], bit-identical
+ * to st_quantize_row_f32_int4/_bf16_int4 (src/io/safetensors.cpp:393-515).
+ * The handle holds 4-bit codes (half the device bytes of int8) and is served
+ * by the exact decode GEMV only: qlm_linear_int8 with QLM_LINEAR_TENSOR on an
+ * int4 handle returns QLM_ERR_UNSUPPORTED. Products are bit-identical to the
+ * reference int4 matmul (src/ops/math_ops.cpp:581-794, 837-854). */
+int qlm_weight_quantize_upload_q4(const void* src, int src_dtype, int64_t src_row_stride, int n_total, int k,
+                                  int row_begin, int row_end, int device, void* stream, qlm_w8** out);
+
 /* Upload an already-quantized weight given in the reference Tensor's int8
  * layout (src/tensor/tensor.hpp:34-41): q [n_total, k] int8 row-major and
  * scales [n_total, ceil(k/32)] fp32; host pointers. Keeps rows
@@ -95,10 +106,18 @@ int qlm_weight_import_int8(const int8_t* q, const float* scales, int n_total, in
  * q [rows, k] int8 and scales [rows, ceil(k/32)] fp32, rows = row_end - row_begin. */
 int qlm_weight_export_int8(const qlm_w8* w, int8_t* q, float* scales);
 
+/* Int4 counterpart of qlm_weight_export_int8 in the reference Tensor's int4
+ * layout (src/tensor/tensor.hpp:45-61): packed [rows, (k+1)/2] bytes, low
+ * nibble = even column, nibble = value + 8, and scales [rows, ceil(k/32)]. */
+int qlm_weight_export_int4(const qlm_w8* w, uint8_t* packed, float* scales);
+
+/* Bits per stored weight code: 8 (int8 handle) or 4 (int4 handle); -1 for NULL. */
+int qlm_weight_bits(const qlm_w8* w);
+
 /* Shape of a handle. Any output pointer may be NULL. */
 int qlm_weight_shape(const qlm_w8* w, int* rows, int* k, int* row_begin, int* row_end, int* n_total);
 
-/* Device bytes read by one M=1 product with this weight: packed int8 plus
+/* Device bytes read by one M=1 product with this weight: packed codes plus
  * scales, the "weight bytes" of the decode roofline. */
 int64_t qlm_weight_bytes(const qlm_w8* w);
 

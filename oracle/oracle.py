@@ -65,12 +65,39 @@ class RefCPU:
         lib.qlmref_matmul_int8_stack.argtypes = [_P, _I, _I, _P, _P, _I, _I, _P, _I,
                                                  ctypes.POINTER(ctypes.c_double)]
         lib.qlmref_greedy_sample.argtypes = [_P, _I, ctypes.POINTER(_I)]
+        lib.qlmref_quantize_int4.argtypes = [_P, _I, _I, _I, _P, _P]
+        lib.qlmref_matmul_int4.argtypes = [_P, _I, _I, _P, _P, _I, _P, _I]
         self.lib = lib
         self.threads = 1
 
     def _rc(self, rc: int) -> None:
         if rc != 0:
             raise RuntimeError(self.lib.qlmref_last_error().decode())
+
+    def quantize_int4(self, w: np.ndarray):
+        """get_tensor_keep_int4 on a [n, k] float32 or bf16-bits matrix ->
+        (packed uint8 [n, (k+1)//2] (value + 8, low nibble = even column),
+        scales float32 [n, ceil(k/32)])."""
+        w = np.ascontiguousarray(w)
+        dt = _check_w(w)
+        n, k = w.shape
+        packed = np.empty((n, (k + 1) // 2), np.uint8)
+        s = np.empty((n, (k + BLOCK - 1) // BLOCK), np.float32)
+        self._rc(self.lib.qlmref_quantize_int4(_ptr(w), dt, n, k, _ptr(packed), _ptr(s)))
+        return packed, s
+
+    def matmul_int4(self, x: np.ndarray, packed: np.ndarray, s: np.ndarray, k: int) -> np.ndarray:
+        """math::matmul(A=x [m, k], B=int4 [n, k] packed) -> y [m, n]."""
+        x = np.ascontiguousarray(x, np.float32)
+        if x.ndim == 1:
+            x = x[None, :]
+        packed = np.ascontiguousarray(packed, np.uint8)
+        s = np.ascontiguousarray(s, np.float32)
+        m = x.shape[0]
+        n = packed.shape[0]
+        y = np.empty((m, n), np.float32)
+        self._rc(self.lib.qlmref_matmul_int4(_ptr(x), m, k, _ptr(packed), _ptr(s), n, _ptr(y), n))
+        return y
 
     def greedy_sample(self, logits: np.ndarray) -> int:
         """DecoderModel::sample(logits, 0, 0) (model/model.cpp:259-272)."""
@@ -136,6 +163,7 @@ class COracle:
             raise FileNotFoundError(f"{path} missing: run `make -C oracle oracle`")
         lib = ctypes.CDLL(path)
         lib.qlmo_quantize.argtypes = [_P, _I, _I, _I, _P, _P]
+        lib.qlmo_quantize_q4.argtypes = [_P, _I, _I, _I, _P, _P]
         lib.qlmo_matmul_int8.argtypes = [_P, _I, _I, _P, _P, _I, _P, _I]
         self.lib = lib
 
@@ -146,6 +174,17 @@ class COracle:
         q = np.empty((n, k), np.int8)
         s = np.empty((n, num_blocks(k)), np.float32)
         self.lib.qlmo_quantize(_ptr(w), dt, n, k, _ptr(q), _ptr(s))
+        return q, s
+
+    def quantize_q4(self, w: np.ndarray):
+        """int4 quantizer restatement -> (signed values int8 [n, k] in [-8, 7],
+        scales [n, ceil(k/32)]); pack_q4 gives the reference's byte layout."""
+        w = np.ascontiguousarray(w)
+        dt = _check_w(w)
+        n, k = w.shape
+        q = np.empty((n, k), np.int8)
+        s = np.empty((n, (k + BLOCK - 1) // BLOCK), np.float32)
+        self.lib.qlmo_quantize_q4(_ptr(w), dt, n, k, _ptr(q), _ptr(s))
         return q, s
 
     def matmul(self, x: np.ndarray, q: np.ndarray, s: np.ndarray) -> np.ndarray:
@@ -187,3 +226,25 @@ def greedy_argmax(logits: np.ndarray) -> int:
     finite = ~np.isnan(v)
     m = v[finite].max()
     return int(np.flatnonzero(finite & (v == m))[0])
+
+
+def pack_q4(q: np.ndarray) -> np.ndarray:
+    """Signed int4 values [n, k] -> the reference's packed bytes [n, (k+1)//2]
+    (value + 8, low nibble = even column; a missing odd partner is nibble 8)."""
+    q = np.asarray(q, np.int16)
+    n, k = q.shape
+    u = (q + 8).astype(np.uint8)
+    if k % 2:
+        u = np.concatenate([u, np.full((n, 1), 8, np.uint8)], axis=1)
+    return (u[:, 0::2] | (u[:, 1::2] << 4)).astype(np.uint8)
+
+
+def unpack_q4(packed: np.ndarray, k: int) -> np.ndarray:
+    """Inverse of pack_q4: signed values int8 [n, k]."""
+    p = np.asarray(packed, np.uint8)
+    lo = (p & 0x0F).astype(np.int16) - 8
+    hi = (p >> 4).astype(np.int16) - 8
+    out = np.empty((p.shape[0], 2 * p.shape[1]), np.int16)
+    out[:, 0::2] = lo
+    out[:, 1::2] = hi
+    return out[:, :k].astype(np.int8)

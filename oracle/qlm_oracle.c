@@ -48,6 +48,8 @@ static inline int32_t cvt_lround_int(float v) {
 }
 
 static inline int8_t clamp127(int32_t q) { return (int8_t)(q < -127 ? -127 : (q > 127 ? 127 : q)); }
+/* int4: clamp to [-8, 7] (io/safetensors.cpp:436-437, 452-453). */
+static inline int8_t clamp_q4(int32_t q) { return (int8_t)(q < -8 ? -8 : (q > 7 ? 7 : q)); }
 
 static inline float bf16_to_f32(uint16_t h) {
     uint32_t bits = (uint32_t)h << 16;
@@ -59,7 +61,8 @@ static inline float bf16_to_f32(uint16_t h) {
 /* One block [k0, k1) of a row, values supplied by get(i). Restates the loop
  * body of st_quantize_row_f32 / st_quantize_row_bf16 (io/safetensors.cpp:
  * 353-390 / 301-344). */
-#define QLMO_QUANT_BLOCK(GET)                                                          \
+#define QLMO_QUANT_BLOCK(GET) QLMO_QUANT_BLOCK_T(GET, 127.0f, clamp127)
+#define QLMO_QUANT_BLOCK_T(GET, DIV, CLAMP)                                            \
     do {                                                                               \
         float lane[8] = {0, 0, 0, 0, 0, 0, 0, 0}; /* vmax = _mm256_setzero_ps() */   \
         int k = k0;                                                                    \
@@ -72,13 +75,13 @@ static inline float bf16_to_f32(uint16_t h) {
         m1 = maxps(m1, m3);                                                            \
         float max_abs = maxps(m0, m1);                                                 \
         for (; k < k1; ++k) max_abs = stdmax(max_abs, fabsf(GET(k)));                 \
-        float scale = (max_abs > 0.0f) ? (max_abs / 127.0f) : 1.0f;                    \
+        float scale = (max_abs > 0.0f) ? (max_abs / (DIV)) : 1.0f;                     \
         scales[blk] = scale;                                                           \
         float inv = 1.0f / scale;                                                      \
         k = k0;                                                                        \
         for (; k + 8 <= k1; k += 8)                                                    \
-            for (int i = 0; i < 8; ++i) out[k + i] = clamp127(cvt_rne_indefinite(GET(k + i) * inv)); \
-        for (; k < k1; ++k) out[k] = clamp127(cvt_lround_int(GET(k) * inv));          \
+            for (int i = 0; i < 8; ++i) out[k + i] = CLAMP(cvt_rne_indefinite(GET(k + i) * inv)); \
+        for (; k < k1; ++k) out[k] = CLAMP(cvt_lround_int(GET(k) * inv));             \
     } while (0)
 
 /* st_quantize_row_f32 (io/safetensors.cpp:348-391). */
@@ -114,6 +117,21 @@ void qlmo_quantize(const void* w, int dtype, int n, int k, int8_t* q, float* s) 
             qlmo_quantize_row_bf16((const uint16_t*)w + (size_t)r * k, k, q + (size_t)r * k, s + (size_t)r * nb);
         else
             qlmo_quantize_row_f32((const float*)w + (size_t)r * k, k, q + (size_t)r * k, s + (size_t)r * nb);
+    }
+}
+
+void qlmo_quantize_row_f32_q4(const float* row, int K, int8_t* out, float* scales);
+void qlmo_quantize_row_bf16_q4(const uint16_t* row, int K, int8_t* out, float* scales);
+
+/* get_tensor_keep_int4 over a whole [n, k] matrix (io/safetensors.cpp, the
+ * int4 loader); q receives signed values in [-8, 7]. */
+void qlmo_quantize_q4(const void* w, int dtype, int n, int k, int8_t* q, float* s) {
+    int nb = (k + QLMO_BLOCK - 1) / QLMO_BLOCK;
+    for (int r = 0; r < n; ++r) {
+        if (dtype == 1)
+            qlmo_quantize_row_bf16_q4((const uint16_t*)w + (size_t)r * k, k, q + (size_t)r * k, s + (size_t)r * nb);
+        else
+            qlmo_quantize_row_f32_q4((const float*)w + (size_t)r * k, k, q + (size_t)r * k, s + (size_t)r * nb);
     }
 }
 
@@ -159,4 +177,31 @@ void qlmo_matmul_int8(const float* A, int M, int K, const int8_t* q, const float
     for (int m = 0; m < M; ++m)
         for (int n = 0; n < N; ++n)
             C[(size_t)m * ldc + n] = qlmo_dot_int8(A + (size_t)m * K, q + (size_t)n * K, s + (size_t)n * nb, K);
+}
+
+/* st_quantize_row_f32_int4 / st_quantize_row_bf16_int4 (io/safetensors.cpp:
+ * 393-515): the same block loop with scale = max|v| / 8 and values clamped to
+ * [-8, 7]. out receives the SIGNED values (one per element); the reference
+ * stores value + 8 two per byte (low nibble = even column), which the caller
+ * packs. Its scalar tail defaults a missing odd partner to nibble 8 (value 0). */
+void qlmo_quantize_row_f32_q4(const float* row, int K, int8_t* out, float* scales) {
+    int nb = (K + QLMO_BLOCK - 1) / QLMO_BLOCK;
+    for (int blk = 0; blk < nb; ++blk) {
+        int k0 = blk * QLMO_BLOCK;
+        int k1 = k0 + QLMO_BLOCK < K ? k0 + QLMO_BLOCK : K;
+#define QLMO_GET_F32(i) (row[(i)])
+        QLMO_QUANT_BLOCK_T(QLMO_GET_F32, 8.0f, clamp_q4);
+#undef QLMO_GET_F32
+    }
+}
+
+void qlmo_quantize_row_bf16_q4(const uint16_t* row, int K, int8_t* out, float* scales) {
+    int nb = (K + QLMO_BLOCK - 1) / QLMO_BLOCK;
+    for (int blk = 0; blk < nb; ++blk) {
+        int k0 = blk * QLMO_BLOCK;
+        int k1 = k0 + QLMO_BLOCK < K ? k0 + QLMO_BLOCK : K;
+#define QLMO_GET_BF16(i) (bf16_to_f32(row[(i)]))
+        QLMO_QUANT_BLOCK_T(QLMO_GET_BF16, 8.0f, clamp_q4);
+#undef QLMO_GET_BF16
+    }
 }

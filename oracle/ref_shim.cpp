@@ -16,6 +16,12 @@
 //   qlmref_init_threads -> math::init_thread_pool (ops/math_ops.cpp:161-171)
 //   qlmref_greedy_sample -> DecoderModel::sample(logits, 0, 0), the greedy branch
 //                          (model/model.cpp:259-272)
+//   qlmref_quantize_int4 -> SafetensorsLoader::get_tensor_keep_int4, which runs
+//                          st_quantize_row_f32_int4 / st_quantize_row_bf16_int4
+//                          (io/safetensors.cpp:393-515)
+//   qlmref_matmul_int4  -> math::matmul with an int4 B operand
+//                          (ops/math_ops.cpp:852-855 -> int4_gemv_range 771-794
+//                          -> dot8/dot4/dot_avx2_int4 581-769)
 //
 // The reference quantizer only reads safetensors files, so qlmref_quantize
 // writes the matrix to a private temporary file first.
@@ -117,6 +123,61 @@ int qlmref_quantize(const void* w, int dtype, int n, int k, int8_t* q_out, float
     }
     std::remove(path.c_str());
     return rc;
+}
+
+// The int4 counterpart of qlmref_quantize: packed_out [n, (k+1)/2] bytes (two
+// values per byte, low nibble = even column, value + 8), s_out [n, ceil(k/32)].
+int qlmref_quantize_int4(const void* w, int dtype, int n, int k, uint8_t* packed_out, float* s_out) {
+    if (!w || n <= 0 || k <= 0 || !packed_out || !s_out || (dtype != 0 && dtype != 1)) return fail("bad args");
+    const char* tmp = std::getenv("TMPDIR");
+    std::string pat = std::string(tmp && *tmp ? tmp : "/tmp") + "/qlmref_XXXXXX";
+    std::vector<char> buf(pat.begin(), pat.end());
+    buf.push_back('\0');
+    int fd = mkstemp(buf.data());
+    if (fd < 0) return fail("mkstemp failed");
+    close(fd);
+    std::string path(buf.data());
+    int rc = 0;
+    try {
+        if (!write_safetensors(path, w, dtype, n, k)) {
+            rc = fail("could not write temporary safetensors file");
+        } else {
+            SafetensorsLoader loader;
+            if (!loader.open(path)) {
+                rc = fail("SafetensorsLoader::open failed");
+            } else {
+                Tensor t = loader.get_tensor_keep_int4("w");
+                const int nb = (k + Tensor::INT4_BLOCK_SIZE - 1) / Tensor::INT4_BLOCK_SIZE;
+                std::memcpy(packed_out, t.int4_data, (size_t)n * ((k + 1) / 2));
+                std::memcpy(s_out, t.int4_scales->data(), (size_t)n * nb * sizeof(float));
+            }
+        }
+    } catch (const std::exception& e) {
+        rc = fail(e.what());
+    }
+    std::remove(path.c_str());
+    return rc;
+}
+
+// y = x . W^T through math::matmul with W in the reference's int4 layout.
+int qlmref_matmul_int4(const float* x, int m, int k, const uint8_t* packed, const float* s, int n, float* c,
+                       int ldc) {
+    if (!x || !packed || !s || !c || m <= 0 || k <= 0 || n <= 0 || ldc < n) return fail("bad args");
+    try {
+        const int nb = (k + Tensor::INT4_BLOCK_SIZE - 1) / Tensor::INT4_BLOCK_SIZE;
+        Tensor A(std::vector<int>{m, k}, const_cast<float*>(x));
+        Tensor B;
+        B.shape = {n, k};
+        B.compute_strides();
+        B.int4_data = packed;
+        B.int4_scales = std::make_shared<std::vector<float>>(s, s + (size_t)n * nb);
+        Tensor C(std::vector<int>{m, n}, c);
+        C.strides[0] = ldc;
+        math::matmul(A, B, C, true);
+        return 0;
+    } catch (const std::exception& e) {
+        return fail(e.what());
+    }
 }
 
 // y[m, :] = x[m, :] . W^T through math::matmul, W given in the reference's

@@ -37,7 +37,7 @@ ABI_SYMBOLS = (
     "qlm_weight_export_int8", "qlm_weight_shape", "qlm_weight_bytes", "qlm_weight_free", "qlm_linear_int8",
     "qlm_device_status", "qlm_stream_sync", "qlm_linear_int8_tc_noalloc", "qlm_comm_handle_bytes",
     "qlm_comm_create", "qlm_comm_connect", "qlm_comm_free", "qlm_linear_int8_allgather", "qlm_argmax_f32",
-    "qlm_linear_int8_grouped",
+    "qlm_linear_int8_grouped", "qlm_weight_quantize_upload_q4", "qlm_weight_export_int4", "qlm_weight_bits",
 )
 
 _STATUS = {0: "OK", 1: "INVALID_ARG", 2: "CUDA", 3: "OUT_OF_MEMORY", 4: "UNSUPPORTED", 5: "TIMEOUT", 6: "NCCL",
@@ -69,6 +69,9 @@ def load(path: str = LIB_PATH):
     lib.qlm_weight_quantize_upload.argtypes = [P, I, L, I, I, I, I, I, P, ctypes.POINTER(P)]
     lib.qlm_weight_import_int8.argtypes = [P, P, I, I, I, I, I, P, ctypes.POINTER(P)]
     lib.qlm_weight_export_int8.argtypes = [P, P, P]
+    lib.qlm_weight_quantize_upload_q4.argtypes = [P, I, L, I, I, I, I, I, P, ctypes.POINTER(P)]
+    lib.qlm_weight_export_int4.argtypes = [P, P, P]
+    lib.qlm_weight_bits.argtypes = [P]
     lib.qlm_weight_shape.argtypes = [P] + [ctypes.POINTER(I)] * 5
     lib.qlm_weight_bytes.argtypes = [P]
     lib.qlm_weight_bytes.restype = L
@@ -110,8 +113,9 @@ def _stream_ptr(stream) -> int | None:
 
 
 class Int8Weight:
-    """A device-resident int8 weight (rows [row_begin, row_end) of [n_total, k])
-    with per-32-block fp32 scales, owned by a ``qlm_w8`` handle."""
+    """A device-resident quantized weight (rows [row_begin, row_end) of
+    [n_total, k]) with per-32-block fp32 scales, owned by a ``qlm_w8`` handle.
+    ``bits`` is 8 (the reference's int8 tensors) or 4 (its Q4_0 int4 tensors)."""
 
     def __init__(self, handle: int):
         self._h = ctypes.c_void_p(handle)
@@ -119,6 +123,7 @@ class Int8Weight:
         vals = [ctypes.c_int() for _ in range(5)]
         _check(lib.qlm_weight_shape(self._h, *[ctypes.byref(v) for v in vals]))
         self.rows, self.k, self.row_begin, self.row_end, self.n_total = (v.value for v in vals)
+        self.bits = int(lib.qlm_weight_bits(self._h))
         self.device = None
 
     @property
@@ -133,15 +138,20 @@ class Int8Weight:
 
     @property
     def nbytes(self) -> int:
-        """Device bytes one M=1 product reads (packed int8 + scales)."""
+        """Device bytes one M=1 product reads (packed codes + scales)."""
         return int(load().qlm_weight_bytes(self.handle))
 
     @classmethod
-    def quantize(cls, w, device: int = 0, row_begin: int = 0, row_end: int | None = None, stream=None):
+    def quantize(cls, w, device: int = 0, row_begin: int = 0, row_end: int | None = None, stream=None,
+                 bits: int = 8):
         """Quantize an [n, k] float32 (or bf16-bits uint16 / torch bf16)
         matrix on the device. ``w`` is a numpy array (host, e.g. an mmap) or a
-        torch tensor (host or CUDA)."""
+        torch tensor (host or CUDA). ``bits=8`` follows get_tensor_keep_int8,
+        ``bits=4`` get_tensor_keep_int4 (src/io/safetensors.cpp:517, 587)."""
         lib = load()
+        if bits not in (4, 8):
+            raise QlmError(1, f"bits must be 4 or 8, not {bits}")
+        upload = lib.qlm_weight_quantize_upload if bits == 8 else lib.qlm_weight_quantize_upload_q4
         if _is_torch(w):
             import torch
             if w.dim() != 2 or w.stride(1) != 1:
@@ -170,8 +180,7 @@ class Int8Weight:
         if row_end is None:
             row_end = n
         h = ctypes.c_void_p()
-        _check(lib.qlm_weight_quantize_upload(ptr, dt, stride, n, k, row_begin, row_end, device,
-                                              _stream_ptr(stream), ctypes.byref(h)))
+        _check(upload(ptr, dt, stride, n, k, row_begin, row_end, device, _stream_ptr(stream), ctypes.byref(h)))
         del keep
         out = cls(h.value)
         out.device = device
@@ -202,6 +211,14 @@ class Int8Weight:
         _check(load().qlm_weight_export_int8(self.handle, q.ctypes.data, s.ctypes.data))
         return q, s
 
+    def to_int4(self):
+        """(packed uint8 [rows, (k+1)/2], scales float32 [rows, ceil(k/32)]) in
+        the reference Tensor's int4 layout (low nibble = even column, value + 8)."""
+        q = np.empty((self.rows, (self.k + 1) // 2), np.uint8)
+        s = np.empty((self.rows, (self.k + BLOCK - 1) // BLOCK), np.float32)
+        _check(load().qlm_weight_export_int4(self.handle, q.ctypes.data, s.ctypes.data))
+        return q, s
+
     def free(self) -> None:
         if self._h:
             load().qlm_weight_free(self._h)
@@ -215,7 +232,7 @@ class Int8Weight:
 
 
 def matmul(A, B: Int8Weight, C=None, transpose_B: bool = True, flags: int = EXACT, stream=None):
-    """C = A . B^T for an int8 B (``math::matmul`` with transpose_B=true).
+    """C = A . B^T for an int8 or int4 B (``math::matmul`` with transpose_B=true).
 
     * numpy A/C: host buffers; the call copies in, runs, copies out and
       returns with C complete (the reference's synchronous contract).
@@ -224,7 +241,7 @@ def matmul(A, B: Int8Weight, C=None, transpose_B: bool = True, flags: int = EXAC
     A is [M, K] or [K]; C (allocated when None) is [M, N] with any row stride.
     """
     if not transpose_B:
-        raise QlmError(1, "int8 weights are only supported with transpose_B=true, as in the reference")
+        raise QlmError(1, "quantized weights are only supported with transpose_B=true, as in the reference")
     lib = load()
     if _is_torch(A):
         import torch

@@ -115,7 +115,7 @@ bool pdl_enabled() {
     return on;
 }
 
-int alloc_weight(int device, int n_total, int k, int row_begin, int row_end, qlm_w8** out) {
+int alloc_weight(int device, int n_total, int k, int row_begin, int row_end, qlm_w8** out, int bits = 8) {
     qlm_w8* w = new (std::nothrow) qlm_w8();
     if (!w) return set_err(QLM_ERR_OUT_OF_MEMORY, "host allocation failed");
     w->device = device;
@@ -126,7 +126,8 @@ int alloc_weight(int device, int n_total, int k, int row_begin, int row_end, qlm
     w->row_begin = row_begin;
     w->row_end = row_end;
     w->rows = row_end - row_begin;
-    cudaError_t e = cudaMalloc(&w->q, (size_t)w->rows * w->k_pad);
+    w->bits = bits;
+    cudaError_t e = cudaMalloc(&w->q, (size_t)w->rows * w->k_pad * bits / 8);
     if (e == cudaSuccess) e = cudaMalloc(&w->s, (size_t)w->rows * w->nb_pad * sizeof(float));
     if (e == cudaSuccess) e = cudaMalloc(&w->ew, (size_t)w->rows * sizeof(int));
     if (e != cudaSuccess) {
@@ -159,8 +160,13 @@ int qlm_abi_version(void) { return QLM_ABI_VERSION; }
 
 const char* qlm_last_error(void) { return g_err.c_str(); }
 
-int qlm_weight_quantize_upload(const void* src, int src_dtype, int64_t src_row_stride, int n_total, int k,
-                               int row_begin, int row_end, int device, void* stream, qlm_w8** out) {
+}  // extern "C"
+
+namespace {
+
+// Shared body of the int8 and int4 uploads.
+int quantize_upload(const void* src, int src_dtype, int64_t src_row_stride, int n_total, int k, int row_begin,
+                    int row_end, int device, void* stream, qlm_w8** out, int bits) {
     if (!out) return set_err(QLM_ERR_INVALID_ARG, "out is NULL");
     *out = nullptr;
     if (!src) return set_err(QLM_ERR_INVALID_ARG, "src is NULL");
@@ -184,12 +190,14 @@ int qlm_weight_quantize_upload(const void* src, int src_dtype, int64_t src_row_s
         cudaGetLastError();  // clear: plain host pointers may report an error on old drivers
 
     qlm_w8* w = nullptr;
-    if ((rc = alloc_weight(device, n_total, k, row_begin, row_end, &w))) return rc;
+    if ((rc = alloc_weight(device, n_total, k, row_begin, row_end, &w, bits))) return rc;
+    auto pack = bits == 4 ? qlm::launch_quantize_pack_q4 : qlm::launch_quantize_pack;
+    const size_t q_row_bytes = (size_t)w->k_pad * bits / 8;
 
     cudaError_t e = cudaSuccess;
     if (on_device) {
         const char* base = static_cast<const char*>(src) + (size_t)row_begin * src_row_stride * elem;
-        e = qlm::launch_quantize_pack(base, src_dtype, src_row_stride, w->rows, k, w->q, w->s, s);
+        e = pack(base, src_dtype, src_row_stride, w->rows, k, w->q, w->s, s);
         if (e == cudaSuccess) e = cudaStreamSynchronize(s);
     } else {
         // Stage host rows through a bounded device buffer (<= 64 MB per pass).
@@ -205,13 +213,12 @@ int qlm_weight_quantize_upload(const void* src, int src_dtype, int64_t src_row_s
             e = cudaMemcpy2DAsync(stage, row_bytes, hsrc, (size_t)src_row_stride * elem, row_bytes, nr,
                                   cudaMemcpyHostToDevice, s);
             if (e == cudaSuccess)
-                e = qlm::launch_quantize_pack(stage, src_dtype, k, nr, k, w->q + (size_t)r * w->k_pad,
-                                              w->s + (size_t)r * w->nb_pad, s);
+                e = pack(stage, src_dtype, k, nr, k, w->q + (size_t)r * q_row_bytes, w->s + (size_t)r * w->nb_pad, s);
         }
         if (e == cudaSuccess) e = cudaStreamSynchronize(s);
         if (stage) cudaFree(stage);
     }
-    if (e == cudaSuccess) e = qlm::launch_weight_exponents(w->s, w->rows, k, w->ew, s);
+    if (e == cudaSuccess && bits == 8) e = qlm::launch_weight_exponents(w->s, w->rows, k, w->ew, s);  // tensor-core path only
     if (e == cudaSuccess) e = cudaStreamSynchronize(s);
     if (e != cudaSuccess) {
         qlm_weight_free(w);
@@ -219,6 +226,20 @@ int qlm_weight_quantize_upload(const void* src, int src_dtype, int64_t src_row_s
     }
     *out = w;
     return QLM_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int qlm_weight_quantize_upload(const void* src, int src_dtype, int64_t src_row_stride, int n_total, int k,
+                               int row_begin, int row_end, int device, void* stream, qlm_w8** out) {
+    return quantize_upload(src, src_dtype, src_row_stride, n_total, k, row_begin, row_end, device, stream, out, 8);
+}
+
+int qlm_weight_quantize_upload_q4(const void* src, int src_dtype, int64_t src_row_stride, int n_total, int k,
+                                  int row_begin, int row_end, int device, void* stream, qlm_w8** out) {
+    return quantize_upload(src, src_dtype, src_row_stride, n_total, k, row_begin, row_end, device, stream, out, 4);
 }
 
 int qlm_weight_import_int8(const int8_t* q, const float* scales, int n_total, int k, int row_begin, int row_end,
@@ -266,6 +287,7 @@ int qlm_weight_import_int8(const int8_t* q, const float* scales, int n_total, in
 
 int qlm_weight_export_int8(const qlm_w8* w, int8_t* q, float* scales) {
     if (!w || !q || !scales) return set_err(QLM_ERR_INVALID_ARG, "NULL argument");
+    if (w->bits != 8) return set_err(QLM_ERR_INVALID_ARG, "the handle holds int4 weights (qlm_weight_export_int4)");
     DeviceGuard g(w->device);
     if (!g.ok) return set_err(QLM_ERR_CUDA, "cudaSetDevice(%d) failed", w->device);
     const int nb = (w->k + QLM_BLOCK - 1) / QLM_BLOCK;
@@ -288,6 +310,39 @@ int qlm_weight_export_int8(const qlm_w8* w, int8_t* q, float* scales) {
     return QLM_OK;
 }
 
+int qlm_weight_export_int4(const qlm_w8* w, uint8_t* packed, float* scales) {
+    if (!w || !packed || !scales) return set_err(QLM_ERR_INVALID_ARG, "NULL argument");
+    if (w->bits != 4) return set_err(QLM_ERR_INVALID_ARG, "the handle holds int8 weights (qlm_weight_export_int8)");
+    DeviceGuard g(w->device);
+    if (!g.ok) return set_err(QLM_ERR_CUDA, "cudaSetDevice(%d) failed", w->device);
+    const int nb = (w->k + QLM_BLOCK - 1) / QLM_BLOCK;
+    const size_t dev_row = (size_t)w->k_pad / 2, ref_row = (size_t)(w->k + 1) / 2;
+    std::vector<uint8_t> hq;
+    std::vector<float> hs;
+    try {
+        hq.resize((size_t)w->rows * dev_row);
+        hs.resize((size_t)w->rows * w->nb_pad);
+    } catch (...) {
+        return set_err(QLM_ERR_OUT_OF_MEMORY, "host staging allocation failed");
+    }
+    QLM_CUDA(cudaMemcpy(hq.data(), w->q, hq.size(), cudaMemcpyDeviceToHost), "export q");
+    QLM_CUDA(cudaMemcpy(hs.data(), w->s, hs.size() * sizeof(float), cudaMemcpyDeviceToHost), "export scales");
+    for (int r = 0; r < w->rows; ++r) {
+        const uint8_t* src = hq.data() + (size_t)r * dev_row;
+        uint8_t* dst = packed + (size_t)r * ref_row;
+        std::memset(dst, 0x88, ref_row);  // a missing odd partner is nibble 8 (value 0), as the reference writes
+        for (int kk = 0; kk < w->k; ++kk) {
+            const uint8_t nib = (uint8_t)((src[qlm::packed_offset_q4(kk)] >> qlm::packed_shift_q4(kk)) & 0xF);
+            uint8_t& b = dst[kk / 2];
+            b = (kk & 1) ? (uint8_t)((b & 0x0F) | (nib << 4)) : (uint8_t)((b & 0xF0) | nib);
+        }
+        std::memcpy(scales + (size_t)r * nb, hs.data() + (size_t)r * w->nb_pad, nb * sizeof(float));
+    }
+    return QLM_OK;
+}
+
+int qlm_weight_bits(const qlm_w8* w) { return w ? w->bits : -1; }
+
 int qlm_weight_shape(const qlm_w8* w, int* rows, int* k, int* row_begin, int* row_end, int* n_total) {
     if (!w) return set_err(QLM_ERR_INVALID_ARG, "NULL handle");
     if (rows) *rows = w->rows;
@@ -300,7 +355,7 @@ int qlm_weight_shape(const qlm_w8* w, int* rows, int* k, int* row_begin, int* ro
 
 int64_t qlm_weight_bytes(const qlm_w8* w) {
     if (!w) return 0;
-    return (int64_t)w->rows * w->k_pad + (int64_t)w->rows * w->nb_pad * (int64_t)sizeof(float);
+    return (int64_t)w->rows * w->k_pad * w->bits / 8 + (int64_t)w->rows * w->nb_pad * (int64_t)sizeof(float);
 }
 
 void qlm_weight_free(qlm_w8* w) {
@@ -323,6 +378,8 @@ int qlm_linear_int8(const float* x, int M, int k, int64_t ldx, const qlm_w8* w, 
     if (flags & ~(QLM_LINEAR_TENSOR | QLM_LINEAR_HOST_IO | QLM_LINEAR_SYNC))
         return set_err(QLM_ERR_INVALID_ARG, "unknown flags 0x%x", flags);
     const bool tensor = (flags & QLM_LINEAR_TENSOR) != 0;
+    const bool q4 = w->bits == 4;
+    if (tensor && q4) return set_err(QLM_ERR_UNSUPPORTED, "the tensor-core path serves int8 weights; this handle is int4");
     DeviceState* st;
     int rc = device_state(w->device, &st);
     if (rc) return rc;
@@ -333,8 +390,8 @@ int qlm_linear_int8(const float* x, int M, int k, int64_t ldx, const qlm_w8* w, 
     // Exact path: rows of x per launch (all activations of a launch live in
     // shared memory next to the weight slots).
     int mm = 8;
-    while (mm > 1 && !qlm::gemv_supported(mm, w->rows, k, st->sm_count)) --mm;
-    if (!tensor && !qlm::gemv_supported(mm, w->rows, k, st->sm_count))
+    while (mm > 1 && !qlm::gemv_supported(mm, w->rows, k, st->sm_count, q4)) --mm;
+    if (!tensor && !qlm::gemv_supported(mm, w->rows, k, st->sm_count, q4))
         return set_err(QLM_ERR_UNSUPPORTED, "k=%d exceeds the exact path's shared-memory staging limit", k);
     if (tensor) {
         std::lock_guard<std::mutex> lk(g_dev_mu);
@@ -377,7 +434,7 @@ int qlm_linear_int8(const float* x, int M, int k, int64_t ldx, const qlm_w8* w, 
             const int g_rows = (M - m0) < mm ? (M - m0) : mm;
             QLM_CUDA(qlm::launch_gemv_exact(dx + (int64_t)m0 * dldx, dldx, g_rows, w->q, w->s, w->rows, k,
                                             dy + (int64_t)m0 * dldy, dldy, st->status, st->sm_count, s,
-                                            pdl_enabled()),
+                                            pdl_enabled(), nullptr, q4),
                      "gemv launch");
         }
     }
@@ -407,6 +464,7 @@ int qlm_linear_int8_grouped(const float* x, int M, int k, int64_t ldx, const qlm
         if (!w || !ys[g]) return set_err(QLM_ERR_INVALID_ARG, "NULL weight or output %d", g);
         if (w->k != k) return set_err(QLM_ERR_INVALID_ARG, "weight %d has k=%d, expected %d", g, w->k, k);
         if (w->device != ws[0]->device) return set_err(QLM_ERR_INVALID_ARG, "weights on different devices");
+        if (w->bits != ws[0]->bits) return set_err(QLM_ERR_INVALID_ARG, "int8 and int4 weights in one group");
         if (ldys[g] < w->rows) return set_err(QLM_ERR_INVALID_ARG, "ldy %lld < rows %d (weight %d)", (long long)ldys[g], w->rows, g);
         gw[g] = qlm::GemvWeight{w->q, w->s, w->rows, ys[g], ldys[g]};
         rows_total += w->rows;
@@ -418,8 +476,9 @@ int qlm_linear_int8_grouped(const float* x, int M, int k, int64_t ldx, const qlm
     if (!g.ok) return set_err(QLM_ERR_CUDA, "cudaSetDevice(%d) failed", ws[0]->device);
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     int mm = 8;
-    while (mm > 1 && !qlm::gemv_supported(mm, rows_total, k, st->sm_count)) --mm;
-    if (!qlm::gemv_supported(mm, rows_total, k, st->sm_count))
+    const bool q4 = ws[0]->bits == 4;
+    while (mm > 1 && !qlm::gemv_supported(mm, rows_total, k, st->sm_count, q4)) --mm;
+    if (!qlm::gemv_supported(mm, rows_total, k, st->sm_count, q4))
         return set_err(QLM_ERR_UNSUPPORTED, "k=%d exceeds the exact path's shared-memory staging limit", k);
     for (int m0 = 0; m0 < M; m0 += mm) {
         const int rows_m = (M - m0) < mm ? (M - m0) : mm;
@@ -429,7 +488,7 @@ int qlm_linear_int8_grouped(const float* x, int M, int k, int64_t ldx, const qlm
             gm[i].y = gw[i].y + (int64_t)m0 * gw[i].ldy;
         }
         QLM_CUDA(qlm::launch_gemv_grouped(x + (int64_t)m0 * ldx, ldx, rows_m, gm, nw, k, st->status, st->sm_count, s,
-                                          pdl_enabled()),
+                                          pdl_enabled(), nullptr, q4),
                  "grouped gemv launch");
     }
     if (flags & QLM_LINEAR_SYNC) {

@@ -28,6 +28,16 @@ __host__ __device__ inline int packed_offset(int k) {
     return (k & ~(kChunk - 1)) + (k & 7) * 16 + ((k >> 5) & 3) * 4 + ((k >> 3) & 3);
 }
 
+// int4 packing ("P128/4"): k_pad / 2 bytes per row; inside one 128-element
+// chunk (64 bytes) the 8 bytes at l*8 are lane l's: bytes 0..3 hold steps
+// j = 0..3 of blocks 0 (low nibble) and 1 (high nibble), bytes 4..7 those of
+// blocks 2 and 3. A nibble is value + 8 (QuickLM's Q4_0 bias). Byte offset of
+// element k within a packed row, and the shift of its nibble in that byte:
+__host__ __device__ inline int packed_offset_q4(int k) {
+    return ((k & ~(kChunk - 1)) >> 1) + (k & 7) * 8 + (((k >> 5) & 3) >> 1) * 4 + ((k >> 3) & 3);
+}
+__host__ __device__ inline int packed_shift_q4(int k) { return ((k >> 5) & 1) * 4; }
+
 // Position of x[k] in the permuted activation staging used by the GEMV:
 // chunk c, block bb, lane l, j -> c*128 + bb*32 + l*4 + j, so lane l reads
 // the four x values of block bb as one float4 (conflict-free across lanes).

@@ -50,7 +50,10 @@ namespace {
 
 constexpr long long kWaitBudget = 4000000000LL;  // ~2 s of SM clock
 constexpr int kMaxSegChunks = 8;                 // chunks per slot (1024 K elements)
-constexpr int kRowChunkBytes = kChunk + 16;  // one row x one chunk: 128 int8 + 4 fp32 scales
+// One row x one chunk in a slot: the weights (128 int8 or 64 bytes of int4)
+// plus its 4 fp32 scales.
+template <bool Q4>
+__host__ __device__ constexpr int row_chunk_bytes() { return (Q4 ? 64 : 128) + 16; }
 constexpr int kStatusTimeout = 0x201;
 constexpr int kStatusGatherTimeout = 0x202;
 
@@ -115,18 +118,33 @@ __device__ __forceinline__ int xperm(int k) {
 // order. nz = (-0, -0) from the kernel parameters. With FULL = false only
 // the first nblocks blocks enter the chain (the last chunk of a row with
 // K % 128 != 0).
-template <int MM, int R, bool FULL>
+template <int MM, int R, bool FULL, bool Q4>
 __device__ __forceinline__ void chunk_update(const float* __restrict__ xs_chunk, int k_pad, int lane,
                                              const uint8_t* sq, int qstride, const uint8_t* ss, int sstride,
                                              unsigned long long nz, float (&t)[MM][R], int nblocks) {
-    uint4 qv[R];
+    // w4[i][bb]: byte j = the (biased) value of block bb, step j, this lane.
+    uint32_t w4[R][4];
     float4 sv[R];
 #pragma unroll
     for (int i = 0; i < R; ++i) {
-        qv[i] = *reinterpret_cast<const uint4*>(sq + i * qstride);
+        if (Q4) {
+            const uint2 a = *reinterpret_cast<const uint2*>(sq + i * qstride);
+            w4[i][0] = a.x & 0x0F0F0F0Fu;
+            w4[i][1] = (a.x >> 4) & 0x0F0F0F0Fu;
+            w4[i][2] = a.y & 0x0F0F0F0Fu;
+            w4[i][3] = (a.y >> 4) & 0x0F0F0F0Fu;
+        } else {
+            const uint4 a = *reinterpret_cast<const uint4*>(sq + i * qstride);
+            w4[i][0] = a.x ^ 0x80808080u;
+            w4[i][1] = a.y ^ 0x80808080u;
+            w4[i][2] = a.z ^ 0x80808080u;
+            w4[i][3] = a.w ^ 0x80808080u;
+        }
         sv[i] = *reinterpret_cast<const float4*>(ss + i * sstride);
     }
-    const unsigned long long bias = 0x4B0000804B000080ull;  // (2^23 + 128) x 2
+    // (2^23 + bias) x 2: the byte sits in the mantissa of 2^23; int8 bytes
+    // are biased by 128 above, int4 nibbles carry QuickLM's +8.
+    const unsigned long long bias = Q4 ? 0x4B0000084B000008ull : 0x4B0000804B000080ull;
 #pragma unroll
     for (int m = 0; m < MM; ++m) {
         const float* xm = xs_chunk + (size_t)m * k_pad + lane * 4;
@@ -135,8 +153,7 @@ __device__ __forceinline__ void chunk_update(const float* __restrict__ xs_chunk,
         for (int j = 0; j < 4; ++j) xv[j] = *reinterpret_cast<const float4*>(xm + j * 32);
 #pragma unroll
         for (int i = 0; i < R; ++i) {
-            const uint32_t w[4] = {qv[i].x ^ 0x80808080u, qv[i].y ^ 0x80808080u, qv[i].z ^ 0x80808080u,
-                                   qv[i].w ^ 0x80808080u};
+            const uint32_t* w = w4[i];
             float tt = t[m][i];
 #pragma unroll
             for (int h = 0; h < 2; ++h) {
@@ -170,9 +187,11 @@ __device__ __forceinline__ void chunk_update(const float* __restrict__ xs_chunk,
 // served per quarter-warp, so rows of one warp cannot share a load). M = 1:
 // up to 12 warps and 80 registers, so two CTAs fit on an SM and the next
 // kernel's CTA can start its weight copies while this one finishes.
-template <int MM, int R, bool GATHER>
+template <int MM, int R, bool GATHER, bool Q4>
 __global__ void __launch_bounds__(MM == 1 ? 384 : 512, MM == 1 ? 2 : 1)
     gemv_kernel(const __grid_constant__ GemvParams p) {
+    constexpr int CB = Q4 ? 64 : 128;  // weight bytes per row per 128-element chunk
+    constexpr int kRowChunkBytes = row_chunk_bytes<Q4>();
     extern __shared__ __align__(128) uint8_t smem[];
     using namespace sm100;
     const int warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5, lane32 = threadIdx.x & 31;
@@ -209,10 +228,10 @@ __global__ void __launch_bounds__(MM == 1 ? 384 : 512, MM == 1 ? 2 : 1)
         if (lane32 == 0) mbar_arrive_expect_tx(bar, (uint32_t)(valid * n * kRowChunkBytes));
         const int r = lane32 & 15, row = kUnitRows * lu + r;
         if (lane32 < 16 && r < valid)
-            bulk_copy_g2s(dst + r * p.sc * kChunk, W.q + (int64_t)row * p.k_pad + (int64_t)c0 * kChunk,
-                          (uint32_t)(n * kChunk), bar);
+            bulk_copy_g2s(dst + r * p.sc * CB, W.q + (int64_t)row * (p.k_pad / kChunk) * CB + (int64_t)c0 * CB,
+                          (uint32_t)(n * CB), bar);
         else if (lane32 >= 16 && r < valid)
-            bulk_copy_g2s(dst + kUnitRows * p.sc * kChunk + r * p.sc * 16, W.s + (int64_t)row * p.nb_pad + c0 * 4,
+            bulk_copy_g2s(dst + kUnitRows * p.sc * CB + r * p.sc * 16, W.s + (int64_t)row * p.nb_pad + c0 * 4,
                           (uint32_t)(n * 16), bar);
     };
 
@@ -290,20 +309,20 @@ __global__ void __launch_bounds__(MM == 1 ? 384 : 512, MM == 1 ? 2 : 1)
             stop = i;
             break;
         }
-        const uint8_t* sq = my_slots + (size_t)slot * slot_bytes + rsub * p.sc * kChunk + lane * 16;
-        const uint8_t* ss = my_slots + (size_t)slot * slot_bytes + kUnitRows * p.sc * kChunk + rsub * p.sc * 16;
-        const int qstride = p.sc * kChunk, sstride = p.sc * 16;
+        const uint8_t* sq = my_slots + (size_t)slot * slot_bytes + rsub * p.sc * CB + lane * (CB / 8);
+        const uint8_t* ss = my_slots + (size_t)slot * slot_bytes + kUnitRows * p.sc * CB + rsub * p.sc * 16;
+        const int qstride = p.sc * CB, sstride = p.sc * 16;
         const int c0 = g * p.sc;
         const int c1 = min(c0 + p.sc, nchunks);
         const int cf = min(c1, cfull);  // chunks made of four full blocks
         const float* xc = xs + c0 * kChunk;
 #pragma unroll 1
         for (int c = 0; c < cf - c0; ++c) {
-            chunk_update<MM, R, true>(xc + c * kChunk, p.k_pad, lane, sq + c * kChunk, qstride, ss + c * 16, sstride,
+            chunk_update<MM, R, true, Q4>(xc + c * kChunk, p.k_pad, lane, sq + c * CB, qstride, ss + c * 16, sstride,
                                       nz, t, 4);
         }
         if (cf < c1) {  // the chunk holding the last (1..3) full blocks
-            chunk_update<MM, R, false>(xs + cf * kChunk, p.k_pad, lane, sq + (cf - c0) * kChunk, qstride,
+            chunk_update<MM, R, false, Q4>(xs + cf * kChunk, p.k_pad, lane, sq + (cf - c0) * CB, qstride,
                                        ss + (cf - c0) * 16, sstride, nz, t, rem_blocks);
         }
         __syncwarp();
@@ -335,13 +354,15 @@ __global__ void __launch_bounds__(MM == 1 ? 384 : 512, MM == 1 ? 2 : 1)
                     if (row >= W.rows) break;
                     if (p.k > nbf * kBlock) {
                         // Ragged tail: sequential scalar sum times the last block's scale.
-                        const uint8_t* qr = W.q + (int64_t)row * p.k_pad;
+                        const uint8_t* qr = W.q + (int64_t)row * (p.k_pad / kChunk) * CB;
                         const float st = W.s[(int64_t)row * p.nb_pad + nbf];
 #pragma unroll
                         for (int m = 0; m < MM; ++m) {
                             float acc = 0.0f;
                             for (int kk = nbf * kBlock; kk < p.k; ++kk) {
-                                const float qf = (float)(int8_t)qr[packed_offset(kk)];
+                                const float qf =
+                                    Q4 ? (float)((int)((qr[packed_offset_q4(kk)] >> packed_shift_q4(kk)) & 0xF) - 8)
+                                       : (float)(int8_t)qr[packed_offset(kk)];
                                 acc = __fadd_rn(acc, __fmul_rn(xs[m * p.k_pad + xperm(kk)], qf));
                             }
                             t[m][i] = __fadd_rn(t[m][i], __fmul_rn(acc, st));
@@ -420,7 +441,7 @@ int pick_rows_per_thread(int mm, int rows, int sm_count) {
 
 // rows: the rows the launch covers (for several weights, the sum of their
 // rows each rounded up to whole units of the forced R).
-bool make_plan(int mm, int rows, int k, int sm_count, Plan* pl, int force_r = 0) {
+bool make_plan(int mm, int rows, int k, int sm_count, Plan* pl, int force_r = 0, bool q4 = false) {
     const int k_pad = packed_k(k);
     const int nck = k_pad / kChunk;
     const int max_warps = mm == 1 ? 12 : 16;
@@ -433,7 +454,7 @@ bool make_plan(int mm, int rows, int k, int sm_count, Plan* pl, int force_r = 0)
     sc = sc < 2 ? 2 : sc > kMaxSegChunks ? kMaxSegChunks : sc;
     pl->sc = sc < nck ? sc : nck;
     pl->nseg = (nck + pl->sc - 1) / pl->sc;
-    const int slot_bytes = pl->sc * unit_rows * kRowChunkBytes;
+    const int slot_bytes = pl->sc * unit_rows * (q4 ? row_chunk_bytes<true>() : row_chunk_bytes<false>());
     pl->xs_bytes = round_up(mm * k_pad * 4, 128);
     const int units = (rows + unit_rows - 1) / unit_rows;
     pl->ctas = units < sm_count ? units : sm_count;
@@ -459,7 +480,7 @@ bool make_plan(int mm, int rows, int k, int sm_count, Plan* pl, int force_r = 0)
     return true;
 }
 
-template <int MM, int R>
+template <int MM, int R, bool Q4>
 cudaError_t launch_mm(const GemvParams& p0, const Plan& pl, cudaStream_t stream, bool pdl) {
     static bool attr_set[2][64] = {};
     int dev = 0;
@@ -467,7 +488,7 @@ cudaError_t launch_mm(const GemvParams& p0, const Plan& pl, cudaStream_t stream,
     if (e != cudaSuccess) return e;
     if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
     const bool gather = p0.ga.nranks > 0;
-    auto kern = MM == 1 && gather ? gemv_kernel<1, R, true> : gemv_kernel<MM, R, false>;
+    auto kern = MM == 1 && gather ? gemv_kernel<1, R, true, Q4> : gemv_kernel<MM, R, false, Q4>;
     const int gi = gather ? 1 : 0;
     if (!attr_set[gi][dev]) {
         e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 224 * 1024);
@@ -502,13 +523,33 @@ cudaError_t launch_mm(const GemvParams& p0, const Plan& pl, cudaStream_t stream,
 
 }  // namespace
 
-bool gemv_supported(int mm, int rows, int k, int sm_count) {
+bool gemv_supported(int mm, int rows, int k, int sm_count, bool q4) {
     Plan pl;
-    return make_plan(mm, rows, k, sm_count, &pl);
+    return make_plan(mm, rows, k, sm_count, &pl, 0, q4);
 }
 
+namespace {
+
+template <bool Q4>
+cudaError_t launch_mm_any(int mm, const GemvParams& p, const Plan& pl, cudaStream_t stream, bool pdl) {
+    switch (mm) {
+        case 1: return pl.r == 2 ? launch_mm<1, 2, Q4>(p, pl, stream, pdl) : launch_mm<1, 1, Q4>(p, pl, stream, pdl);
+        case 2: return launch_mm<2, 1, Q4>(p, pl, stream, pdl);
+        case 3: return launch_mm<3, 1, Q4>(p, pl, stream, pdl);
+        case 4: return launch_mm<4, 1, Q4>(p, pl, stream, pdl);
+        case 5: return launch_mm<5, 1, Q4>(p, pl, stream, pdl);
+        case 6: return launch_mm<6, 1, Q4>(p, pl, stream, pdl);
+        case 7: return launch_mm<7, 1, Q4>(p, pl, stream, pdl);
+        case 8: return launch_mm<8, 1, Q4>(p, pl, stream, pdl);
+        default: return cudaErrorInvalidValue;
+    }
+}
+
+}  // namespace
+
 cudaError_t launch_gemv_grouped(const float* x, int64_t ldx, int mm, const GemvWeight* ws, int nw, int k,
-                                int* status, int sm_count, cudaStream_t stream, bool pdl, const GatherArgs* gather) {
+                                int* status, int sm_count, cudaStream_t stream, bool pdl, const GatherArgs* gather,
+                                bool q4) {
     if (nw < 1 || nw > kMaxGroup || (gather && (mm != 1 || nw != 1))) return cudaErrorInvalidValue;
     int rows_total = 0;
     for (int g = 0; g < nw; ++g) {
@@ -519,7 +560,7 @@ cudaError_t launch_gemv_grouped(const float* x, int64_t ldx, int mm, const GemvW
     int rows_eff = 0;  // whole units per weight
     for (int g = 0; g < nw; ++g) rows_eff += round_up(ws[g].rows, 4 * r);
     Plan pl;
-    if (!make_plan(mm, rows_eff, k, sm_count, &pl, r)) return cudaErrorInvalidValue;
+    if (!make_plan(mm, rows_eff, k, sm_count, &pl, r, q4)) return cudaErrorInvalidValue;
     GemvParams p{};
     if (gather) p.ga = *gather;
     p.x = x;
@@ -537,24 +578,14 @@ cudaError_t launch_gemv_grouped(const float* x, int64_t ldx, int mm, const GemvW
     p.k = k;
     p.k_pad = packed_k(k);
     p.nb_pad = p.k_pad / kBlock;
-    switch (mm) {
-        case 1: return pl.r == 2 ? launch_mm<1, 2>(p, pl, stream, pdl) : launch_mm<1, 1>(p, pl, stream, pdl);
-        case 2: return launch_mm<2, 1>(p, pl, stream, pdl);
-        case 3: return launch_mm<3, 1>(p, pl, stream, pdl);
-        case 4: return launch_mm<4, 1>(p, pl, stream, pdl);
-        case 5: return launch_mm<5, 1>(p, pl, stream, pdl);
-        case 6: return launch_mm<6, 1>(p, pl, stream, pdl);
-        case 7: return launch_mm<7, 1>(p, pl, stream, pdl);
-        case 8: return launch_mm<8, 1>(p, pl, stream, pdl);
-        default: return cudaErrorInvalidValue;
-    }
+    return q4 ? launch_mm_any<true>(mm, p, pl, stream, pdl) : launch_mm_any<false>(mm, p, pl, stream, pdl);
 }
 
 cudaError_t launch_gemv_exact(const float* x, int64_t ldx, int mm, const uint8_t* q, const float* s, int rows,
                               int k, float* y, int64_t ldy, int* status, int sm_count, cudaStream_t stream, bool pdl,
-                              const GatherArgs* gather) {
+                              const GatherArgs* gather, bool q4) {
     const GemvWeight w{q, s, rows, y, ldy};
-    return launch_gemv_grouped(x, ldx, mm, &w, 1, k, status, sm_count, stream, pdl, gather);
+    return launch_gemv_grouped(x, ldx, mm, &w, 1, k, status, sm_count, stream, pdl, gather, q4);
 }
 
 }  // namespace qlm

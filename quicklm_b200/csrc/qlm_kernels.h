@@ -14,6 +14,11 @@ namespace qlm {
 cudaError_t launch_quantize_pack(const void* src, int dtype, int64_t src_stride, int rows, int k, uint8_t* q,
                                  float* scales, cudaStream_t stream);
 
+// The int4 (Q4_0-style) counterpart: scale = max|v| / 8, values in [-8, 7],
+// q [rows][packed_k(k) / 2] in the P128/4 layout (qlm_device.cuh).
+cudaError_t launch_quantize_pack_q4(const void* src, int dtype, int64_t src_stride, int rows, int k, uint8_t* q,
+                                    float* scales, cudaStream_t stream);
+
 constexpr int kMaxRanks = 8;
 
 // Peer pointers for the fused GEMV + all-gather (M = 1). peer_slots[r] is
@@ -56,7 +61,7 @@ cudaError_t launch_argmax(const float* y, int n, int col0, const ArgmaxArgs& a, 
 // instead of y.
 cudaError_t launch_gemv_exact(const float* x, int64_t ldx, int mm, const uint8_t* q, const float* s, int rows,
                               int k, float* y, int64_t ldy, int* status, int sm_count, cudaStream_t stream, bool pdl,
-                              const GatherArgs* gather = nullptr);
+                              const GatherArgs* gather = nullptr, bool q4 = false);
 
 // One weight of a grouped exact launch (packed q, scales, rows, output).
 constexpr int kMaxGroup = 8;
@@ -73,10 +78,10 @@ struct GemvWeight {
 // launch). Gather requires nw == 1 and mm == 1.
 cudaError_t launch_gemv_grouped(const float* x, int64_t ldx, int mm, const GemvWeight* ws, int nw, int k,
                                 int* status, int sm_count, cudaStream_t stream, bool pdl,
-                                const GatherArgs* gather = nullptr);
+                                const GatherArgs* gather = nullptr, bool q4 = false);
 
 // Whether the exact GEMV can stage mm activation rows of length k.
-bool gemv_supported(int mm, int rows, int k, int sm_count);
+bool gemv_supported(int mm, int rows, int k, int sm_count, bool q4 = false);
 
 // ---- tensor-core prefill GEMM (qlm_gemm_tc.cu) ----
 struct TcMaps {

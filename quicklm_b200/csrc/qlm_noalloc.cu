@@ -86,6 +86,10 @@ extern "C" int qlm_linear_int8_tc_noalloc(const float* x, int M, int k, int64_t 
                       (long long)ldx, (long long)ldy, w->rows);
             break;
         }
+        if (w->bits != 8) {
+            rc = fail(QLM_ERR_UNSUPPORTED, "the tensor-core path serves int8 weights; this handle is int4");
+            break;
+        }
         if (flags & ~QLM_LINEAR_SYNC) {
             rc = fail(QLM_ERR_INVALID_ARG, "only QLM_LINEAR_SYNC is accepted here (device pointers only)");
             break;

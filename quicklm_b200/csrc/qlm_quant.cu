@@ -14,6 +14,12 @@
 // second operand when unordered; cvtps2dq returns 0x80000000; (int)lround of
 // NaN/Inf is 0), so the bytes and scales are identical for every input.
 //
+// The int4 variant (Q4 = true) replaces st_quantize_row_f32_int4 /
+// st_quantize_row_bf16_int4 (src/io/safetensors.cpp:393-515, driven by
+// get_tensor_keep_int4): the same block loop with scale = max_abs / 8 and
+// values clamped to [-8, 7], stored as value + 8 in the P128/4 nibble layout
+// (qlm_device.cuh); padding nibbles are 8 (value 0).
+//
 // Work mapping: one warp per (row, 32 consecutive blocks). The warp stages the
 // 1024 source values through shared memory with coalesced loads, each lane
 // quantizes one block, and the packed bytes go back out through shared memory
@@ -58,6 +64,7 @@ __device__ __forceinline__ float load_src(const void* src, int dtype, int64_t id
     return static_cast<const float*>(src)[idx];
 }
 
+template <bool Q4>
 __global__ void __launch_bounds__(kWarpsPerCta * 32)
 quantize_pack_kernel(const void* __restrict__ src, int dtype, int64_t src_stride, int rows, int k,
                      int k_pad, uint8_t* __restrict__ q, float* __restrict__ scales) {
@@ -100,7 +107,7 @@ quantize_pack_kernel(const void* __restrict__ src, int dtype, int64_t src_stride
         m1 = maxps(m1, m3);
         float max_abs = maxps(m0, m1);
         for (; i < len; ++i) max_abs = stdmax(max_abs, fabsf(v[i]));
-        scale = (max_abs > 0.0f) ? __fdiv_rn(max_abs, 127.0f) : 1.0f;
+        scale = (max_abs > 0.0f) ? __fdiv_rn(max_abs, Q4 ? 8.0f : 127.0f) : 1.0f;
         const float inv = __fdiv_rn(1.0f, scale);
         const int vec_end = len & ~7;  // elements handled by 8-wide steps
 #pragma unroll
@@ -109,10 +116,11 @@ quantize_pack_kernel(const void* __restrict__ src, int dtype, int64_t src_stride
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
                 const int e = 8 * j + l;
-                uint32_t b = 0;
+                uint32_t b = Q4 ? 8u : 0u;  // value 0
                 if (e < len) {
                     const float p = __fmul_rn(v[e], inv);
-                    b = clamp127_byte(e < vec_end ? cvt_rne_indefinite(p) : cvt_lround_int(p));
+                    const int32_t qi = e < vec_end ? cvt_rne_indefinite(p) : cvt_lround_int(p);
+                    b = Q4 ? (uint32_t)((qi < -8 ? -8 : (qi > 7 ? 7 : qi)) + 8) : clamp127_byte(qi);
                 }
                 w |= b << (8 * j);
             }
@@ -120,21 +128,33 @@ quantize_pack_kernel(const void* __restrict__ src, int dtype, int64_t src_stride
         }
     } else {
 #pragma unroll
-        for (int l = 0; l < 8; ++l) words[l] = 0u;
+        for (int l = 0; l < 8; ++l) words[l] = Q4 ? 0x08080808u : 0u;
     }
     if (blk < nb_pad) scales[(int64_t)row * nb_pad + blk] = scale;
 
-    // Packed position inside this segment's 1 KB: chunk (lane/4), lane l, block lane%4.
     uint32_t* pw = reinterpret_cast<uint32_t*>(packed[warp]);
+    if (Q4) {
+        // Segment = 8 chunks x 64 bytes. Blocks 2p (low nibbles) and 2p + 1
+        // (high nibbles) of a chunk share lane slice word p.
 #pragma unroll
-    for (int l = 0; l < 8; ++l) pw[(lane >> 2) * 32 + l * 4 + (lane & 3)] = words[l];
+        for (int l = 0; l < 8; ++l) {
+            const uint32_t partner = __shfl_xor_sync(0xffffffffu, words[l], 1);
+            if ((lane & 1) == 0) pw[(lane >> 2) * 16 + l * 2 + ((lane & 3) >> 1)] = words[l] | (partner << 4);
+        }
+    } else {
+        // Packed position inside this segment's 1 KB: chunk (lane/4), lane l, block lane%4.
+#pragma unroll
+        for (int l = 0; l < 8; ++l) pw[(lane >> 2) * 32 + l * 4 + (lane & 3)] = words[l];
+    }
     __syncwarp();
 
-    // 1 KB = 64 uint4; the segment may stop short of 8 chunks at the row end.
+    // 8 chunks of 128 (int8) or 64 (int4) bytes; the segment may stop short
+    // of 8 chunks at the row end.
+    constexpr int CB = Q4 ? 64 : 128;
     const int chunks = min(8, nb_pad / 4 - seg * 8);
-    uint4* dst = reinterpret_cast<uint4*>(q + (int64_t)row * k_pad + (int64_t)seg * 1024);
+    uint4* dst = reinterpret_cast<uint4*>(q + (int64_t)row * (k_pad / kChunk) * CB + (int64_t)seg * 8 * CB);
     const uint4* s4 = reinterpret_cast<const uint4*>(packed[warp]);
-    for (int i = lane; i < chunks * 8; i += 32) dst[i] = s4[i];
+    for (int i = lane; i < chunks * (CB / 16); i += 32) dst[i] = s4[i];
 }
 
 }  // namespace
@@ -147,8 +167,21 @@ cudaError_t launch_quantize_pack(const void* src, int dtype, int64_t src_stride,
     const int64_t warps = (int64_t)rows * nseg;
     const int64_t ctas = (warps + kWarpsPerCta - 1) / kWarpsPerCta;
     if (ctas > 0x7fffffffLL) return cudaErrorInvalidValue;
-    quantize_pack_kernel<<<(unsigned)ctas, kWarpsPerCta * 32, 0, stream>>>(src, dtype, src_stride, rows, k, k_pad,
-                                                                            q, scales);
+    quantize_pack_kernel<false><<<(unsigned)ctas, kWarpsPerCta * 32, 0, stream>>>(src, dtype, src_stride, rows, k,
+                                                                                   k_pad, q, scales);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_quantize_pack_q4(const void* src, int dtype, int64_t src_stride, int rows, int k, uint8_t* q,
+                                    float* scales, cudaStream_t stream) {
+    if (rows <= 0) return cudaSuccess;
+    const int k_pad = packed_k(k);
+    const int nseg = (k_pad / kBlock + 31) / 32;
+    const int64_t warps = (int64_t)rows * nseg;
+    const int64_t ctas = (warps + kWarpsPerCta - 1) / kWarpsPerCta;
+    if (ctas > 0x7fffffffLL) return cudaErrorInvalidValue;
+    quantize_pack_kernel<true><<<(unsigned)ctas, kWarpsPerCta * 32, 0, stream>>>(src, dtype, src_stride, rows, k,
+                                                                                  k_pad, q, scales);
     return cudaGetLastError();
 }
 

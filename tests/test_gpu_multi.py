@@ -96,6 +96,14 @@ def _worker(rank, world, port, result_dir):
                 if not torch.equal(y.view(torch.int32), y_ref.view(torch.int32)):
                     msg = f"odd width, call {i}: gathered output differs"
                     break
+            # the same exchange serves int4 shards
+            shard4 = q.Int8Weight.quantize(wod, device=rank, row_begin=b2, row_end=e2, bits=4)
+            full4 = q.Int8Weight.quantize(wod, device=rank, bits=4)
+            y4_ref = q.matmul(xod, full4, flags=q.SYNC)
+            for i in range(2):
+                y4 = q.matmul_allgather(xod, shard4, comm2, flags=q.SYNC)
+                if msg == "ok" and not torch.equal(y4.view(torch.int32), y4_ref.view(torch.int32)):
+                    msg = f"int4, call {i}: gathered output differs"
             # greedy choice over a row-sharded lm_head: each rank reduces its own
             # logits, one word per rank crosses NVLink (QuickLM's sample(), model.cpp:259-272)
             from oracle.oracle import greedy_argmax

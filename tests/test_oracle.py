@@ -126,3 +126,41 @@ def test_greedy_argmax_matches_reference(refcpu):
     from oracle.oracle import greedy_argmax
     for v in greedy_cases():
         assert greedy_argmax(v) == refcpu.greedy_sample(v), v
+
+
+def test_q4_quantizer_matches_reference(coracle, refcpu):
+    """int4 (Q4_0-style) quantizer restatement == get_tensor_keep_int4
+    (io/safetensors.cpp:393-515), bytes and scales, on fuzzed F32/BF16 rows
+    with specials and odd K."""
+    from oracle.oracle import pack_q4, unpack_q4
+    rng = np.random.default_rng(4)
+    for t in range(150):
+        n, k = int(rng.integers(1, 12)), int(rng.integers(1, 260))
+        w = (rng.standard_normal((n, k)) * (10.0 ** rng.integers(-6, 6))).astype(np.float32)
+        if t % 5 == 1:
+            idx = rng.integers(0, w.size, size=max(1, w.size // 7))
+            w.ravel()[idx] = rng.choice(np.array([np.nan, np.inf, -np.inf, 0.0, -0.0, 1e-40], np.float32),
+                                        size=idx.size)
+        src = (w.view(np.uint32) >> 16).astype(np.uint16) if t % 4 == 3 else w
+        packed, s_ref = refcpu.quantize_int4(src)
+        q, s = coracle.quantize_q4(src)
+        assert np.array_equal(pack_q4(q), packed), (n, k, t)
+        assert np.array_equal(s.view(np.uint32), s_ref.view(np.uint32)), (n, k, t)
+        assert np.array_equal(unpack_q4(packed, k), q)
+
+
+def test_q4_matmul_is_the_int8_arithmetic(coracle, refcpu):
+    """QuickLM's int4 matmul (ops/math_ops.cpp:581-794) performs the int8
+    path's exact per-element sequence on value = nibble - 8: the reference's
+    int4 output equals its int8 output (and the C restatement's) on the
+    unpacked values, bit for bit, ragged K included."""
+    from oracle.oracle import unpack_q4
+    rng = np.random.default_rng(5)
+    for n, k, m in [(9, 64, 1), (17, 100, 3), (33, 2048, 2), (8, 37, 5), (40, 1000, 8)]:
+        w = (rng.standard_normal((n, k)) * 0.02).astype(np.float32)
+        x = rng.standard_normal((m, k)).astype(np.float32)
+        packed, s = refcpu.quantize_int4(w)
+        y4 = refcpu.matmul_int4(x, packed, s, k)
+        y8, _ = refcpu.matmul(x, unpack_q4(packed, k), s)
+        assert bits_equal(y4, y8)
+        assert bits_equal(y4, coracle.matmul(x, unpack_q4(packed, k), s))

@@ -60,3 +60,15 @@ def test_noalloc_rejects_oversize(qlm_lib, cuda_device):
     rc = qlm_lib.qlm_linear_int8_tc_noalloc(x.data_ptr(), m, k, k, w.handle, y.data_ptr(), 128, 0, None)
     assert rc == 1
     assert b"static scratch" in qlm_lib.qlm_last_error()
+
+
+def test_noalloc_rejects_int4(qlm_lib, cuda_device):
+    import torch
+    import quicklm_b200 as q
+
+    w = q.Int8Weight.quantize(np.zeros((64, 256), np.float32), bits=4)
+    x = torch.zeros((4, 256), device="cuda")
+    y = torch.zeros((4, 64), device="cuda")
+    rc = qlm_lib.qlm_linear_int8_tc_noalloc(x.data_ptr(), 4, 256, 256, w.handle, y.data_ptr(), 64, 0, None)
+    assert rc == 4
+    assert b"int4" in qlm_lib.qlm_last_error()
