@@ -130,11 +130,17 @@ int alloc_weight(int device, int n_total, int k, int row_begin, int row_end, qlm
     cudaError_t e = cudaMalloc(&w->q, (size_t)w->rows * w->k_pad * bits / 8);
     if (e == cudaSuccess) e = cudaMalloc(&w->s, (size_t)w->rows * w->nb_pad * sizeof(float));
     if (e == cudaSuccess) e = cudaMalloc(&w->ew, (size_t)w->rows * sizeof(int));
+    const char* what = "cudaMalloc(weight)";
+    if (e == cudaSuccess) {
+        e = qlm::gemv_make_maps(w->q, w->s, w->rows, k, bits == 4, &w->gmaps);
+        what = "GEMV tensor maps";
+    }
     if (e != cudaSuccess) {
         if (w->q) cudaFree(w->q);
         if (w->s) cudaFree(w->s);
+        if (w->ew) cudaFree(w->ew);
         delete w;
-        return cuda_err(e, "cudaMalloc(weight)");
+        return cuda_err(e, what);
     }
     *out = w;
     return QLM_OK;
@@ -364,6 +370,7 @@ void qlm_weight_free(qlm_w8* w) {
     if (w->q) cudaFree(w->q);
     if (w->s) cudaFree(w->s);
     if (w->ew) cudaFree(w->ew);
+    if (w->gmaps.dev) cudaFree(w->gmaps.dev);
     delete w->maps;
     delete w;
 }
@@ -432,7 +439,7 @@ int qlm_linear_int8(const float* x, int M, int k, int64_t ldx, const qlm_w8* w, 
     } else {
         for (int m0 = 0; m0 < M; m0 += mm) {
             const int g_rows = (M - m0) < mm ? (M - m0) : mm;
-            QLM_CUDA(qlm::launch_gemv_exact(dx + (int64_t)m0 * dldx, dldx, g_rows, w->q, w->s, w->rows, k,
+            QLM_CUDA(qlm::launch_gemv_exact(dx + (int64_t)m0 * dldx, dldx, g_rows, w->q, w->s, w->gmaps, w->rows, k,
                                             dy + (int64_t)m0 * dldy, dldy, st->status, st->sm_count, s,
                                             pdl_enabled(), nullptr, q4),
                      "gemv launch");
@@ -466,7 +473,7 @@ int qlm_linear_int8_grouped(const float* x, int M, int k, int64_t ldx, const qlm
         if (w->device != ws[0]->device) return set_err(QLM_ERR_INVALID_ARG, "weights on different devices");
         if (w->bits != ws[0]->bits) return set_err(QLM_ERR_INVALID_ARG, "int8 and int4 weights in one group");
         if (ldys[g] < w->rows) return set_err(QLM_ERR_INVALID_ARG, "ldy %lld < rows %d (weight %d)", (long long)ldys[g], w->rows, g);
-        gw[g] = qlm::GemvWeight{w->q, w->s, w->rows, ys[g], ldys[g]};
+        gw[g] = qlm::GemvWeight{w->q, w->s, &w->gmaps, w->rows, ys[g], ldys[g]};
         rows_total += w->rows;
     }
     DeviceState* st;

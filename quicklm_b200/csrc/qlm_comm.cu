@@ -168,8 +168,8 @@ int qlm_linear_int8_allgather(const float* x, int M, int k, int64_t ldx, const q
     ga.rank = c->rank;
     ga.col0 = w->row_begin;
     ga.n_total = w->n_total;
-    cudaError_t e = qlm::launch_gemv_exact(x, ldx, 1, w->q, w->s, w->rows, k, y, ldy, c->state + 2, c->sm_count, s,
-                                           true, &ga, w->bits == 4);
+    cudaError_t e = qlm::launch_gemv_exact(x, ldx, 1, w->q, w->s, w->gmaps, w->rows, k, y, ldy, c->state + 2,
+                                           c->sm_count, s, true, &ga, w->bits == 4);
     if (e != cudaSuccess) return cuda_fail(e, "fused GEMV + all-gather launch");
     if (flags & QLM_LINEAR_SYNC) {
         e = cudaStreamSynchronize(s);

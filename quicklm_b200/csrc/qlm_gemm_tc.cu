@@ -553,6 +553,8 @@ int sm_count_of_current_device() {
 
 }  // namespace
 
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() { return encode_fn(); }
+
 cudaError_t tc_make_weight_maps(const uint8_t* q, const float* s, int rows, int k_pad, TcMaps* out) {
     auto enc = encode_fn();
     if (!enc) return cudaErrorNotSupported;

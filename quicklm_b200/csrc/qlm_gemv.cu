@@ -31,9 +31,19 @@
 // compile-time -0.0 addend is folded and contracted the same way.
 //
 // Memory: each warp streams its units' packed rows (and their scales) into
-// private shared-memory slots with 1-D cp.async.bulk copies completing on an
-// mbarrier, one slot per (unit, segment of the row), so the chain starts on a
-// row's first segment while the rest is still in flight. A warp issues its
+// private shared-memory slots, one slot per (unit, segment of the row), so the
+// chain starts on a row's first segment while the rest is still in flight.
+// Kernels that refill slots (more items than slots) fill each slot with two
+// TMA loads (codes, scales) issued by one lane: the packed codes are described
+// as a 2-D tensor of 8-byte elements [rows][row bytes / 8] and the scales as
+// [rows][k_pad / 32], so one box of 4R rows x one segment lands in the
+// [row][chunk][bytes] order the arithmetic reads. Per-row 1-D bulk copies
+// issued by 16 lanes cost about as many instructions as the arithmetic there
+// (the copy takes uniform operands, so a lane-divergent issue is serialised
+// lane by lane): the lm_head 151936 x 2560 runs in 79 us with TMA, 102 us with
+// bulk copies. Kernels whose slots are all issued at the start (a decode-sized
+// matrix) keep the per-row bulk copies, which start sooner than a first TMA
+// load (config 1: 5.6 us vs 5.8 us per launch in a graph). A warp issues its
 // first slots BEFORE the programmatic-dependent-launch wait, so a kernel in a
 // stream or CUDA graph starts pulling weights from HBM while its predecessor
 // is still computing; with one CTA per SM and a balanced contiguous unit range
@@ -54,6 +64,20 @@ constexpr int kMaxSegChunks = 8;                 // chunks per slot (1024 K elem
 // plus its 4 fp32 scales.
 template <bool Q4>
 __host__ __device__ constexpr int row_chunk_bytes() { return (Q4 ? 64 : 128) + 16; }
+// Bytes of one slot (4R rows x sc chunks), padded so that every slot and its
+// scale part start on a 128-byte boundary (TMA destinations).
+template <bool Q4>
+__host__ __device__ constexpr int slot_stride(int sc, int unit_rows) {
+    return (unit_rows * sc * row_chunk_bytes<Q4>() + 127) / 128 * 128;
+}
+// Chunks per segment: about four segments per row, so a row's chain starts on
+// its first quarter while the rest is in flight. The GEMV descriptors are
+// built with the same value.
+int seg_chunks(int nck) {
+    int sc = (nck + 3) / 4;
+    sc = sc < 2 ? 2 : sc > kMaxSegChunks ? kMaxSegChunks : sc;
+    return sc < nck ? sc : nck;
+}
 constexpr int kStatusTimeout = 0x201;
 constexpr int kStatusGatherTimeout = 0x202;
 
@@ -61,6 +85,8 @@ constexpr int kStatusGatherTimeout = 0x202;
 // the activations (q/k/v, gate/up): their units are concatenated, weight g
 // owning units [ubase, ubase + ceil(rows / (4 R))).
 struct GemvGroup {
+    const CUtensorMap* mq;  // codes, box of 4R rows x sc chunks (device copy of GemvMaps::q[R - 1])
+    const CUtensorMap* ms;  // scales, same box
     const uint8_t* q;
     const float* s;
     float* y;
@@ -187,19 +213,23 @@ __device__ __forceinline__ void chunk_update(const float* __restrict__ xs_chunk,
 // served per quarter-warp, so rows of one warp cannot share a load). M = 1:
 // up to 12 warps and 80 registers, so two CTAs fit on an SM and the next
 // kernel's CTA can start its weight copies while this one finishes.
-template <int MM, int R, bool GATHER, bool Q4>
+// TMA: fill slots by TMA (GemvGroup::mq/ms) instead of per-row bulk copies.
+template <int MM, int R, bool GATHER, bool Q4, bool TMA>
 __global__ void __launch_bounds__(MM == 1 ? 384 : 512, MM == 1 ? 2 : 1)
     gemv_kernel(const __grid_constant__ GemvParams p) {
     constexpr int CB = Q4 ? 64 : 128;  // weight bytes per row per 128-element chunk
     constexpr int kRowChunkBytes = row_chunk_bytes<Q4>();
-    extern __shared__ __align__(128) uint8_t smem[];
+    extern __shared__ __align__(128) uint8_t smem_raw[];
+    // TMA destinations need 128-byte alignment: align the base explicitly (the
+    // plan requests 128 spare bytes).
+    uint8_t* smem = smem_raw + ((128u - (sm100::smem_u32(smem_raw) & 127u)) & 127u);
     using namespace sm100;
     const int warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5, lane32 = threadIdx.x & 31;
     const int lane = threadIdx.x & 7;                // reference lane l
     const int rsub = ((threadIdx.x >> 3) & 3) * R;   // first of the thread's R rows within the unit
     constexpr int kUnitRows = 4 * R;
 
-    const int slot_bytes = p.sc * kUnitRows * kRowChunkBytes;
+    const int slot_bytes = slot_stride<Q4>(p.sc, kUnitRows);
     float* xs = reinterpret_cast<float*>(smem);
     uint8_t* my_slots = smem + p.xs_bytes + (size_t)warp * p.d * slot_bytes;
     const uint32_t bars = smem_u32(smem + p.xs_bytes + (size_t)nwarps * p.d * slot_bytes) + warp * p.d * 8;
@@ -213,17 +243,28 @@ __global__ void __launch_bounds__(MM == 1 ? 384 : 512, MM == 1 ? 2 : 1)
     int my_units = 0;
     for (int u = u_begin + warp; u < u_end; u += nwarps) ++my_units;
     const int items = my_units * p.nseg;
-    const int nck = p.k_pad >> 7;
 
-    // Whole warp: lane r < 4R copies row r's int8 slice, lane 16 + r its scales.
+    // Fill `slot` with the unit's codes and scales for segment g; called by
+    // the whole warp. TMA: one lane, two boxes; rows past the weight's end and
+    // chunks past k_pad arrive as zeros (never stored), and the transaction
+    // count is the full box either way. Bulk: lane r < 4R copies row r's
+    // codes, lane 16 + r its scales, valid rows and chunks only.
     auto issue = [&](int uu, int g, int slot) {
         const int u = u_begin + warp + uu * nwarps;
         const GemvGroup& W = p.grp[unit_group(p, u)];
         const int lu = u - W.ubase;  // unit within its weight
-        const int c0 = g * p.sc;
-        const int n = min(p.sc, nck - c0);
         const uint32_t bar = bars + slot * 8;
         const uint32_t dst = smem_u32(my_slots + (size_t)slot * slot_bytes);
+        if (TMA) {
+            if (lane32 == 0) {
+                mbar_arrive_expect_tx(bar, (uint32_t)(kUnitRows * p.sc * kRowChunkBytes));
+                tma_load_2d(dst, W.mq, g * p.sc * (CB / 8), kUnitRows * lu, bar);
+                tma_load_2d(dst + kUnitRows * p.sc * CB, W.ms, g * p.sc * 4, kUnitRows * lu, bar);
+            }
+            return;
+        }
+        const int c0 = g * p.sc;
+        const int n = min(p.sc, (p.k_pad >> 7) - c0);
         const int valid = min(kUnitRows, W.rows - kUnitRows * lu);
         if (lane32 == 0) mbar_arrive_expect_tx(bar, (uint32_t)(valid * n * kRowChunkBytes));
         const int r = lane32 & 15, row = kUnitRows * lu + r;
@@ -328,6 +369,7 @@ __global__ void __launch_bounds__(MM == 1 ? 384 : 512, MM == 1 ? 2 : 1)
         __syncwarp();
         if (i + p.d < items) {
             fence_proxy_async_smem();
+            __syncwarp();
             issue(uu2, g2, slot);
         }
         if (++g2 == p.nseg) { g2 = 0; ++uu2; }
@@ -426,7 +468,7 @@ __global__ void __launch_bounds__(MM == 1 ? 384 : 512, MM == 1 ? 2 : 1)
 }
 
 struct Plan {
-    int mm, r, sc, nseg, d, nwarps, ctas, xs_bytes, smem;
+    int mm, r, sc, nseg, d, nwarps, ctas, xs_bytes, smem, tma;
 };
 
 // Rows per thread (measured on B200, M = 1): R = 2 pays from ~48 rows per SM
@@ -448,13 +490,9 @@ bool make_plan(int mm, int rows, int k, int sm_count, Plan* pl, int force_r = 0,
     pl->mm = mm;
     pl->r = force_r ? force_r : pick_rows_per_thread(mm, rows, sm_count);
     const int unit_rows = 4 * pl->r;
-    // About four segments per row, so a row's chain starts on its first
-    // quarter while the rest is in flight.
-    int sc = (nck + 3) / 4;
-    sc = sc < 2 ? 2 : sc > kMaxSegChunks ? kMaxSegChunks : sc;
-    pl->sc = sc < nck ? sc : nck;
+    pl->sc = seg_chunks(nck);
     pl->nseg = (nck + pl->sc - 1) / pl->sc;
-    const int slot_bytes = pl->sc * unit_rows * (q4 ? row_chunk_bytes<true>() : row_chunk_bytes<false>());
+    const int slot_bytes = q4 ? slot_stride<true>(pl->sc, unit_rows) : slot_stride<false>(pl->sc, unit_rows);
     pl->xs_bytes = round_up(mm * k_pad * 4, 128);
     const int units = (rows + unit_rows - 1) / unit_rows;
     pl->ctas = units < sm_count ? units : sm_count;
@@ -463,10 +501,12 @@ bool make_plan(int mm, int rows, int k, int sm_count, Plan* pl, int force_r = 0,
     // for the next kernel's CTA on the same SM. Long ones: up to 200 KB.
     const int small_budget = 110 * 1024, big_budget = 200 * 1024;
     int max_slots = (small_budget - pl->xs_bytes - 1024) / slot_bytes;
+    pl->tma = 0;
     if (max_slots >= 1 && upc <= max_warps && upc * pl->nseg <= max_slots) {
         pl->nwarps = upc;
         pl->d = pl->nseg;
     } else {
+        pl->tma = 1;
         max_slots = (big_budget - pl->xs_bytes - 1024) / slot_bytes;
         if (max_slots < 1) return false;
         pl->nwarps = upc < max_warps ? upc : max_warps;
@@ -476,20 +516,21 @@ bool make_plan(int mm, int rows, int k, int sm_count, Plan* pl, int force_r = 0,
         const int items_per_warp = ((upc + pl->nwarps - 1) / pl->nwarps) * pl->nseg;
         if (pl->d > items_per_warp) pl->d = items_per_warp;
     }
-    pl->smem = pl->xs_bytes + pl->nwarps * pl->d * (slot_bytes + 8) + 16;
+    pl->smem = 128 + pl->xs_bytes + pl->nwarps * pl->d * (slot_bytes + 8) + 16;
     return true;
 }
 
 template <int MM, int R, bool Q4>
 cudaError_t launch_mm(const GemvParams& p0, const Plan& pl, cudaStream_t stream, bool pdl) {
-    static bool attr_set[2][64] = {};
+    static bool attr_set[4][64] = {};
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
     if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
     const bool gather = p0.ga.nranks > 0;
-    auto kern = MM == 1 && gather ? gemv_kernel<1, R, true, Q4> : gemv_kernel<MM, R, false, Q4>;
-    const int gi = gather ? 1 : 0;
+    auto kern = MM == 1 && gather ? (pl.tma ? gemv_kernel<1, R, true, Q4, true> : gemv_kernel<1, R, true, Q4, false>)
+                                  : (pl.tma ? gemv_kernel<MM, R, false, Q4, true> : gemv_kernel<MM, R, false, Q4, false>);
+    const int gi = (gather ? 2 : 0) + (pl.tma ? 1 : 0);
     if (!attr_set[gi][dev]) {
         e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 224 * 1024);
         if (e != cudaSuccess) return e;
@@ -553,7 +594,7 @@ cudaError_t launch_gemv_grouped(const float* x, int64_t ldx, int mm, const GemvW
     if (nw < 1 || nw > kMaxGroup || (gather && (mm != 1 || nw != 1))) return cudaErrorInvalidValue;
     int rows_total = 0;
     for (int g = 0; g < nw; ++g) {
-        if (ws[g].rows < 1) return cudaErrorInvalidValue;
+        if (ws[g].rows < 1 || !ws[g].maps) return cudaErrorInvalidValue;
         rows_total += ws[g].rows;
     }
     const int r = pick_rows_per_thread(mm, rows_total, sm_count);
@@ -567,6 +608,9 @@ cudaError_t launch_gemv_grouped(const float* x, int64_t ldx, int mm, const GemvW
     p.ldx = ldx;
     p.zero_neg = -0.0f;
     for (int g = 0; g < nw; ++g) {
+        if (ws[g].maps->sc != pl.sc || !ws[g].maps->dev) return cudaErrorInvalidValue;  // built for another k
+        p.grp[g].mq = ws[g].maps->dev + (r - 1);
+        p.grp[g].ms = ws[g].maps->dev + 2 + (r - 1);
         p.grp[g].q = ws[g].q;
         p.grp[g].s = ws[g].s;
         p.grp[g].y = ws[g].y;
@@ -581,11 +625,52 @@ cudaError_t launch_gemv_grouped(const float* x, int64_t ldx, int mm, const GemvW
     return q4 ? launch_mm_any<true>(mm, p, pl, stream, pdl) : launch_mm_any<false>(mm, p, pl, stream, pdl);
 }
 
-cudaError_t launch_gemv_exact(const float* x, int64_t ldx, int mm, const uint8_t* q, const float* s, int rows,
-                              int k, float* y, int64_t ldy, int* status, int sm_count, cudaStream_t stream, bool pdl,
-                              const GatherArgs* gather, bool q4) {
-    const GemvWeight w{q, s, rows, y, ldy};
+cudaError_t launch_gemv_exact(const float* x, int64_t ldx, int mm, const uint8_t* q, const float* s,
+                              const GemvMaps& maps, int rows, int k, float* y, int64_t ldy, int* status, int sm_count,
+                              cudaStream_t stream, bool pdl, const GatherArgs* gather, bool q4) {
+    const GemvWeight w{q, s, &maps, rows, y, ldy};
     return launch_gemv_grouped(x, ldx, mm, &w, 1, k, status, sm_count, stream, pdl, gather, q4);
+}
+
+cudaError_t gemv_make_maps(const uint8_t* q, const float* s, int rows, int k, bool q4, GemvMaps* out) {
+    auto enc = tensor_map_encoder();
+    if (!enc) return cudaErrorNotSupported;
+    const int nck = packed_k(k) / kChunk;
+    const int cb = q4 ? 64 : 128;
+    out->sc = seg_chunks(nck);
+    // Codes as 8-byte elements: a segment of sc chunks is sc * cb / 8 <= 128
+    // elements, one box row. Scales: 4 per chunk.
+    for (int r = 1; r <= 2; ++r) {
+        const cuuint32_t ur = 4 * r;
+        const cuuint32_t estr[2] = {1, 1};
+        {
+            const cuuint64_t dims[2] = {(cuuint64_t)nck * cb / 8, (cuuint64_t)rows};
+            const cuuint64_t strides[1] = {(cuuint64_t)nck * cb};
+            const cuuint32_t box[2] = {(cuuint32_t)(out->sc * cb / 8), ur};
+            if (enc(&out->q[r - 1], CU_TENSOR_MAP_DATA_TYPE_UINT64, 2, const_cast<uint8_t*>(q), dims, strides, box,
+                    estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+                return cudaErrorInvalidValue;
+        }
+        {
+            const cuuint64_t dims[2] = {(cuuint64_t)nck * 4, (cuuint64_t)rows};
+            const cuuint64_t strides[1] = {(cuuint64_t)nck * 16};
+            const cuuint32_t box[2] = {(cuuint32_t)(out->sc * 4), ur};
+            if (enc(&out->s[r - 1], CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(s), dims, strides, box,
+                    estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+                return cudaErrorInvalidValue;
+        }
+    }
+    static_assert(offsetof(GemvMaps, s) == 2 * sizeof(CUtensorMap), "q and s descriptors must be contiguous");
+    cudaError_t e = cudaMalloc(&out->dev, 4 * sizeof(CUtensorMap));
+    if (e != cudaSuccess) return e;
+    e = cudaMemcpy(out->dev, out->q, 4 * sizeof(CUtensorMap), cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) {
+        cudaFree(out->dev);
+        out->dev = nullptr;
+    }
+    return e;
 }
 
 }  // namespace qlm

@@ -4,6 +4,7 @@
 #include <cstddef>
 #include <cstdint>
 #include <cuda.h>
+#include <cudaTypedefs.h>
 #include <cuda_runtime.h>
 
 namespace qlm {
@@ -55,19 +56,39 @@ struct ArgmaxArgs {
 cudaError_t launch_argmax(const float* y, int n, int col0, const ArgmaxArgs& a, int* out_idx, float* out_val,
                           cudaStream_t stream, bool pdl);
 
+// TMA descriptors through which the exact GEMV reads a packed weight: the
+// codes as a 2-D tensor of 8-byte elements [rows][row bytes / 8], the scales
+// as [rows][k_pad / 32]. One load brings a unit of 4R rows x `sc` chunks (one
+// work item) into shared memory in the [row][chunk][bytes] order the
+// arithmetic reads; index r - 1 serves R = r rows per thread. The kernel
+// reads them from `dev`, a device copy of q[0], q[1], s[0], s[1] (kept out of
+// the kernel parameters, which every launch copies).
+struct GemvMaps {
+    alignas(64) CUtensorMap q[2];
+    alignas(64) CUtensorMap s[2];
+    int sc;                         // chunks per box: the segment length the GEMV plans for this k
+    CUtensorMap* dev = nullptr;     // device copy (owned by the weight handle)
+};
+
+// Build the GEMV descriptors of a packed weight and their device copy
+// (allocates out->dev; the caller frees it with cudaFree).
+cudaError_t gemv_make_maps(const uint8_t* q, const float* s, int rows, int k, bool q4, GemvMaps* out);
+
 // Bit-exact y[m][0:rows] = x[m][0:k] . W^T for m < mm (1..8), W packed.
 // status: device int set non-zero if a bounded wait gave up. With gather
 // (mm == 1 only) the rows are stored into every rank's exchange buffer
 // instead of y.
-cudaError_t launch_gemv_exact(const float* x, int64_t ldx, int mm, const uint8_t* q, const float* s, int rows,
-                              int k, float* y, int64_t ldy, int* status, int sm_count, cudaStream_t stream, bool pdl,
-                              const GatherArgs* gather = nullptr, bool q4 = false);
+cudaError_t launch_gemv_exact(const float* x, int64_t ldx, int mm, const uint8_t* q, const float* s,
+                              const GemvMaps& maps, int rows, int k, float* y, int64_t ldy, int* status, int sm_count,
+                              cudaStream_t stream, bool pdl, const GatherArgs* gather = nullptr, bool q4 = false);
 
-// One weight of a grouped exact launch (packed q, scales, rows, output).
+// One weight of a grouped exact launch (packed q, scales, their descriptors,
+// rows, output).
 constexpr int kMaxGroup = 8;
 struct GemvWeight {
     const uint8_t* q;
     const float* s;
+    const GemvMaps* maps;
     int rows;
     float* y;
     int64_t ldy;
@@ -88,6 +109,9 @@ struct TcMaps {
     alignas(64) CUtensorMap w;  // packed int8 rows, 128 x 128-byte boxes
     alignas(64) CUtensorMap s;  // fp32 scales
 };
+
+// The driver's tensor-map encoder (nullptr if the driver lacks it).
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder();
 
 // TMA descriptors for a packed weight (built once per weight).
 cudaError_t tc_make_weight_maps(const uint8_t* q, const float* s, int rows, int k_pad, TcMaps* out);
