@@ -22,6 +22,11 @@ linear); value aggregates all ranks' weight bytes ("weak" scaling).
 
 ``--impl reference`` times the reference's CPU implementation instead and
 prints the same line with "impl": "reference".
+
+``--shape N,K [--bits 4|8] [--m M]`` times the exact GEMV on one other weight
+shape (seeded random weights on the device, enough distinct copies to exceed
+L2, one CUDA graph of one launch per copy) and prints a per-shape line; it is
+also the command behind the per-shape ncu summaries in profiles/.
 """
 from __future__ import annotations
 
@@ -230,6 +235,61 @@ def run_reference(args):
     return 0
 
 
+def shape_leg(args):
+    """Exact GEMV on one [N, K] weight (int8 or int4), M activation rows."""
+    import torch
+    import quicklm_b200 as qlm
+    n, k = (int(v) for v in args.shape.split(","))
+    g = torch.Generator(device="cuda").manual_seed(n * 131 + k)
+    wd = torch.randn((n, k), device="cuda", generator=g) * 0.02
+    w0 = qlm.Int8Weight.quantize(wd, bits=args.bits)
+    copies = max(2, -(-300_000_000 // w0.nbytes))
+    ws = [w0] + [qlm.Int8Weight.quantize(wd, bits=args.bits) for _ in range(copies - 1)]
+    del wd
+    x = torch.randn((args.m, k), device="cuda", generator=g)
+    ys = [torch.empty((args.m, n), device="cuda") for _ in range(copies)]
+    stream = torch.cuda.Stream()
+
+    def step():
+        for i in range(copies):
+            qlm.matmul(x, ws[i], ys[i], stream=stream)
+
+    with torch.cuda.stream(stream):
+        for _ in range(args.warmup):
+            step()
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        step()
+    with torch.cuda.stream(stream):
+        for _ in range(args.warmup):
+            graph.replay()
+    torch.cuda.synchronize()
+    clocks = ClockSampler(0)
+    clocks.start()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record(stream)
+    with torch.cuda.stream(stream):
+        for _ in range(args.steps):
+            graph.replay()
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    us = ev0.elapsed_time(ev1) * 1000.0 / (args.steps * copies)
+    peak, peak_kind = measured_peaks()
+    gbs = w0.nbytes / us / 1e3
+    print(json.dumps({
+        "metric": f"exact GEMV weight GB/s, W [{n},{k}] int{args.bits}, M={args.m}", "value": round(gbs, 2),
+        "unit": "GB/s", "us_per_launch": round(us, 3), "weight_bytes": w0.nbytes, "copies": copies,
+        "steps": args.steps, "warmup": args.warmup, "pct_hbm_peak": round(100.0 * gbs / peak, 2),
+        "peak_source": f"MEASURED_PEAKS.json hbm_gbs ({peak_kind})", "clocks": clk,
+        "gpu_launches": args.steps * copies, "data": "synthetic (torch seeded N(0, 0.02^2) weights)"}), flush=True)
+    del graph
+    for w in ws:
+        w.free()
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -241,10 +301,15 @@ def main():
     ap.add_argument("--e2e-calls", type=int, default=2000)
     ap.add_argument("--no-prefill", action="store_true")
     ap.add_argument("--prefill-steps", type=int, default=50)
+    ap.add_argument("--shape", help="N,K: time the exact GEMV on this weight shape only")
+    ap.add_argument("--bits", type=int, default=8, choices=[4, 8])
+    ap.add_argument("--m", type=int, default=1)
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.impl == "reference":
         return run_reference(args)
+    if args.shape:
+        return shape_leg(args)
 
     import torch
     import quicklm_b200 as qlm
