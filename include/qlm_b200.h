@@ -102,6 +102,13 @@ int qlm_weight_quantize_upload_q4(const void* src, int src_dtype, int64_t src_ro
 int qlm_weight_import_int8(const int8_t* q, const float* scales, int n_total, int k, int row_begin,
                            int row_end, int device, void* stream, qlm_w8** out);
 
+/* Int4 counterpart of qlm_weight_import_int8: packed [n_total, (k+1)/2] bytes
+ * in the reference Tensor's int4 layout (src/tensor/tensor.hpp:45-61: value + 8,
+ * low nibble = even column) and scales [n_total, ceil(k/32)]. Both imports
+ * take host or device pointers and repack on the device. */
+int qlm_weight_import_int4(const uint8_t* packed, const float* scales, int n_total, int k, int row_begin,
+                           int row_end, int device, void* stream, qlm_w8** out);
+
 /* Copy a handle's rows back into the reference layout (host pointers):
  * q [rows, k] int8 and scales [rows, ceil(k/32)] fp32, rows = row_end - row_begin. */
 int qlm_weight_export_int8(const qlm_w8* w, int8_t* q, float* scales);
@@ -120,6 +127,22 @@ int qlm_weight_shape(const qlm_w8* w, int* rows, int* k, int* row_begin, int* ro
 /* Device bytes read by one M=1 product with this weight: packed codes plus
  * scales, the "weight bytes" of the decode roofline. */
 int64_t qlm_weight_bytes(const qlm_w8* w);
+
+/* Pre-quantized weights on disk: a standard safetensors file holding, per
+ * weight, its codes in the reference Tensor's layout (dtype "I8" [rows, k], or
+ * "U8" [rows, (k+1)/2] for int4), "<name>.qscale" F32 [rows, ceil(k/32)], and
+ * "__metadata__" entry "qlm.<name>" = "int8 k=<k>" | "int4 k=<k>". Loading
+ * skips quantization, which QuickLM's loader always performs because it
+ * accepts only F32/BF16 tensors (src/io/safetensors.cpp:524-527).
+ *   qlm_store_save: write n handles (their rows) under the given names.
+ *   qlm_store_load: map the file, check the header (offsets inside the file,
+ *                   sizes matching shapes) and upload rows [row_begin,
+ *                   row_end) of `name` (row_end < 0: all rows).
+ *   qlm_store_info: code width (8 or 4), rows and k of `name`; host only. */
+int qlm_store_save(const char* path, int n, const char* const* names, const qlm_w8* const* weights);
+int qlm_store_load(const char* path, const char* name, int row_begin, int row_end, int device, void* stream,
+                   qlm_w8** out);
+int qlm_store_info(const char* path, const char* name, int* bits, int64_t* rows, int64_t* k);
 
 /* Release a handle and its device memory (NULL is a no-op). */
 void qlm_weight_free(qlm_w8* w);

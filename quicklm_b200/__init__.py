@@ -24,7 +24,7 @@ import os
 import numpy as np
 
 __all__ = ["QlmError", "Int8Weight", "matmul", "matmul_grouped", "argmax", "load", "LIB_PATH", "EXACT", "TENSOR", "HOST_IO", "SYNC",
-           "BLOCK", "Comm", "shard_rows", "matmul_allgather"]
+           "BLOCK", "Comm", "shard_rows", "matmul_allgather", "save", "store_info"]
 
 LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "lib", "libqlm_b200.so")
 BLOCK = 32
@@ -38,6 +38,7 @@ ABI_SYMBOLS = (
     "qlm_device_status", "qlm_stream_sync", "qlm_linear_int8_tc_noalloc", "qlm_comm_handle_bytes",
     "qlm_comm_create", "qlm_comm_connect", "qlm_comm_free", "qlm_linear_int8_allgather", "qlm_argmax_f32",
     "qlm_linear_int8_grouped", "qlm_weight_quantize_upload_q4", "qlm_weight_export_int4", "qlm_weight_bits",
+    "qlm_weight_import_int4", "qlm_store_save", "qlm_store_load", "qlm_store_info",
 )
 
 _STATUS = {0: "OK", 1: "INVALID_ARG", 2: "CUDA", 3: "OUT_OF_MEMORY", 4: "UNSUPPORTED", 5: "TIMEOUT", 6: "NCCL",
@@ -72,6 +73,11 @@ def load(path: str = LIB_PATH):
     lib.qlm_weight_quantize_upload_q4.argtypes = [P, I, L, I, I, I, I, I, P, ctypes.POINTER(P)]
     lib.qlm_weight_export_int4.argtypes = [P, P, P]
     lib.qlm_weight_bits.argtypes = [P]
+    lib.qlm_weight_import_int4.argtypes = [P, P, I, I, I, I, I, P, ctypes.POINTER(P)]
+    lib.qlm_store_save.argtypes = [ctypes.c_char_p, I, P, P]
+    lib.qlm_store_load.argtypes = [ctypes.c_char_p, ctypes.c_char_p, I, I, I, P, ctypes.POINTER(P)]
+    lib.qlm_store_info.argtypes = [ctypes.c_char_p, ctypes.c_char_p, ctypes.POINTER(I), ctypes.POINTER(L),
+                                   ctypes.POINTER(L)]
     lib.qlm_weight_shape.argtypes = [P] + [ctypes.POINTER(I)] * 5
     lib.qlm_weight_bytes.argtypes = [P]
     lib.qlm_weight_bytes.restype = L
@@ -204,6 +210,35 @@ class Int8Weight:
         out.device = device
         return out
 
+    @classmethod
+    def from_int4(cls, packed: np.ndarray, scales: np.ndarray, k: int, device: int = 0, row_begin: int = 0,
+                  row_end: int | None = None, stream=None):
+        """Upload a weight already in the reference Tensor's int4 layout
+        (packed [n, (k+1)/2] uint8, value + 8, low nibble = even column)."""
+        packed = np.ascontiguousarray(packed, np.uint8)
+        scales = np.ascontiguousarray(scales, np.float32)
+        n = packed.shape[0]
+        if packed.shape != (n, (k + 1) // 2) or scales.shape != (n, (k + BLOCK - 1) // BLOCK):
+            raise QlmError(1, f"shapes {packed.shape}, {scales.shape} do not match k={k}")
+        if row_end is None:
+            row_end = n
+        h = ctypes.c_void_p()
+        _check(load().qlm_weight_import_int4(packed.ctypes.data, scales.ctypes.data, n, k, row_begin, row_end, device,
+                                             _stream_ptr(stream), ctypes.byref(h)))
+        out = cls(h.value)
+        out.device = device
+        return out
+
+    @classmethod
+    def from_file(cls, path: str, name: str, device: int = 0, row_begin: int = 0, row_end: int = -1, stream=None):
+        """Load a pre-quantized weight written by :func:`save` (no quantization)."""
+        h = ctypes.c_void_p()
+        _check(load().qlm_store_load(os.fsencode(path), name.encode(), row_begin, row_end, device,
+                                     _stream_ptr(stream), ctypes.byref(h)))
+        out = cls(h.value)
+        out.device = device
+        return out
+
     def to_int8(self):
         """(q int8 [rows, k], scales float32 [rows, ceil(k/32)]) in the reference layout."""
         q = np.empty((self.rows, self.k), np.int8)
@@ -229,6 +264,21 @@ class Int8Weight:
             self.free()
         except Exception:
             pass
+
+
+def save(path: str, weights: dict) -> None:
+    """Write {name: Int8Weight} as a pre-quantized safetensors file."""
+    names = list(weights)
+    c_names = (ctypes.c_char_p * len(names))(*[n.encode() for n in names])
+    c_ws = (ctypes.c_void_p * len(names))(*[weights[n].handle.value for n in names])
+    _check(load().qlm_store_save(os.fsencode(path), len(names), c_names, c_ws))
+
+
+def store_info(path: str, name: str):
+    """(bits, rows, k) of a pre-quantized weight in a file (no GPU needed)."""
+    b, r, k = ctypes.c_int(), ctypes.c_int64(), ctypes.c_int64()
+    _check(load().qlm_store_info(os.fsencode(path), name.encode(), ctypes.byref(b), ctypes.byref(r), ctypes.byref(k)))
+    return b.value, r.value, k.value
 
 
 def matmul(A, B: Int8Weight, C=None, transpose_B: bool = True, flags: int = EXACT, stream=None):

@@ -234,6 +234,78 @@ int quantize_upload(const void* src, int src_dtype, int64_t src_row_stride, int 
     return QLM_OK;
 }
 
+// Shared body of the int8 and int4 imports: codes in the reference Tensor's
+// layout (int8 [n_total][k]; int4 [n_total][(k+1)/2] bytes) and scales
+// [n_total][ceil(k/32)], host or device memory. Rows [row_begin, row_end) are
+// moved (host memory through a bounded device staging buffer) and repacked on
+// the device.
+int import_quantized(const void* codes, const float* scales, int n_total, int k, int row_begin, int row_end,
+                     int device, void* stream, qlm_w8** out, int bits) {
+    if (!out) return set_err(QLM_ERR_INVALID_ARG, "out is NULL");
+    *out = nullptr;
+    if (!codes || !scales) return set_err(QLM_ERR_INVALID_ARG, "codes/scales is NULL");
+    int rc = check_shard(n_total, k, row_begin, row_end);
+    if (rc) return rc;
+    DeviceState* st;
+    if ((rc = device_state(device, &st))) return rc;
+    DeviceGuard g(device);
+    if (!g.ok) return set_err(QLM_ERR_CUDA, "cudaSetDevice(%d) failed", device);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+
+    const int nb = (k + QLM_BLOCK - 1) / QLM_BLOCK;
+    const size_t code_row = bits == 8 ? (size_t)k : (size_t)(k + 1) / 2;
+    auto on_device = [](const void* p) {
+        cudaPointerAttributes attr;
+        if (cudaPointerGetAttributes(&attr, p) != cudaSuccess) {
+            cudaGetLastError();
+            return false;
+        }
+        return attr.type == cudaMemoryTypeDevice || attr.type == cudaMemoryTypeManaged;
+    };
+    const bool dev_codes = on_device(codes), dev_scales = on_device(scales);
+
+    qlm_w8* w = nullptr;
+    if ((rc = alloc_weight(device, n_total, k, row_begin, row_end, &w, bits))) return rc;
+    const size_t q_row_bytes = (size_t)w->k_pad * bits / 8;
+    const uint8_t* csrc = static_cast<const uint8_t*>(codes) + (size_t)row_begin * code_row;
+    const float* ssrc = scales + (size_t)row_begin * nb;
+
+    cudaError_t e = cudaSuccess;
+    if (dev_codes && dev_scales) {
+        e = qlm::launch_repack(csrc, (int64_t)code_row, ssrc, nb, w->rows, k, bits == 4, w->q, w->s, s);
+    } else {
+        // <= 64 MB of rows per pass through one staging buffer (codes, then scales).
+        const size_t row_bytes = code_row + (size_t)nb * sizeof(float);
+        int chunk = (int)((64u << 20) / row_bytes);
+        if (chunk < 1) chunk = 1;
+        if (chunk > w->rows) chunk = w->rows;
+        uint8_t* stage = nullptr;
+        const size_t scale_off = ((size_t)chunk * code_row + 15) / 16 * 16;
+        e = cudaMalloc(&stage, scale_off + (size_t)chunk * nb * sizeof(float));
+        for (int r = 0; e == cudaSuccess && r < w->rows; r += chunk) {
+            const int nr = (w->rows - r) < chunk ? (w->rows - r) : chunk;
+            float* sstage = reinterpret_cast<float*>(stage + scale_off);
+            e = cudaMemcpyAsync(stage, csrc + (size_t)r * code_row, (size_t)nr * code_row, cudaMemcpyDefault, s);
+            if (e == cudaSuccess)
+                e = cudaMemcpyAsync(sstage, ssrc + (size_t)r * nb, (size_t)nr * nb * sizeof(float),
+                                    cudaMemcpyDefault, s);
+            if (e == cudaSuccess)
+                e = qlm::launch_repack(stage, (int64_t)code_row, sstage, nb, nr, k, bits == 4,
+                                       w->q + (size_t)r * q_row_bytes, w->s + (size_t)r * w->nb_pad, s);
+        }
+        if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+        if (stage) cudaFree(stage);
+    }
+    if (e == cudaSuccess && bits == 8) e = qlm::launch_weight_exponents(w->s, w->rows, k, w->ew, s);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+    if (e != cudaSuccess) {
+        qlm_weight_free(w);
+        return cuda_err(e, "import upload");
+    }
+    *out = w;
+    return QLM_OK;
+}
+
 }  // namespace
 
 extern "C" {
@@ -250,45 +322,12 @@ int qlm_weight_quantize_upload_q4(const void* src, int src_dtype, int64_t src_ro
 
 int qlm_weight_import_int8(const int8_t* q, const float* scales, int n_total, int k, int row_begin, int row_end,
                            int device, void* stream, qlm_w8** out) {
-    if (!out) return set_err(QLM_ERR_INVALID_ARG, "out is NULL");
-    *out = nullptr;
-    if (!q || !scales) return set_err(QLM_ERR_INVALID_ARG, "q/scales is NULL");
-    int rc = check_shard(n_total, k, row_begin, row_end);
-    if (rc) return rc;
-    DeviceState* st;
-    if ((rc = device_state(device, &st))) return rc;
-    DeviceGuard g(device);
-    if (!g.ok) return set_err(QLM_ERR_CUDA, "cudaSetDevice(%d) failed", device);
+    return import_quantized(q, scales, n_total, k, row_begin, row_end, device, stream, out, 8);
+}
 
-    const int k_pad = qlm::packed_k(k), nb_pad = k_pad / QLM_BLOCK, nb = (k + QLM_BLOCK - 1) / QLM_BLOCK;
-    const int rows = row_end - row_begin;
-    std::vector<uint8_t> hq;
-    std::vector<float> hs;
-    try {
-        hq.assign((size_t)rows * k_pad, 0);
-        hs.assign((size_t)rows * nb_pad, 0.0f);
-    } catch (...) {
-        return set_err(QLM_ERR_OUT_OF_MEMORY, "host staging allocation failed");
-    }
-    for (int r = 0; r < rows; ++r) {
-        const int8_t* src = q + (size_t)(row_begin + r) * k;
-        uint8_t* dst = hq.data() + (size_t)r * k_pad;
-        for (int kk = 0; kk < k; ++kk) dst[qlm::packed_offset(kk)] = (uint8_t)src[kk];
-        std::memcpy(hs.data() + (size_t)r * nb_pad, scales + (size_t)(row_begin + r) * nb, nb * sizeof(float));
-    }
-    qlm_w8* w = nullptr;
-    if ((rc = alloc_weight(device, n_total, k, row_begin, row_end, &w))) return rc;
-    cudaStream_t s = static_cast<cudaStream_t>(stream);
-    cudaError_t e = cudaMemcpyAsync(w->q, hq.data(), hq.size(), cudaMemcpyHostToDevice, s);
-    if (e == cudaSuccess) e = cudaMemcpyAsync(w->s, hs.data(), hs.size() * sizeof(float), cudaMemcpyHostToDevice, s);
-    if (e == cudaSuccess) e = qlm::launch_weight_exponents(w->s, w->rows, k, w->ew, s);
-    if (e == cudaSuccess) e = cudaStreamSynchronize(s);
-    if (e != cudaSuccess) {
-        qlm_weight_free(w);
-        return cuda_err(e, "import upload");
-    }
-    *out = w;
-    return QLM_OK;
+int qlm_weight_import_int4(const uint8_t* packed, const float* scales, int n_total, int k, int row_begin,
+                           int row_end, int device, void* stream, qlm_w8** out) {
+    return import_quantized(packed, scales, n_total, k, row_begin, row_end, device, stream, out, 4);
 }
 
 int qlm_weight_export_int8(const qlm_w8* w, int8_t* q, float* scales) {

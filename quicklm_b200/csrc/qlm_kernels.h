@@ -20,6 +20,14 @@ cudaError_t launch_quantize_pack(const void* src, int dtype, int64_t src_stride,
 cudaError_t launch_quantize_pack_q4(const void* src, int dtype, int64_t src_stride, int rows, int k, uint8_t* q,
                                     float* scales, cudaStream_t stream);
 
+// Move already-quantized codes from the reference Tensor's layouts (int8
+// [rows][k] with row stride code_stride bytes; int4 [rows][(k+1)/2] bytes, low
+// nibble = even column) and their scales [rows][ceil(k/32)] (row stride
+// scale_stride floats) into the packed layout and padded scales. Device
+// pointers.
+cudaError_t launch_repack(const uint8_t* codes, int64_t code_stride, const float* scales, int64_t scale_stride,
+                          int rows, int k, bool q4, uint8_t* q, float* s, cudaStream_t stream);
+
 constexpr int kMaxRanks = 8;
 
 // Peer pointers for the fused GEMV + all-gather (M = 1). peer_slots[r] is

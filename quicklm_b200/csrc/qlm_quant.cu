@@ -24,6 +24,11 @@
 // 1024 source values through shared memory with coalesced loads, each lane
 // quantizes one block, and the packed bytes go back out through shared memory
 // as one contiguous 1 KB store (the P128 layout keeps 8 chunks contiguous).
+//
+// repack_kernel moves codes that are already quantized, in the reference
+// Tensor's own layouts (int8 [rows][k]; int4 [rows][(k+1)/2] bytes, low nibble
+// = even column), into the packed layouts, with the scales copied into the
+// padded [rows][k_pad/32] array: the load path of pre-quantized weights.
 #include "qlm_device.cuh"
 #include "qlm_kernels.h"
 
@@ -182,6 +187,71 @@ cudaError_t launch_quantize_pack_q4(const void* src, int dtype, int64_t src_stri
     if (ctas > 0x7fffffffLL) return cudaErrorInvalidValue;
     quantize_pack_kernel<true><<<(unsigned)ctas, kWarpsPerCta * 32, 0, stream>>>(src, dtype, src_stride, rows, k,
                                                                                   k_pad, q, scales);
+    return cudaGetLastError();
+}
+
+namespace {
+
+// One thread per (row, 128-element chunk, lane l): the 16 int8 bytes (or 8
+// int4 bytes) lane l of the GEMV reads from the chunk, gathered from the row-
+// major codes; lanes 0..3 also move the chunk's four scales.
+template <bool Q4>
+__global__ void repack_kernel(const uint8_t* __restrict__ codes, int64_t code_stride, const float* __restrict__ sin,
+                              int64_t s_stride, int rows, int k, int k_pad, uint8_t* __restrict__ q,
+                              float* __restrict__ sout) {
+    const int nck = k_pad / kChunk, nb = (k + kBlock - 1) / kBlock, nb_pad = k_pad / kBlock;
+    const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (t >= (int64_t)rows * nck * 8) return;
+    const int l = (int)(t & 7);
+    const int64_t rc = t >> 3;
+    const int c = (int)(rc % nck);
+    const int64_t row = rc / nck;
+    const uint8_t* src = codes + row * code_stride;
+    const int k0 = c * kChunk + l;
+    if (!Q4) {
+        uint32_t w[4];
+#pragma unroll
+        for (int bb = 0; bb < 4; ++bb) {
+            uint32_t v = 0;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const int kk = k0 + 32 * bb + 8 * j;
+                v |= (uint32_t)(kk < k ? src[kk] : 0u) << (8 * j);
+            }
+            w[bb] = v;
+        }
+        *reinterpret_cast<uint4*>(q + (row * nck + c) * kChunk + l * 16) = make_uint4(w[0], w[1], w[2], w[3]);
+    } else {
+        auto nib = [&](int kk) -> uint32_t { return kk < k ? (uint32_t)(src[kk >> 1] >> ((kk & 1) * 4)) & 0xFu : 8u; };
+        uint32_t lo = 0, hi = 0;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            lo |= (nib(k0 + 8 * j) | nib(k0 + 32 + 8 * j) << 4) << (8 * j);
+            hi |= (nib(k0 + 64 + 8 * j) | nib(k0 + 96 + 8 * j) << 4) << (8 * j);
+        }
+        *reinterpret_cast<uint2*>(q + (row * nck + c) * (kChunk / 2) + l * 8) = make_uint2(lo, hi);
+    }
+    if (l < 4) {
+        const int blk = 4 * c + l;
+        sout[row * nb_pad + blk] = blk < nb ? sin[row * s_stride + blk] : 0.0f;
+    }
+}
+
+}  // namespace
+
+cudaError_t launch_repack(const uint8_t* codes, int64_t code_stride, const float* scales, int64_t scale_stride,
+                          int rows, int k, bool q4, uint8_t* q, float* s, cudaStream_t stream) {
+    if (rows <= 0) return cudaSuccess;
+    const int k_pad = packed_k(k);
+    const int64_t threads = (int64_t)rows * (k_pad / kChunk) * 8;
+    const int64_t ctas = (threads + 255) / 256;
+    if (ctas > 0x7fffffffLL) return cudaErrorInvalidValue;
+    if (q4)
+        repack_kernel<true><<<(unsigned)ctas, 256, 0, stream>>>(codes, code_stride, scales, scale_stride, rows, k,
+                                                                k_pad, q, s);
+    else
+        repack_kernel<false><<<(unsigned)ctas, 256, 0, stream>>>(codes, code_stride, scales, scale_stride, rows, k,
+                                                                 k_pad, q, s);
     return cudaGetLastError();
 }
 
