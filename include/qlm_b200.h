@@ -144,6 +144,32 @@ int qlm_store_load(const char* path, const char* name, int row_begin, int row_en
                    qlm_w8** out);
 int qlm_store_info(const char* path, const char* name, int* bits, int64_t* rows, int64_t* k);
 
+/* Per-layer ops on device-resident fp32 activations (device pointers,
+ * asynchronous on `stream`), so a decoder layer's activations can stay in HBM
+ * between its projections:
+ *   qlm_rms_norm      y = rms_norm(x) per row of `size`, zero-centred gain
+ *                     (1 + w): math::rms_norm (src/ops/math_ops.cpp:1055-1074).
+ *                     x and y may be the same buffer. Bit-identical.
+ *   qlm_add_rms_norm  residual += delta; out = rms_norm(residual):
+ *                     math::add_rms_norm (math_ops.cpp:1133-1174). Bit-identical.
+ *   qlm_silu_mul      a = silu(a) * b: math::silu_mul (math_ops.cpp:1122-1131);
+ *                     within 2 ulp (exp in double, rounded once, vs host expf).
+ *   qlm_rope_neox     partial NeoX RoPE of t [num_tokens][num_heads][head_dim]
+ *                     (first rotary_dim dims per head) with per-token cos/sin
+ *                     tables [num_tokens][rotary_dim/2] in device memory:
+ *                     math::apply_rope_neox (math_ops.cpp:1237-1291). Bit-identical
+ *                     with tables from qlm_rope_neox_tables.
+ *   qlm_rope_neox_tables  host: cos/sin for positions pos0 .. pos0+num_tokens-1,
+ *                     computed with the reference's own float expressions and
+ *                     libm calls (math_ops.cpp:1256-1271). */
+int qlm_rms_norm(const float* x, const float* w, float* y, int rows, int size, float eps, void* stream);
+int qlm_add_rms_norm(float* residual, const float* delta, const float* w, float* out, int rows, int size, float eps,
+                     void* stream);
+int qlm_silu_mul(float* a, const float* b, int64_t n, void* stream);
+int qlm_rope_neox(float* t, int num_tokens, int num_heads, int head_dim, int rotary_dim, const float* cos_tab,
+                  const float* sin_tab, void* stream);
+int qlm_rope_neox_tables(int pos0, int num_tokens, float rope_theta, int rotary_dim, float* cos_out, float* sin_out);
+
 /* Release a handle and its device memory (NULL is a no-op). */
 void qlm_weight_free(qlm_w8* w);
 

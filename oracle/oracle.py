@@ -67,6 +67,11 @@ class RefCPU:
         lib.qlmref_greedy_sample.argtypes = [_P, _I, ctypes.POINTER(_I)]
         lib.qlmref_quantize_int4.argtypes = [_P, _I, _I, _I, _P, _P]
         lib.qlmref_matmul_int4.argtypes = [_P, _I, _I, _P, _P, _I, _P, _I]
+        _F = ctypes.c_float
+        lib.qlmref_rms_norm.argtypes = [_P, _P, _P, _I, _I, _F]
+        lib.qlmref_add_rms_norm.argtypes = [_P, _P, _P, _P, _I, _I, _F]
+        lib.qlmref_silu_mul.argtypes = [_P, _P, _I]
+        lib.qlmref_rope_neox.argtypes = [_P, _I, _I, _I, _F, _I]
         self.lib = lib
         self.threads = 1
 
@@ -98,6 +103,38 @@ class RefCPU:
         y = np.empty((m, n), np.float32)
         self._rc(self.lib.qlmref_matmul_int4(_ptr(x), m, k, _ptr(packed), _ptr(s), n, _ptr(y), n))
         return y
+
+    def rms_norm(self, x: np.ndarray, w: np.ndarray, eps: float) -> np.ndarray:
+        """math::rms_norm over the rows of x [rows, size]."""
+        x = np.ascontiguousarray(x, np.float32)
+        w = np.ascontiguousarray(w, np.float32)
+        y = np.empty_like(x)
+        self._rc(self.lib.qlmref_rms_norm(_ptr(x), _ptr(w), _ptr(y), x.shape[0], x.shape[1], ctypes.c_float(eps)))
+        return y
+
+    def add_rms_norm(self, res: np.ndarray, delta: np.ndarray, w: np.ndarray, eps: float):
+        """math::add_rms_norm -> (updated residual, normalised output)."""
+        r = np.array(res, np.float32, copy=True, order="C")
+        d = np.ascontiguousarray(delta, np.float32)
+        w = np.ascontiguousarray(w, np.float32)
+        out = np.empty_like(r)
+        self._rc(self.lib.qlmref_add_rms_norm(_ptr(r), _ptr(d), _ptr(w), _ptr(out), r.shape[0], r.shape[1],
+                                               ctypes.c_float(eps)))
+        return r, out
+
+    def silu_mul(self, a: np.ndarray, b: np.ndarray) -> np.ndarray:
+        """math::silu_mul: silu(a) * b (a copy is updated)."""
+        a = np.array(a, np.float32, copy=True).ravel()
+        b = np.ascontiguousarray(b, np.float32).ravel()
+        self._rc(self.lib.qlmref_silu_mul(_ptr(a), _ptr(b), a.size))
+        return a
+
+    def rope_neox(self, t: np.ndarray, pos: int, theta: float, rotary_dim: int) -> np.ndarray:
+        """math::apply_rope_neox on one token's t [num_heads, head_dim] (a copy)."""
+        t = np.array(t, np.float32, copy=True, order="C")
+        self._rc(self.lib.qlmref_rope_neox(_ptr(t), t.shape[0], t.shape[1], int(pos), ctypes.c_float(theta),
+                                           int(rotary_dim)))
+        return t
 
     def greedy_sample(self, logits: np.ndarray) -> int:
         """DecoderModel::sample(logits, 0, 0) (model/model.cpp:259-272)."""

@@ -14,6 +14,9 @@
 //                          (ops/math_ops.cpp:820-900 -> int8_gemv_range 558-579
 //                          -> dot8/dot4/dot_avx2_int8 414-553)
 //   qlmref_init_threads -> math::init_thread_pool (ops/math_ops.cpp:161-171)
+//   qlmref_rms_norm / qlmref_add_rms_norm / qlmref_silu_mul / qlmref_rope_neox
+//                       -> math::rms_norm, add_rms_norm, silu_mul, apply_rope_neox
+//                          (ops/math_ops.cpp:1055-1074, 1133-1174, 1122-1131, 1237-1291)
 //   qlmref_greedy_sample -> DecoderModel::sample(logits, 0, 0), the greedy branch
 //                          (model/model.cpp:259-272)
 //   qlmref_quantize_int4 -> SafetensorsLoader::get_tensor_keep_int4, which runs
@@ -209,6 +212,42 @@ int qlmref_matmul_int8(const float* x, int m, int k, const int8_t* q, const floa
     } catch (const std::exception& e) {
         return fail(e.what());
     }
+}
+
+// Per-layer ops on host buffers, through the reference's own functions.
+int qlmref_rms_norm(const float* x, const float* w, float* y, int rows, int size, float eps) {
+    if (!x || !w || !y || rows <= 0 || size <= 0) return fail("bad args");
+    Tensor in(std::vector<int>{rows, size}, const_cast<float*>(x));
+    Tensor wt(std::vector<int>{size}, const_cast<float*>(w));
+    Tensor out(std::vector<int>{rows, size}, y);
+    math::rms_norm(in, wt, out, eps);
+    return 0;
+}
+
+int qlmref_add_rms_norm(float* res, const float* delta, const float* w, float* out, int rows, int size, float eps) {
+    if (!res || !delta || !w || !out || rows <= 0 || size <= 0) return fail("bad args");
+    Tensor r(std::vector<int>{rows, size}, res);
+    Tensor d(std::vector<int>{rows, size}, const_cast<float*>(delta));
+    Tensor wt(std::vector<int>{size}, const_cast<float*>(w));
+    Tensor o(std::vector<int>{rows, size}, out);
+    math::add_rms_norm(r, d, wt, o, eps);
+    return 0;
+}
+
+int qlmref_silu_mul(float* a, const float* b, int n) {
+    if (!a || !b || n <= 0) return fail("bad args");
+    Tensor A(std::vector<int>{n}, a);
+    Tensor B(std::vector<int>{n}, const_cast<float*>(b));
+    math::silu_mul(A, B);
+    return 0;
+}
+
+// One token: t [num_heads, head_dim] at position pos.
+int qlmref_rope_neox(float* t, int num_heads, int head_dim, int pos, float theta, int rotary_dim) {
+    if (!t || num_heads <= 0 || head_dim <= 0) return fail("bad args");
+    Tensor T(std::vector<int>{num_heads, head_dim}, t);
+    math::apply_rope_neox(T, pos, theta, head_dim, rotary_dim);
+    return 0;
 }
 
 // Streams `g` distinct int8 weights (all [n, k]) through math::matmul once

@@ -24,7 +24,8 @@ import os
 import numpy as np
 
 __all__ = ["QlmError", "Int8Weight", "matmul", "matmul_grouped", "argmax", "load", "LIB_PATH", "EXACT", "TENSOR", "HOST_IO", "SYNC",
-           "BLOCK", "Comm", "shard_rows", "matmul_allgather", "save", "store_info"]
+           "BLOCK", "Comm", "shard_rows", "matmul_allgather", "save", "store_info", "rms_norm", "add_rms_norm",
+           "silu_mul", "rope_neox", "rope_neox_tables"]
 
 LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "lib", "libqlm_b200.so")
 BLOCK = 32
@@ -38,7 +39,8 @@ ABI_SYMBOLS = (
     "qlm_device_status", "qlm_stream_sync", "qlm_linear_int8_tc_noalloc", "qlm_comm_handle_bytes",
     "qlm_comm_create", "qlm_comm_connect", "qlm_comm_free", "qlm_linear_int8_allgather", "qlm_argmax_f32",
     "qlm_linear_int8_grouped", "qlm_weight_quantize_upload_q4", "qlm_weight_export_int4", "qlm_weight_bits",
-    "qlm_weight_import_int4", "qlm_store_save", "qlm_store_load", "qlm_store_info",
+    "qlm_weight_import_int4", "qlm_store_save", "qlm_store_load", "qlm_store_info", "qlm_rms_norm",
+    "qlm_add_rms_norm", "qlm_silu_mul", "qlm_rope_neox", "qlm_rope_neox_tables",
 )
 
 _STATUS = {0: "OK", 1: "INVALID_ARG", 2: "CUDA", 3: "OUT_OF_MEMORY", 4: "UNSUPPORTED", 5: "TIMEOUT", 6: "NCCL",
@@ -78,6 +80,12 @@ def load(path: str = LIB_PATH):
     lib.qlm_store_load.argtypes = [ctypes.c_char_p, ctypes.c_char_p, I, I, I, P, ctypes.POINTER(P)]
     lib.qlm_store_info.argtypes = [ctypes.c_char_p, ctypes.c_char_p, ctypes.POINTER(I), ctypes.POINTER(L),
                                    ctypes.POINTER(L)]
+    F = ctypes.c_float
+    lib.qlm_rms_norm.argtypes = [P, P, P, I, I, F, P]
+    lib.qlm_add_rms_norm.argtypes = [P, P, P, P, I, I, F, P]
+    lib.qlm_silu_mul.argtypes = [P, P, L, P]
+    lib.qlm_rope_neox.argtypes = [P, I, I, I, I, P, P, P]
+    lib.qlm_rope_neox_tables.argtypes = [I, I, F, I, P, P]
     lib.qlm_weight_shape.argtypes = [P] + [ctypes.POINTER(I)] * 5
     lib.qlm_weight_bytes.argtypes = [P]
     lib.qlm_weight_bytes.restype = L
@@ -413,6 +421,74 @@ def argmax(logits, comm: "Comm" = None, col0: int = 0, stream=None):
         _check(lib.qlm_argmax_f32(v.data_ptr(), v.numel(), int(col0), comm.handle if comm is not None else None,
                                   out_i.data_ptr(), out_v.data_ptr(), SYNC, st))
     return int(out_i.item()), float(out_v.item())
+
+
+def _dev_f32(t, name):
+    import torch
+    if not (_is_torch(t) and t.is_cuda and t.dtype == torch.float32 and t.is_contiguous()):
+        raise QlmError(1, f"{name} must be a contiguous float32 CUDA tensor")
+    return t
+
+
+def _torch_stream(stream):
+    import torch
+    return _stream_ptr(stream) if stream is not None else torch.cuda.current_stream().cuda_stream
+
+
+def rms_norm(x, w, eps: float, out=None, stream=None):
+    """math::rms_norm on device rows of w.numel(): out = x * rsqrt(mean(x^2) + eps) * (1 + w)."""
+    _dev_f32(x, "x"), _dev_f32(w, "w")
+    size = w.numel()
+    if x.numel() % size:
+        raise QlmError(1, "x is not a whole number of rows")
+    out = x.new_empty(x.shape) if out is None else _dev_f32(out, "out")
+    _check(load().qlm_rms_norm(x.data_ptr(), w.data_ptr(), out.data_ptr(), x.numel() // size, size, eps,
+                               _torch_stream(stream)))
+    return out
+
+
+def add_rms_norm(residual, delta, w, eps: float, out=None, stream=None):
+    """math::add_rms_norm: residual += delta (in place); returns rms_norm(residual)."""
+    _dev_f32(residual, "residual"), _dev_f32(delta, "delta"), _dev_f32(w, "w")
+    size = w.numel()
+    if residual.numel() % size or delta.numel() != residual.numel():
+        raise QlmError(1, "residual/delta shapes do not match w")
+    out = residual.new_empty(residual.shape) if out is None else _dev_f32(out, "out")
+    _check(load().qlm_add_rms_norm(residual.data_ptr(), delta.data_ptr(), w.data_ptr(), out.data_ptr(),
+                                   residual.numel() // size, size, eps, _torch_stream(stream)))
+    return out
+
+
+def silu_mul(a, b, stream=None):
+    """math::silu_mul: a = silu(a) * b in place (within 2 ulp of the reference)."""
+    _dev_f32(a, "a"), _dev_f32(b, "b")
+    if a.numel() != b.numel():
+        raise QlmError(1, "a and b differ in size")
+    _check(load().qlm_silu_mul(a.data_ptr(), b.data_ptr(), a.numel(), _torch_stream(stream)))
+    return a
+
+
+def rope_neox_tables(pos0: int, num_tokens: int, theta: float, rotary_dim: int):
+    """Host cos/sin tables [num_tokens, rotary_dim/2] for positions pos0.., as the reference computes them."""
+    c = np.empty((num_tokens, rotary_dim // 2), np.float32)
+    s = np.empty_like(c)
+    _check(load().qlm_rope_neox_tables(pos0, num_tokens, theta, rotary_dim, c.ctypes.data, s.ctypes.data))
+    return c, s
+
+
+def rope_neox(t, pos0: int, theta: float, rotary_dim: int, tables=None, stream=None):
+    """math::apply_rope_neox in place on t [num_tokens, num_heads, head_dim] (token i at pos0 + i)."""
+    import torch
+    _dev_f32(t, "t")
+    if t.dim() != 3:
+        raise QlmError(1, "t must be [num_tokens, num_heads, head_dim]")
+    n_tok, heads, head_dim = t.shape
+    if tables is None:
+        c, s = rope_neox_tables(pos0, n_tok, theta, rotary_dim)
+        tables = (torch.from_numpy(c).to(t.device), torch.from_numpy(s).to(t.device))
+    _check(load().qlm_rope_neox(t.data_ptr(), n_tok, heads, head_dim, rotary_dim, tables[0].data_ptr(),
+                                tables[1].data_ptr(), _torch_stream(stream)))
+    return t
 
 
 def matmul_grouped(x, weights, ys=None, flags: int = 0, stream=None):

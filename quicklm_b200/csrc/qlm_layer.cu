@@ -1,0 +1,243 @@
+// qlm_layer.cu — per-layer elementwise/normalisation ops on device-resident
+// activations, so a decoder layer's activations can stay in HBM between its
+// projections. Restatements of QuickLM src/ops/math_ops.cpp:
+//
+//   rms_norm      (:1055-1074, sumsq :990-1019, norm_apply_zc :1021-1032)
+//   add_rms_norm  (:1133-1174)
+//   silu_mul      (:1122-1131)
+//   apply_rope_neox (:1237-1291)
+//
+// rms_norm, add_rms_norm and the RoPE rotation are bit-identical to the
+// reference (strict build, no contraction): the sums of squares follow its
+// exact accumulation order and reduction tree, the scale is the IEEE
+// 1 / sqrt(ss / n + eps), and the RoPE cos/sin tables are computed on the host
+// with the same libm calls the reference makes (qlm_rope_neox_tables). SiLU
+// needs exp: the device evaluates it in double precision and rounds once, so
+// it agrees with the host's expf except where that is not correctly rounded;
+// a 1-ulp difference there can move 1 + e, the quotient and the product by one
+// rounding each, so silu_mul is specified to 2 ulp of the reference (equal on
+// more than 99% of inputs, NaN/Inf alike).
+#include <cmath>
+#include <cstdint>
+#include <string>
+
+#include "qlm_b200.h"
+#include "qlm_device.cuh"
+
+namespace qlm {
+namespace {
+
+constexpr int kThreads = 256;
+constexpr int kStageFloats = 12000;  // rows up to this size are staged in shared memory (< 48 KB with the static part)
+
+// ---- sums of squares, in the reference's order ------------------------------
+
+// sumsq (math_ops.cpp:990-1019): accumulators a0..a3 of 8 lanes; a_g lane l
+// takes x[32 i + 8 g + l] by FMA, i ascending; then the 8-wide remainder
+// into a0; then per lane (a0 + a1) + (a2 + a3), the 8 -> 4 -> 1 tree
+// (lo_i = s_i + s_{i+4}; two hadds), then the scalar tail r += x * x. Warp 0.
+__device__ float sumsq_ref(const float* __restrict__ x, int n) {
+    const int t = threadIdx.x & 31;
+    const int g = t >> 3, l = t & 7;
+    const int limit = n - (n % 32);
+    float a = 0.0f;
+#pragma unroll 4
+    for (int i = 0; i < limit; i += 32) a = __fmaf_rn(x[i + 8 * g + l], x[i + 8 * g + l], a);
+    int i = limit;
+    for (; i + 8 <= n; i += 8)
+        if (g == 0) a = __fmaf_rn(x[i + l], x[i + l], a);
+    // per lane: (a0 + a1) + (a2 + a3)
+    const float a1 = __shfl_sync(0xffffffffu, a, 8 + l);
+    const float a2 = __shfl_sync(0xffffffffu, a, 16 + l);
+    const float a3 = __shfl_sync(0xffffffffu, a, 24 + l);
+    const float s = __fadd_rn(__fadd_rn(a, a1), __fadd_rn(a2, a3));  // valid in lanes 0..7
+    const float s_hi = __shfl_sync(0xffffffffu, s, (l & 3) + 4);
+    const float lo = __fadd_rn(s, s_hi);  // lanes 0..3: lo_l = s_l + s_{l+4}
+    const float lo0 = __shfl_sync(0xffffffffu, lo, 0), lo1 = __shfl_sync(0xffffffffu, lo, 1);
+    const float lo2 = __shfl_sync(0xffffffffu, lo, 2), lo3 = __shfl_sync(0xffffffffu, lo, 3);
+    float r = __fadd_rn(__fadd_rn(lo0, lo1), __fadd_rn(lo2, lo3));
+    for (; i < n; ++i) r = __fadd_rn(r, __fmul_rn(x[i], x[i]));
+    return r;
+}
+
+// add_rms_norm's sum (math_ops.cpp:1148-1166): one 8-lane accumulator, lane l
+// takes v[8 i + l] by FMA; the 8 -> 4 -> 1 tree; then ss += v * v over the tail.
+__device__ float sumsq_one_acc(const float* __restrict__ v, int n) {
+    const int l = threadIdx.x & 7;
+    const int full = n - (n % 8);
+    float a = 0.0f;
+#pragma unroll 8
+    for (int i = 0; i < full; i += 8) a = __fmaf_rn(v[i + l], v[i + l], a);
+    const float a_hi = __shfl_sync(0xffffffffu, a, (l & 3) + 4);
+    const float lo = __fadd_rn(a, a_hi);
+    const float lo0 = __shfl_sync(0xffffffffu, lo, 0), lo1 = __shfl_sync(0xffffffffu, lo, 1);
+    const float lo2 = __shfl_sync(0xffffffffu, lo, 2), lo3 = __shfl_sync(0xffffffffu, lo, 3);
+    float r = __fadd_rn(__fadd_rn(lo0, lo1), __fadd_rn(lo2, lo3));
+    for (int i = full; i < n; ++i) r = __fadd_rn(r, __fmul_rn(v[i], v[i]));
+    return r;
+}
+
+__device__ __forceinline__ float rms_scale(float ss, int n, float eps) {
+    return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)n), eps)));
+}
+
+// norm_apply_zc: out = (in * s) * (1 + w), vector body and scalar tail alike.
+// in and out may be the same row (each element is read and written by one thread).
+__device__ __forceinline__ void apply_zc(const float* in, const float* __restrict__ w, float* out, float s, int n) {
+    for (int i = threadIdx.x; i < n; i += blockDim.x) out[i] = __fmul_rn(__fmul_rn(in[i], s), __fadd_rn(1.0f, w[i]));
+}
+
+// One CTA per row. Rows up to kStageFloats are first staged in shared memory
+// with coalesced loads, so the ordered accumulation chains read on-chip data.
+__global__ void __launch_bounds__(kThreads) rms_norm_kernel(const float* x, const float* __restrict__ w, float* y,
+                                                            int size, float eps) {
+    extern __shared__ float stage[];
+    __shared__ float s_scale;
+    const float* xr = x + (int64_t)blockIdx.x * size;
+    if (size <= kStageFloats) {
+        for (int i = threadIdx.x; i < size; i += blockDim.x) stage[i] = xr[i];
+        __syncthreads();
+        xr = stage;
+    }
+    if (threadIdx.x < 32) {
+        const float ss = sumsq_ref(xr, size);
+        if (threadIdx.x == 0) s_scale = rms_scale(ss, size, eps);
+    }
+    __syncthreads();
+    apply_zc(xr, w, y + (int64_t)blockIdx.x * size, s_scale, size);
+}
+
+// One CTA per row: residual += delta (stored), then out = rms_norm(residual).
+__global__ void __launch_bounds__(kThreads) add_rms_norm_kernel(float* res, const float* __restrict__ delta,
+                                                                const float* __restrict__ w, float* out, int size,
+                                                                float eps) {
+    extern __shared__ float stage[];
+    __shared__ float s_scale;
+    float* rr = res + (int64_t)blockIdx.x * size;
+    const float* dr = delta + (int64_t)blockIdx.x * size;
+    const bool staged = size <= kStageFloats;
+    for (int i = threadIdx.x; i < size; i += blockDim.x) {
+        const float v = __fadd_rn(rr[i], dr[i]);
+        rr[i] = v;
+        if (staged) stage[i] = v;
+    }
+    __syncthreads();  // the row's sums are visible to warp 0
+    const float* v = staged ? stage : rr;
+    if (threadIdx.x < 32) {
+        const float ss = sumsq_one_acc(v, size);
+        if (threadIdx.x == 0) s_scale = rms_scale(ss, size, eps);
+    }
+    __syncthreads();
+    apply_zc(v, w, out + (int64_t)blockIdx.x * size, s_scale, size);
+}
+
+// a = (x / (1 + exp(-x))) * b with exp evaluated in double and rounded once.
+__global__ void __launch_bounds__(kThreads) silu_mul_kernel(float* __restrict__ a, const float* __restrict__ b,
+                                                            int64_t n) {
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+        const float x = a[i];
+        const float e = (float)exp(-(double)x);
+        a[i] = __fmul_rn(__fdiv_rn(x, __fadd_rn(1.0f, e)), b[i]);
+    }
+}
+
+// t [tokens][heads][head_dim]; cos/sin [tokens][rotary_dim / 2].
+__global__ void __launch_bounds__(kThreads) rope_neox_kernel(float* __restrict__ t, const float* __restrict__ ct,
+                                                             const float* __restrict__ st, int heads, int head_dim,
+                                                             int half) {
+    const int tok = blockIdx.y;
+    const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (idx >= (int64_t)heads * half) return;
+    const int h = (int)(idx / half), i = (int)(idx % half);
+    float* hd = t + ((int64_t)tok * heads + h) * head_dim;
+    const float c = ct[(int64_t)tok * half + i], s = st[(int64_t)tok * half + i];
+    const float x1 = hd[i], x2 = hd[i + half];
+    hd[i] = __fsub_rn(__fmul_rn(x1, c), __fmul_rn(x2, s));
+    hd[i + half] = __fadd_rn(__fmul_rn(x2, c), __fmul_rn(x1, s));
+}
+
+}  // namespace
+}  // namespace qlm
+
+namespace qlm_internal {
+void set_last_error(const std::string& msg);
+}
+
+namespace {
+
+int layer_fail(int code, const char* msg) {
+    qlm_internal::set_last_error(msg);
+    return code;
+}
+
+int launched(const char* what) {
+    const cudaError_t e = cudaGetLastError();
+    if (e == cudaSuccess) return QLM_OK;
+    qlm_internal::set_last_error(std::string(what) + ": " + cudaGetErrorString(e));
+    return QLM_ERR_CUDA;
+}
+
+}  // namespace
+
+extern "C" {
+
+int qlm_rms_norm(const float* x, const float* w, float* y, int rows, int size, float eps, void* stream) {
+    if (!x || !w || !y) return layer_fail(QLM_ERR_INVALID_ARG, "NULL argument");
+    if (rows <= 0 || size <= 0) return layer_fail(QLM_ERR_INVALID_ARG, "rows and size must be positive");
+    const size_t smem = size <= qlm::kStageFloats ? (size_t)size * sizeof(float) : 0;
+    qlm::rms_norm_kernel<<<rows, qlm::kThreads, smem, static_cast<cudaStream_t>(stream)>>>(x, w, y, size, eps);
+    return launched("rms_norm launch");
+}
+
+int qlm_add_rms_norm(float* residual, const float* delta, const float* w, float* out, int rows, int size, float eps,
+                     void* stream) {
+    if (!residual || !delta || !w || !out) return layer_fail(QLM_ERR_INVALID_ARG, "NULL argument");
+    if (rows <= 0 || size <= 0) return layer_fail(QLM_ERR_INVALID_ARG, "rows and size must be positive");
+    const size_t smem = size <= qlm::kStageFloats ? (size_t)size * sizeof(float) : 0;
+    qlm::add_rms_norm_kernel<<<rows, qlm::kThreads, smem, static_cast<cudaStream_t>(stream)>>>(residual, delta, w,
+                                                                                             out, size, eps);
+    return launched("add_rms_norm launch");
+}
+
+int qlm_silu_mul(float* a, const float* b, int64_t n, void* stream) {
+    if (!a || !b) return layer_fail(QLM_ERR_INVALID_ARG, "NULL argument");
+    if (n <= 0) return layer_fail(QLM_ERR_INVALID_ARG, "n must be positive");
+    int64_t blocks = (n + qlm::kThreads - 1) / qlm::kThreads;
+    if (blocks > 148 * 64) blocks = 148 * 64;
+    qlm::silu_mul_kernel<<<(unsigned)blocks, qlm::kThreads, 0, static_cast<cudaStream_t>(stream)>>>(a, b, n);
+    return launched("silu_mul launch");
+}
+
+int qlm_rope_neox(float* t, int num_tokens, int num_heads, int head_dim, int rotary_dim, const float* cos_tab,
+                  const float* sin_tab, void* stream) {
+    if (!t || !cos_tab || !sin_tab) return layer_fail(QLM_ERR_INVALID_ARG, "NULL argument");
+    if (num_tokens <= 0 || num_heads <= 0 || head_dim <= 0 || rotary_dim < 2 || rotary_dim > head_dim ||
+        rotary_dim % 2 || num_tokens > 65535)
+        return layer_fail(QLM_ERR_INVALID_ARG, "bad RoPE shape");
+    const int half = rotary_dim / 2;
+    const int64_t per_tok = (int64_t)num_heads * half;
+    const dim3 grid((unsigned)((per_tok + qlm::kThreads - 1) / qlm::kThreads), (unsigned)num_tokens);
+    qlm::rope_neox_kernel<<<grid, qlm::kThreads, 0, static_cast<cudaStream_t>(stream)>>>(t, cos_tab, sin_tab,
+                                                                                       num_heads, head_dim, half);
+    return launched("rope_neox launch");
+}
+
+int qlm_rope_neox_tables(int pos0, int num_tokens, float rope_theta, int rotary_dim, float* cos_out, float* sin_out) {
+    if (!cos_out || !sin_out) return layer_fail(QLM_ERR_INVALID_ARG, "NULL argument");
+    if (num_tokens <= 0 || rotary_dim < 2 || rotary_dim % 2 || pos0 < 0)
+        return layer_fail(QLM_ERR_INVALID_ARG, "bad RoPE table shape");
+    const int half = rotary_dim / 2;
+    for (int tok = 0; tok < num_tokens; ++tok) {
+        const int pos = pos0 + tok;
+        for (int i = 0; i < half; ++i) {
+            // The reference's float expressions (math_ops.cpp:1260-1270), same libm calls.
+            const float inv_freq = 1.0f / std::pow(rope_theta, (2.0f * i) / rotary_dim);
+            const float angle = pos * inv_freq;
+            cos_out[(size_t)tok * half + i] = std::cos(angle);
+            sin_out[(size_t)tok * half + i] = std::sin(angle);
+        }
+    }
+    return QLM_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,119 @@
+"""Device layer ops against QuickLM's own functions (oracle/_ref build):
+rms_norm, add_rms_norm and the NeoX RoPE rotation bit-identical; silu_mul
+within 2 ulp (exp is evaluated differently on the device: a 1-ulp difference
+in exp can move 1 + e, the quotient and the product by one rounding each),
+with equal NaN/Inf behaviour."""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+from tests.conftest import bits_equal
+
+pytestmark = pytest.mark.gpu
+
+# hidden sizes of the configs (1024, 2560), one with an 8-wide remainder
+# (1000 = 31*32 + 8), one with a scalar tail (1003), a tiny one (7), 4096
+SIZES = [1024, 2560, 1000, 1003, 7, 4096]
+
+
+@pytest.fixture(scope="module")
+def q(qlm_lib, cuda_device):
+    import quicklm_b200
+    return quicklm_b200
+
+
+def _rows(rng, rows, size, special):
+    x = rng.standard_normal((rows, size)).astype(np.float32)
+    if special == "scaled":
+        x *= (10.0 ** rng.integers(-20, 20, size=(rows, 1))).astype(np.float32)
+    elif special == "zeros":
+        x[:] = 0.0
+    elif special == "nan":
+        x[0, size // 2] = np.nan
+    return x
+
+
+@pytest.mark.parametrize("size", SIZES)
+@pytest.mark.parametrize("rows", [1, 3, 64])
+@pytest.mark.parametrize("special", [None, "scaled", "zeros", "nan"])
+def test_rms_norm_bit_exact(q, refcpu, size, rows, special):
+    import torch
+    rng = np.random.default_rng(size * 31 + rows)
+    x = _rows(rng, rows, size, special)
+    w = (rng.standard_normal(size) * 0.1).astype(np.float32)
+    eps = 1e-6
+    y_ref = refcpu.rms_norm(x, w, eps)
+    xd = torch.from_numpy(x).cuda()
+    y = q.rms_norm(xd, torch.from_numpy(w).cuda(), eps)
+    assert bits_equal(y.cpu().numpy(), y_ref)
+    q.rms_norm(xd, torch.from_numpy(w).cuda(), eps, out=xd)  # in place
+    assert bits_equal(xd.cpu().numpy(), y_ref)
+
+
+@pytest.mark.parametrize("size", SIZES)
+@pytest.mark.parametrize("rows", [1, 5])
+@pytest.mark.parametrize("special", [None, "scaled", "nan"])
+def test_add_rms_norm_bit_exact(q, refcpu, size, rows, special):
+    import torch
+    rng = np.random.default_rng(size * 7 + rows)
+    r = _rows(rng, rows, size, special)
+    d = rng.standard_normal((rows, size)).astype(np.float32)
+    w = (rng.standard_normal(size) * 0.1).astype(np.float32)
+    eps = 1e-6
+    r_ref, o_ref = refcpu.add_rms_norm(r, d, w, eps)
+    rd = torch.from_numpy(r).cuda()
+    o = q.add_rms_norm(rd, torch.from_numpy(d).cuda(), torch.from_numpy(w).cuda(), eps)
+    assert bits_equal(rd.cpu().numpy(), r_ref)
+    assert bits_equal(o.cpu().numpy(), o_ref)
+
+
+def _ulp_diff(a, b):
+    ai = a.view(np.int32).astype(np.int64)
+    bi = b.view(np.int32).astype(np.int64)
+    ai = np.where(ai < 0, -(ai & 0x7FFFFFFF), ai)
+    bi = np.where(bi < 0, -(bi & 0x7FFFFFFF), bi)
+    return np.abs(ai - bi)
+
+
+def test_silu_mul_within_two_ulp(q, refcpu):
+    import torch
+    rng = np.random.default_rng(3)
+    n = 1 << 20
+    a = (rng.standard_normal(n) * 4).astype(np.float32)
+    a[:8] = [0.0, -0.0, np.inf, -np.inf, np.nan, 88.0, -88.0, -104.0]
+    b = rng.standard_normal(n).astype(np.float32)
+    ref = refcpu.silu_mul(a, b)
+    ad = torch.from_numpy(a).cuda()
+    q.silu_mul(ad, torch.from_numpy(b).cuda())
+    got = ad.cpu().numpy()
+    nan_ref, nan_got = np.isnan(ref), np.isnan(got)
+    assert np.array_equal(nan_ref, nan_got)
+    ok = ~nan_ref
+    assert _ulp_diff(got[ok], ref[ok]).max() <= 2
+    # the device and the host agree exactly on the vast majority of inputs
+    assert (_ulp_diff(got[ok], ref[ok]) == 0).mean() > 0.99
+
+
+@pytest.mark.parametrize("theta,heads,head_dim,rotary_dim", [(10000000.0, 16, 256, 64), (10000.0, 4, 64, 64),
+                                                               (1e6, 8, 128, 32)])
+def test_rope_neox_bit_exact(q, refcpu, theta, heads, head_dim, rotary_dim):
+    import torch
+    rng = np.random.default_rng(heads * head_dim)
+    pos0, n_tok = 1000, 7
+    t = rng.standard_normal((n_tok, heads, head_dim)).astype(np.float32)
+    ref = np.stack([refcpu.rope_neox(t[i], pos0 + i, theta, rotary_dim) for i in range(n_tok)])
+    td = torch.from_numpy(t).cuda()
+    q.rope_neox(td, pos0, theta, rotary_dim)
+    assert bits_equal(td.cpu().numpy(), ref)
+
+
+def test_layer_arg_checks(q):
+    import torch
+    x = torch.zeros((2, 8), device="cuda")
+    with pytest.raises(q.QlmError):
+        q.rms_norm(x, torch.zeros(3, device="cuda"), 1e-6)  # not whole rows
+    with pytest.raises(q.QlmError):
+        q.silu_mul(x, torch.zeros(3, device="cuda"))
+    with pytest.raises(q.QlmError):
+        q.rope_neox(torch.zeros((1, 2, 8), device="cuda"), 0, 1e4, 10)  # rotary_dim > head_dim
