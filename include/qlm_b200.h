@@ -161,7 +161,17 @@ int qlm_store_info(const char* path, const char* name, int* bits, int64_t* rows,
  *                     with tables from qlm_rope_neox_tables.
  *   qlm_rope_neox_tables  host: cos/sin for positions pos0 .. pos0+num_tokens-1,
  *                     computed with the reference's own float expressions and
- *                     libm calls (math_ops.cpp:1256-1271). */
+ *                     libm calls (math_ops.cpp:1256-1271).
+ *   qlm_silu          x = x / (1 + exp(-x)): math::silu (math_ops.cpp:1076-1084)
+ *                     and the gated-delta-net conv activation (model/attention.cpp
+ *                     :452-457); within 2 ulp, like qlm_silu_mul.
+ *   qlm_conv1d_update_tapmajor  one depthwise causal-conv step on a tap-major
+ *                     ring: math::causal_conv1d_update_tapmajor (math_ops.cpp
+ *                     :1321-1366); the caller advances oldest_tap as the model
+ *                     does (attention.cpp:444-448). Bit-identical.
+ *   qlm_l2norm_heads  x_h /= sqrt(sumsq(x_h) + eps) per head row: the q/k
+ *                     normalisation of the gated-delta-net step (attention.cpp
+ *                     :462-470). Bit-identical. */
 int qlm_rms_norm(const float* x, const float* w, float* y, int rows, int size, float eps, void* stream);
 int qlm_add_rms_norm(float* residual, const float* delta, const float* w, float* out, int rows, int size, float eps,
                      void* stream);
@@ -169,6 +179,10 @@ int qlm_silu_mul(float* a, const float* b, int64_t n, void* stream);
 int qlm_rope_neox(float* t, int num_tokens, int num_heads, int head_dim, int rotary_dim, const float* cos_tab,
                   const float* sin_tab, void* stream);
 int qlm_rope_neox_tables(int pos0, int num_tokens, float rope_theta, int rotary_dim, float* cos_out, float* sin_out);
+int qlm_silu(float* x, int64_t n, void* stream);
+int qlm_conv1d_update_tapmajor(const float* input, float* state, int oldest_tap, const float* weight_t,
+                               float* output, int conv_dim, int kernel_size, void* stream);
+int qlm_l2norm_heads(float* x, int heads, int head_dim, float eps, void* stream);
 
 /* Release a handle and its device memory (NULL is a no-op). */
 void qlm_weight_free(qlm_w8* w);

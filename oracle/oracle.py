@@ -72,6 +72,9 @@ class RefCPU:
         lib.qlmref_add_rms_norm.argtypes = [_P, _P, _P, _P, _I, _I, _F]
         lib.qlmref_silu_mul.argtypes = [_P, _P, _I]
         lib.qlmref_rope_neox.argtypes = [_P, _I, _I, _I, _F, _I]
+        lib.qlmref_silu.argtypes = [_P, _I]
+        lib.qlmref_conv1d_update_tapmajor.argtypes = [_P, _P, _I, _P, _P, _I, _I]
+        lib.qlmref_l2norm_heads.argtypes = [_P, _I, _I, _F]
         self.lib = lib
         self.threads = 1
 
@@ -128,6 +131,28 @@ class RefCPU:
         b = np.ascontiguousarray(b, np.float32).ravel()
         self._rc(self.lib.qlmref_silu_mul(_ptr(a), _ptr(b), a.size))
         return a
+
+    def silu(self, x: np.ndarray) -> np.ndarray:
+        """math::silu (a copy)."""
+        x = np.array(x, np.float32, copy=True).ravel()
+        self._rc(self.lib.qlmref_silu(_ptr(x), x.size))
+        return x
+
+    def conv1d_update_tapmajor(self, inp, state, oldest_tap: int, weight_t):
+        """math::causal_conv1d_update_tapmajor -> (output, updated state copy)."""
+        inp = np.ascontiguousarray(inp, np.float32)
+        st = np.array(state, np.float32, copy=True, order="C")
+        wt = np.ascontiguousarray(weight_t, np.float32)
+        out = np.empty_like(inp)
+        self._rc(self.lib.qlmref_conv1d_update_tapmajor(_ptr(inp), _ptr(st), int(oldest_tap), _ptr(wt), _ptr(out),
+                                                        inp.size, wt.shape[0]))
+        return out, st
+
+    def l2norm_heads(self, x: np.ndarray, eps: float) -> np.ndarray:
+        """The gated-delta-net q/k normalisation on x [heads, head_dim] (a copy)."""
+        x = np.array(x, np.float32, copy=True, order="C")
+        self._rc(self.lib.qlmref_l2norm_heads(_ptr(x), x.shape[0], x.shape[1], ctypes.c_float(eps)))
+        return x
 
     def rope_neox(self, t: np.ndarray, pos: int, theta: float, rotary_dim: int) -> np.ndarray:
         """math::apply_rope_neox on one token's t [num_heads, head_dim] (a copy)."""

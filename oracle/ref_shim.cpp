@@ -34,6 +34,7 @@
 #include "safetensors.hpp"
 
 #include <chrono>
+#include <cmath>
 #include <cstdint>
 #include <cstdio>
 #include <cstdlib>
@@ -239,6 +240,32 @@ int qlmref_silu_mul(float* a, const float* b, int n) {
     Tensor A(std::vector<int>{n}, a);
     Tensor B(std::vector<int>{n}, const_cast<float*>(b));
     math::silu_mul(A, B);
+    return 0;
+}
+
+int qlmref_silu(float* x, int n) {
+    if (!x || n <= 0) return fail("bad args");
+    Tensor X(std::vector<int>{n}, x);
+    math::silu(X, X);
+    return 0;
+}
+
+int qlmref_conv1d_update_tapmajor(const float* input, float* state, int oldest_tap, const float* weight_t,
+                                  float* output, int conv_dim, int kernel_size) {
+    if (!input || !state || !weight_t || !output) return fail("bad args");
+    math::causal_conv1d_update_tapmajor(input, state, oldest_tap, weight_t, output, conv_dim, kernel_size);
+    return 0;
+}
+
+// The gated-delta-net q/k normalisation as the model writes it
+// (model/attention.cpp:466-469), through the reference's sumsq / vec_div_inplace.
+int qlmref_l2norm_heads(float* x, int heads, int head_dim, float eps) {
+    if (!x || heads <= 0 || head_dim <= 0) return fail("bad args");
+    for (int h = 0; h < heads; ++h) {
+        float* xh = x + (size_t)h * head_dim;
+        const float n = std::sqrt(math::sumsq(xh, head_dim) + eps);
+        math::vec_div_inplace(xh, n, head_dim);
+    }
     return 0;
 }
 

@@ -25,7 +25,7 @@ import numpy as np
 
 __all__ = ["QlmError", "Int8Weight", "matmul", "matmul_grouped", "argmax", "load", "LIB_PATH", "EXACT", "TENSOR", "HOST_IO", "SYNC",
            "BLOCK", "Comm", "shard_rows", "matmul_allgather", "save", "store_info", "rms_norm", "add_rms_norm",
-           "silu_mul", "rope_neox", "rope_neox_tables"]
+           "silu_mul", "rope_neox", "rope_neox_tables", "silu", "conv1d_update_tapmajor", "l2norm_heads"]
 
 LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "lib", "libqlm_b200.so")
 BLOCK = 32
@@ -40,7 +40,8 @@ ABI_SYMBOLS = (
     "qlm_comm_create", "qlm_comm_connect", "qlm_comm_free", "qlm_linear_int8_allgather", "qlm_argmax_f32",
     "qlm_linear_int8_grouped", "qlm_weight_quantize_upload_q4", "qlm_weight_export_int4", "qlm_weight_bits",
     "qlm_weight_import_int4", "qlm_store_save", "qlm_store_load", "qlm_store_info", "qlm_rms_norm",
-    "qlm_add_rms_norm", "qlm_silu_mul", "qlm_rope_neox", "qlm_rope_neox_tables",
+    "qlm_add_rms_norm", "qlm_silu_mul", "qlm_rope_neox", "qlm_rope_neox_tables", "qlm_silu",
+    "qlm_conv1d_update_tapmajor", "qlm_l2norm_heads",
 )
 
 _STATUS = {0: "OK", 1: "INVALID_ARG", 2: "CUDA", 3: "OUT_OF_MEMORY", 4: "UNSUPPORTED", 5: "TIMEOUT", 6: "NCCL",
@@ -86,6 +87,9 @@ def load(path: str = LIB_PATH):
     lib.qlm_silu_mul.argtypes = [P, P, L, P]
     lib.qlm_rope_neox.argtypes = [P, I, I, I, I, P, P, P]
     lib.qlm_rope_neox_tables.argtypes = [I, I, F, I, P, P]
+    lib.qlm_silu.argtypes = [P, L, P]
+    lib.qlm_conv1d_update_tapmajor.argtypes = [P, P, I, P, P, I, I, P]
+    lib.qlm_l2norm_heads.argtypes = [P, I, I, F, P]
     lib.qlm_weight_shape.argtypes = [P] + [ctypes.POINTER(I)] * 5
     lib.qlm_weight_bytes.argtypes = [P]
     lib.qlm_weight_bytes.restype = L
@@ -466,6 +470,36 @@ def silu_mul(a, b, stream=None):
         raise QlmError(1, "a and b differ in size")
     _check(load().qlm_silu_mul(a.data_ptr(), b.data_ptr(), a.numel(), _torch_stream(stream)))
     return a
+
+
+def silu(x, stream=None):
+    """x = x / (1 + exp(-x)) in place (math::silu; within 2 ulp of the reference)."""
+    _dev_f32(x, "x")
+    _check(load().qlm_silu(x.data_ptr(), x.numel(), _torch_stream(stream)))
+    return x
+
+
+def conv1d_update_tapmajor(inp, state, oldest_tap: int, weight_t, out=None, stream=None):
+    """One causal-conv step on a tap-major ring: state [ntaps, conv_dim], weight_t
+    [ntaps + 1, conv_dim]; returns out [conv_dim]. The caller advances oldest_tap."""
+    _dev_f32(inp, "input"), _dev_f32(state, "state"), _dev_f32(weight_t, "weight_t")
+    conv_dim = inp.numel()
+    ks = weight_t.shape[0]
+    if weight_t.numel() != ks * conv_dim or state.numel() != (ks - 1) * conv_dim:
+        raise QlmError(1, "state/weight_t shapes do not match the input")
+    out = inp.new_empty(inp.shape) if out is None else _dev_f32(out, "out")
+    _check(load().qlm_conv1d_update_tapmajor(inp.data_ptr(), state.data_ptr(), oldest_tap, weight_t.data_ptr(),
+                                             out.data_ptr(), conv_dim, ks, _torch_stream(stream)))
+    return out
+
+
+def l2norm_heads(x, head_dim: int, eps: float = 1e-6, stream=None):
+    """x_h /= sqrt(sumsq(x_h) + eps) in place for each head row of head_dim."""
+    _dev_f32(x, "x")
+    if x.numel() % head_dim:
+        raise QlmError(1, "x is not a whole number of heads")
+    _check(load().qlm_l2norm_heads(x.data_ptr(), x.numel() // head_dim, head_dim, eps, _torch_stream(stream)))
+    return x
 
 
 def rope_neox_tables(pos0: int, num_tokens: int, theta: float, rotary_dim: int):

@@ -4,8 +4,11 @@
 //
 //   rms_norm      (:1055-1074, sumsq :990-1019, norm_apply_zc :1021-1032)
 //   add_rms_norm  (:1133-1174)
-//   silu_mul      (:1122-1131)
+//   silu_mul      (:1122-1131), silu (:1076-1084)
 //   apply_rope_neox (:1237-1291)
+//   causal_conv1d_update_tapmajor (:1321-1366)
+//   the per-head L2 normalisation of the gated-delta-net step
+//     (src/model/attention.cpp:462-470: sqrt(sumsq + eps), vec_div_inplace)
 //
 // rms_norm, add_rms_norm and the RoPE rotation are bit-identical to the
 // reference (strict build, no contraction): the sums of squares follow its
@@ -141,6 +144,44 @@ __global__ void __launch_bounds__(kThreads) silu_mul_kernel(float* __restrict__ 
     }
 }
 
+// x = x / (1 + exp(-x)), exp as in silu_mul_kernel.
+__global__ void __launch_bounds__(kThreads) silu_kernel(float* __restrict__ x, int64_t n) {
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+        const float v = x[i];
+        x[i] = __fdiv_rn(v, __fadd_rn(1.0f, (float)exp(-(double)v)));
+    }
+}
+
+// Depthwise causal conv step on a tap-major ring (state [ntaps][conv_dim],
+// row (oldest + j) % ntaps is the j-th oldest tap; weight_t [ntaps + 1][conv_dim]):
+// out[c] = (((0 + s_0 w_0) + s_1 w_1) + ...) + in w_last, products and sums
+// rounded separately; the oldest row then takes the input. One thread per channel.
+__global__ void __launch_bounds__(kThreads) conv1d_tapmajor_kernel(const float* __restrict__ in, float* state,
+                                                                   int oldest, const float* __restrict__ wt,
+                                                                   float* __restrict__ out, int conv_dim, int ntaps) {
+    const int c = blockIdx.x * blockDim.x + threadIdx.x;
+    if (c >= conv_dim) return;
+    float sum = 0.0f;
+    for (int j = 0; j < ntaps; ++j) {
+        const int row = (oldest + j) % ntaps;
+        sum = __fadd_rn(sum, __fmul_rn(state[(int64_t)row * conv_dim + c], wt[(int64_t)j * conv_dim + c]));
+    }
+    const float x = in[c];
+    out[c] = __fadd_rn(sum, __fmul_rn(x, wt[(int64_t)ntaps * conv_dim + c]));
+    state[(int64_t)oldest * conv_dim + c] = x;
+}
+
+// x_h /= sqrt(sumsq(x_h) + eps) for each head row (one warp per head).
+__global__ void __launch_bounds__(kThreads) l2norm_heads_kernel(float* x, int heads, int head_dim, float eps) {
+    const int h = blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
+    if (h >= heads) return;  // whole warps
+    float* xh = x + (int64_t)h * head_dim;
+    const float ss = sumsq_ref(xh, head_dim);
+    const float n = __fsqrt_rn(__fadd_rn(ss, eps));
+    __syncwarp();
+    for (int i = threadIdx.x & 31; i < head_dim; i += 32) xh[i] = __fdiv_rn(xh[i], n);
+}
+
 // t [tokens][heads][head_dim]; cos/sin [tokens][rotary_dim / 2].
 __global__ void __launch_bounds__(kThreads) rope_neox_kernel(float* __restrict__ t, const float* __restrict__ ct,
                                                              const float* __restrict__ st, int heads, int head_dim,
@@ -220,6 +261,35 @@ int qlm_rope_neox(float* t, int num_tokens, int num_heads, int head_dim, int rot
     qlm::rope_neox_kernel<<<grid, qlm::kThreads, 0, static_cast<cudaStream_t>(stream)>>>(t, cos_tab, sin_tab,
                                                                                        num_heads, head_dim, half);
     return launched("rope_neox launch");
+}
+
+int qlm_silu(float* x, int64_t n, void* stream) {
+    if (!x) return layer_fail(QLM_ERR_INVALID_ARG, "NULL argument");
+    if (n <= 0) return layer_fail(QLM_ERR_INVALID_ARG, "n must be positive");
+    int64_t blocks = (n + qlm::kThreads - 1) / qlm::kThreads;
+    if (blocks > 148 * 64) blocks = 148 * 64;
+    qlm::silu_kernel<<<(unsigned)blocks, qlm::kThreads, 0, static_cast<cudaStream_t>(stream)>>>(x, n);
+    return launched("silu launch");
+}
+
+int qlm_conv1d_update_tapmajor(const float* input, float* state, int oldest_tap, const float* weight_t,
+                               float* output, int conv_dim, int kernel_size, void* stream) {
+    if (!input || !state || !weight_t || !output) return layer_fail(QLM_ERR_INVALID_ARG, "NULL argument");
+    if (conv_dim <= 0 || kernel_size < 2 || oldest_tap < 0 || oldest_tap >= kernel_size - 1)
+        return layer_fail(QLM_ERR_INVALID_ARG, "bad conv1d shape or ring position");
+    qlm::conv1d_tapmajor_kernel<<<(conv_dim + qlm::kThreads - 1) / qlm::kThreads, qlm::kThreads, 0,
+                                  static_cast<cudaStream_t>(stream)>>>(input, state, oldest_tap, weight_t, output,
+                                                                       conv_dim, kernel_size - 1);
+    return launched("conv1d launch");
+}
+
+int qlm_l2norm_heads(float* x, int heads, int head_dim, float eps, void* stream) {
+    if (!x) return layer_fail(QLM_ERR_INVALID_ARG, "NULL argument");
+    if (heads <= 0 || head_dim <= 0) return layer_fail(QLM_ERR_INVALID_ARG, "heads and head_dim must be positive");
+    const int per_cta = qlm::kThreads / 32;
+    qlm::l2norm_heads_kernel<<<(heads + per_cta - 1) / per_cta, qlm::kThreads, 0,
+                               static_cast<cudaStream_t>(stream)>>>(x, heads, head_dim, eps);
+    return launched("l2norm launch");
 }
 
 int qlm_rope_neox_tables(int pos0, int num_tokens, float rope_theta, int rotary_dim, float* cos_out, float* sin_out) {

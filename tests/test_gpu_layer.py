@@ -117,3 +117,49 @@ def test_layer_arg_checks(q):
         q.silu_mul(x, torch.zeros(3, device="cuda"))
     with pytest.raises(q.QlmError):
         q.rope_neox(torch.zeros((1, 2, 8), device="cuda"), 0, 1e4, 10)  # rotary_dim > head_dim
+
+
+def test_silu_within_two_ulp(q, refcpu):
+    import torch
+    rng = np.random.default_rng(13)
+    x = (rng.standard_normal(1 << 18) * 4).astype(np.float32)
+    x[:6] = [0.0, -0.0, np.inf, -np.inf, np.nan, -104.0]
+    ref = refcpu.silu(x)
+    xd = torch.from_numpy(x).cuda()
+    got = q.silu(xd).cpu().numpy()
+    assert np.array_equal(np.isnan(ref), np.isnan(got))
+    ok = ~np.isnan(ref)
+    assert _ulp_diff(got[ok], ref[ok]).max() <= 2
+    assert (_ulp_diff(got[ok], ref[ok]) == 0).mean() > 0.99
+
+
+@pytest.mark.parametrize("conv_dim,ks", [(6144, 4), (1000, 4), (37, 2), (512, 5)])
+def test_conv1d_tapmajor_bit_exact(q, refcpu, conv_dim, ks):
+    """Several steps around the ring, state carried on both sides."""
+    import torch
+    rng = np.random.default_rng(conv_dim + ks)
+    ntaps = ks - 1
+    wt = rng.standard_normal((ks, conv_dim)).astype(np.float32)
+    st_ref = rng.standard_normal((ntaps, conv_dim)).astype(np.float32)
+    st_dev = torch.from_numpy(st_ref.copy()).cuda()
+    wt_dev = torch.from_numpy(wt).cuda()
+    ring = 0
+    for step in range(2 * ks):
+        x = rng.standard_normal(conv_dim).astype(np.float32)
+        y_ref, st_ref = refcpu.conv1d_update_tapmajor(x, st_ref, ring, wt)
+        y = q.conv1d_update_tapmajor(torch.from_numpy(x).cuda(), st_dev, ring, wt_dev)
+        assert bits_equal(y.cpu().numpy(), y_ref), step
+        assert bits_equal(st_dev.cpu().numpy(), st_ref), step
+        ring = (ring + 1) % ntaps
+
+
+@pytest.mark.parametrize("heads,head_dim", [(16, 128), (32, 128), (3, 7), (5, 1000)])
+def test_l2norm_heads_bit_exact(q, refcpu, heads, head_dim):
+    import torch
+    rng = np.random.default_rng(heads * head_dim)
+    x = rng.standard_normal((heads, head_dim)).astype(np.float32)
+    x[0] *= 1e-4
+    ref = refcpu.l2norm_heads(x, 1e-6)
+    xd = torch.from_numpy(x).cuda()
+    q.l2norm_heads(xd, head_dim, 1e-6)
+    assert bits_equal(xd.cpu().numpy(), ref)
