@@ -171,7 +171,15 @@ int qlm_store_info(const char* path, const char* name, int* bits, int64_t* rows,
  *                     does (attention.cpp:444-448). Bit-identical.
  *   qlm_l2norm_heads  x_h /= sqrt(sumsq(x_h) + eps) per head row: the q/k
  *                     normalisation of the gated-delta-net step (attention.cpp
- *                     :462-470). Bit-identical. */
+ *                     :462-470). Bit-identical.
+ *   qlm_gdn_gates     per-head decay exp(-exp(A_log) softplus(a + dt_bias)) and
+ *                     write gate sigmoid(b) (attention.cpp:472-482); libm calls
+ *                     evaluated in double and rounded once (a few ulp).
+ *   qlm_gdn_recurrence the gated delta rule for all heads: state [heads][d][d]
+ *                     updated in place, out [heads][d] (attention.cpp:498-560).
+ *                     Bit-identical given the same inputs.
+ *   qlm_rms_norm_gain rms_norm with a plain gain w (the head-wise output norm,
+ *                     attention.cpp:573-577). Bit-identical. */
 int qlm_rms_norm(const float* x, const float* w, float* y, int rows, int size, float eps, void* stream);
 int qlm_add_rms_norm(float* residual, const float* delta, const float* w, float* out, int rows, int size, float eps,
                      void* stream);
@@ -183,6 +191,11 @@ int qlm_silu(float* x, int64_t n, void* stream);
 int qlm_conv1d_update_tapmajor(const float* input, float* state, int oldest_tap, const float* weight_t,
                                float* output, int conv_dim, int kernel_size, void* stream);
 int qlm_l2norm_heads(float* x, int heads, int head_dim, float eps, void* stream);
+int qlm_gdn_gates(const float* a_raw, const float* b_raw, const float* A_log, const float* dt_bias, float* decay,
+                  float* beta, int heads, void* stream);
+int qlm_gdn_recurrence(float* state, const float* q, const float* k, const float* v, const float* decay,
+                       const float* beta, float* out, int heads, int head_dim, void* stream);
+int qlm_rms_norm_gain(const float* x, const float* w, float* y, int rows, int size, float eps, void* stream);
 
 /* Release a handle and its device memory (NULL is a no-op). */
 void qlm_weight_free(qlm_w8* w);

@@ -75,6 +75,12 @@ class RefCPU:
         lib.qlmref_silu.argtypes = [_P, _I]
         lib.qlmref_conv1d_update_tapmajor.argtypes = [_P, _P, _I, _P, _P, _I, _I]
         lib.qlmref_l2norm_heads.argtypes = [_P, _I, _I, _F]
+        lib.qlmref_gdn_recurrence.argtypes = [_P, _P, _P, _P, _P, _P, _I, _I, _P]
+        lib.qlmref_gdn_gates.argtypes = [_P, _P, _P, _P, _P, _P, _I]
+        lib.qlmref_rms_norm_gain.argtypes = [_P, _P, _P, _I, _I, _F]
+        gdn = [_I, _I, _I, _I, _I] + [_P] * 9 + [_I, _P, _P]
+        lib.qlmref_gdn_module_steps.argtypes = gdn
+        lib.qlmref_gdn_restated_steps.argtypes = gdn
         self.lib = lib
         self.threads = 1
 
@@ -153,6 +159,49 @@ class RefCPU:
         x = np.array(x, np.float32, copy=True, order="C")
         self._rc(self.lib.qlmref_l2norm_heads(_ptr(x), x.shape[0], x.shape[1], ctypes.c_float(eps)))
         return x
+
+    def gdn_recurrence(self, state, q, k, v, dec, beta):
+        """The restated delta-rule recurrence (model/attention.cpp:498-560) ->
+        (out [heads, d], updated state copy)."""
+        st = np.array(state, np.float32, copy=True, order="C")
+        heads, d = st.shape[0], st.shape[1]
+        arrs = [np.ascontiguousarray(a, np.float32) for a in (q, k, v, dec, beta)]
+        out = np.empty((heads, d), np.float32)
+        self._rc(self.lib.qlmref_gdn_recurrence(_ptr(st), *[_ptr(a) for a in arrs], heads, d, _ptr(out)))
+        return out, st
+
+    def gdn_gates(self, a_raw, b_raw, A_log, dt_bias):
+        """The restated per-head gates (model/attention.cpp:472-482) -> (decay, beta)."""
+        arrs = [np.ascontiguousarray(x, np.float32) for x in (a_raw, b_raw, A_log, dt_bias)]
+        heads = arrs[0].size
+        dec = np.empty(heads, np.float32)
+        beta = np.empty(heads, np.float32)
+        self._rc(self.lib.qlmref_gdn_gates(*[_ptr(x) for x in arrs], _ptr(dec), _ptr(beta), heads))
+        return dec, beta
+
+    def rms_norm_gain(self, x: np.ndarray, w: np.ndarray, eps: float) -> np.ndarray:
+        """Head-wise RMSNorm with a plain gain (model/attention.cpp:573-577)."""
+        x = np.ascontiguousarray(x, np.float32)
+        w = np.ascontiguousarray(w, np.float32)
+        y = np.empty_like(x)
+        self._rc(self.lib.qlmref_rms_norm_gain(_ptr(x), _ptr(w), _ptr(y), x.shape[0], x.shape[1], ctypes.c_float(eps)))
+        return y
+
+    def gdn_steps(self, w: dict, inputs: np.ndarray, restated: bool = False) -> np.ndarray:
+        """Qwen3_5GatedDeltaNet decode steps over inputs [steps, hin] with F32
+        weights w (w_qkv, w_z, w_b, w_a, conv_w [3H, ks], norm_w, A_log, dt_bias,
+        w_out): the reference module, or (restated=True) this oracle's restatement."""
+        keys = ("w_qkv", "w_z", "w_b", "w_a", "conv_w", "norm_w", "A_log", "dt_bias", "w_out")
+        a = {k_: np.ascontiguousarray(w[k_], np.float32) for k_ in keys}
+        inputs = np.ascontiguousarray(inputs, np.float32)
+        heads, hin = a["w_b"].shape
+        d = a["norm_w"].size
+        ks = a["conv_w"].shape[1]
+        hout = a["w_out"].shape[0]
+        out = np.empty((inputs.shape[0], hout), np.float32)
+        fn = self.lib.qlmref_gdn_restated_steps if restated else self.lib.qlmref_gdn_module_steps
+        self._rc(fn(hin, heads, d, ks, hout, *[_ptr(a[k_]) for k_ in keys], inputs.shape[0], _ptr(inputs), _ptr(out)))
+        return out
 
     def rope_neox(self, t: np.ndarray, pos: int, theta: float, rotary_dim: int) -> np.ndarray:
         """math::apply_rope_neox on one token's t [num_heads, head_dim] (a copy)."""

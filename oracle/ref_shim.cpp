@@ -29,10 +29,12 @@
 // The reference quantizer only reads safetensors files, so qlmref_quantize
 // writes the matrix to a private temporary file first.
 
+#include "attention.hpp"
 #include "math_ops.hpp"
 #include "model.hpp"
 #include "safetensors.hpp"
 
+#include <algorithm>
 #include <chrono>
 #include <cmath>
 #include <cstdint>
@@ -267,6 +269,171 @@ int qlmref_l2norm_heads(float* x, int heads, int head_dim, float eps) {
         math::vec_div_inplace(xh, n, head_dim);
     }
     return 0;
+}
+
+// ---- gated-delta-net decode step (model/attention.cpp:414-591) ----------------
+//
+// qlmref_gdn_module_steps drives the reference module itself
+// (Qwen3_5GatedDeltaNet::init + forward, seq_len 1) over `steps` tokens.
+// qlmref_gdn_restated_steps is this oracle's restatement of the same step,
+// built on the reference's standalone functions where the model calls them
+// (matmul, causal_conv1d_update_tapmajor, sumsq, vec_div_inplace,
+// norm_apply_gain) and restating the inline parts: the SiLU, the gates
+// (attention.cpp:472-482) and the delta-rule recurrence (qlmref_gdn_recurrence,
+// attention.cpp:498-560). Equal outputs over several steps pin the restated
+// recurrence, which the device kernel is then tested against.
+
+// The recurrence for all heads: state [heads][d][d] row-major, q/k/v [heads][d],
+// dec/beta [heads]; out [heads][d]. The model's 8-wide body uses FMAs, its scalar
+// tail (j >= d - d % 8) separate products and sums.
+int qlmref_gdn_recurrence(float* state, const float* q, const float* k, const float* v, const float* dec,
+                          const float* beta, int heads, int d, float* out) {
+    if (!state || !q || !k || !v || !dec || !beta || !out || heads <= 0 || d <= 0) return fail("bad args");
+    const int d8 = d - d % 8;
+    const float q_scale = 1.0f / std::sqrt(static_cast<float>(d));
+    std::vector<float> kv(d), delta(d);
+    for (int h = 0; h < heads; ++h) {
+        float* S = state + (size_t)h * d * d;
+        const float* qh = q + (size_t)h * d;
+        const float* kh = k + (size_t)h * d;
+        const float* vh = v + (size_t)h * d;
+        float* oh = out + (size_t)h * d;
+        std::fill(kv.begin(), kv.end(), 0.0f);
+        for (int i = 0; i < d; ++i) {
+            float* row = S + (size_t)i * d;
+            for (int j = 0; j < d; ++j) {
+                const float r = row[j] * dec[h];
+                row[j] = r;
+                kv[j] = j < d8 ? std::fma(kh[i], r, kv[j]) : kv[j] + kh[i] * r;
+            }
+        }
+        for (int j = 0; j < d; ++j) delta[j] = vh[j] - kv[j];
+        for (int i = 0; i < d; ++i) {
+            const float s = beta[h] * kh[i];
+            float* row = S + (size_t)i * d;
+            for (int j = 0; j < d; ++j) row[j] = j < d8 ? std::fma(s, delta[j], row[j]) : row[j] + s * delta[j];
+        }
+        for (int j = 0; j < d; ++j) oh[j] = 0.0f;
+        for (int i = 0; i < d; ++i) {
+            const float* row = S + (size_t)i * d;
+            for (int j = 0; j < d; ++j) oh[j] = j < d8 ? std::fma(qh[i], row[j], oh[j]) : oh[j] + qh[i] * row[j];
+        }
+        for (int j = 0; j < d; ++j) oh[j] *= q_scale;
+    }
+    return 0;
+}
+
+// The per-head decay and write gates (model/attention.cpp:472-482).
+int qlmref_gdn_gates(const float* a_raw, const float* b_raw, const float* A_log, const float* dt_bias, float* dec,
+                     float* beta, int heads) {
+    if (!a_raw || !b_raw || !A_log || !dt_bias || !dec || !beta || heads <= 0) return fail("bad args");
+    for (int h = 0; h < heads; ++h) {
+        const float dt_in = a_raw[h] + dt_bias[h];
+        const float sp = (dt_in > 20.0f) ? dt_in : std::log1p(std::exp(dt_in));
+        const float alpha = -std::exp(A_log[h]) * sp;
+        dec[h] = std::exp(alpha);
+        beta[h] = 1.0f / (1.0f + std::exp(-b_raw[h]));
+    }
+    return 0;
+}
+
+// The head-wise output norm with a plain gain (model/attention.cpp:573-577).
+int qlmref_rms_norm_gain(const float* x, const float* w, float* y, int rows, int size, float eps) {
+    if (!x || !w || !y || rows <= 0 || size <= 0) return fail("bad args");
+    for (int r = 0; r < rows; ++r) {
+        const float sc = 1.0f / std::sqrt((math::sumsq(x + (size_t)r * size, size) / size) + eps);
+        math::norm_apply_gain(x + (size_t)r * size, w, y + (size_t)r * size, sc, size);
+    }
+    return 0;
+}
+
+namespace {
+struct GdnWeights {
+    int hin, heads, d, ks, hout;
+    const float *w_qkv, *w_z, *w_b, *w_a, *conv_w, *norm_w, *A_log, *dt_bias, *w_out;
+};
+Tensor owned(const std::vector<int>& shape, const float* src, size_t n) {
+    Tensor t(shape);
+    std::memcpy(t.data, src, n * sizeof(float));
+    return t;
+}
+}  // namespace
+
+int qlmref_gdn_module_steps(int hin, int heads, int d, int ks, int hout, const float* w_qkv, const float* w_z,
+                            const float* w_b, const float* w_a, const float* conv_w, const float* norm_w,
+                            const float* A_log, const float* dt_bias, const float* w_out, int steps,
+                            const float* inputs, float* outputs) {
+    if (steps <= 0 || !inputs || !outputs) return fail("bad args");
+    try {
+        const int H = heads * d;
+        Qwen3_5GatedDeltaNet m;
+        m.init(owned({3 * H, hin}, w_qkv, (size_t)3 * H * hin), owned({H, hin}, w_z, (size_t)H * hin),
+               owned({heads, hin}, w_b, (size_t)heads * hin), owned({heads, hin}, w_a, (size_t)heads * hin),
+               owned({3 * H, 1, ks}, conv_w, (size_t)3 * H * ks), owned({d}, norm_w, (size_t)d),
+               owned({heads}, A_log, (size_t)heads), owned({heads}, dt_bias, (size_t)heads),
+               owned({hout, H}, w_out, (size_t)hout * H), heads, d, steps);
+        m.reset_states();
+        for (int s = 0; s < steps; ++s) {
+            Tensor in(std::vector<int>{hin}, const_cast<float*>(inputs + (size_t)s * hin));
+            Tensor out(std::vector<int>{hout}, outputs + (size_t)s * hout);
+            Context ctx;
+            ctx.pos = s;
+            ctx.seq_len = 1;
+            m.forward(in, out, ctx);
+        }
+        return 0;
+    } catch (const std::exception& e) {
+        return fail(e.what());
+    }
+}
+
+int qlmref_gdn_restated_steps(int hin, int heads, int d, int ks, int hout, const float* w_qkv, const float* w_z,
+                              const float* w_b, const float* w_a, const float* conv_w, const float* norm_w,
+                              const float* A_log, const float* dt_bias, const float* w_out, int steps,
+                              const float* inputs, float* outputs) {
+    if (steps <= 0 || !inputs || !outputs) return fail("bad args");
+    try {
+        const int H = heads * d, C = 3 * H, ntaps = ks - 1;
+        Tensor Wqkv = owned({C, hin}, w_qkv, (size_t)C * hin), Wz = owned({H, hin}, w_z, (size_t)H * hin);
+        Tensor Wb = owned({heads, hin}, w_b, (size_t)heads * hin), Wa = owned({heads, hin}, w_a, (size_t)heads * hin);
+        Tensor Wout = owned({hout, H}, w_out, (size_t)hout * H);
+        std::vector<float> wt((size_t)ks * C), conv_state((size_t)ntaps * C, 0.0f), S((size_t)heads * d * d, 0.0f);
+        for (int c = 0; c < C; ++c)
+            for (int t = 0; t < ks; ++t) wt[(size_t)t * C + c] = conv_w[(size_t)c * ks + t];
+        std::vector<float> qkv(C), z(H), b(heads), a(heads), conv(C), y(H), dec(heads), beta(heads);
+        int ring = 0;
+        for (int s = 0; s < steps; ++s) {
+            Tensor in(std::vector<int>{hin}, const_cast<float*>(inputs + (size_t)s * hin));
+            Tensor tq(std::vector<int>{C}, qkv.data()), tz(std::vector<int>{H}, z.data());
+            Tensor tb(std::vector<int>{heads}, b.data()), ta(std::vector<int>{heads}, a.data());
+            math::matmul(in, Wqkv, tq, true);
+            math::matmul(in, Wz, tz, true);
+            math::matmul(in, Wb, tb, true);
+            math::matmul(in, Wa, ta, true);
+            math::causal_conv1d_update_tapmajor(qkv.data(), conv_state.data(), ring, wt.data(), conv.data(), C, ks);
+            ring = (ring + 1) % ntaps;
+            for (int i = 0; i < C; ++i) conv[i] = conv[i] / (1.0f + std::exp(-conv[i]));
+            float* qp = conv.data();
+            float* kp = conv.data() + H;
+            const float* vp = conv.data() + 2 * H;
+            for (int h = 0; h < heads; ++h) {
+                const float qn = std::sqrt(math::sumsq(qp + (size_t)h * d, d) + 1e-6f);
+                const float kn = std::sqrt(math::sumsq(kp + (size_t)h * d, d) + 1e-6f);
+                math::vec_div_inplace(qp + (size_t)h * d, qn, d);
+                math::vec_div_inplace(kp + (size_t)h * d, kn, d);
+            }
+            qlmref_gdn_gates(a.data(), b.data(), A_log, dt_bias, dec.data(), beta.data(), heads);
+            qlmref_gdn_recurrence(S.data(), qp, kp, vp, dec.data(), beta.data(), heads, d, y.data());
+            qlmref_rms_norm_gain(y.data(), norm_w, y.data(), heads, d, 1e-6f);
+            for (int i = 0; i < H; ++i) y[i] *= z[i] / (1.0f + std::exp(-z[i]));
+            Tensor ty(std::vector<int>{1, H}, y.data());
+            Tensor to(std::vector<int>{hout}, outputs + (size_t)s * hout);
+            math::matmul(ty, Wout, to, true);
+        }
+        return 0;
+    } catch (const std::exception& e) {
+        return fail(e.what());
+    }
 }
 
 // One token: t [num_heads, head_dim] at position pos.

@@ -25,7 +25,8 @@ import numpy as np
 
 __all__ = ["QlmError", "Int8Weight", "matmul", "matmul_grouped", "argmax", "load", "LIB_PATH", "EXACT", "TENSOR", "HOST_IO", "SYNC",
            "BLOCK", "Comm", "shard_rows", "matmul_allgather", "save", "store_info", "rms_norm", "add_rms_norm",
-           "silu_mul", "rope_neox", "rope_neox_tables", "silu", "conv1d_update_tapmajor", "l2norm_heads"]
+           "silu_mul", "rope_neox", "rope_neox_tables", "silu", "conv1d_update_tapmajor", "l2norm_heads",
+           "gdn_gates", "gdn_recurrence", "rms_norm_gain"]
 
 LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "lib", "libqlm_b200.so")
 BLOCK = 32
@@ -41,7 +42,7 @@ ABI_SYMBOLS = (
     "qlm_linear_int8_grouped", "qlm_weight_quantize_upload_q4", "qlm_weight_export_int4", "qlm_weight_bits",
     "qlm_weight_import_int4", "qlm_store_save", "qlm_store_load", "qlm_store_info", "qlm_rms_norm",
     "qlm_add_rms_norm", "qlm_silu_mul", "qlm_rope_neox", "qlm_rope_neox_tables", "qlm_silu",
-    "qlm_conv1d_update_tapmajor", "qlm_l2norm_heads",
+    "qlm_conv1d_update_tapmajor", "qlm_l2norm_heads", "qlm_gdn_gates", "qlm_gdn_recurrence", "qlm_rms_norm_gain",
 )
 
 _STATUS = {0: "OK", 1: "INVALID_ARG", 2: "CUDA", 3: "OUT_OF_MEMORY", 4: "UNSUPPORTED", 5: "TIMEOUT", 6: "NCCL",
@@ -90,6 +91,9 @@ def load(path: str = LIB_PATH):
     lib.qlm_silu.argtypes = [P, L, P]
     lib.qlm_conv1d_update_tapmajor.argtypes = [P, P, I, P, P, I, I, P]
     lib.qlm_l2norm_heads.argtypes = [P, I, I, F, P]
+    lib.qlm_gdn_gates.argtypes = [P, P, P, P, P, P, I, P]
+    lib.qlm_gdn_recurrence.argtypes = [P, P, P, P, P, P, P, I, I, P]
+    lib.qlm_rms_norm_gain.argtypes = [P, P, P, I, I, F, P]
     lib.qlm_weight_shape.argtypes = [P] + [ctypes.POINTER(I)] * 5
     lib.qlm_weight_bytes.argtypes = [P]
     lib.qlm_weight_bytes.restype = L
@@ -500,6 +504,42 @@ def l2norm_heads(x, head_dim: int, eps: float = 1e-6, stream=None):
         raise QlmError(1, "x is not a whole number of heads")
     _check(load().qlm_l2norm_heads(x.data_ptr(), x.numel() // head_dim, head_dim, eps, _torch_stream(stream)))
     return x
+
+
+def gdn_gates(a_raw, b_raw, A_log, dt_bias, stream=None):
+    """Per-head (decay, write gate) of the gated-delta-net step, as device tensors."""
+    for t, nm in ((a_raw, "a_raw"), (b_raw, "b_raw"), (A_log, "A_log"), (dt_bias, "dt_bias")):
+        _dev_f32(t, nm)
+    heads = a_raw.numel()
+    dec, beta = a_raw.new_empty(heads), a_raw.new_empty(heads)
+    _check(load().qlm_gdn_gates(a_raw.data_ptr(), b_raw.data_ptr(), A_log.data_ptr(), dt_bias.data_ptr(),
+                                dec.data_ptr(), beta.data_ptr(), heads, _torch_stream(stream)))
+    return dec, beta
+
+
+def gdn_recurrence(state, q, k, v, decay, beta, out=None, stream=None):
+    """Gated delta rule for all heads: state [heads, d, d] updated in place; returns out [heads, d]."""
+    for t, nm in ((state, "state"), (q, "q"), (k, "k"), (v, "v"), (decay, "decay"), (beta, "beta")):
+        _dev_f32(t, nm)
+    heads, d = state.shape[0], state.shape[-1]
+    if state.numel() != heads * d * d or q.numel() != heads * d or k.numel() != heads * d or v.numel() != heads * d:
+        raise QlmError(1, "state/q/k/v shapes do not match [heads, d, d] / [heads, d]")
+    out = q.new_empty((heads, d)) if out is None else _dev_f32(out, "out")
+    _check(load().qlm_gdn_recurrence(state.data_ptr(), q.data_ptr(), k.data_ptr(), v.data_ptr(), decay.data_ptr(),
+                                     beta.data_ptr(), out.data_ptr(), heads, d, _torch_stream(stream)))
+    return out
+
+
+def rms_norm_gain(x, w, eps: float, out=None, stream=None):
+    """rms_norm with a plain gain w (the gated-delta-net head norm)."""
+    _dev_f32(x, "x"), _dev_f32(w, "w")
+    size = w.numel()
+    if x.numel() % size:
+        raise QlmError(1, "x is not a whole number of rows")
+    out = x.new_empty(x.shape) if out is None else _dev_f32(out, "out")
+    _check(load().qlm_rms_norm_gain(x.data_ptr(), w.data_ptr(), out.data_ptr(), x.numel() // size, size, eps,
+                                    _torch_stream(stream)))
+    return out
 
 
 def rope_neox_tables(pos0: int, num_tokens: int, theta: float, rotary_dim: int):

@@ -7,8 +7,9 @@
 //   silu_mul      (:1122-1131), silu (:1076-1084)
 //   apply_rope_neox (:1237-1291)
 //   causal_conv1d_update_tapmajor (:1321-1366)
-//   the per-head L2 normalisation of the gated-delta-net step
-//     (src/model/attention.cpp:462-470: sqrt(sumsq + eps), vec_div_inplace)
+//   the gated-delta-net decode step (src/model/attention.cpp): the per-head
+//     L2 normalisation (:462-470), the decay/write gates (:472-482), the
+//     delta-rule recurrence (:498-560) and the head-wise output norm (:573-577)
 //
 // rms_norm, add_rms_norm and the RoPE rotation are bit-identical to the
 // reference (strict build, no contraction): the sums of squares follow its
@@ -84,14 +85,19 @@ __device__ __forceinline__ float rms_scale(float ss, int n, float eps) {
     return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)n), eps)));
 }
 
-// norm_apply_zc: out = (in * s) * (1 + w), vector body and scalar tail alike.
-// in and out may be the same row (each element is read and written by one thread).
+// norm_apply_zc: out = (in * s) * (1 + w); norm_apply_gain (ZC = false):
+// out = (in * s) * w; vector body and scalar tail alike. in and out may be the
+// same row (each element is read and written by one thread).
+template <bool ZC = true>
 __device__ __forceinline__ void apply_zc(const float* in, const float* __restrict__ w, float* out, float s, int n) {
-    for (int i = threadIdx.x; i < n; i += blockDim.x) out[i] = __fmul_rn(__fmul_rn(in[i], s), __fadd_rn(1.0f, w[i]));
+    for (int i = threadIdx.x; i < n; i += blockDim.x)
+        out[i] = __fmul_rn(__fmul_rn(in[i], s), ZC ? __fadd_rn(1.0f, w[i]) : w[i]);
 }
 
 // One CTA per row. Rows up to kStageFloats are first staged in shared memory
 // with coalesced loads, so the ordered accumulation chains read on-chip data.
+// ZC: zero-centred gain (1 + w) as math::rms_norm; else the plain gain w.
+template <bool ZC>
 __global__ void __launch_bounds__(kThreads) rms_norm_kernel(const float* x, const float* __restrict__ w, float* y,
                                                             int size, float eps) {
     extern __shared__ float stage[];
@@ -107,7 +113,7 @@ __global__ void __launch_bounds__(kThreads) rms_norm_kernel(const float* x, cons
         if (threadIdx.x == 0) s_scale = rms_scale(ss, size, eps);
     }
     __syncthreads();
-    apply_zc(xr, w, y + (int64_t)blockIdx.x * size, s_scale, size);
+    apply_zc<ZC>(xr, w, y + (int64_t)blockIdx.x * size, s_scale, size);
 }
 
 // One CTA per row: residual += delta (stored), then out = rms_norm(residual).
@@ -182,6 +188,74 @@ __global__ void __launch_bounds__(kThreads) l2norm_heads_kernel(float* x, int he
     for (int i = threadIdx.x & 31; i < head_dim; i += 32) xh[i] = __fdiv_rn(xh[i], n);
 }
 
+// The delta-rule recurrence; CTA (head h, block of 32 state columns), one
+// thread per column j: S = dec * S; kv = k . S; S += (beta k) outer (v - kv);
+// out = (q . S) / sqrt(d). The reference's 8-wide body (j < d - d % 8) uses
+// FMAs, its scalar tail separate products and sums; each column's operations
+// run in the reference's order, and the update of a column and its output sum
+// touch only that column, so fusing the update and output passes changes no
+// rounding. The CTA's [d][32] slice of the state is loaded into shared memory
+// with independent coalesced loads (128 bytes per row), updated there, and
+// written back.
+__global__ void __launch_bounds__(32) gdn_recurrence_kernel(float* __restrict__ state, const float* __restrict__ q,
+                                                            const float* __restrict__ k, const float* __restrict__ v,
+                                                            const float* __restrict__ dec,
+                                                            const float* __restrict__ beta, float* __restrict__ out,
+                                                            int d) {
+    extern __shared__ float sh[];  // q_h [d], k_h [d], slice [d][32]
+    const int h = blockIdx.x, lane = threadIdx.x, j = blockIdx.y * 32 + lane;
+    float* qs = sh;
+    float* ks = sh + d;
+    float* tile = sh + 2 * d;
+    for (int i = lane; i < d; i += 32) {
+        qs[i] = q[(int64_t)h * d + i];
+        ks[i] = k[(int64_t)h * d + i];
+    }
+    float* S = state + (int64_t)h * d * d + j;
+    const bool live = j < d;
+#pragma unroll 8
+    for (int i = 0; i < d; ++i) tile[i * 32 + lane] = live ? S[(int64_t)i * d] : 0.0f;
+    __syncwarp();
+    if (live) {
+        const bool body = j < d - d % 8;
+        const float dh = dec[h], bh = beta[h];
+        float kv = 0.0f;
+#pragma unroll 8
+        for (int i = 0; i < d; ++i) {
+            const float r = __fmul_rn(tile[i * 32 + lane], dh);
+            tile[i * 32 + lane] = r;
+            kv = body ? __fmaf_rn(ks[i], r, kv) : __fadd_rn(kv, __fmul_rn(ks[i], r));
+        }
+        const float delta = __fsub_rn(v[(int64_t)h * d + j], kv);
+        float o = 0.0f;
+#pragma unroll 8
+        for (int i = 0; i < d; ++i) {
+            const float s = __fmul_rn(bh, ks[i]);
+            float r = tile[i * 32 + lane];
+            r = body ? __fmaf_rn(s, delta, r) : __fadd_rn(r, __fmul_rn(s, delta));
+            tile[i * 32 + lane] = r;
+            o = body ? __fmaf_rn(qs[i], r, o) : __fadd_rn(o, __fmul_rn(qs[i], r));
+        }
+        out[(int64_t)h * d + j] = __fmul_rn(o, __fdiv_rn(1.0f, __fsqrt_rn((float)d)));
+#pragma unroll 8
+        for (int i = 0; i < d; ++i) S[(int64_t)i * d] = tile[i * 32 + lane];
+    }
+}
+
+// Per-head gates; each libm call is evaluated in double and rounded once, as
+// a correctly rounded float function would.
+__global__ void gdn_gates_kernel(const float* __restrict__ a_raw, const float* __restrict__ b_raw,
+                                 const float* __restrict__ A_log, const float* __restrict__ dt_bias,
+                                 float* __restrict__ dec, float* __restrict__ beta, int heads) {
+    const int h = blockIdx.x * blockDim.x + threadIdx.x;
+    if (h >= heads) return;
+    const float dt_in = __fadd_rn(a_raw[h], dt_bias[h]);
+    const float sp = dt_in > 20.0f ? dt_in : (float)log1p((double)(float)exp((double)dt_in));
+    const float alpha = __fmul_rn(-(float)exp((double)A_log[h]), sp);
+    dec[h] = (float)exp((double)alpha);
+    beta[h] = __fdiv_rn(1.0f, __fadd_rn(1.0f, (float)exp(-(double)b_raw[h])));
+}
+
 // t [tokens][heads][head_dim]; cos/sin [tokens][rotary_dim / 2].
 __global__ void __launch_bounds__(kThreads) rope_neox_kernel(float* __restrict__ t, const float* __restrict__ ct,
                                                              const float* __restrict__ st, int heads, int head_dim,
@@ -226,8 +300,46 @@ int qlm_rms_norm(const float* x, const float* w, float* y, int rows, int size, f
     if (!x || !w || !y) return layer_fail(QLM_ERR_INVALID_ARG, "NULL argument");
     if (rows <= 0 || size <= 0) return layer_fail(QLM_ERR_INVALID_ARG, "rows and size must be positive");
     const size_t smem = size <= qlm::kStageFloats ? (size_t)size * sizeof(float) : 0;
-    qlm::rms_norm_kernel<<<rows, qlm::kThreads, smem, static_cast<cudaStream_t>(stream)>>>(x, w, y, size, eps);
+    qlm::rms_norm_kernel<true><<<rows, qlm::kThreads, smem, static_cast<cudaStream_t>(stream)>>>(x, w, y, size, eps);
     return launched("rms_norm launch");
+}
+
+int qlm_rms_norm_gain(const float* x, const float* w, float* y, int rows, int size, float eps, void* stream) {
+    if (!x || !w || !y) return layer_fail(QLM_ERR_INVALID_ARG, "NULL argument");
+    if (rows <= 0 || size <= 0) return layer_fail(QLM_ERR_INVALID_ARG, "rows and size must be positive");
+    const size_t smem = size <= qlm::kStageFloats ? (size_t)size * sizeof(float) : 0;
+    qlm::rms_norm_kernel<false><<<rows, qlm::kThreads, smem, static_cast<cudaStream_t>(stream)>>>(x, w, y, size, eps);
+    return launched("rms_norm_gain launch");
+}
+
+int qlm_gdn_recurrence(float* state, const float* q, const float* k, const float* v, const float* decay,
+                       const float* beta, float* out, int heads, int head_dim, void* stream) {
+    if (!state || !q || !k || !v || !decay || !beta || !out) return layer_fail(QLM_ERR_INVALID_ARG, "NULL argument");
+    if (heads <= 0 || head_dim <= 0 || head_dim > 1024)
+        return layer_fail(QLM_ERR_INVALID_ARG, "heads must be positive and head_dim in [1, 1024]");
+    const dim3 grid((unsigned)heads, (unsigned)((head_dim + 31) / 32));
+    const size_t smem = (size_t)(2 + 32) * head_dim * sizeof(float);  // <= 136 KB at head_dim 1024
+    static bool attr_set[64] = {};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return layer_fail(QLM_ERR_CUDA, "cudaGetDevice");
+    if (!attr_set[dev]) {
+        if (cudaFuncSetAttribute(qlm::gdn_recurrence_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (2 + 32) * 1024 * (int)sizeof(float)) != cudaSuccess)
+            return launched("gdn_recurrence attribute");
+        attr_set[dev] = true;
+    }
+    qlm::gdn_recurrence_kernel<<<grid, 32, smem, static_cast<cudaStream_t>(stream)>>>(state, q, k, v, decay, beta,
+                                                                                     out, head_dim);
+    return launched("gdn_recurrence launch");
+}
+
+int qlm_gdn_gates(const float* a_raw, const float* b_raw, const float* A_log, const float* dt_bias, float* decay,
+                  float* beta, int heads, void* stream) {
+    if (!a_raw || !b_raw || !A_log || !dt_bias || !decay || !beta) return layer_fail(QLM_ERR_INVALID_ARG, "NULL argument");
+    if (heads <= 0) return layer_fail(QLM_ERR_INVALID_ARG, "heads must be positive");
+    qlm::gdn_gates_kernel<<<(heads + 127) / 128, 128, 0, static_cast<cudaStream_t>(stream)>>>(a_raw, b_raw, A_log,
+                                                                                            dt_bias, decay, beta, heads);
+    return launched("gdn_gates launch");
 }
 
 int qlm_add_rms_norm(float* residual, const float* delta, const float* w, float* out, int rows, int size, float eps,

@@ -163,3 +163,61 @@ def test_l2norm_heads_bit_exact(q, refcpu, heads, head_dim):
     xd = torch.from_numpy(x).cuda()
     q.l2norm_heads(xd, head_dim, 1e-6)
     assert bits_equal(xd.cpu().numpy(), ref)
+
+
+@pytest.mark.parametrize("heads,d", [(16, 128), (3, 20), (2, 7), (1, 256)])
+def test_gdn_recurrence_bit_exact(q, refcpu, heads, d):
+    """Several tokens with the state carried on both sides, against the
+    restated recurrence (itself pinned to Qwen3_5GatedDeltaNet::forward by
+    tests/test_gdn_cpu.py)."""
+    import torch
+    rng = np.random.default_rng(heads * 1000 + d)
+    st_ref = (rng.standard_normal((heads, d, d)) * 0.1).astype(np.float32)
+    st_dev = torch.from_numpy(st_ref.copy()).cuda()
+    for step in range(4):
+        qv, kv, vv = (rng.standard_normal((heads, d)).astype(np.float32) for _ in range(3))
+        qv /= np.linalg.norm(qv, axis=1, keepdims=True)
+        kv /= np.linalg.norm(kv, axis=1, keepdims=True)
+        dec = rng.uniform(0.5, 1.0, heads).astype(np.float32)
+        beta = rng.uniform(0.0, 1.0, heads).astype(np.float32)
+        out_ref, st_ref = refcpu.gdn_recurrence(st_ref, qv, kv, vv, dec, beta)
+        t = [torch.from_numpy(a).cuda() for a in (qv, kv, vv, dec, beta)]
+        out = q.gdn_recurrence(st_dev, *t)
+        assert bits_equal(out.cpu().numpy(), out_ref), step
+        assert bits_equal(st_dev.cpu().numpy(), st_ref), step
+
+
+def test_gdn_gates_within_a_few_ulp(q, refcpu):
+    import torch
+    rng = np.random.default_rng(17)
+    heads = 4096
+    a = (rng.standard_normal(heads) * 3).astype(np.float32)
+    a[:4] = [25.0, 19.9, -30.0, 0.0]  # both softplus branches
+    b = (rng.standard_normal(heads) * 4).astype(np.float32)
+    A_log = (rng.standard_normal(heads) * 0.5).astype(np.float32)
+    dt = (rng.standard_normal(heads) * 0.5).astype(np.float32)
+    dec_ref, beta_ref = refcpu.gdn_gates(a, b, A_log, dt)
+    dec, beta = q.gdn_gates(*[torch.from_numpy(x).cuda() for x in (a, b, A_log, dt)])
+    dec = dec.cpu().numpy()
+    # decay = exp(alpha): a 1-ulp difference in alpha (from exp/log1p last bits)
+    # is a relative error of |alpha| ulp in decay, so the bound scales with
+    # |alpha| = -ln(decay): 2 ulp x (2 + |alpha|) on the normal range.
+    d_ref = dec_ref.astype(np.float64)
+    normal = d_ref > 1e-30
+    alpha = -np.log(d_ref[normal])
+    rel = np.abs(dec[normal] - d_ref[normal]) / d_ref[normal]
+    assert (rel <= 2.4e-7 * (2.0 + alpha)).all()
+    assert np.all(np.abs(dec[~normal]) <= 1e-29)
+    assert _ulp_diff(beta.cpu().numpy(), beta_ref).max() <= 2
+    assert (_ulp_diff(dec, dec_ref) == 0).mean() > 0.75
+
+
+@pytest.mark.parametrize("rows,size", [(16, 128), (3, 20), (5, 1003)])
+def test_rms_norm_gain_bit_exact(q, refcpu, rows, size):
+    import torch
+    rng = np.random.default_rng(rows + size)
+    x = rng.standard_normal((rows, size)).astype(np.float32)
+    w = (1.0 + rng.standard_normal(size) * 0.1).astype(np.float32)
+    ref = refcpu.rms_norm_gain(x, w, 1e-6)
+    y = q.rms_norm_gain(torch.from_numpy(x).cuda(), torch.from_numpy(w).cuda(), 1e-6)
+    assert bits_equal(y.cpu().numpy(), ref)
