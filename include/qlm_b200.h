@@ -179,7 +179,13 @@ int qlm_store_info(const char* path, const char* name, int* bits, int64_t* rows,
  *                     updated in place, out [heads][d] (attention.cpp:498-560).
  *                     Bit-identical given the same inputs.
  *   qlm_rms_norm_gain rms_norm with a plain gain w (the head-wise output norm,
- *                     attention.cpp:573-577). Bit-identical. */
+ *                     attention.cpp:573-577). Bit-identical.
+ *   qlm_gqa_attend    GQA attention of one decode token over cached positions
+ *                     0..pos: q [heads][q_stride] (query in the first head_dim),
+ *                     caches [T][kv_heads][head_dim], out [heads][head_dim]
+ *                     (attention.cpp:17-81, 202-213). Scores, sums and the V
+ *                     accumulation in the reference's order; exp in double, so
+ *                     within a few ulp. Contexts up to ~50K positions. */
 int qlm_rms_norm(const float* x, const float* w, float* y, int rows, int size, float eps, void* stream);
 int qlm_add_rms_norm(float* residual, const float* delta, const float* w, float* out, int rows, int size, float eps,
                      void* stream);
@@ -196,6 +202,8 @@ int qlm_gdn_gates(const float* a_raw, const float* b_raw, const float* A_log, co
 int qlm_gdn_recurrence(float* state, const float* q, const float* k, const float* v, const float* decay,
                        const float* beta, float* out, int heads, int head_dim, void* stream);
 int qlm_rms_norm_gain(const float* x, const float* w, float* y, int rows, int size, float eps, void* stream);
+int qlm_gqa_attend(const float* q, int q_stride, const float* k_cache, const float* v_cache, float* out, int pos,
+                   int heads, int kv_heads, int head_dim, void* stream);
 
 /* Release a handle and its device memory (NULL is a no-op). */
 void qlm_weight_free(qlm_w8* w);

@@ -81,6 +81,10 @@ class RefCPU:
         gdn = [_I, _I, _I, _I, _I] + [_P] * 9 + [_I, _P, _P]
         lib.qlmref_gdn_module_steps.argtypes = gdn
         lib.qlmref_gdn_restated_steps.argtypes = gdn
+        lib.qlmref_gqa_attend.argtypes = [_P, _I, _P, _P, _P, _I, _I, _I, _I]
+        attn = [_I, _I, _I, _I, _I, _F, _I] + [_P] * 6 + [_I, _P, _P]
+        lib.qlmref_attn_module_steps.argtypes = attn
+        lib.qlmref_attn_restated_steps.argtypes = attn
         self.lib = lib
         self.threads = 1
 
@@ -201,6 +205,33 @@ class RefCPU:
         out = np.empty((inputs.shape[0], hout), np.float32)
         fn = self.lib.qlmref_gdn_restated_steps if restated else self.lib.qlmref_gdn_module_steps
         self._rc(fn(hin, heads, d, ks, hout, *[_ptr(a[k_]) for k_ in keys], inputs.shape[0], _ptr(inputs), _ptr(out)))
+        return out
+
+    def gqa_attend(self, q, k_cache, v_cache, pos: int, kv_heads: int) -> np.ndarray:
+        """The restated per-head attention (model/attention.cpp:17-81) for one
+        token: q [heads, q_stride] (query in the first d), caches [T, kv_heads, d]."""
+        q = np.ascontiguousarray(q, np.float32)
+        kc = np.ascontiguousarray(k_cache, np.float32)
+        vc = np.ascontiguousarray(v_cache, np.float32)
+        heads, q_stride = q.shape
+        d = kc.shape[-1]
+        out = np.empty((heads, d), np.float32)
+        self._rc(self.lib.qlmref_gqa_attend(_ptr(q), q_stride, _ptr(kc), _ptr(vc), _ptr(out), int(pos), heads,
+                                            int(kv_heads), d))
+        return out
+
+    def attn_steps(self, w: dict, inputs: np.ndarray, heads: int, kv_heads: int, d: int, rot: int, theta: float,
+                   restated: bool = False) -> np.ndarray:
+        """Qwen3_5Attention decode steps (gated q_proj, QK-norm, partial RoPE, no
+        biases, F32 weights w_q, w_k, w_v, w_o, q_norm, k_norm) over inputs [steps, hin]."""
+        keys = ("w_q", "w_k", "w_v", "w_o", "q_norm", "k_norm")
+        a = {k_: np.ascontiguousarray(w[k_], np.float32) for k_ in keys}
+        inputs = np.ascontiguousarray(inputs, np.float32)
+        hin, hout = inputs.shape[1], a["w_o"].shape[0]
+        out = np.empty((inputs.shape[0], hout), np.float32)
+        fn = self.lib.qlmref_attn_restated_steps if restated else self.lib.qlmref_attn_module_steps
+        self._rc(fn(hin, heads, kv_heads, d, rot, ctypes.c_float(theta), hout, *[_ptr(a[k_]) for k_ in keys],
+                    inputs.shape[0], _ptr(inputs), _ptr(out)))
         return out
 
     def rope_neox(self, t: np.ndarray, pos: int, theta: float, rotary_dim: int) -> np.ndarray:

@@ -436,6 +436,147 @@ int qlmref_gdn_restated_steps(int hin, int heads, int d, int ks, int hout, const
     }
 }
 
+// ---- GQA attention decode step (model/attention.cpp:138-235) ---------------
+//
+// qlmref_attn_module_steps drives Qwen3_5Attention::init + forward (seq_len 1,
+// F32 weights, no biases, gated q_proj) over `steps` tokens;
+// qlmref_attn_restated_steps restates the step on the reference's standalone
+// functions (matmul, sumsq, norm_apply_zc, apply_rope_neox) with the restated
+// per-head attention (qlmref_gqa_attend, attention.cpp:17-81) and output gate.
+
+namespace {
+// dot_f32 (attention.cpp:17-37): two 8-lane FMA accumulators over 16-wide
+// steps, an 8-wide remainder into the first, the lane tree, the scalar tail.
+float dot_ref(const float* a, const float* b, int n) {
+    float a0[8] = {0, 0, 0, 0, 0, 0, 0, 0}, a1[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    int i = 0;
+    for (; i + 16 <= n; i += 16)
+        for (int l = 0; l < 8; ++l) {
+            a0[l] = std::fma(a[i + l], b[i + l], a0[l]);
+            a1[l] = std::fma(a[i + 8 + l], b[i + 8 + l], a1[l]);
+        }
+    for (; i + 8 <= n; i += 8)
+        for (int l = 0; l < 8; ++l) a0[l] = std::fma(a[i + l], b[i + l], a0[l]);
+    float s[8], lo[4];
+    for (int l = 0; l < 8; ++l) s[l] = a0[l] + a1[l];
+    for (int l = 0; l < 4; ++l) lo[l] = s[l] + s[l + 4];
+    float r = (lo[0] + lo[1]) + (lo[2] + lo[3]);
+    for (; i < n; ++i) r += a[i] * b[i];
+    return r;
+}
+}  // namespace
+
+// All heads of one token: q [heads][q_stride] (query in the first d), caches
+// [T][kv_heads][d] with positions 0..pos valid, out [heads][d].
+int qlmref_gqa_attend(const float* q, int q_stride, const float* k_cache, const float* v_cache, float* out, int pos,
+                      int heads, int kv_heads, int d) {
+    if (!q || !k_cache || !v_cache || !out || heads <= 0 || kv_heads <= 0 || d <= 0 || pos < 0) return fail("bad args");
+    const int kv_size = kv_heads * d, group = heads / kv_heads, d8 = d - d % 8;
+    const float scale = 1.0f / std::sqrt(static_cast<float>(d));
+    std::vector<float> sc(pos + 1);
+    for (int h = 0; h < heads; ++h) {
+        const float* qh = q + (size_t)h * q_stride;
+        const int off = (h / group) * d;
+        for (int p = 0; p <= pos; ++p) sc[p] = dot_ref(qh, k_cache + (size_t)p * kv_size + off, d) * scale;
+        float m = sc[0];
+        for (int p = 1; p <= pos; ++p)
+            if (sc[p] > m) m = sc[p];
+        float sum = 0.0f;
+        for (int p = 0; p <= pos; ++p) {
+            sc[p] = std::exp(sc[p] - m);
+            sum += sc[p];
+        }
+        for (int p = 0; p <= pos; ++p) sc[p] /= sum;
+        float* oh = out + (size_t)h * d;
+        for (int i = 0; i < d; ++i) oh[i] = 0.0f;
+        for (int p = 0; p <= pos; ++p) {
+            const float* vp = v_cache + (size_t)p * kv_size + off;
+            for (int i = 0; i < d; ++i) oh[i] = i < d8 ? std::fma(sc[p], vp[i], oh[i]) : oh[i] + sc[p] * vp[i];
+        }
+    }
+    return 0;
+}
+
+int qlmref_attn_module_steps(int hin, int heads, int kv_heads, int d, int rot, float theta, int hout,
+                             const float* w_q, const float* w_k, const float* w_v, const float* w_o,
+                             const float* q_norm, const float* k_norm, int steps, const float* inputs,
+                             float* outputs) {
+    if (steps <= 0 || !inputs || !outputs) return fail("bad args");
+    try {
+        Qwen3_5Attention m;
+        m.init(owned({heads * 2 * d, hin}, w_q, (size_t)heads * 2 * d * hin),
+               owned({kv_heads * d, hin}, w_k, (size_t)kv_heads * d * hin),
+               owned({kv_heads * d, hin}, w_v, (size_t)kv_heads * d * hin),
+               owned({hout, heads * d}, w_o, (size_t)hout * heads * d), Tensor(), Tensor(), Tensor(),
+               owned({d}, q_norm, (size_t)d), owned({d}, k_norm, (size_t)d), heads, kv_heads, d, rot, theta, steps);
+        m.reset_states();
+        for (int s = 0; s < steps; ++s) {
+            Tensor in(std::vector<int>{hin}, const_cast<float*>(inputs + (size_t)s * hin));
+            Tensor out(std::vector<int>{hout}, outputs + (size_t)s * hout);
+            Context ctx;
+            ctx.pos = s;
+            ctx.seq_len = 1;
+            m.forward(in, out, ctx);
+        }
+        return 0;
+    } catch (const std::exception& e) {
+        return fail(e.what());
+    }
+}
+
+int qlmref_attn_restated_steps(int hin, int heads, int kv_heads, int d, int rot, float theta, int hout,
+                               const float* w_q, const float* w_k, const float* w_v, const float* w_o,
+                               const float* q_norm, const float* k_norm, int steps, const float* inputs,
+                               float* outputs) {
+    if (steps <= 0 || !inputs || !outputs) return fail("bad args");
+    try {
+        const int qd = 2 * d, kv_size = kv_heads * d;
+        Tensor Wq = owned({heads * qd, hin}, w_q, (size_t)heads * qd * hin);
+        Tensor Wk = owned({kv_size, hin}, w_k, (size_t)kv_size * hin);
+        Tensor Wv = owned({kv_size, hin}, w_v, (size_t)kv_size * hin);
+        Tensor Wo = owned({hout, heads * d}, w_o, (size_t)hout * heads * d);
+        std::vector<float> kc((size_t)steps * kv_size), vc((size_t)steps * kv_size);
+        std::vector<float> qv((size_t)heads * qd), kv(kv_size), vv(kv_size), att((size_t)heads * d);
+        for (int s = 0; s < steps; ++s) {
+            Tensor in(std::vector<int>{hin}, const_cast<float*>(inputs + (size_t)s * hin));
+            Tensor tq(std::vector<int>{heads, qd}, qv.data()), tk(std::vector<int>{kv_heads, d}, kv.data());
+            Tensor tv(std::vector<int>{kv_heads, d}, vv.data());
+            math::matmul(in, Wq, tq, true);
+            math::matmul(in, Wk, tk, true);
+            math::matmul(in, Wv, tv, true);
+            for (int h = 0; h < heads; ++h) {
+                float* qh = qv.data() + (size_t)h * qd;
+                const float sc = 1.0f / std::sqrt((math::sumsq(qh, d) / d) + 1e-6f);
+                math::norm_apply_zc(qh, q_norm, qh, sc, d);
+            }
+            for (int h = 0; h < kv_heads; ++h) {
+                float* kh = kv.data() + (size_t)h * d;
+                const float sc = 1.0f / std::sqrt((math::sumsq(kh, d) / d) + 1e-6f);
+                math::norm_apply_zc(kh, k_norm, kh, sc, d);
+            }
+            math::apply_rope_neox(tk, s, theta, d, rot);
+            for (int h = 0; h < heads; ++h) {
+                Tensor qview(std::vector<int>{1, d}, qv.data() + (size_t)h * qd);
+                math::apply_rope_neox(qview, s, theta, d, rot);
+            }
+            std::memcpy(kc.data() + (size_t)s * kv_size, kv.data(), kv_size * sizeof(float));
+            std::memcpy(vc.data() + (size_t)s * kv_size, vv.data(), kv_size * sizeof(float));
+            qlmref_gqa_attend(qv.data(), qd, kc.data(), vc.data(), att.data(), s, heads, kv_heads, d);
+            for (int h = 0; h < heads; ++h)
+                for (int i = 0; i < d; ++i) {
+                    const float g = qv[(size_t)h * qd + d + i];
+                    att[(size_t)h * d + i] *= 1.0f / (1.0f + std::exp(-g));
+                }
+            Tensor ta(std::vector<int>{1, heads * d}, att.data());
+            Tensor to(std::vector<int>{hout}, outputs + (size_t)s * hout);
+            math::matmul(ta, Wo, to, true);
+        }
+        return 0;
+    } catch (const std::exception& e) {
+        return fail(e.what());
+    }
+}
+
 // One token: t [num_heads, head_dim] at position pos.
 int qlmref_rope_neox(float* t, int num_heads, int head_dim, int pos, float theta, int rotary_dim) {
     if (!t || num_heads <= 0 || head_dim <= 0) return fail("bad args");

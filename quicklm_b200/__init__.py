@@ -26,7 +26,7 @@ import numpy as np
 __all__ = ["QlmError", "Int8Weight", "matmul", "matmul_grouped", "argmax", "load", "LIB_PATH", "EXACT", "TENSOR", "HOST_IO", "SYNC",
            "BLOCK", "Comm", "shard_rows", "matmul_allgather", "save", "store_info", "rms_norm", "add_rms_norm",
            "silu_mul", "rope_neox", "rope_neox_tables", "silu", "conv1d_update_tapmajor", "l2norm_heads",
-           "gdn_gates", "gdn_recurrence", "rms_norm_gain"]
+           "gdn_gates", "gdn_recurrence", "rms_norm_gain", "gqa_attend"]
 
 LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "lib", "libqlm_b200.so")
 BLOCK = 32
@@ -43,6 +43,7 @@ ABI_SYMBOLS = (
     "qlm_weight_import_int4", "qlm_store_save", "qlm_store_load", "qlm_store_info", "qlm_rms_norm",
     "qlm_add_rms_norm", "qlm_silu_mul", "qlm_rope_neox", "qlm_rope_neox_tables", "qlm_silu",
     "qlm_conv1d_update_tapmajor", "qlm_l2norm_heads", "qlm_gdn_gates", "qlm_gdn_recurrence", "qlm_rms_norm_gain",
+    "qlm_gqa_attend",
 )
 
 _STATUS = {0: "OK", 1: "INVALID_ARG", 2: "CUDA", 3: "OUT_OF_MEMORY", 4: "UNSUPPORTED", 5: "TIMEOUT", 6: "NCCL",
@@ -94,6 +95,7 @@ def load(path: str = LIB_PATH):
     lib.qlm_gdn_gates.argtypes = [P, P, P, P, P, P, I, P]
     lib.qlm_gdn_recurrence.argtypes = [P, P, P, P, P, P, P, I, I, P]
     lib.qlm_rms_norm_gain.argtypes = [P, P, P, I, I, F, P]
+    lib.qlm_gqa_attend.argtypes = [P, I, P, P, P, I, I, I, I, P]
     lib.qlm_weight_shape.argtypes = [P] + [ctypes.POINTER(I)] * 5
     lib.qlm_weight_bytes.argtypes = [P]
     lib.qlm_weight_bytes.restype = L
@@ -539,6 +541,19 @@ def rms_norm_gain(x, w, eps: float, out=None, stream=None):
     out = x.new_empty(x.shape) if out is None else _dev_f32(out, "out")
     _check(load().qlm_rms_norm_gain(x.data_ptr(), w.data_ptr(), out.data_ptr(), x.numel() // size, size, eps,
                                     _torch_stream(stream)))
+    return out
+
+
+def gqa_attend(q, k_cache, v_cache, pos: int, out=None, stream=None):
+    """GQA attention of one decode token: q [heads, q_stride] (query first), caches
+    [T, kv_heads, d] with positions 0..pos valid; returns out [heads, d]."""
+    for t, nm in ((q, "q"), (k_cache, "k_cache"), (v_cache, "v_cache")):
+        _dev_f32(t, nm)
+    heads, q_stride = q.shape
+    kv_heads, d = k_cache.shape[-2], k_cache.shape[-1]
+    out = q.new_empty((heads, d)) if out is None else _dev_f32(out, "out")
+    _check(load().qlm_gqa_attend(q.data_ptr(), q_stride, k_cache.data_ptr(), v_cache.data_ptr(), out.data_ptr(), pos,
+                                 heads, kv_heads, d, _torch_stream(stream)))
     return out
 
 

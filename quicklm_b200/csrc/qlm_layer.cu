@@ -7,6 +7,8 @@
 //   silu_mul      (:1122-1131), silu (:1076-1084)
 //   apply_rope_neox (:1237-1291)
 //   causal_conv1d_update_tapmajor (:1321-1366)
+//   the GQA attention of one decode token (src/model/attention.cpp:17-81,
+//     gqa_attend_head: dot_f32 scores, max, exp, sum, normalise, axpy over V)
 //   the gated-delta-net decode step (src/model/attention.cpp): the per-head
 //     L2 normalisation (:462-470), the decay/write gates (:472-482), the
 //     delta-rule recurrence (:498-560) and the head-wise output norm (:573-577)
@@ -242,6 +244,113 @@ __global__ void __launch_bounds__(32) gdn_recurrence_kernel(float* __restrict__ 
     }
 }
 
+// GQA attention for one decode token, one CTA per query head h (kv head
+// h / (heads / kv_heads)). Scores follow dot_f32 (attention.cpp:17-37) exactly:
+// a 16-thread group per position, lane a accumulating elements 16c + a (the
+// two 8-lane accumulators), an 8-wide remainder into the first, the lane tree,
+// the scalar tail, times 1/sqrt(d). The max is order-free (the sign of a zero
+// maximum cannot change s - max's exp), except that a NaN first score makes it
+// NaN as in the sequential scan. exp is evaluated in double and rounded once;
+// the sum runs in position order on one thread; each output element then
+// accumulates its positions in order (FMA in the 8-wide body, mul+add in the
+// tail), as axpy_f32 does. Shared memory: q [d], scores [pos + 1], 34 floats.
+__global__ void __launch_bounds__(256) gqa_attend_kernel(const float* __restrict__ q, int q_stride,
+                                                         const float* __restrict__ kc, const float* __restrict__ vc,
+                                                         float* __restrict__ out, int pos, int heads, int kv_heads,
+                                                         int d) {
+    extern __shared__ float sh[];
+    float* qs = sh;
+    float* sc = sh + d;
+    float* red = sc + pos + 1;  // 32 partial maxima, the max, the sum
+    const int h = blockIdx.x, tid = threadIdx.x;
+    const int kv_size = kv_heads * d, off = (h / (heads / kv_heads)) * d;
+    for (int i = tid; i < d; i += blockDim.x) qs[i] = q[(int64_t)h * q_stride + i];
+    __syncthreads();
+    const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)d));
+    const int groups = blockDim.x / 16, g = tid >> 4, a = tid & 15;
+    const int n16 = d / 16, i8 = 16 * n16;
+    for (int p0 = 0; p0 <= pos; p0 += groups) {  // warp-uniform trip count
+        const int p = min(p0 + g, pos);
+        const float* kp = kc + (int64_t)p * kv_size + off;
+        float acc = 0.0f;
+        for (int c0 = 0; c0 < n16; c0 += 8) {  // this position's K loads first, then the ordered chain
+            float kk[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u)
+                if (c0 + u < n16) kk[u] = kp[16 * (c0 + u) + a];
+#pragma unroll
+            for (int u = 0; u < 8; ++u)
+                if (c0 + u < n16) acc = __fmaf_rn(qs[16 * (c0 + u) + a], kk[u], acc);
+        }
+        int tail = i8;
+        if (i8 + 8 <= d) {
+            if (a < 8) acc = __fmaf_rn(qs[i8 + a], kp[i8 + a], acc);
+            tail = i8 + 8;
+        }
+        const float s = __fadd_rn(acc, __shfl_down_sync(0xffffffffu, acc, 8, 16));   // lanes 0..7: a0 + a1
+        const float lo = __fadd_rn(s, __shfl_down_sync(0xffffffffu, s, 4, 16));      // lanes 0..3
+        const float l1 = __shfl_down_sync(0xffffffffu, lo, 1, 16);
+        const float l2 = __shfl_down_sync(0xffffffffu, lo, 2, 16);
+        const float l3 = __shfl_down_sync(0xffffffffu, lo, 3, 16);
+        if (a == 0 && p0 + g <= pos) {
+            float r = __fadd_rn(__fadd_rn(lo, l1), __fadd_rn(l2, l3));
+            for (int i = tail; i < d; ++i) r = __fadd_rn(r, __fmul_rn(qs[i], kp[i]));
+            sc[p] = __fmul_rn(r, scale);
+        }
+    }
+    __syncthreads();
+    // max over the non-NaN scores
+    float m = -INFINITY;
+    for (int p = tid; p <= pos; p += blockDim.x)
+        if (sc[p] > m) m = sc[p];
+    for (int o = 16; o; o >>= 1) {
+        const float t = __shfl_xor_sync(0xffffffffu, m, o);
+        m = t > m ? t : m;
+    }
+    if ((tid & 31) == 0) red[tid >> 5] = m;
+    __syncthreads();
+    if (tid == 0) {
+        float mm = red[0];
+        for (int w = 1; w < (int)(blockDim.x >> 5); ++w) mm = red[w] > mm ? red[w] : mm;
+        red[32] = isnan(sc[0]) ? sc[0] : mm;
+    }
+    __syncthreads();
+    m = red[32];
+    for (int p = tid; p <= pos; p += blockDim.x) sc[p] = (float)exp((double)__fsub_rn(sc[p], m));
+    __syncthreads();
+    if (tid == 0) {
+        float sum = 0.0f;
+#pragma unroll 8
+        for (int p = 0; p <= pos; ++p) sum = __fadd_rn(sum, sc[p]);
+        red[33] = sum;
+    }
+    __syncthreads();
+    const float sum = red[33];
+    for (int p = tid; p <= pos; p += blockDim.x) sc[p] = __fdiv_rn(sc[p], sum);
+    __syncthreads();
+    const int d8 = d - d % 8;
+    constexpr int kVBatch = 32;  // V rows loaded ahead of the ordered accumulation
+    for (int i = tid; i < d; i += blockDim.x) {
+        float o = 0.0f;
+        const float* vp = vc + off + i;
+        const bool body = i < d8;
+        for (int p0 = 0; p0 <= pos; p0 += kVBatch) {
+            const int n = min(kVBatch, pos + 1 - p0);
+            float vv[kVBatch];
+#pragma unroll
+            for (int u = 0; u < kVBatch; ++u)
+                if (u < n) vv[u] = vp[(int64_t)(p0 + u) * kv_size];
+#pragma unroll
+            for (int u = 0; u < kVBatch; ++u)
+                if (u < n) {
+                    const float w = sc[p0 + u];
+                    o = body ? __fmaf_rn(w, vv[u], o) : __fadd_rn(o, __fmul_rn(w, vv[u]));
+                }
+        }
+        out[(int64_t)h * d + i] = o;
+    }
+}
+
 // Per-head gates; each libm call is evaluated in double and rounded once, as
 // a correctly rounded float function would.
 __global__ void gdn_gates_kernel(const float* __restrict__ a_raw, const float* __restrict__ b_raw,
@@ -331,6 +440,28 @@ int qlm_gdn_recurrence(float* state, const float* q, const float* k, const float
     qlm::gdn_recurrence_kernel<<<grid, 32, smem, static_cast<cudaStream_t>(stream)>>>(state, q, k, v, decay, beta,
                                                                                      out, head_dim);
     return launched("gdn_recurrence launch");
+}
+
+int qlm_gqa_attend(const float* q, int q_stride, const float* k_cache, const float* v_cache, float* out, int pos,
+                   int heads, int kv_heads, int head_dim, void* stream) {
+    if (!q || !k_cache || !v_cache || !out) return layer_fail(QLM_ERR_INVALID_ARG, "NULL argument");
+    if (heads <= 0 || kv_heads <= 0 || heads % kv_heads || head_dim <= 0 || pos < 0 || q_stride < head_dim)
+        return layer_fail(QLM_ERR_INVALID_ARG, "bad attention shape");
+    constexpr size_t kMaxSmem = 200 * 1024;
+    const size_t smem = ((size_t)head_dim + (size_t)pos + 1 + 34) * sizeof(float);
+    if (smem > kMaxSmem) return layer_fail(QLM_ERR_UNSUPPORTED, "context too long for the one-CTA-per-head kernel");
+    static bool attr_set[64] = {};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return layer_fail(QLM_ERR_CUDA, "cudaGetDevice");
+    if (!attr_set[dev]) {
+        if (cudaFuncSetAttribute(qlm::gqa_attend_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)kMaxSmem) != cudaSuccess)
+            return launched("gqa_attend attribute");
+        attr_set[dev] = true;
+    }
+    qlm::gqa_attend_kernel<<<heads, 256, smem, static_cast<cudaStream_t>(stream)>>>(q, q_stride, k_cache, v_cache, out,
+                                                                                  pos, heads, kv_heads, head_dim);
+    return launched("gqa_attend launch");
 }
 
 int qlm_gdn_gates(const float* a_raw, const float* b_raw, const float* A_log, const float* dt_bias, float* decay,

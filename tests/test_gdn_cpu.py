@@ -30,3 +30,19 @@ def test_restated_step_equals_module(refcpu, hin, heads, d, ks, hout):
     y_res = refcpu.gdn_steps(w, x, restated=True)
     assert np.isfinite(y_mod).all()
     assert np.array_equal(y_mod.view(np.uint32), y_res.view(np.uint32))
+
+
+@pytest.mark.parametrize("hin,heads,kv_heads,d,rot", [(64, 4, 2, 32, 16), (96, 2, 1, 20, 8), (128, 4, 1, 256, 64)])
+def test_restated_attention_equals_module(refcpu, hin, heads, kv_heads, d, rot):
+    """The same pin for the GQA attention decode step (Qwen3_5Attention::forward,
+    model/attention.cpp:138-235): the restated per-head attention
+    (qlmref_gqa_attend) the device kernel is checked against."""
+    rng = np.random.default_rng(hin + heads + d)
+    f = lambda *s: rng.standard_normal(s).astype(np.float32)
+    w = {"w_q": f(heads * 2 * d, hin) * 0.2, "w_k": f(kv_heads * d, hin) * 0.2, "w_v": f(kv_heads * d, hin) * 0.2,
+         "w_o": f(48, heads * d) * 0.1, "q_norm": f(d) * 0.1, "k_norm": f(d) * 0.1}
+    x = f(7, hin)
+    y_mod = refcpu.attn_steps(w, x, heads, kv_heads, d, rot, 1e7)
+    y_res = refcpu.attn_steps(w, x, heads, kv_heads, d, rot, 1e7, restated=True)
+    assert np.isfinite(y_mod).all()
+    assert np.array_equal(y_mod.view(np.uint32), y_res.view(np.uint32))

@@ -221,3 +221,25 @@ def test_rms_norm_gain_bit_exact(q, refcpu, rows, size):
     ref = refcpu.rms_norm_gain(x, w, 1e-6)
     y = q.rms_norm_gain(torch.from_numpy(x).cuda(), torch.from_numpy(w).cuda(), 1e-6)
     assert bits_equal(y.cpu().numpy(), ref)
+
+
+@pytest.mark.parametrize("heads,kv_heads,d", [(8, 2, 256), (4, 4, 128), (3, 1, 20)])
+@pytest.mark.parametrize("pos", [0, 5, 300, 2047])
+def test_gqa_attend(q, refcpu, heads, kv_heads, d, pos):
+    """Against the restated per-head attention (pinned to Qwen3_5Attention::forward
+    by tests/test_gdn_cpu.py). Scores, the max, the sum order and the V
+    accumulation are the reference's; exp is evaluated in double, and where the
+    host's expf is off by an ulp the weights move by ~2 ulp, so outputs agree
+    within 1e-6 x max|v| (exactly at pos 0, where the single weight is 1)."""
+    import torch
+    rng = np.random.default_rng(heads * 7 + d + pos)
+    T = pos + 3
+    qv = rng.standard_normal((heads, 2 * d)).astype(np.float32)  # [query | gate] per head
+    kc = rng.standard_normal((T, kv_heads, d)).astype(np.float32)
+    vc = rng.standard_normal((T, kv_heads, d)).astype(np.float32)
+    ref = refcpu.gqa_attend(qv, kc, vc, pos, kv_heads)
+    got = q.gqa_attend(*[torch.from_numpy(a).cuda() for a in (qv, kc, vc)], pos).cpu().numpy()
+    if pos == 0:
+        assert bits_equal(got, ref)
+    else:
+        assert np.abs(got - ref).max() <= 1e-6 * np.abs(vc).max()
