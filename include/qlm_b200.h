@@ -185,7 +185,10 @@ int qlm_store_info(const char* path, const char* name, int* bits, int64_t* rows,
  *                     caches [T][kv_heads][head_dim], out [heads][head_dim]
  *                     (attention.cpp:17-81, 202-213). Scores, sums and the V
  *                     accumulation in the reference's order; exp in double, so
- *                     within a few ulp. Contexts up to ~50K positions. */
+ *                     within a few ulp. Contexts up to ~50K positions. With a
+ *                     device scratch of heads * (pos + 1) floats the work is
+ *                     spread over (head, position block) and (head, 32 outputs)
+ *                     CTAs in two launches (same results); NULL: one CTA per head. */
 int qlm_rms_norm(const float* x, const float* w, float* y, int rows, int size, float eps, void* stream);
 int qlm_add_rms_norm(float* residual, const float* delta, const float* w, float* out, int rows, int size, float eps,
                      void* stream);
@@ -203,7 +206,7 @@ int qlm_gdn_recurrence(float* state, const float* q, const float* k, const float
                        const float* beta, float* out, int heads, int head_dim, void* stream);
 int qlm_rms_norm_gain(const float* x, const float* w, float* y, int rows, int size, float eps, void* stream);
 int qlm_gqa_attend(const float* q, int q_stride, const float* k_cache, const float* v_cache, float* out, int pos,
-                   int heads, int kv_heads, int head_dim, void* stream);
+                   int heads, int kv_heads, int head_dim, float* scratch, void* stream);
 
 /* Release a handle and its device memory (NULL is a no-op). */
 void qlm_weight_free(qlm_w8* w);

@@ -95,7 +95,7 @@ def load(path: str = LIB_PATH):
     lib.qlm_gdn_gates.argtypes = [P, P, P, P, P, P, I, P]
     lib.qlm_gdn_recurrence.argtypes = [P, P, P, P, P, P, P, I, I, P]
     lib.qlm_rms_norm_gain.argtypes = [P, P, P, I, I, F, P]
-    lib.qlm_gqa_attend.argtypes = [P, I, P, P, P, I, I, I, I, P]
+    lib.qlm_gqa_attend.argtypes = [P, I, P, P, P, I, I, I, I, P, P]
     lib.qlm_weight_shape.argtypes = [P] + [ctypes.POINTER(I)] * 5
     lib.qlm_weight_bytes.argtypes = [P]
     lib.qlm_weight_bytes.restype = L
@@ -544,16 +544,21 @@ def rms_norm_gain(x, w, eps: float, out=None, stream=None):
     return out
 
 
-def gqa_attend(q, k_cache, v_cache, pos: int, out=None, stream=None):
+def gqa_attend(q, k_cache, v_cache, pos: int, out=None, scratch=None, parallel: bool = True, stream=None):
     """GQA attention of one decode token: q [heads, q_stride] (query first), caches
-    [T, kv_heads, d] with positions 0..pos valid; returns out [heads, d]."""
+    [T, kv_heads, d] with positions 0..pos valid; returns out [heads, d].
+    parallel: spread over (head, position block) CTAs through a score scratch of
+    heads * (pos + 1) floats (allocated when not given); same results."""
     for t, nm in ((q, "q"), (k_cache, "k_cache"), (v_cache, "v_cache")):
         _dev_f32(t, nm)
     heads, q_stride = q.shape
     kv_heads, d = k_cache.shape[-2], k_cache.shape[-1]
     out = q.new_empty((heads, d)) if out is None else _dev_f32(out, "out")
+    if parallel and scratch is None:
+        scratch = q.new_empty(heads * (pos + 1))
+    sp = scratch.data_ptr() if parallel else None
     _check(load().qlm_gqa_attend(q.data_ptr(), q_stride, k_cache.data_ptr(), v_cache.data_ptr(), out.data_ptr(), pos,
-                                 heads, kv_heads, d, _torch_stream(stream)))
+                                 heads, kv_heads, d, sp, _torch_stream(stream)))
     return out
 
 

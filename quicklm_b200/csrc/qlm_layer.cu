@@ -351,6 +351,109 @@ __global__ void __launch_bounds__(256) gqa_attend_kernel(const float* __restrict
     }
 }
 
+// Position-parallel form of gqa_attend_kernel for long contexts, in two
+// launches with the same arithmetic. Scores: CTA (head, block of 64 positions),
+// 16-thread groups as above, into scratch [heads][pos + 1].
+__global__ void __launch_bounds__(256) gqa_scores_kernel(const float* __restrict__ q, int q_stride,
+                                                         const float* __restrict__ kc, float* __restrict__ scores,
+                                                         int pos, int heads, int kv_heads, int d) {
+    extern __shared__ float qs[];
+    const int h = blockIdx.x, tid = threadIdx.x;
+    const int kv_size = kv_heads * d, off = (h / (heads / kv_heads)) * d;
+    for (int i = tid; i < d; i += blockDim.x) qs[i] = q[(int64_t)h * q_stride + i];
+    __syncthreads();
+    const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)d));
+    const int g = tid >> 4, a = tid & 15;
+    const int n16 = d / 16, i8 = 16 * n16;
+    const int pbeg = blockIdx.y * 64;
+    for (int it = 0; it < 4; ++it) {  // warp-uniform
+        const int pw = pbeg + it * 16 + g;
+        const int p = min(pw, pos);
+        const float* kp = kc + (int64_t)p * kv_size + off;
+        float acc = 0.0f;
+        for (int c0 = 0; c0 < n16; c0 += 8) {
+            float kk[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u)
+                if (c0 + u < n16) kk[u] = kp[16 * (c0 + u) + a];
+#pragma unroll
+            for (int u = 0; u < 8; ++u)
+                if (c0 + u < n16) acc = __fmaf_rn(qs[16 * (c0 + u) + a], kk[u], acc);
+        }
+        int tail = i8;
+        if (i8 + 8 <= d) {
+            if (a < 8) acc = __fmaf_rn(qs[i8 + a], kp[i8 + a], acc);
+            tail = i8 + 8;
+        }
+        const float s = __fadd_rn(acc, __shfl_down_sync(0xffffffffu, acc, 8, 16));
+        const float lo = __fadd_rn(s, __shfl_down_sync(0xffffffffu, s, 4, 16));
+        const float l1 = __shfl_down_sync(0xffffffffu, lo, 1, 16);
+        const float l2 = __shfl_down_sync(0xffffffffu, lo, 2, 16);
+        const float l3 = __shfl_down_sync(0xffffffffu, lo, 3, 16);
+        if (a == 0 && pw <= pos) {
+            float r = __fadd_rn(__fadd_rn(lo, l1), __fadd_rn(l2, l3));
+            for (int i = tail; i < d; ++i) r = __fadd_rn(r, __fmul_rn(qs[i], kp[i]));
+            scores[(int64_t)h * (pos + 1) + p] = __fmul_rn(r, scale);
+        }
+    }
+}
+
+// Softmax and V: CTA (head, block of 32 output elements), one warp. Every CTA
+// of a head recomputes the (cheap) softmax of the head's scores into shared
+// memory — max with the NaN rule, exp in double, the sum in position order,
+// the division — then each lane accumulates its output element over the
+// positions in order.
+__global__ void __launch_bounds__(32) gqa_softmax_v_kernel(const float* __restrict__ scores,
+                                                           const float* __restrict__ vc, float* __restrict__ out,
+                                                           int pos, int heads, int kv_heads, int d) {
+    extern __shared__ float pr[];  // [pos + 1]
+    const int h = blockIdx.x, lane = threadIdx.x;
+    const int kv_size = kv_heads * d, off = (h / (heads / kv_heads)) * d;
+    const float* sc = scores + (int64_t)h * (pos + 1);
+    float m = -INFINITY;
+    for (int p = lane; p <= pos; p += 32) {
+        const float v = sc[p];
+        pr[p] = v;
+        if (v > m) m = v;
+    }
+    for (int o = 16; o; o >>= 1) {
+        const float t = __shfl_xor_sync(0xffffffffu, m, o);
+        m = t > m ? t : m;
+    }
+    __syncwarp();
+    if (isnan(pr[0])) m = pr[0];
+    for (int p = lane; p <= pos; p += 32) pr[p] = (float)exp((double)__fsub_rn(pr[p], m));
+    __syncwarp();
+    float sum = 0.0f;
+    if (lane == 0) {
+#pragma unroll 8
+        for (int p = 0; p <= pos; ++p) sum = __fadd_rn(sum, pr[p]);
+    }
+    sum = __shfl_sync(0xffffffffu, sum, 0);
+    for (int p = lane; p <= pos; p += 32) pr[p] = __fdiv_rn(pr[p], sum);
+    __syncwarp();
+    const int i = blockIdx.y * 32 + lane;
+    if (i >= d) return;
+    const bool body = i < d - d % 8;
+    const float* vp = vc + off + i;
+    constexpr int kVBatch = 32;
+    float o = 0.0f;
+    for (int p0 = 0; p0 <= pos; p0 += kVBatch) {
+        const int n = min(kVBatch, pos + 1 - p0);
+        float vv[kVBatch];
+#pragma unroll
+        for (int u = 0; u < kVBatch; ++u)
+            if (u < n) vv[u] = vp[(int64_t)(p0 + u) * kv_size];
+#pragma unroll
+        for (int u = 0; u < kVBatch; ++u)
+            if (u < n) {
+                const float w = pr[p0 + u];
+                o = body ? __fmaf_rn(w, vv[u], o) : __fadd_rn(o, __fmul_rn(w, vv[u]));
+            }
+    }
+    out[(int64_t)h * d + i] = o;
+}
+
 // Per-head gates; each libm call is evaluated in double and rounded once, as
 // a correctly rounded float function would.
 __global__ void gdn_gates_kernel(const float* __restrict__ a_raw, const float* __restrict__ b_raw,
@@ -443,25 +546,39 @@ int qlm_gdn_recurrence(float* state, const float* q, const float* k, const float
 }
 
 int qlm_gqa_attend(const float* q, int q_stride, const float* k_cache, const float* v_cache, float* out, int pos,
-                   int heads, int kv_heads, int head_dim, void* stream) {
+                   int heads, int kv_heads, int head_dim, float* scratch, void* stream) {
     if (!q || !k_cache || !v_cache || !out) return layer_fail(QLM_ERR_INVALID_ARG, "NULL argument");
     if (heads <= 0 || kv_heads <= 0 || heads % kv_heads || head_dim <= 0 || pos < 0 || q_stride < head_dim)
         return layer_fail(QLM_ERR_INVALID_ARG, "bad attention shape");
     constexpr size_t kMaxSmem = 200 * 1024;
     const size_t smem = ((size_t)head_dim + (size_t)pos + 1 + 34) * sizeof(float);
-    if (smem > kMaxSmem) return layer_fail(QLM_ERR_UNSUPPORTED, "context too long for the one-CTA-per-head kernel");
+    if (smem > kMaxSmem) return layer_fail(QLM_ERR_UNSUPPORTED, "context too long for the attention kernels");
     static bool attr_set[64] = {};
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return layer_fail(QLM_ERR_CUDA, "cudaGetDevice");
     if (!attr_set[dev]) {
         if (cudaFuncSetAttribute(qlm::gqa_attend_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)kMaxSmem) != cudaSuccess ||
+            cudaFuncSetAttribute(qlm::gqa_softmax_v_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  (int)kMaxSmem) != cudaSuccess)
             return launched("gqa_attend attribute");
         attr_set[dev] = true;
     }
-    qlm::gqa_attend_kernel<<<heads, 256, smem, static_cast<cudaStream_t>(stream)>>>(q, q_stride, k_cache, v_cache, out,
-                                                                                  pos, heads, kv_heads, head_dim);
-    return launched("gqa_attend launch");
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (!scratch) {
+        qlm::gqa_attend_kernel<<<heads, 256, smem, s>>>(q, q_stride, k_cache, v_cache, out, pos, heads, kv_heads,
+                                                        head_dim);
+        return launched("gqa_attend launch");
+    }
+    const dim3 g1((unsigned)heads, (unsigned)((pos + 64) / 64));
+    qlm::gqa_scores_kernel<<<g1, 256, (size_t)head_dim * sizeof(float), s>>>(q, q_stride, k_cache, scratch, pos, heads,
+                                                                            kv_heads, head_dim);
+    int rc = launched("gqa_scores launch");
+    if (rc) return rc;
+    const dim3 g2((unsigned)heads, (unsigned)((head_dim + 31) / 32));
+    qlm::gqa_softmax_v_kernel<<<g2, 32, (size_t)(pos + 1) * sizeof(float), s>>>(scratch, v_cache, out, pos, heads,
+                                                                                kv_heads, head_dim);
+    return launched("gqa_softmax_v launch");
 }
 
 int qlm_gdn_gates(const float* a_raw, const float* b_raw, const float* A_log, const float* dt_bias, float* decay,

@@ -238,7 +238,10 @@ def test_gqa_attend(q, refcpu, heads, kv_heads, d, pos):
     kc = rng.standard_normal((T, kv_heads, d)).astype(np.float32)
     vc = rng.standard_normal((T, kv_heads, d)).astype(np.float32)
     ref = refcpu.gqa_attend(qv, kc, vc, pos, kv_heads)
-    got = q.gqa_attend(*[torch.from_numpy(a).cuda() for a in (qv, kc, vc)], pos).cpu().numpy()
+    dev = [torch.from_numpy(a).cuda() for a in (qv, kc, vc)]
+    got = q.gqa_attend(*dev, pos, parallel=False).cpu().numpy()
+    par = q.gqa_attend(*dev, pos, parallel=True).cpu().numpy()
+    assert bits_equal(par, got)  # the two-launch form computes the same values
     if pos == 0:
         assert bits_equal(got, ref)
     else:
