@@ -218,6 +218,9 @@ void qlm_weight_free(qlm_w8* w);
  *   flags QLM_LINEAR_*; device pointers unless QLM_LINEAR_HOST_IO.
  * Both paths accept any M >= 1 and any k (the exact path up to k = 51200).
  * QLM_LINEAR_TENSOR is never substituted silently: the caller chooses it.
+ * An int4 handle (qlm_weight_quantize_upload_q4 / import_int4) runs the exact
+ * int4 product (the int4 branch of math::matmul, math_ops.cpp:837-854);
+ * QLM_LINEAR_TENSOR on an int4 handle returns QLM_ERR_UNSUPPORTED.
  * Asynchronous on `stream` unless HOST_IO/SYNC. */
 int qlm_linear_int8(const float* x, int M, int k, int64_t ldx, const qlm_w8* w, float* y, int64_t ldy, int flags,
                     void* stream);
@@ -228,7 +231,8 @@ int qlm_linear_int8(const float* x, int M, int k, int64_t ldx, const qlm_w8* w, 
  * weight; every output is bit-identical to qlm_linear_int8's exact path. The
  * int8 counterpart of math::matmul_batched (src/ops/math_ops.cpp:902-954),
  * which QuickLM runs for bf16 weights only. ws: handles on one device with the
- * same k; ys / ldys: device outputs [M, rows_g] with row strides >= rows_g.
+ * same k and the same code width (all int8 or all int4); ys / ldys: device
+ * outputs [M, rows_g] with row strides >= rows_g.
  * flags: 0 or QLM_LINEAR_SYNC (device pointers). */
 int qlm_linear_int8_grouped(const float* x, int M, int k, int64_t ldx, const qlm_w8* const* ws, int nw,
                             float* const* ys, const int64_t* ldys, int flags, void* stream);
@@ -244,6 +248,7 @@ int qlm_linear_int8_grouped(const float* x, int M, int k, int64_t ldx, const qlm
  *   Limit: M <= 16384 and M * round_up(k, 128) * 2 bytes <= 8 MiB - 64 KiB - 256;
  *          larger requests return QLM_ERR_INVALID_ARG.
  *   flags: 0, or QLM_LINEAR_SYNC to wait and report device-side timeouts.
+ *   int4 handles return QLM_ERR_UNSUPPORTED (the tensor-core path is int8).
  * The first call on a device looks up the array's device address
  * (cudaGetSymbolAddress) with that device current; make that first call
  * before any stream capture. All calls on a device share the array, so calls
