@@ -187,8 +187,10 @@ int qlm_store_info(const char* path, const char* name, int* bits, int64_t* rows,
  *                     accumulation in the reference's order; exp in double, so
  *                     within a few ulp. Contexts up to ~50K positions. With a
  *                     device scratch of heads * (pos + 1) floats the work is
- *                     spread over (head, position block) and (head, 32 outputs)
- *                     CTAs in two launches (same results); NULL: one CTA per head. */
+ *                     spread over three launches — scores over (head, position
+ *                     block) CTAs, the softmax per head, V over (head, 32
+ *                     outputs) CTAs — with the same results; NULL: one CTA per
+ *                     head. */
 int qlm_rms_norm(const float* x, const float* w, float* y, int rows, int size, float eps, void* stream);
 int qlm_add_rms_norm(float* residual, const float* delta, const float* w, float* out, int rows, int size, float eps,
                      void* stream);

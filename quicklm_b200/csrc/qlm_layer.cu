@@ -351,7 +351,7 @@ __global__ void __launch_bounds__(256) gqa_attend_kernel(const float* __restrict
     }
 }
 
-// Position-parallel form of gqa_attend_kernel for long contexts, in two
+// Position-parallel form of gqa_attend_kernel for long contexts, in three
 // launches with the same arithmetic. Scores: CTA (head, block of 64 positions),
 // 16-thread groups as above, into scratch [heads][pos + 1].
 __global__ void __launch_bounds__(256) gqa_scores_kernel(const float* __restrict__ q, int q_stride,
@@ -398,39 +398,51 @@ __global__ void __launch_bounds__(256) gqa_scores_kernel(const float* __restrict
     }
 }
 
-// Softmax and V: CTA (head, block of 32 output elements), one warp. Every CTA
-// of a head recomputes the (cheap) softmax of the head's scores into shared
-// memory — max with the NaN rule, exp in double, the sum in position order,
-// the division — then each lane accumulates its output element over the
-// positions in order.
-__global__ void __launch_bounds__(32) gqa_softmax_v_kernel(const float* __restrict__ scores,
-                                                           const float* __restrict__ vc, float* __restrict__ out,
-                                                           int pos, int heads, int kv_heads, int d) {
-    extern __shared__ float pr[];  // [pos + 1]
-    const int h = blockIdx.x, lane = threadIdx.x;
-    const int kv_size = kv_heads * d, off = (h / (heads / kv_heads)) * d;
-    const float* sc = scores + (int64_t)h * (pos + 1);
+// Softmax of one head's scores in place, one CTA per head: max with the NaN
+// rule, exp in double, the sum in position order, the division.
+__global__ void __launch_bounds__(256) gqa_softmax_kernel(float* __restrict__ scores, int pos) {
+    __shared__ float red[34];
+    float* sc = scores + (int64_t)blockIdx.x * (pos + 1);
+    const int tid = threadIdx.x;
     float m = -INFINITY;
-    for (int p = lane; p <= pos; p += 32) {
-        const float v = sc[p];
-        pr[p] = v;
-        if (v > m) m = v;
-    }
+    for (int p = tid; p <= pos; p += blockDim.x)
+        if (sc[p] > m) m = sc[p];
     for (int o = 16; o; o >>= 1) {
         const float t = __shfl_xor_sync(0xffffffffu, m, o);
         m = t > m ? t : m;
     }
-    __syncwarp();
-    if (isnan(pr[0])) m = pr[0];
-    for (int p = lane; p <= pos; p += 32) pr[p] = (float)exp((double)__fsub_rn(pr[p], m));
-    __syncwarp();
-    float sum = 0.0f;
-    if (lane == 0) {
-#pragma unroll 8
-        for (int p = 0; p <= pos; ++p) sum = __fadd_rn(sum, pr[p]);
+    if ((tid & 31) == 0) red[tid >> 5] = m;
+    __syncthreads();
+    if (tid == 0) {
+        float mm = red[0];
+        for (int w = 1; w < (int)(blockDim.x >> 5); ++w) mm = red[w] > mm ? red[w] : mm;
+        red[32] = isnan(sc[0]) ? sc[0] : mm;
     }
-    sum = __shfl_sync(0xffffffffu, sum, 0);
-    for (int p = lane; p <= pos; p += 32) pr[p] = __fdiv_rn(pr[p], sum);
+    __syncthreads();
+    m = red[32];
+    for (int p = tid; p <= pos; p += blockDim.x) sc[p] = (float)exp((double)__fsub_rn(sc[p], m));
+    __syncthreads();
+    if (tid == 0) {
+        float sum = 0.0f;
+#pragma unroll 8
+        for (int p = 0; p <= pos; ++p) sum = __fadd_rn(sum, sc[p]);
+        red[33] = sum;
+    }
+    __syncthreads();
+    const float sum = red[33];
+    for (int p = tid; p <= pos; p += blockDim.x) sc[p] = __fdiv_rn(sc[p], sum);
+}
+
+// V: CTA (head, block of 32 output elements), one warp; the head's weights are
+// staged in shared memory, then each lane accumulates its output element over
+// the positions in order.
+__global__ void __launch_bounds__(32) gqa_v_kernel(const float* __restrict__ probs, const float* __restrict__ vc,
+                                                   float* __restrict__ out, int pos, int heads, int kv_heads, int d) {
+    extern __shared__ float pr[];  // [pos + 1]
+    const int h = blockIdx.x, lane = threadIdx.x;
+    const int kv_size = kv_heads * d, off = (h / (heads / kv_heads)) * d;
+    const float* src = probs + (int64_t)h * (pos + 1);
+    for (int p = lane; p <= pos; p += 32) pr[p] = src[p];
     __syncwarp();
     const int i = blockIdx.y * 32 + lane;
     if (i >= d) return;
@@ -559,7 +571,7 @@ int qlm_gqa_attend(const float* q, int q_stride, const float* k_cache, const flo
     if (!attr_set[dev]) {
         if (cudaFuncSetAttribute(qlm::gqa_attend_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  (int)kMaxSmem) != cudaSuccess ||
-            cudaFuncSetAttribute(qlm::gqa_softmax_v_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+            cudaFuncSetAttribute(qlm::gqa_v_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  (int)kMaxSmem) != cudaSuccess)
             return launched("gqa_attend attribute");
         attr_set[dev] = true;
@@ -575,10 +587,12 @@ int qlm_gqa_attend(const float* q, int q_stride, const float* k_cache, const flo
                                                                             kv_heads, head_dim);
     int rc = launched("gqa_scores launch");
     if (rc) return rc;
+    qlm::gqa_softmax_kernel<<<heads, 256, 0, s>>>(scratch, pos);
+    if ((rc = launched("gqa_softmax launch"))) return rc;
     const dim3 g2((unsigned)heads, (unsigned)((head_dim + 31) / 32));
-    qlm::gqa_softmax_v_kernel<<<g2, 32, (size_t)(pos + 1) * sizeof(float), s>>>(scratch, v_cache, out, pos, heads,
-                                                                                kv_heads, head_dim);
-    return launched("gqa_softmax_v launch");
+    qlm::gqa_v_kernel<<<g2, 32, (size_t)(pos + 1) * sizeof(float), s>>>(scratch, v_cache, out, pos, heads, kv_heads,
+                                                                        head_dim);
+    return launched("gqa_v launch");
 }
 
 int qlm_gdn_gates(const float* a_raw, const float* b_raw, const float* A_log, const float* dt_bias, float* decay,
