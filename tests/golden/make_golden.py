@@ -16,6 +16,10 @@ Writes:
   (cfg1 GEMV, cfg2 prefill, cfg4 projection sweep). Inputs are regenerated
   from the seed at test time; the input hash pins the generator.
 * ``cfg1_y.npy`` — the reference's config-1 output vector (6144 floats).
+* ``small_cases_int4.npz`` — the same small cases through the reference's int4
+  path: get_tensor_keep_int4's packed bytes ((K+1)/2 per row, value + 8, low
+  nibble = even column) and scales, and its int4 math::matmul output
+  (``--int4-only`` writes just this file).
 
 Synthetic-input convention: numpy ``default_rng(seed)``; W ~ N(0, 0.02^2)
 drawn first as float64 and cast to float32, then x ~ N(0, 1) likewise.
@@ -46,9 +50,21 @@ def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--skip-large", action="store_true", help="skip the lm_head-sized cfg4 shape")
     ap.add_argument("--threads", type=int, default=os.cpu_count() or 1)
+    ap.add_argument("--int4-only", action="store_true", help="write only small_cases_int4.npz")
     args = ap.parse_args()
     ref = RefCPU()
     ref.init_threads(args.threads)
+
+    arrays4 = {}
+    for i, spec in enumerate(SMALL_CASES):
+        x, w = make_small_case(spec)
+        p4, s4 = ref.quantize_int4(w)
+        arrays4[f"c{i}_p"] = p4
+        arrays4[f"c{i}_s"] = s4
+        arrays4[f"c{i}_y"] = ref.matmul_int4(x, p4, s4, w.shape[1])
+    np.savez_compressed(os.path.join(HERE, "small_cases_int4.npz"), **arrays4)
+    if args.int4_only:
+        return
 
     arrays = {}
     for i, spec in enumerate(SMALL_CASES):

@@ -41,6 +41,33 @@ def test_c_oracle_matmul_matches_golden(coracle, small_cases):
         assert bits_equal(y, arr["y"]), spec
 
 
+def _int4_golden():
+    return np.load(os.path.join(GOLDEN, "small_cases_int4.npz"))
+
+
+def test_c_oracle_q4_matches_golden(coracle, small_cases):
+    """The int4 restatement against the reference's int4 fixtures: packed bytes,
+    scales, and the int4 product as the int8 arithmetic on the unpacked values."""
+    from oracle.oracle import pack_q4, unpack_q4
+    z = _int4_golden()
+    for i, (spec, arr) in enumerate(small_cases):
+        v, s = coracle.quantize_q4(arr["w"])
+        assert np.array_equal(pack_q4(v), z[f"c{i}_p"]), spec
+        assert np.array_equal(s.view(np.uint32), z[f"c{i}_s"].view(np.uint32)), spec
+        k = arr["w"].shape[1]
+        y = coracle.matmul(arr["x"], unpack_q4(z[f"c{i}_p"], k), z[f"c{i}_s"])
+        assert bits_equal(y, z[f"c{i}_y"]), spec
+
+
+def test_reference_build_matches_golden_q4(refcpu, small_cases):
+    z = _int4_golden()
+    for i, (spec, arr) in enumerate(small_cases):
+        p, s = refcpu.quantize_int4(arr["w"])
+        assert np.array_equal(p, z[f"c{i}_p"]) and np.array_equal(s.view(np.uint32), z[f"c{i}_s"].view(np.uint32))
+        y = refcpu.matmul_int4(arr["x"], p, s, arr["w"].shape[1])
+        assert bits_equal(y, z[f"c{i}_y"]), spec
+
+
 def test_reference_build_matches_golden(refcpu, small_cases):
     """The prebuilt reference library reproduces the fixtures it generated."""
     for spec, arr in small_cases:
