@@ -1,4 +1,4 @@
-"""Benchmark of the int8 decode GEMV hot path (BASELINE metric, config 1).
+"""Benchmark of the int8 decode GEMV hot path (headline metric, configuration 1).
 
 Workload (N=1): config 1 — y = x . W^T with x fp32 [1, 2048] and W [6144, 2048]
 quantized by QuickLM's int8 scheme (per-32-block fp32 scales), computed by the

@@ -251,10 +251,14 @@ int qlm_linear_int8_grouped(const float* x, int M, int k, int64_t ldx, const qlm
  *          larger requests return QLM_ERR_INVALID_ARG.
  *   flags: 0, or QLM_LINEAR_SYNC to wait and report device-side timeouts.
  *   int4 handles return QLM_ERR_UNSUPPORTED (the tensor-core path is int8).
- * The first call on a device looks up the array's device address
- * (cudaGetSymbolAddress) with that device current; make that first call
- * before any stream capture. All calls on a device share the array, so calls
- * that may overlap on the GPU (unordered streams) race; order them. */
+ * Every call looks up the array's device address (cudaGetSymbolAddress) with
+ * the weight's device current. The first call on a device loads the library's
+ * device code there, which is when the array itself is allocated: make one
+ * call at start-up, before any stream capture. All calls on a device share
+ * the array and keep the last call's contents, so calls that may overlap on
+ * the GPU (unordered streams) race; order them. Device-side timeouts set a
+ * sticky status word in the array; qlm_device_status(device, reset) reports
+ * (and with reset != 0 clears) it, as does this call with QLM_LINEAR_SYNC. */
 int qlm_linear_int8_tc_noalloc(const float* x, int M, int k, int64_t ldx, const qlm_w8* w, float* y, int64_t ldy,
                                int flags, void* stream);
 
@@ -299,7 +303,8 @@ int qlm_argmax_f32(const float* logits, int n, int64_t col0, qlm_comm* c, int* o
 
 /* Status of bounded device-side waits on `device`: QLM_OK, or QLM_ERR_TIMEOUT
  * if a kernel gave up waiting since the last reset (reset != 0 clears it).
- * Synchronous tensor-core calls check this themselves. */
+ * Covers every entry point, qlm_linear_int8_tc_noalloc's status word included.
+ * Synchronous calls check this themselves. */
 int qlm_device_status(int device, int reset);
 
 /* Block until all work queued on `stream` is done (reports async errors). */

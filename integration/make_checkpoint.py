@@ -1,6 +1,6 @@
 """Write a seeded random-init QuickLM checkpoint (config.json + BF16 safetensors).
 
-Architecture = BASELINE config 3 (a Qwen3.5-style hybrid decoder): 24 layers,
+Architecture = benchmark configuration 3 (a Qwen3.5-style hybrid decoder): 24 layers,
 hidden 1024, 3 Gated-DeltaNet layers per full-attention layer (16 query heads,
 4 KV heads, head_dim 64, output-gated), DeltaNet 16 heads x 128, SwiGLU MLP
 3584, vocab 151936 (lm_head tied to the embedding), RoPE theta 1e6.

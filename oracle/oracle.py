@@ -30,6 +30,25 @@ def num_blocks(k: int) -> int:
     return (k + BLOCK - 1) // BLOCK
 
 
+def reference_root() -> str | None:
+    """QuickLM's source tree, if this machine has it: ``$QLM_REFERENCE_SRC``,
+    else the ``reference_path`` recorded in the repository's BASELINE.json.
+    None when neither names an existing directory (the GPU box: there the
+    prebuilt ``oracle/_ref`` files are used)."""
+    cand = os.environ.get("QLM_REFERENCE_SRC")
+    if not cand:
+        meta = os.path.join(os.path.dirname(HERE), "BASELINE.json")
+        try:
+            import json
+            with open(meta) as f:
+                cand = json.load(f).get("reference_path")
+        except (OSError, ValueError):
+            cand = None
+    if cand and os.path.isfile(os.path.join(cand, "src", "ops", "math_ops.cpp")):
+        return cand
+    return None
+
+
 def build(ref_root: str | None = None) -> None:
     """Compile both checkers with oracle/Makefile (the _ref part only when the
     reference tree is present)."""

@@ -158,6 +158,8 @@ int check_shard(int n_total, int k, int row_begin, int row_end) {
 
 namespace qlm_internal {
 void set_last_error(const std::string& msg) { g_err = msg; }
+// qlm_noalloc.cu: the allocation-free entry point's status word.
+cudaError_t noalloc_status(int device, int reset, int* code);
 }  // namespace qlm_internal
 
 extern "C" {
@@ -548,13 +550,18 @@ int qlm_device_status(int device, int reset) {
     DeviceState* st;
     int rc = device_state(device, &st);
     if (rc) return rc;
-    if (!st->status) return QLM_OK;
     DeviceGuard g(device);
     if (!g.ok) return set_err(QLM_ERR_CUDA, "cudaSetDevice(%d) failed", device);
     int code = 0;
-    QLM_CUDA(cudaMemcpy(&code, st->status, sizeof(int), cudaMemcpyDeviceToHost), "read status");
+    if (st->status) {
+        QLM_CUDA(cudaMemcpy(&code, st->status, sizeof(int), cudaMemcpyDeviceToHost), "read status");
+        if (code != 0 && reset) QLM_CUDA(cudaMemset(st->status, 0, sizeof(int)), "reset status");
+    }
+    // The allocation-free entry point keeps its own (sticky) word in its static scratch.
+    int code_na = 0;
+    QLM_CUDA(qlm_internal::noalloc_status(device, reset, &code_na), "read no-alloc status");
+    if (code == 0) code = code_na;
     if (code == 0) return QLM_OK;
-    if (reset) QLM_CUDA(cudaMemset(st->status, 0, sizeof(int)), "reset status");
     return set_err(QLM_ERR_TIMEOUT, "a device-side wait gave up (code 0x%x); results of that call are invalid", code);
 }
 

@@ -13,14 +13,19 @@
 // exponents (M ints) and a status word. Requests that do not fit are rejected.
 // Every call on a device shares the same array: calls whose work can overlap
 // on the GPU (different streams, no ordering between them) race on it.
+//
+// The status word is sticky: the array is zero when the module loads and no
+// call clears the word, so a device-side wait that gave up in an asynchronous
+// call (flags = 0) stays visible until qlm_device_status(device, reset != 0)
+// or a QLM_LINEAR_SYNC call of this entry point reads and clears it.
 #include "../../include/qlm_b200.h"
 #include "qlm_device.cuh"
 #include "qlm_handle.h"
 #include "qlm_kernels.h"
 
+#include <atomic>
 #include <cstdarg>
 #include <cstdio>
-#include <mutex>
 #include <string>
 
 namespace {
@@ -34,8 +39,9 @@ constexpr size_t kActBytes = kExpOffset;                          // fp16 activa
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
 
 constexpr int kMaxDevices = 64;
-void* g_scratch_addr[kMaxDevices] = {};
-std::mutex g_setup_mu;
+// Devices on which this entry point has run (so the status check below never
+// loads the module, and with it the 8 MiB array, on a device that never used it).
+std::atomic<bool> g_used[kMaxDevices];
 
 thread_local std::string g_err_local;
 
@@ -49,21 +55,18 @@ int fail(int code, const char* fmt, ...) {
     return code;
 }
 
-// Device address of the static scratch on `dev` (which must be current).
-// The host-side name g_noalloc_scratch is only a stand-in; the address comes
-// from cudaGetSymbolAddress, once per device.
-int scratch_for(int dev, unsigned char** out) {
-    if (dev < 0 || dev >= kMaxDevices) return fail(QLM_ERR_INVALID_ARG, "device %d out of range", dev);
-    std::lock_guard<std::mutex> lk(g_setup_mu);
-    if (!g_scratch_addr[dev]) {
-        void* ptr = nullptr;
-        const cudaError_t e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
-        if (e != cudaSuccess || !ptr)
-            return fail(QLM_ERR_CUDA, "cudaGetSymbolAddress(static scratch): %s", cudaGetErrorString(e));
-        g_scratch_addr[dev] = ptr;
-    }
-    *out = static_cast<unsigned char*>(g_scratch_addr[dev]);
-    return QLM_OK;
+// Device address of the static scratch on the current device. The host-side
+// name g_noalloc_scratch is only a stand-in for it. The address is looked up
+// on every call (cheap once the module is loaded), so a context that was
+// reset and reloaded never sees a stale pointer. The first lookup on a device
+// loads the library's device code there, which is when the array is
+// allocated: make one call at start-up, before any stream capture.
+cudaError_t scratch_here(unsigned char** out) {
+    void* ptr = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
+    if (e == cudaSuccess && !ptr) return cudaErrorInvalidSymbol;
+    *out = static_cast<unsigned char*>(ptr);
+    return e;
 }
 
 }  // namespace
@@ -71,7 +74,22 @@ int scratch_for(int dev, unsigned char** out) {
 // Defined in qlm_capi.cu: records the message for qlm_last_error().
 namespace qlm_internal {
 void set_last_error(const std::string& msg);
+
+// Status word of this entry point on `device` (which must be current): 0, or
+// the code of a device-side wait that gave up; cleared when reset != 0.
+// Reads nothing on a device where the entry point never ran.
+cudaError_t noalloc_status(int device, int reset, int* code) {
+    *code = 0;
+    if (device < 0 || device >= kMaxDevices || !g_used[device].load()) return cudaSuccess;
+    unsigned char* base = nullptr;
+    cudaError_t e = scratch_here(&base);
+    if (e != cudaSuccess) return e;
+    int* status = reinterpret_cast<int*>(base + kStatusOffset);
+    e = cudaMemcpy(code, status, sizeof(int), cudaMemcpyDeviceToHost);
+    if (e == cudaSuccess && *code != 0 && reset) e = cudaMemset(status, 0, sizeof(int));
+    return e;
 }
+}  // namespace qlm_internal
 
 extern "C" int qlm_linear_int8_tc_noalloc(const float* x, int M, int k, int64_t ldx, const qlm_w8* w, float* y,
                                           int64_t ldy, int flags, void* stream) {
@@ -109,13 +127,15 @@ extern "C" int qlm_linear_int8_tc_noalloc(const float* x, int M, int k, int64_t 
             break;
         }
         unsigned char* base = nullptr;
-        rc = scratch_for(w->device, &base);
         cudaStream_t s = static_cast<cudaStream_t>(stream);
-        if (rc == QLM_OK) {
+        cudaError_t e = scratch_here(&base);
+        if (e != cudaSuccess) {
+            rc = fail(QLM_ERR_CUDA, "cudaGetSymbolAddress(static scratch): %s", cudaGetErrorString(e));
+        } else {
+            if (w->device >= 0 && w->device < kMaxDevices) g_used[w->device].store(true);
             qlm::TcMaps maps;  // on the stack: encoding a tensor map allocates nothing
-            cudaError_t e = qlm::tc_make_weight_maps(w->q, w->s, w->rows, w->k_pad, &maps);
-            int* status = reinterpret_cast<int*>(base + kStatusOffset);
-            if (e == cudaSuccess) e = cudaMemsetAsync(status, 0, sizeof(int), s);  // must start at zero
+            e = qlm::tc_make_weight_maps(w->q, w->s, w->rows, w->k_pad, &maps);
+            int* status = reinterpret_cast<int*>(base + kStatusOffset);  // sticky: never cleared here
             if (e == cudaSuccess)
                 e = qlm::launch_gemm_tc(maps, w->ew, w->rows, k, x, ldx, M, base, reinterpret_cast<int*>(base + kExpOffset),
                                         y, ldy, status, s, false);
@@ -123,8 +143,12 @@ extern "C" int qlm_linear_int8_tc_noalloc(const float* x, int M, int k, int64_t 
                 e = cudaStreamSynchronize(s);
                 int code = 0;
                 if (e == cudaSuccess) e = cudaMemcpy(&code, status, sizeof(int), cudaMemcpyDeviceToHost);
-                if (e == cudaSuccess && code != 0)
-                    rc = fail(QLM_ERR_TIMEOUT, "a device-side wait gave up (code 0x%x)", code);
+                if (e == cudaSuccess && code != 0) {
+                    e = cudaMemset(status, 0, sizeof(int));
+                    if (e == cudaSuccess)
+                        rc = fail(QLM_ERR_TIMEOUT, "a device-side wait gave up (code 0x%x); results are invalid",
+                                  code);
+                }
             }
             if (e != cudaSuccess) rc = fail(QLM_ERR_CUDA, "tensor-core GEMM (static scratch): %s", cudaGetErrorString(e));
         }

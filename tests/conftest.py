@@ -18,7 +18,7 @@ if ROOT not in sys.path:
 
 def pytest_configure(config):
     config.addinivalue_line("markers", "gpu: needs a CUDA GPU (B200, sm_100a)")
-    config.addinivalue_line("markers", "slow: full-size BASELINE shapes")
+    config.addinivalue_line("markers", "slow: full-size benchmark shapes")
 
 
 @pytest.fixture(scope="session")
@@ -34,8 +34,8 @@ def refcpu():
     """QuickLM's own int8 path compiled from its sources (prebuilt .so)."""
     from oracle import oracle as o
     if not os.path.exists(o.REF_LIB):
-        ref_root = "/root/reference"  # development container only
-        if os.path.isdir(ref_root):
+        ref_root = o.reference_root()
+        if ref_root:
             o.build(ref_root)
     if not os.path.exists(o.REF_LIB):
         pytest.skip("reference build oracle/_ref/libqlm_refcpu.so not available")

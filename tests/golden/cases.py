@@ -1,6 +1,6 @@
 """Case definitions shared by the golden generator and the tests.
 
-The shapes are BASELINE's configs:
+The shapes are the benchmark configurations:
 * CFG1 — decode GEMV: x [1, 2048], W [6144, 2048], seed 0.
 * CFG2 — prefill GEMM: M in {64, 512, 2048} with W [6144, 2048] and
   [2048, 6144]; seed 1, 2, 3 for M = 64, 512, 2048.

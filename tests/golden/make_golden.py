@@ -1,10 +1,10 @@
 """Generate the committed golden fixtures from QuickLM's OWN int8 path.
 
-Run in the development container, where the reference tree exists and
+Run where the reference tree exists, so that
 ``oracle/_ref/libqlm_refcpu.so`` (compiled from the reference sources by
 ``oracle/Makefile``) can be built:
 
-    make -C oracle all && python tests/golden/make_golden.py [--skip-large]
+    make -C oracle all REF=<QuickLM source root> && python tests/golden/make_golden.py [--skip-large]
 
 Writes:
 * ``small_cases.npz`` — full inputs and outputs of small cases covering the
@@ -12,7 +12,7 @@ Writes:
   8/4, M > 8, all-zero blocks, NaN/Inf/subnormal weights, NaN/Inf
   activations, bf16 sources).
 * ``config_hashes.json`` — sha256 of the seeded inputs, of the reference's
-  quantized bytes/scales and of its outputs for every BASELINE config shape
+  quantized bytes/scales and of its outputs for every benchmark configuration shape
   (cfg1 GEMV, cfg2 prefill, cfg4 projection sweep). Inputs are regenerated
   from the seed at test time; the input hash pins the generator.
 * ``cfg1_y.npy`` — the reference's config-1 output vector (6144 floats).

@@ -1,4 +1,4 @@
-"""End to end: greedy decode of a seeded random-init
+"""End to end, benchmark configuration 3: greedy decode of a seeded random-init
 24-layer hybrid decoder (BF16 checkpoint, int8 weights), 64-token prompt of
 random ids, 128 new tokens — QuickLM's own model code with the int8 matmuls on
 the B200 (integration/_build/qlm_decode) against QuickLM entirely on the CPU

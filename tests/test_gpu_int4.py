@@ -65,7 +65,7 @@ def test_int4_row_shards(q, refcpu, m):
         w4.free()
 
 
-# BASELINE-sized projections (the first is a large vocabulary head): the
+# Benchmark-sized projections (the first is a large vocabulary head): the
 # quantizer is row-local, so a sample of rows is checked against the reference,
 # and the full product against the int8 path fed the unpacked int4 values.
 FULL = [(6144, 2048), (9728, 2560), (2560, 9728), (151936, 2560)]
