@@ -13,12 +13,25 @@ one GEMV each; the step is captured once as a CUDA graph and replayed.
 * roofline: algorithmic bytes per launch (weights + x + y) / mean launch time,
            against the measured HBM copy bandwidth
 * cpu_baseline: QuickLM's own AVX2 int8 path (compiled from its sources) on
-           this host's cores, same shapes, bounded sample
+           this host's cores, same shapes, bounded sample (N=1 only; also
+           on one thread)
+* parity: configuration 1's rows of every output against the hash of
+           QuickLM's own output; with N > 1 every gathered row against the
+           exact per-shard products gathered by NCCL. A mismatch fails the run.
+* sharded: configuration-4 shapes [151936,2560], [9728,2560], [2560,9728]
+           at M=1, row-sharded over the N ranks (strong scaling), each checked
+           against the reference output hash, the fused NVLink gather timed
+           beside the GEMV + NCCL all-gather
+* decode:  configuration 3 greedy decode tok/s through QuickLM's own model
+           code with the int8 path on the GPU, against QuickLM on the host
+           cores; token streams must be identical (N=1)
 
 With --gpus N > 1 (launched by torchrun) every rank holds its own 6144-row
-shard of a [6144*N, 2048] weight per stack entry and the outputs are
-all-gathered over NCCL after every GEMV (row-sharded, column-parallel
-linear); value aggregates all ranks' weight bytes ("weak" scaling).
+shard of a [6144*N, 2048] weight per stack entry (rank r's rows drawn with
+seed r; x is configuration 1's on every rank) and every GEMV gathers the
+full output on every rank (row-sharded, column-parallel linear; the gather is
+fused into the GEMV over NVLink); value aggregates all ranks' weight bytes
+("weak" scaling).
 
 ``--impl reference`` times the reference's CPU implementation instead and
 prints the same line with "impl": "reference".
@@ -181,25 +194,214 @@ def prefill_leg(qlm, torch, steps=50, warmup=5):
             "gpu_launches": 2 * launches}
 
 
-def cpu_baseline(x, q, s, seconds=10.0):
+# Configuration-4 projection shapes timed row-sharded (M=1): (rows, k, seed);
+# seed = 40 + the shape's index in the configuration, as the golden hashes use.
+SHARDED = [(151936, 2560, 44), (9728, 2560, 42), (2560, 9728, 43)]
+
+
+def golden_case(tag):
+    with open(os.path.join(ROOT, "tests", "golden", "config_hashes.json")) as f:
+        return json.load(f)["cases"][tag]
+
+
+def seeded_weight_cuda(torch, n, k, seed, chunk=8192):
+    """The benchmark's seeded W [n, k] ~ N(0, 0.02^2) (drawn in row chunks,
+    which gives the same numbers as one draw) straight into a CUDA tensor, and
+    x [1, k] ~ N(0, 1) drawn after it."""
+    rng = np.random.default_rng(seed)
+    w = torch.empty((n, k), dtype=torch.float32, device="cuda")
+    for s in range(0, n, chunk):
+        e = min(n, s + chunk)
+        w[s:e] = torch.from_numpy((rng.standard_normal((e - s, k)) * 0.02).astype(np.float32))
+    return w, rng.standard_normal((1, k)).astype(np.float32)
+
+
+def sha256_f32(t):
+    import hashlib
+    return hashlib.sha256(np.ascontiguousarray(t.detach().cpu().numpy()).tobytes()).hexdigest()
+
+
+def same_bits(torch, a, b):
+    return a.shape == b.shape and bool(torch.equal(a.contiguous().view(torch.int32), b.contiguous().view(torch.int32)))
+
+
+def sharded_leg(qlm, torch, dist, comm, world, rank, local, reps=20):
+    """Configuration-4 shapes at M=1, row-sharded over the N ranks (strong
+    scaling: the whole matrix is split, each rank quantizes and keeps its
+    rows). Per shape: every rank's gathered output is checked bit for bit
+    against the hash of QuickLM's own output for this seeded case (golden
+    fixtures made from the reference build), then timed as a CUDA graph over
+    enough weight copies to exceed L2 — the fused NVLink gather beside the
+    same GEMV followed by an NCCL all-gather. N=1: the unsharded GEMV."""
+    rows_out, ok_all = [], True
+    for n, k, seed in SHARDED:
+        h = golden_case(f"cfg4_m1_n{n}_k{k}")
+        w_full, x_np = seeded_weight_cuda(torch, n, k, seed)
+        b, e = qlm.shard_rows(n, world, rank)
+        w0 = qlm.Int8Weight.quantize(w_full, device=local, row_begin=b, row_end=e)
+        copies = max(2, -(-300_000_000 // w0.nbytes))
+        ws = [w0] + [qlm.Int8Weight.quantize(w_full, device=local, row_begin=b, row_end=e)
+                     for _ in range(copies - 1)]
+        del w_full
+        x = torch.from_numpy(x_np).cuda()
+        ys = [torch.empty((1, n), device="cuda") for _ in range(copies)]
+        stream = torch.cuda.Stream()
+
+        def calls():
+            for i in range(copies):
+                if world == 1:
+                    qlm.matmul(x, ws[i], ys[i], stream=stream)
+                else:
+                    qlm.matmul_allgather(x, ws[i], comm, ys[i], stream=stream)
+
+        with torch.cuda.stream(stream):
+            calls()
+        torch.cuda.synchronize()
+        ok = sha256_f32(ys[0]) == h["y"] and all(same_bits(torch, ys[i], ys[0]) for i in range(1, copies))
+        nccl_us = None
+        if world > 1 and n % world == 0:
+            yl = [torch.empty((1, e - b), device="cuda") for _ in range(copies)]
+            gl = [torch.empty((world, e - b), device="cuda") for _ in range(copies)]
+
+            def nccl_calls():
+                for i in range(copies):
+                    qlm.matmul(x, ws[i], yl[i], stream=stream)
+                    dist.all_gather_into_tensor(gl[i], yl[i])
+
+            with torch.cuda.stream(stream):
+                nccl_calls()
+            torch.cuda.synchronize()
+            ok = ok and same_bits(torch, gl[0].view(1, -1), ys[0])
+            dist.barrier()
+            n0, n1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            with torch.cuda.stream(stream):
+                n0.record(stream)
+                for _ in range(reps):
+                    nccl_calls()
+                n1.record(stream)
+            torch.cuda.synchronize()
+            t = torch.tensor([n0.elapsed_time(n1)], device="cuda")
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            nccl_us = float(t.item()) * 1000.0 / (reps * copies)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            calls()
+        with torch.cuda.stream(stream):
+            graph.replay()
+        torch.cuda.synchronize()
+        if dist is not None:
+            dist.barrier()
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(stream):
+            ev0.record(stream)
+            for _ in range(reps):
+                graph.replay()
+            ev1.record(stream)
+        torch.cuda.synchronize()
+        ms = ev0.elapsed_time(ev1)
+        if dist is not None:
+            t = torch.tensor([ms], device="cuda")
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+        us = ms * 1000.0 / (reps * copies)
+        ok = ok and qlm.load().qlm_device_status(local, 1) == 0
+        del graph
+        total_bytes = weight_bytes(n, k)
+        rows_out.append({"shape": [n, k], "rows_per_rank": e - b, "fused_us": round(us, 3),
+                         "fused_tb_s": round(total_bytes / us / 1e6, 3),
+                         "nccl_allgather_us": None if nccl_us is None else round(nccl_us, 3),
+                         "parity": "bit-exact (reference output hash)" if ok else "MISMATCH"})
+        ok_all = ok_all and ok
+        for w in ws:
+            w.free()
+        del ys, x
+        torch.cuda.empty_cache()
+    if dist is not None:
+        t = torch.tensor([1 if ok_all else 0], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MIN)
+        ok_all = bool(t.item())
+    return rows_out, ok_all
+
+
+def decode_leg(n_new=128, seed=7, prompt_len=64):
+    """Configuration 3 greedy decode (24-layer hybrid, hidden 1024, vocab
+    151936; seeded random-init BF16 checkpoint, int8 weights; 64-token prompt,
+    128 new tokens): QuickLM's own model code with the int8 path on this GPU
+    (integration/_build/qlm_decode) against QuickLM entirely on the host cores
+    (oracle/_ref/ref_decode). The token streams must be identical."""
+    import shutil
+    import tempfile
+    sys.path.insert(0, os.path.join(ROOT, "integration"))
+    from make_checkpoint import build as build_ckpt
+    gpu_bin = os.path.join(ROOT, "integration", "_build", "qlm_decode")
+    ref_bin = os.path.join(ROOT, "oracle", "_ref", "ref_decode")
+    for b in (gpu_bin, ref_bin):
+        if not os.path.exists(b):
+            return {"error": f"{os.path.relpath(b, ROOT)} missing (built by __graft_entry__.build())"}
+    d = tempfile.mkdtemp(prefix="qlm_cfg3_")
+    try:
+        build_ckpt(d, seed=seed, prompt_len=prompt_len)
+        threads = len(os.sched_getaffinity(0))
+        res = {}
+        for name, b in (("gpu", gpu_bin), ("reference", ref_bin)):
+            out = subprocess.run([b, d, os.path.join(d, "prompt_ids.txt"), str(n_new), str(threads)],
+                                 capture_output=True, text=True, timeout=1200)
+            if out.returncode != 0:
+                return {"error": f"{name} decode rc={out.returncode}: {out.stderr[-400:]}"}
+            res[name] = json.loads(out.stdout.strip().splitlines()[-1])
+        g, r = res["gpu"], res["reference"]
+        same = g["tokens"] == r["tokens"]
+        return {"metric": "greedy decode tok/s (cfg3, batch 1, 128 new tokens after a 64-token prompt)",
+                "value": round(g["decode_tok_s"], 2), "unit": "tok/s",
+                "reference_tok_s": round(r["decode_tok_s"], 2), "reference_threads": threads,
+                "speedup": round(g["decode_tok_s"] / r["decode_tok_s"], 3),
+                "prefill_s": {"gpu": g["prefill_s"], "reference": r["prefill_s"]},
+                "tokens_identical": same, "n_tokens": len(g["tokens"]),
+                "how": "integration/_build/qlm_decode vs oracle/_ref/ref_decode, host wall clock of the decode loop"}
+    finally:
+        shutil.rmtree(d, ignore_errors=True)
+
+
+def physical_cores(cpus):
+    """Physical cores among the logical CPUs `cpus` (from /proc/cpuinfo)."""
+    try:
+        seen, cur = set(), {}
+        with open("/proc/cpuinfo") as f:
+            for line in f.read().split("\n\n"):
+                kv = dict(ln.split(":", 1) for ln in line.splitlines() if ":" in ln)
+                kv = {a.strip(): b.strip() for a, b in kv.items()}
+                if "processor" in kv and int(kv["processor"]) in cpus:
+                    seen.add((kv.get("physical id", "0"), kv.get("core id", kv["processor"])))
+        return len(seen) or len(cpus)
+    except (OSError, ValueError):
+        return len(cpus)
+
+
+def cpu_baseline(x, q, s, seconds=10.0, seconds_1t=4.0):
     """QuickLM's own int8 math::matmul (oracle/_ref, strict build) on this
-    host's cores: M=1 GEMVs rotating over STACK copies (larger than the LLC)."""
+    host's cores: M=1 GEMVs rotating over STACK copies (larger than the LLC),
+    with one thread per logical CPU of this process, and with one thread."""
     from oracle.oracle import RefCPU
-    cores = len(os.sched_getaffinity(0))
+    cpus = sorted(os.sched_getaffinity(0))
     ref = RefCPU()
-    ref.init_threads(cores)
     qs = [q.copy() for _ in range(STACK)]
     ss = [s.copy() for _ in range(STACK)]
-    ref.matmul_stack_ms(x, qs, ss, rounds=1)  # warm-up
-    rounds, total_ms = 0, 0.0
-    while total_ms < seconds * 1000.0:
-        total_ms += ref.matmul_stack_ms(x, qs, ss, rounds=1)
-        rounds += 1
-    gemvs = rounds * STACK
-    gbs = gemvs * weight_bytes() / (total_ms / 1000.0) / 1e9
-    return {"value": round(gbs, 3), "unit": "GB/s", "cores": cores, "kind": "reference",
+
+    def rate(threads, budget):
+        ref.init_threads(threads)
+        ref.matmul_stack_ms(x, qs, ss, rounds=1)  # warm-up
+        rounds, total_ms = 0, 0.0
+        while total_ms < budget * 1000.0:
+            total_ms += ref.matmul_stack_ms(x, qs, ss, rounds=1)
+            rounds += 1
+        return rounds * STACK * weight_bytes() / (total_ms / 1000.0) / 1e9, rounds * STACK, total_ms / 1000.0
+
+    gbs, gemvs, secs = rate(len(cpus), seconds)
+    gbs1, gemvs1, secs1 = rate(1, seconds_1t)
+    return {"value": round(gbs, 3), "unit": "GB/s", "cores": len(cpus), "physical_cores": physical_cores(set(cpus)),
+            "kind": "reference", "one_thread": {"value": round(gbs1, 3), "unit": "GB/s", "sample": f"{gemvs1} GEMVs ({secs1:.1f} s)"},
             "sample": f"{gemvs} M=1 GEMVs [6144,2048] over {STACK} rotating weight copies "
-                      f"({total_ms / 1000.0:.1f} s), math::init_thread_pool({cores})"}
+                      f"({secs:.1f} s), math::init_thread_pool({len(cpus)})"}
 
 
 def run_reference(args):
@@ -304,6 +506,8 @@ def main():
     ap.add_argument("--shape", help="N,K: time the exact GEMV on this weight shape only")
     ap.add_argument("--bits", type=int, default=8, choices=[4, 8])
     ap.add_argument("--m", type=int, default=1)
+    ap.add_argument("--no-decode", action="store_true", help="skip the configuration-3 decode leg")
+    ap.add_argument("--no-sharded", action="store_true", help="skip the configuration-4 sharded-shape table")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.impl == "reference":
@@ -329,7 +533,8 @@ def main():
 
     # Inputs: rank r holds rows [6144 r, 6144 (r+1)) of a [6144 N, 2048] weight
     # (rank 0's rows are config 1's W); x is config 1's x on every rank.
-    x_np, w_np = synth_case(1, N_ROWS, K_DIM, 0 + rank)
+    x_np = synth_case(1, N_ROWS, K_DIM, 0)[0]
+    w_np = synth_case(1, N_ROWS, K_DIM, rank)[1]
     n_total = N_ROWS * world
     w_glob = torch.empty((n_total, K_DIM), device="cuda")
     w_glob[rank * N_ROWS:(rank + 1) * N_ROWS] = torch.from_numpy(w_np).cuda()
@@ -358,6 +563,23 @@ def main():
         for _ in range(3):
             step()
     torch.cuda.synchronize()
+    # Parity before timing: rows [0, 6144) of every output are configuration 1
+    # (seed 0), checked against the hash of QuickLM's own output; with N > 1
+    # every gathered row is checked against the exact per-shard products
+    # gathered by NCCL.
+    cfg1_hash = golden_case("cfg1")["y"]
+    parity_ok = all(sha256_f32(ys[i][:, :N_ROWS]) == cfg1_hash for i in range(STACK))
+    if world > 1:
+        yl = torch.empty((1, N_ROWS), device="cuda")
+        gl = torch.empty((world, N_ROWS), device="cuda")
+        for i in range(STACK):
+            qlm.matmul(x, weights[i], yl)
+            dist.all_gather_into_tensor(gl, yl)
+            parity_ok = parity_ok and same_bits(torch, gl.view(1, -1), ys[i])
+        t = torch.tensor([1 if parity_ok else 0], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MIN)
+        parity_ok = bool(t.item())
+        del yl, gl
     nccl_gbs = None
     if world > 1:
         # Reference point: the same shards gathered with NCCL after every GEMV (eager).
@@ -460,6 +682,10 @@ def main():
         e2e_s = float(t.item())
     e2e = args.e2e_calls * weight_bytes() * world / e2e_s / 1e9
 
+    sharded, sharded_ok = None, True
+    if not args.no_sharded:
+        sharded, sharded_ok = sharded_leg(qlm, torch, dist, comm, world, rank, local)
+
     prefill = None
     if world == 1 and not args.no_prefill:
         try:
@@ -468,9 +694,17 @@ def main():
             prefill = {"error": f"{type(exc).__name__}: {exc}"}
 
     base = None
-    if rank == 0 and not args.no_cpu_baseline:
+    if world == 1 and not args.no_cpu_baseline:  # never while other ranks spin in a collective
         q_ref, s_ref = weights[0].to_int8()
         base = cpu_baseline(x_np, q_ref, s_ref, args.cpu_seconds)
+
+    decode = None
+    if world == 1 and not args.no_decode:
+        try:
+            decode = decode_leg()
+        except Exception as exc:  # reported, never hidden
+            decode = {"error": f"{type(exc).__name__}: {exc}"}
+    all_ok = parity_ok and sharded_ok and (decode is None or decode.get("tokens_identical", True))
 
     used_graph = graph is not None
     graph = None
@@ -485,7 +719,7 @@ def main():
                        "l2": f"inputs larger than L2 ({STACK}x{weight_bytes() / 1e6:.2f} MB weights per step)",
                        "parallelism": "single GPU" if world == 1 else
                        f"row-sharded x{world}, all-gather fused into the GEMV (NVLink peer stores)",
-                       "kernel": "gemv_kernel<1,R> (CUDA cores, bit-exact)" if world == 1 else
+                       "kernel": "gemv_dec_kernel (CUDA cores, bit-exact)" if world == 1 else
                        "gemv_kernel<1,R,gather> (fused NVLink all-gather)", "cuda_graph": used_graph,
                        "pdl": os.environ.get("QLM_PDL", "1") != "0"},
             "pct_hbm_peak": round(100.0 * value / world / peak, 2),
@@ -501,6 +735,11 @@ def main():
             "clocks": clk,
             "cpu_baseline": base,
             "prefill": prefill,
+            "parity": "bit-exact" if parity_ok and sharded_ok else "MISMATCH",
+            "parity_how": "cfg1 rows vs the reference output hash; N>1: gathered rows vs NCCL-gathered exact shards; "
+                          "sharded shapes vs the reference output hashes",
+            "sharded": sharded,
+            "decode": decode,
         }
         print(json.dumps(line), flush=True)
     for w in weights:
@@ -512,7 +751,7 @@ def main():
     if dist is not None:
         dist.barrier()
         dist.destroy_process_group()
-    return 0
+    return 0 if all_ok else 1
 
 
 if __name__ == "__main__":

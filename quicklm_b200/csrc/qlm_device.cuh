@@ -81,6 +81,12 @@ __device__ __forceinline__ void bulk_copy_g2s(uint32_t dst, const void* src, uin
                  "l"(src), "r"(bytes), "r"(bar)
                  : "memory");
 }
+// Bring `bytes` (a multiple of 16) of global memory at `src` (16-byte
+// aligned) into L2 without a destination: the copy engine fetches it while
+// the issuing thread goes on.
+__device__ __forceinline__ void prefetch_l2_bulk(const void* src, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
 // Order this thread's earlier generic-proxy shared-memory accesses before
 // later async-proxy (bulk copy) writes to the same memory.
 __device__ __forceinline__ void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }

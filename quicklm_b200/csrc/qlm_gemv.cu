@@ -51,6 +51,8 @@
 // microsecond. The activations for all MM rows are staged once per CTA in a
 // lane-permuted shared layout (one conflict-free float4 per lane per step).
 // Waits are bounded: on give-up the kernel records a status code and stops.
+#include <cstdlib>
+
 #include "qlm_device.cuh"
 #include "qlm_kernels.h"
 #include "qlm_sm100.cuh"
@@ -571,6 +573,16 @@ bool gemv_supported(int mm, int rows, int k, int sm_count, bool q4) {
 
 namespace {
 
+// QLM_GEMV_DECODE=0 selects the single-role kernel for M = 1 as well (for
+// comparisons); the default is the producer/consumer decode form.
+bool decode_form_enabled() {
+    static const bool on = [] {
+        const char* e = std::getenv("QLM_GEMV_DECODE");
+        return !(e && e[0] == '0');
+    }();
+    return on;
+}
+
 template <bool Q4>
 cudaError_t launch_mm_any(int mm, const GemvParams& p, const Plan& pl, cudaStream_t stream, bool pdl) {
     switch (mm) {
@@ -597,6 +609,8 @@ cudaError_t launch_gemv_grouped(const float* x, int64_t ldx, int mm, const GemvW
         if (ws[g].rows < 1 || !ws[g].maps) return cudaErrorInvalidValue;
         rows_total += ws[g].rows;
     }
+    if (mm == 1 && !gather && decode_form_enabled() && gemv_decode_supported(rows_total, nw, k, sm_count, q4))
+        return launch_gemv_decode(x, ws, nw, k, status, sm_count, stream, pdl, q4);
     const int r = pick_rows_per_thread(mm, rows_total, sm_count);
     int rows_eff = 0;  // whole units per weight
     for (int g = 0; g < nw; ++g) rows_eff += round_up(ws[g].rows, 4 * r);

@@ -112,6 +112,13 @@ cudaError_t launch_gemv_grouped(const float* x, int64_t ldx, int mm, const GemvW
 // Whether the exact GEMV can stage mm activation rows of length k.
 bool gemv_supported(int mm, int rows, int k, int sm_count, bool q4 = false);
 
+// Decode (M = 1) form of the exact GEMV (qlm_gemv_decode.cu): producer warps
+// form block sums with the activations in registers, chain warps run the
+// ordered FMA chains; bit-identical outputs. Serves k up to 12 * 8 * 128.
+bool gemv_decode_supported(int rows_total, int nw, int k, int sm_count, bool q4);
+cudaError_t launch_gemv_decode(const float* x, const GemvWeight* ws, int nw, int k, int* status, int sm_count,
+                               cudaStream_t stream, bool pdl, bool q4);
+
 // ---- tensor-core prefill GEMM (qlm_gemm_tc.cu) ----
 struct TcMaps {
     alignas(64) CUtensorMap w;  // packed int8 rows, 128 x 128-byte boxes
