@@ -280,6 +280,20 @@ int qlm_comm_create(int device, int rank, int nranks, int64_t max_out, qlm_comm*
 int qlm_comm_connect(qlm_comm* c, const void* all_handles);
 void qlm_comm_free(qlm_comm* c);
 
+/* Failure detection for the row-sharded calls below (no counterpart in the
+ * reference, which is single-process). Every wait of this rank's kernels for a
+ * peer's data is bounded: after `us` microseconds (default 2 s) the kernel gives
+ * up, records a status code and returns. From then on the communicator is
+ * failed: its kernels do nothing and every call on it returns
+ * QLM_ERR_TIMEOUT; free it and create a new one on every rank (new exchange
+ * buffers and epochs) to go on.
+ *   qlm_comm_set_timeout_us: the wait limit for later calls (1 us .. 600 s).
+ *   qlm_comm_status:         QLM_OK, or QLM_ERR_TIMEOUT if a wait of this
+ *                            rank's calls gave up (reads the device status;
+ *                            synchronous). SYNC calls check it themselves. */
+int qlm_comm_set_timeout_us(qlm_comm* c, int64_t us);
+int qlm_comm_status(qlm_comm* c);
+
 /* y[0, 0:n_total] = x[0, 0:k] . W^T for a row-sharded W: this rank's shard w
  * (rows [row_begin, row_end) of n_total) is computed and stored into every
  * rank's exchange buffer over NVLink by the GEMV kernel itself; a bounded wait

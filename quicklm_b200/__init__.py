@@ -24,7 +24,7 @@ import os
 import numpy as np
 
 __all__ = ["QlmError", "Int8Weight", "matmul", "matmul_grouped", "argmax", "load", "LIB_PATH", "EXACT", "TENSOR", "HOST_IO", "SYNC",
-           "BLOCK", "Comm", "shard_rows", "matmul_allgather", "save", "store_info", "rms_norm", "add_rms_norm",
+           "BLOCK", "Comm", "exchange_handles", "shard_rows", "matmul_allgather", "save", "store_info", "rms_norm", "add_rms_norm",
            "silu_mul", "rope_neox", "rope_neox_tables", "silu", "conv1d_update_tapmajor", "l2norm_heads",
            "gdn_gates", "gdn_recurrence", "rms_norm_gain", "gqa_attend"]
 
@@ -43,7 +43,7 @@ ABI_SYMBOLS = (
     "qlm_weight_import_int4", "qlm_store_save", "qlm_store_load", "qlm_store_info", "qlm_rms_norm",
     "qlm_add_rms_norm", "qlm_silu_mul", "qlm_rope_neox", "qlm_rope_neox_tables", "qlm_silu",
     "qlm_conv1d_update_tapmajor", "qlm_l2norm_heads", "qlm_gdn_gates", "qlm_gdn_recurrence", "qlm_rms_norm_gain",
-    "qlm_gqa_attend",
+    "qlm_gqa_attend", "qlm_comm_set_timeout_us", "qlm_comm_status",
 )
 
 _STATUS = {0: "OK", 1: "INVALID_ARG", 2: "CUDA", 3: "OUT_OF_MEMORY", 4: "UNSUPPORTED", 5: "TIMEOUT", 6: "NCCL",
@@ -110,6 +110,8 @@ def load(path: str = LIB_PATH):
     lib.qlm_comm_connect.argtypes = [P, P]
     lib.qlm_comm_free.argtypes = [P]
     lib.qlm_comm_free.restype = None
+    lib.qlm_comm_set_timeout_us.argtypes = [P, L]
+    lib.qlm_comm_status.argtypes = [P]
     lib.qlm_linear_int8_allgather.argtypes = [P, I, I, L, P, P, P, L, I, P]
     lib.qlm_argmax_f32.argtypes = [P, I, L, P, P, P, I, P]
     lib.qlm_linear_int8_grouped.argtypes = [P, I, I, L, P, I, P, P, I, P]
@@ -354,6 +356,18 @@ def shard_rows(n: int, nranks: int, rank: int):
     return begin, begin + q + (1 if rank < r else 0)
 
 
+def exchange_handles(local: bytes, nranks: int, exchange) -> bytes:
+    """All ranks' exchange handles, in rank order, as one buffer for
+    qlm_comm_connect. ``exchange(local)`` must return every rank's handle in
+    rank order (e.g. ``all_gather_object`` over torch.distributed); each must
+    be as long as this rank's."""
+    handles = exchange(bytes(local))
+    if handles is None or len(handles) != nranks or any(not isinstance(h, (bytes, bytearray)) or
+                                                        len(h) != len(local) for h in handles):
+        raise QlmError(1, "handle exchange returned the wrong number or size of handles")
+    return b"".join(bytes(h) for h in handles)
+
+
 class Comm:
     """One rank's NVLink exchange buffer for row-sharded outputs.
 
@@ -369,12 +383,21 @@ class Comm:
         _check(lib.qlm_comm_create(device, rank, nranks, max_out, ctypes.byref(h), buf))
         self._h = h
         self.device, self.rank, self.nranks, self.max_out = device, rank, nranks, max_out
-        handles = exchange(buf.raw)
-        if len(handles) != nranks or any(len(x) != nb for x in handles):
+        try:
+            allb = exchange_handles(buf.raw, nranks, exchange)
+        except QlmError:
             self.free()
-            raise QlmError(1, "handle exchange returned the wrong number or size of handles")
-        allb = ctypes.create_string_buffer(b"".join(handles), nb * nranks)
-        _check(lib.qlm_comm_connect(self._h, allb))
+            raise
+        _check(lib.qlm_comm_connect(self._h, ctypes.create_string_buffer(allb, len(allb))))
+
+    def set_timeout(self, seconds: float) -> None:
+        """Bound of every wait for a peer in later calls (default 2 s)."""
+        _check(load().qlm_comm_set_timeout_us(self.handle, max(1, int(seconds * 1e6))))
+
+    def status(self) -> None:
+        """Raise QlmError (TIMEOUT) if a wait of this rank gave up; the
+        communicator must then be freed and recreated on every rank."""
+        _check(load().qlm_comm_status(self.handle))
 
     @property
     def handle(self):

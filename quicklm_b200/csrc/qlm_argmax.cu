@@ -25,7 +25,6 @@ namespace qlm {
 namespace {
 
 constexpr int kThreads = 1024;
-constexpr long long kWaitBudget = 4000000000LL;  // ~2 s of SM clock
 constexpr int kStatusArgmaxTimeout = 0x203;
 constexpr uint32_t kIdxNone = 0xFFFFFFu;     // no non-NaN logit in the shard
 constexpr uint32_t kIdxFirstNan = 0xFFFFFEu;  // global logit 0 is NaN: the answer is 0
@@ -96,6 +95,8 @@ __global__ void __launch_bounds__(kThreads) argmax_kernel(const float* __restric
         }
         return;
     }
+    // A failed communicator (a bounded wait gave up earlier): do nothing.
+    if (a.status && *reinterpret_cast<volatile const int*>(a.status) != 0) return;
     const int e = *reinterpret_cast<volatile const int*>(a.epoch) + 1;
     const unsigned long long* mine = a.peer_words[a.rank] + (e & 1) * kMaxRanks;
     if (threadIdx.x == 0) {
@@ -108,11 +109,11 @@ __global__ void __launch_bounds__(kThreads) argmax_kernel(const float* __restric
     }
     if ((int)threadIdx.x < a.nranks) {
         const int r = threadIdx.x;
-        const long long t0 = clock64();
+        const long long t0 = globaltimer_ns();
         unsigned long long w = ld_relaxed_sys_u64(mine + r);
         bool ok = true;
         while ((int)(w >> 56) != (0x80 | (e & 0x7F))) {
-            if (clock64() - t0 > kWaitBudget) {
+            if (globaltimer_ns() - t0 > a.wait_ns) {
                 ok = false;
                 if (a.status) atomicCAS(a.status, 0, kStatusArgmaxTimeout);
                 break;
@@ -140,7 +141,7 @@ __global__ void __launch_bounds__(kThreads) argmax_kernel(const float* __restric
             *out_idx = best.i;
             *out_val = best.i < 0 ? __int_as_float(0x7fc00000) : best.v;
         }
-        *const_cast<volatile int*>(a.epoch) = e;
+        if (*reinterpret_cast<volatile const int*>(a.status) == 0) *const_cast<volatile int*>(a.epoch) = e;
     }
 }
 

@@ -36,6 +36,8 @@ struct qlm_comm {
     char* peers[qlm::kMaxRanks] = {};  // every rank's buffer as seen from this device
     bool opened[qlm::kMaxRanks] = {};
     int* state = nullptr;              // [0] CTA counter, [1] epoch, [2] status
+    long long wait_ns = 2000000000LL;  // bounded waits for peers give up after this long
+    bool failed = false;               // a wait gave up: every later call is refused
 };
 
 namespace qlm_internal {
@@ -115,6 +117,28 @@ int qlm_comm_create(int device, int rank, int nranks, int64_t max_out, qlm_comm*
 
 int qlm_comm_handle_bytes(void) { return (int)sizeof(cudaIpcMemHandle_t); }
 
+int qlm_comm_set_timeout_us(qlm_comm* c, int64_t us) {
+    if (!c) return fail(QLM_ERR_INVALID_ARG, "NULL communicator");
+    if (us < 1 || us > 600000000LL) return fail(QLM_ERR_INVALID_ARG, "timeout %lld us not in [1, 6e8]", (long long)us);
+    c->wait_ns = (long long)us * 1000LL;
+    return QLM_OK;
+}
+
+int qlm_comm_status(qlm_comm* c) {
+    if (!c) return fail(QLM_ERR_INVALID_ARG, "NULL communicator");
+    if (c->failed) return fail(QLM_ERR_TIMEOUT, "the communicator failed earlier (a peer did not answer); free and recreate it");
+    Dev g(c->device);
+    if (!g.ok) return fail(QLM_ERR_CUDA, "cudaSetDevice(%d) failed", c->device);
+    int code = 0;
+    const cudaError_t e = cudaMemcpy(&code, c->state + 2, sizeof(int), cudaMemcpyDeviceToHost);
+    if (e != cudaSuccess) return cuda_fail(e, "read status");
+    if (code) {
+        c->failed = true;
+        return fail(QLM_ERR_TIMEOUT, "a bounded wait for peer ranks gave up (code 0x%x); free and recreate the communicator", code);
+    }
+    return QLM_OK;
+}
+
 int qlm_comm_connect(qlm_comm* c, const void* all_handles) {
     if (!c || !all_handles) return fail(QLM_ERR_INVALID_ARG, "NULL argument");
     Dev g(c->device);
@@ -153,11 +177,13 @@ int qlm_linear_int8_allgather(const float* x, int M, int k, int64_t ldx, const q
     if (flags & ~QLM_LINEAR_SYNC) return fail(QLM_ERR_INVALID_ARG, "only QLM_LINEAR_SYNC is accepted (device pointers)");
     for (int r = 0; r < c->nranks; ++r)
         if (!c->peers[r]) return fail(QLM_ERR_INVALID_ARG, "communicator not connected (rank %d)", r);
+    if (c->failed) return fail(QLM_ERR_TIMEOUT, "the communicator failed earlier (a peer did not answer); free and recreate it");
     Dev g(c->device);
     if (!g.ok) return fail(QLM_ERR_CUDA, "cudaSetDevice(%d) failed", c->device);
     cudaStream_t s = static_cast<cudaStream_t>(stream);
 
     qlm::GatherArgs ga{};
+    ga.wait_ns = c->wait_ns;
     for (int r = 0; r < c->nranks; ++r) {
         ga.peer_slots[r] = reinterpret_cast<unsigned long long*>(c->peers[r] + kHeaderBytes);
     }
@@ -178,8 +204,8 @@ int qlm_linear_int8_allgather(const float* x, int M, int k, int64_t ldx, const q
         e = cudaMemcpy(&code, c->state + 2, sizeof(int), cudaMemcpyDeviceToHost);
         if (e != cudaSuccess) return cuda_fail(e, "read status");
         if (code) {
-            cudaMemset(c->state + 2, 0, sizeof(int));
-            return fail(QLM_ERR_TIMEOUT, "a bounded wait for peer ranks gave up (code 0x%x)", code);
+            c->failed = true;  // the status word stays set: later kernels on c do nothing
+            return fail(QLM_ERR_TIMEOUT, "a bounded wait for peer ranks gave up (code 0x%x); free and recreate the communicator", code);
         }
     }
     return QLM_OK;
@@ -198,7 +224,9 @@ int qlm_argmax_f32(const float* logits, int n, int64_t col0, qlm_comm* c, int* o
     if (c) {
         for (int r = 0; r < c->nranks; ++r)
             if (!c->peers[r]) return fail(QLM_ERR_INVALID_ARG, "communicator not connected (rank %d)", r);
+        if (c->failed) return fail(QLM_ERR_TIMEOUT, "the communicator failed earlier (a peer did not answer); free and recreate it");
         for (int r = 0; r < c->nranks; ++r) a.peer_words[r] = reinterpret_cast<unsigned long long*>(c->peers[r]);
+        a.wait_ns = c->wait_ns;
         a.epoch = c->state + 1;
         a.status = c->state + 2;
         a.nranks = c->nranks;
@@ -221,8 +249,8 @@ int qlm_argmax_f32(const float* logits, int n, int64_t col0, qlm_comm* c, int* o
             e = cudaMemcpy(&code, c->state + 2, sizeof(int), cudaMemcpyDeviceToHost);
             if (e != cudaSuccess) return cuda_fail(e, "read status");
             if (code) {
-                cudaMemset(c->state + 2, 0, sizeof(int));
-                return fail(QLM_ERR_TIMEOUT, "a bounded wait for peer ranks gave up (code 0x%x)", code);
+                c->failed = true;
+                return fail(QLM_ERR_TIMEOUT, "a bounded wait for peer ranks gave up (code 0x%x); free and recreate the communicator", code);
             }
         }
     }

@@ -165,6 +165,13 @@ __device__ __forceinline__ unsigned long long ld_relaxed_sys_u64(const unsigned 
     return v;
 }
 
+// Nanoseconds of the GPU's global timer (for wait limits given in time).
+__device__ __forceinline__ long long globaltimer_ns() {
+    long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
 // Programmatic dependent launch (sm_90+): let the next kernel in the stream
 // start launching, and wait until the previous kernel's results are visible.
 // Both are no-ops when the launch did not opt in.

@@ -226,6 +226,9 @@ __global__ void __launch_bounds__(MM == 1 ? 384 : 512, MM == 1 ? 2 : 1)
     // plan requests 128 spare bytes).
     uint8_t* smem = smem_raw + ((128u - (sm100::smem_u32(smem_raw) & 127u)) & 127u);
     using namespace sm100;
+    // A communicator whose bounded wait gave up is failed: do nothing (the
+    // host reports QLM_ERR_TIMEOUT until it is freed and recreated).
+    if (GATHER && *reinterpret_cast<volatile const int*>(p.status) != 0) return;
     const int warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5, lane32 = threadIdx.x & 31;
     const int lane = threadIdx.x & 7;                // reference lane l
     const int rsub = ((threadIdx.x >> 3) & 3) * R;   // first of the thread's R rows within the unit
@@ -445,11 +448,11 @@ __global__ void __launch_bounds__(MM == 1 ? 384 : 512, MM == 1 ? 2 : 1)
         const int per = (p.ga.n_total + (int)gridDim.x - 1) / (int)gridDim.x;
         const int c0 = min((int)blockIdx.x * per, p.ga.n_total), c1 = min(c0 + per, p.ga.n_total);
         const unsigned long long* mine = p.ga.peer_slots[p.ga.rank] + g_half;
-        const long long t0 = clock64();
+        const long long t0 = globaltimer_ns();
         for (int i = c0 + (int)threadIdx.x; i < c1; i += blockDim.x) {
             unsigned long long v = ld_relaxed_sys_u64(mine + i);
             while ((int)(v >> 32) != g_epoch) {
-                if (clock64() - t0 > kWaitBudget) {
+                if (globaltimer_ns() - t0 > p.ga.wait_ns) {
                     if (p.status) atomicCAS(p.status, 0, kStatusGatherTimeout);
                     break;
                 }
@@ -460,10 +463,15 @@ __global__ void __launch_bounds__(MM == 1 ? 384 : 512, MM == 1 ? 2 : 1)
         }
         __syncthreads();
         if (threadIdx.x == 0) {
+            __threadfence();
             is_last = atomicAdd(p.ga.counter, 1) == (int)gridDim.x - 1;
             if (is_last) {
+                __threadfence();
                 *p.ga.counter = 0;
-                *const_cast<volatile int*>(p.ga.epoch) = g_epoch;
+                // After a give-up the communicator is failed: its epoch stays
+                // where it was and every later call returns at entry.
+                if (*reinterpret_cast<volatile int*>(p.status) == 0)
+                    *const_cast<volatile int*>(p.ga.epoch) = g_epoch;
             }
         }
     }

@@ -81,6 +81,12 @@ __device__ __forceinline__ int dec_weight_of(const DecParams& p, int g) {
     return w;
 }
 
+__device__ __forceinline__ float4 lds_f4(uint32_t addr) {
+    float4 v;
+    asm volatile("ld.shared.v4.f32 {%0,%1,%2,%3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(addr));
+    return v;
+}
+
 __device__ __forceinline__ void sts_u64x2(uint32_t addr, unsigned long long a, unsigned long long b) {
     asm volatile("st.shared.v2.u64 [%0], {%1, %2};" ::"r"(addr), "l"(a), "l"(b) : "memory");
 }
@@ -284,20 +290,20 @@ __global__ void __launch_bounds__(CPT == 1 ? 512 : 384, 2) gemv_dec_kernel(const
             if (lane32 == 0 && p.status) atomicCAS(p.status, 0, kDecStatusTimeout);
             break;
         }
-        const uint8_t* sb = slots + (size_t)slot * p.slot_bytes;
-        const float4* bsp = reinterpret_cast<const float4*>(sb + bs_off) + ri * p.nck * 8 + l;
-        const float4* scp = reinterpret_cast<const float4*>(sb + sc_off) + ri * p.nck;
+        const uint32_t sb = smem_u32(slots + (size_t)slot * p.slot_bytes);
+        const uint32_t bsp = sb + bs_off + (ri * p.nck * 8 + l) * 16;  // + c * 128 per chunk
+        const uint32_t scp = sb + sc_off + ri * p.nck * 16;             // + c * 16 per chunk
         float t = 0.0f;
 #pragma unroll 4
         for (int c = 0; c < cfull; ++c) {
-            const float4 v = bsp[c * 8], s = scp[c];
+            const float4 v = lds_f4(bsp + c * 128), s = lds_f4(scp + c * 16);
             t = __fmaf_rn(v.x, s.x, t);
             t = __fmaf_rn(v.y, s.y, t);
             t = __fmaf_rn(v.z, s.z, t);
             t = __fmaf_rn(v.w, s.w, t);
         }
         if (rem_blocks) {
-            const float4 v = bsp[cfull * 8], s = scp[cfull];
+            const float4 v = lds_f4(bsp + cfull * 128), s = lds_f4(scp + cfull * 16);
             t = __fmaf_rn(v.x, s.x, t);
             if (rem_blocks > 1) t = __fmaf_rn(v.y, s.y, t);
             if (rem_blocks > 2) t = __fmaf_rn(v.z, s.z, t);
@@ -373,7 +379,11 @@ bool dec_plan(int groups, int k, bool q4, int sm_count, DecPlan* pl) {
     pl->cpt = cpt;
     pl->S = S;
     pl->C = C;
-    pl->ctas = groups < sm_count ? groups : sm_count;
+    // One CTA per SM, so the next GEMV's CTA fits beside it and starts its
+    // copies early; long matrices (>= 24 groups per SM) run two per SM
+    // instead, for twice the warps and slots in flight.
+    const int max_ctas = groups >= 24 * sm_count ? 2 * sm_count : sm_count;
+    pl->ctas = groups < max_ctas ? groups : max_ctas;
     const int gpc = (groups + pl->ctas - 1) / pl->ctas;
     int P = max_warps / (S + C);
     if (P > 4) P = 4;

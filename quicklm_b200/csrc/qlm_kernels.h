@@ -45,6 +45,7 @@ struct GatherArgs {
     int nranks;  // 0 = no gather
     int rank;
     int col0;    // this shard's first output column
+    long long wait_ns;  // give up waiting for peers after this long (status 0x202)
 };
 
 // Greedy selection across ranks: peer_words[r] is rank r's exchange header
@@ -53,9 +54,10 @@ struct GatherArgs {
 struct ArgmaxArgs {
     unsigned long long* peer_words[kMaxRanks];
     const int* epoch;
-    int* status;
+    int* status;        // the communicator's: non-zero = failed, the kernel does nothing
     int nranks;
     int rank;
+    long long wait_ns;  // give up waiting for peers after this long
 };
 
 // out_idx / out_val (device) = the reference's greedy choice over the logits

@@ -151,3 +151,99 @@ def test_fused_allgather_two_gpus(tmp_path, qlm_lib):
                        start_method="spawn")
     for r in range(world):
         assert (tmp_path / f"r{r}").read_text() == "ok"
+
+
+def _timeout_worker(rank, world, port, result_dir):
+    """Rank 1 skips one call; rank 0's bounded wait must give up within its
+    short limit and report QLM_ERR_TIMEOUT; the failed communicator refuses
+    further calls at once; new communicators on both ranks work again. The
+    failure is made on the host (a rank that does not call): nothing faults
+    or hangs a GPU, every device wait is bounded."""
+    import datetime
+    import time
+    import torch
+    import torch.distributed as dist
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    torch.cuda.set_device(rank)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
+    msg = "ok"
+    try:
+        import quicklm_b200 as q
+        from oracle.oracle import synth_case
+        x_np, w_np = synth_case(1, 1024, 512, 9)
+        wd = torch.from_numpy(w_np).cuda()
+        b, e = q.shard_rows(1024, world, rank)
+        shard = q.Int8Weight.quantize(wd, device=rank, row_begin=b, row_end=e)
+        full = q.Int8Weight.quantize(wd, device=rank)
+        x = torch.from_numpy(x_np).cuda()
+        y_ref = q.matmul(x, full, flags=q.SYNC)
+
+        def exchange(h):
+            out = [None] * world
+            dist.all_gather_object(out, h)
+            return out
+
+        comm = q.Comm(rank, rank, world, 1024, exchange)
+        comm.set_timeout(0.2)
+        y = q.matmul_allgather(x, shard, comm, flags=q.SYNC)
+        if not torch.equal(y.view(torch.int32), y_ref.view(torch.int32)):
+            msg = "first call: gathered output differs"
+        dist.barrier()
+        if rank == 0:
+            t0 = time.perf_counter()
+            try:
+                q.matmul_allgather(x, shard, comm, flags=q.SYNC)
+                msg = "the call without its peer did not report a timeout"
+            except q.QlmError as exc:
+                dt = time.perf_counter() - t0
+                if exc.status != 5:
+                    msg = f"expected QLM_ERR_TIMEOUT, got {exc}"
+                elif dt > 10.0:
+                    msg = f"the timeout took {dt:.1f} s against a 0.2 s limit"
+            t0 = time.perf_counter()
+            try:  # a failed communicator refuses further work at once
+                q.matmul_allgather(x, shard, comm, flags=q.SYNC)
+                if msg == "ok":
+                    msg = "a failed communicator accepted a call"
+            except q.QlmError as exc:
+                if msg == "ok" and (exc.status != 5 or time.perf_counter() - t0 > 1.0):
+                    msg = f"failed communicator: {exc}"
+            try:
+                comm.status()
+                if msg == "ok":
+                    msg = "comm.status() did not report the failure"
+            except q.QlmError:
+                pass
+        torch.cuda.synchronize()
+        dist.barrier()  # rank 1 skipped the call: nothing of it is in flight anywhere
+        comm.free()
+        comm = q.Comm(rank, rank, world, 1024, exchange)
+        comm.set_timeout(2.0)
+        for i in range(3):
+            y = q.matmul_allgather(x, shard, comm, flags=q.SYNC)
+            if msg == "ok" and not torch.equal(y.view(torch.int32), y_ref.view(torch.int32)):
+                msg = f"recreated communicator, call {i}: gathered output differs"
+        comm.status()
+        torch.cuda.synchronize()
+        dist.barrier()
+        comm.free()
+    except Exception as exc:  # reported through the result file
+        msg = f"{type(exc).__name__}: {exc}"
+    finally:
+        with open(os.path.join(result_dir, f"r{rank}"), "w") as f:
+            f.write(msg)
+        dist.destroy_process_group()
+
+
+def test_gather_timeout_recovery_two_gpus(tmp_path, qlm_lib):
+    import torch
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    import torch.multiprocessing as mp
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    world = 2
+    mp.start_processes(_timeout_worker, args=(world, _free_port(), str(tmp_path)), nprocs=world, join=True,
+                       start_method="spawn")
+    for r in range(world):
+        assert (tmp_path / f"r{r}").read_text() == "ok"

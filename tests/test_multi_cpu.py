@@ -1,7 +1,8 @@
 """World-size-2 CPU tests (gloo) of the row-sharded path's host logic: the
-row partition, the handle exchange a Comm performs, and the assembly order
-of the gathered output — checked against the unsharded product. The device
-data path is covered by tests/test_gpu_multi.py on real GPUs."""
+product's row partition (shard_rows) and handle exchange (exchange_handles,
+what Comm passes to qlm_comm_connect), and the assembly order of the gathered
+output — checked against the unsharded product. The device data path is
+covered by tests/test_gpu_multi.py on real GPUs."""
 from __future__ import annotations
 
 import os
@@ -49,16 +50,27 @@ def _gloo_worker(rank, world, port, result_dir):
         y_shard = co.matmul(x, qs, ss)[0]
         parts = [None] * world
         dist.all_gather_object(parts, (b, e, y_shard))
-        # the handle exchange a Comm performs, over the same transport
-        handles = [None] * world
-        dist.all_gather_object(handles, bytes([rank]) * 64)
+
+        def exchange(h):
+            out = [None] * world
+            dist.all_gather_object(out, h)
+            return out
+
+        # the product's handle exchange (what Comm passes to qlm_comm_connect)
+        nb = 64
+        allb = q.exchange_handles(bytes([rank]) * nb, world, exchange)
+        ok_h = allb == b"".join(bytes([r]) * nb for r in range(world))
+        try:  # a transport that loses a rank's handle is refused, not connected
+            q.exchange_handles(bytes([rank]) * nb, world, lambda h: [h])
+            ok_h = False
+        except q.QlmError:
+            pass
         y = np.empty(w.shape[0], np.float32)
         for (pb, pe, ys) in parts:
             y[pb:pe] = ys
         qf, sf = co.quantize(w)
         y_full = co.matmul(x, qf, sf)[0]
-        ok = np.array_equal(y.view(np.uint32), y_full.view(np.uint32)) and \
-            [h[0] for h in handles] == list(range(world)) and all(len(h) == 64 for h in handles)
+        ok = np.array_equal(y.view(np.uint32), y_full.view(np.uint32)) and ok_h
         with open(os.path.join(result_dir, f"r{rank}"), "w") as f:
             f.write("ok" if ok else "mismatch")
     finally:
