@@ -22,9 +22,10 @@ one GEMV each; the step is captured once as a CUDA graph and replayed.
            at M=1, row-sharded over the N ranks (strong scaling), each checked
            against the reference output hash, the fused NVLink gather timed
            beside the GEMV + NCCL all-gather
-* decode:  configuration 3 greedy decode tok/s through QuickLM's own model
-           code with the int8 path on the GPU, against QuickLM on the host
-           cores; token streams must be identical (N=1)
+* decode:  configuration 3 greedy decode tok/s with the whole step on the
+           GPU (activations in HBM), beside QuickLM's own model code with only
+           the int8 matmuls on the GPU and QuickLM on the host cores; token
+           streams must be identical (N=1)
 
 With --gpus N > 1 (launched by torchrun) every rank holds its own 6144-row
 shard of a [6144*N, 2048] weight per stack entry (rank r's rows drawn with
@@ -326,16 +327,19 @@ def sharded_leg(qlm, torch, dist, comm, world, rank, local, reps=20):
 def decode_leg(n_new=128, seed=7, prompt_len=64):
     """Configuration 3 greedy decode (24-layer hybrid, hidden 1024, vocab
     151936; seeded random-init BF16 checkpoint, int8 weights; 64-token prompt,
-    128 new tokens): QuickLM's own model code with the int8 path on this GPU
-    (integration/_build/qlm_decode) against QuickLM entirely on the host cores
-    (oracle/_ref/ref_decode). The token streams must be identical."""
+    128 new tokens), three ways on the same checkpoint: the whole step on the
+    GPU with activations in HBM (integration/_build/qlm_device_decode, the
+    value), QuickLM's own model code with only the int8 matmuls on the GPU
+    (integration/_build/qlm_decode), and QuickLM entirely on the host cores
+    (oracle/_ref/ref_decode). Token streams must equal the reference's."""
     import shutil
     import tempfile
     sys.path.insert(0, os.path.join(ROOT, "integration"))
     from make_checkpoint import build as build_ckpt
-    gpu_bin = os.path.join(ROOT, "integration", "_build", "qlm_decode")
-    ref_bin = os.path.join(ROOT, "oracle", "_ref", "ref_decode")
-    for b in (gpu_bin, ref_bin):
+    bins = {"device": os.path.join(ROOT, "integration", "_build", "qlm_device_decode"),
+            "dropin": os.path.join(ROOT, "integration", "_build", "qlm_decode"),
+            "reference": os.path.join(ROOT, "oracle", "_ref", "ref_decode")}
+    for b in bins.values():
         if not os.path.exists(b):
             return {"error": f"{os.path.relpath(b, ROOT)} missing (built by __graft_entry__.build())"}
     d = tempfile.mkdtemp(prefix="qlm_cfg3_")
@@ -343,21 +347,24 @@ def decode_leg(n_new=128, seed=7, prompt_len=64):
         build_ckpt(d, seed=seed, prompt_len=prompt_len)
         threads = len(os.sched_getaffinity(0))
         res = {}
-        for name, b in (("gpu", gpu_bin), ("reference", ref_bin)):
-            out = subprocess.run([b, d, os.path.join(d, "prompt_ids.txt"), str(n_new), str(threads)],
+        for name, b in bins.items():
+            last = "0" if name == "device" else str(threads)
+            out = subprocess.run([b, d, os.path.join(d, "prompt_ids.txt"), str(n_new), last],
                                  capture_output=True, text=True, timeout=1200)
             if out.returncode != 0:
                 return {"error": f"{name} decode rc={out.returncode}: {out.stderr[-400:]}"}
             res[name] = json.loads(out.stdout.strip().splitlines()[-1])
-        g, r = res["gpu"], res["reference"]
-        same = g["tokens"] == r["tokens"]
+        g, p, r = res["device"], res["dropin"], res["reference"]
         return {"metric": "greedy decode tok/s (cfg3, batch 1, 128 new tokens after a 64-token prompt)",
                 "value": round(g["decode_tok_s"], 2), "unit": "tok/s",
                 "reference_tok_s": round(r["decode_tok_s"], 2), "reference_threads": threads,
                 "speedup": round(g["decode_tok_s"] / r["decode_tok_s"], 3),
-                "prefill_s": {"gpu": g["prefill_s"], "reference": r["prefill_s"]},
-                "tokens_identical": same, "n_tokens": len(g["tokens"]),
-                "how": "integration/_build/qlm_decode vs oracle/_ref/ref_decode, host wall clock of the decode loop"}
+                "dropin_tok_s": round(p["decode_tok_s"], 2),
+                "prefill_s": {"device": g["prefill_s"], "dropin": p["prefill_s"], "reference": r["prefill_s"]},
+                "tokens_identical": g["tokens"] == r["tokens"] and p["tokens"] == r["tokens"],
+                "n_tokens": len(g["tokens"]),
+                "how": "device: qlm_model_decode per token (activations in HBM, token id out); dropin: "
+                       "QuickLM's model code with qlm_linear_int8 per matmul; host wall clock of the decode loop"}
     finally:
         shutil.rmtree(d, ignore_errors=True)
 
@@ -719,7 +726,7 @@ def main():
                        "l2": f"inputs larger than L2 ({STACK}x{weight_bytes() / 1e6:.2f} MB weights per step)",
                        "parallelism": "single GPU" if world == 1 else
                        f"row-sharded x{world}, all-gather fused into the GEMV (NVLink peer stores)",
-                       "kernel": "gemv_dec_kernel (CUDA cores, bit-exact)" if world == 1 else
+                       "kernel": "gemv_kernel<1,R> (CUDA cores, bit-exact)" if world == 1 else
                        "gemv_kernel<1,R,gather> (fused NVLink all-gather)", "cuda_graph": used_graph,
                        "pdl": os.environ.get("QLM_PDL", "1") != "0"},
             "pct_hbm_peak": round(100.0 * value / world / peak, 2),

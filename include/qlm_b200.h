@@ -210,6 +210,36 @@ int qlm_rms_norm_gain(const float* x, const float* w, float* y, int rows, int si
 int qlm_gqa_attend(const float* q, int q_stride, const float* k_cache, const float* v_cache, float* out, int pos,
                    int heads, int kv_heads, int head_dim, float* scratch, void* stream);
 
+/* ---- A device-resident decode step for a whole model ----------------------
+ * QuickLM's Qwen3.5 hybrid decoder (gated-delta-net and gated GQA layers)
+ * run with every activation in HBM: DecoderModel::forward + sample(logits, 0,
+ * 0) (src/model/model.cpp:151-199, 259-272; layers src/model/modules.hpp:
+ * 210-241, src/model/attention.cpp:138-235, 414-591), where the reference keeps
+ * activations on the host and calls math::matmul per projection. Built from
+ * this library's kernels: matmuls bit-exact int8 (weights quantized on the
+ * device at load as get_tensor_keep_int8 does), norms, RoPE, conv and delta
+ * rule bit-identical given their inputs; the libm exp/log1p of SiLU, the
+ * gates and softmax evaluated in double and rounded once (within a few ulp of
+ * the host's), so logits agree to a few ulp, not bit for bit.
+ *   qlm_model_load:   read a checkpoint directory as DecoderModel::load does
+ *                     (config.json + *.safetensors, F32/BF16; src/model/
+ *                     model.cpp:34-131, src/arch/qwen3_5.cpp) onto `device`,
+ *                     with KV caches for max_seq positions.
+ *   qlm_model_reset:  clear the KV caches and the recurrent/conv states
+ *                     (DecoderModel::reset_states).
+ *   qlm_model_decode: one step at position pos for input token `token`:
+ *                     *next_token = the greedy choice over the logits; logits
+ *                     (optional HOST pointer, vocab floats) receives them.
+ *                     Prefill = one call per prompt token, pos 0, 1, ...
+ *                     (the reference's chunked prefill computes the same).
+ *   qlm_model_info:   vocab (lm_head rows), hidden size, layers, max_seq. */
+typedef struct qlm_model qlm_model;
+int qlm_model_load(const char* dir, int device, int max_seq, qlm_model** out);
+int qlm_model_reset(qlm_model* m);
+int qlm_model_decode(qlm_model* m, int token, int pos, int* next_token, float* logits);
+int qlm_model_info(const qlm_model* m, int* vocab, int* hidden, int* layers, int* max_seq);
+void qlm_model_free(qlm_model* m);
+
 /* Release a handle and its device memory (NULL is a no-op). */
 void qlm_weight_free(qlm_w8* w);
 

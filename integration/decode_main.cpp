@@ -65,9 +65,16 @@ int main(int argc, char** argv) {
         Tensor logits({vocab});
         std::vector<int> out;
         int next = prompt.back();
+        const char* dump = std::getenv("QLM_DUMP_LOGITS");  // first decode step's logits, raw float32
         for (int i = 0; i < n_new; ++i) {
             ctx.pos = pos++;
             model.forward(next, logits, ctx);
+            if (i == 0 && dump && *dump) {
+                if (FILE* f = std::fopen(dump, "wb")) {
+                    std::fwrite(logits.data, sizeof(float), (size_t)vocab, f);
+                    std::fclose(f);
+                }
+            }
             next = model.sample(logits, 0.0f, 0);
             out.push_back(next);
         }

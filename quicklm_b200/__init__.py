@@ -43,7 +43,8 @@ ABI_SYMBOLS = (
     "qlm_weight_import_int4", "qlm_store_save", "qlm_store_load", "qlm_store_info", "qlm_rms_norm",
     "qlm_add_rms_norm", "qlm_silu_mul", "qlm_rope_neox", "qlm_rope_neox_tables", "qlm_silu",
     "qlm_conv1d_update_tapmajor", "qlm_l2norm_heads", "qlm_gdn_gates", "qlm_gdn_recurrence", "qlm_rms_norm_gain",
-    "qlm_gqa_attend", "qlm_comm_set_timeout_us", "qlm_comm_status",
+    "qlm_gqa_attend", "qlm_comm_set_timeout_us", "qlm_comm_status", "qlm_model_load", "qlm_model_reset",
+    "qlm_model_decode", "qlm_model_info", "qlm_model_free",
 )
 
 _STATUS = {0: "OK", 1: "INVALID_ARG", 2: "CUDA", 3: "OUT_OF_MEMORY", 4: "UNSUPPORTED", 5: "TIMEOUT", 6: "NCCL",
@@ -111,6 +112,12 @@ def load(path: str = LIB_PATH):
     lib.qlm_comm_free.argtypes = [P]
     lib.qlm_comm_free.restype = None
     lib.qlm_comm_set_timeout_us.argtypes = [P, L]
+    lib.qlm_model_load.argtypes = [ctypes.c_char_p, I, I, ctypes.POINTER(P)]
+    lib.qlm_model_reset.argtypes = [P]
+    lib.qlm_model_decode.argtypes = [P, I, I, ctypes.POINTER(I), P]
+    lib.qlm_model_info.argtypes = [P] + [ctypes.POINTER(I)] * 4
+    lib.qlm_model_free.argtypes = [P]
+    lib.qlm_model_free.restype = None
     lib.qlm_comm_status.argtypes = [P]
     lib.qlm_linear_int8_allgather.argtypes = [P, I, I, L, P, P, P, L, I, P]
     lib.qlm_argmax_f32.argtypes = [P, I, L, P, P, P, I, P]

@@ -581,8 +581,9 @@ bool gemv_supported(int mm, int rows, int k, int sm_count, bool q4) {
 
 namespace {
 
-// QLM_GEMV_DECODE=0 selects the single-role kernel for M = 1 as well (for
-// comparisons); the default is the producer/consumer decode form.
+// QLM_GEMV_DECODE=0 selects the single-role kernel for every M = 1 launch
+// (for comparisons); by default the producer/consumer form takes the small
+// matrices (below).
 bool decode_form_enabled() {
     static const bool on = [] {
         const char* e = std::getenv("QLM_GEMV_DECODE");
@@ -617,7 +618,14 @@ cudaError_t launch_gemv_grouped(const float* x, int64_t ldx, int mm, const GemvW
         if (ws[g].rows < 1 || !ws[g].maps) return cudaErrorInvalidValue;
         rows_total += ws[g].rows;
     }
-    if (mm == 1 && !gather && decode_form_enabled() && gemv_decode_supported(rows_total, nw, k, sm_count, q4))
+    // M = 1: the producer/consumer form serves matrices of fewer than 32 rows
+    // per SM, where one thread per (row, lane) would leave most of the SM idle;
+    // measured on B200 (CUDA graph, rotating weights): [512,2560] 3.2 vs 8.0 us,
+    // [2560,9728] 12.0 vs 16.1 us, [1024,3584] 3.6 vs 7.0 us, while from ~40 rows
+    // per SM the single-role kernel is faster (config 1 [6144,2048] 5.6 vs
+    // 6.9 us, lm_head [151936,2560] 76 vs 107 us).
+    if (mm == 1 && !gather && decode_form_enabled() && rows_total < 32 * sm_count &&
+        gemv_decode_supported(rows_total, nw, k, sm_count, q4))
         return launch_gemv_decode(x, ws, nw, k, status, sm_count, stream, pdl, q4);
     const int r = pick_rows_per_thread(mm, rows_total, sm_count);
     int rows_eff = 0;  // whole units per weight

@@ -140,7 +140,8 @@ __device__ __forceinline__ void chunk_block_sums(const uint4& a, const unsigned 
 // same address; int4 codes are half as wide, so their sums go to a separate
 // area), then the rows' scales (4 x nck float4). Shared memory: P*D slots,
 // then the landed and full mbarriers and the last group issued into each
-// slot (P*D each), then the abort flag.
+// slot (P*D each), the abort flag, and 512 bytes per producer warp that lanes
+// past a row's end compute into (so the loop has no divergent branch).
 template <bool Q4, int CPT>
 __global__ void __launch_bounds__(CPT == 1 ? 512 : 384, 2) gemv_dec_kernel(const __grid_constant__ DecParams p) {
     using namespace sm100;
@@ -157,6 +158,8 @@ __global__ void __launch_bounds__(CPT == 1 ? 512 : 384, 2) gemv_dec_kernel(const
     const uint32_t full0 = landed0 + nslots * 8;
     int* issued = reinterpret_cast<int*>(smem + (size_t)nslots * p.slot_bytes + nslots * 16);
     volatile int* abort_flag = issued + nslots;
+    // Per producer warp, 512 bytes that lanes past a row's end compute into.
+    uint8_t* dummy_base = smem + (((size_t)nslots * p.slot_bytes + nslots * 20 + 4 + 15) & ~(size_t)15);
     const int codes_bytes = 4 * p.row_bytes;                // codes of a group
     const int bs_off = Q4 ? codes_bytes : 0;                // block sums
     const int sc_off = Q4 ? codes_bytes + 512 * p.nck : codes_bytes;  // scales
@@ -179,11 +182,16 @@ __global__ void __launch_bounds__(CPT == 1 ? 512 : 384, 2) gemv_dec_kernel(const
         const int n = g_count > pp ? (g_count - pp + p.P - 1) / p.P : 0;  // groups of this pipe
         int cj[CPT];
         bool vj[CPT];
+        uint32_t loff[CPT], soff[CPT];  // this lane's code / block-sum bytes of row 0 within a slot
 #pragma unroll
         for (int j = 0; j < CPT; ++j) {
             cj[j] = sw * 4 * CPT + cl + 4 * j;
             vj[j] = cj[j] < p.nck;
+            loff[j] = (uint32_t)(cj[j] * CB + l * (CB / 8));
+            soff[j] = (uint32_t)(bs_off + (cj[j] * 8 + l) * 16);
         }
+        const uint32_t rs_ld = (uint32_t)(p.nck * CB), rs_st = (uint32_t)(p.nck * 128);  // per row of a group
+        const uint32_t dummy = smem_u32(dummy_base) + (uint32_t)(warp * 512 + lane32 * 16);
         pdl_launch_dependents();
         pdl_wait();
         unsigned long long xp[CPT][2][4];
@@ -199,34 +207,54 @@ __global__ void __launch_bounds__(CPT == 1 ? 512 : 384, 2) gemv_dec_kernel(const
                     xp[j][h][jj] = f2pack(x0, x1);
                 }
         const unsigned long long nz = f2pack(p.zero_neg, p.zero_neg);
+        // Group i sits in slot i % D of the pipe, phase (i / D) & 1; tracked
+        // incrementally.
+        int si = 0;
+        uint32_t par = 0;
         for (int i = 0; i < n; ++i) {
-            const int slot = pp * p.D + i % p.D;
-            const bool ok = mbar_wait(landed0 + slot * 8, (uint32_t)((i / p.D) & 1), abort_flag, kDecWaitBudget);
+            const int slot = pp * p.D + si;
+            if (++si == p.D) si = 0;
+            const uint32_t this_par = par;
+            if (si == 0) par ^= 1u;
+            const bool ok = mbar_wait(landed0 + slot * 8, this_par, abort_flag, kDecWaitBudget);
             if (!__all_sync(0xffffffffu, ok)) {
                 *abort_flag = 1;
                 if (lane32 == 0 && p.status) atomicCAS(p.status, 0, kDecStatusTimeout);
                 break;
             }
             const uint32_t sb = smem_u32(slots + (size_t)slot * p.slot_bytes);
-#pragma unroll
-            for (int r = 0; r < 4; ++r) {
+            // Branch-free: a lane whose chunk is past the row's end computes on
+            // its private dummy line instead (its result is never read). The
+            // rows' codes are loaded ahead of their arithmetic (all four rows
+            // with one chunk per thread, two ahead with two), so the loads of
+            // later rows are in flight while earlier rows compute.
+            constexpr int PRE = CPT == 1 ? 4 : 2;
+            uint4 cw[4][CPT];
+            auto load_row = [&](int r) {
 #pragma unroll
                 for (int j = 0; j < CPT; ++j) {
-                    if (vj[j]) {
-                        const uint32_t at = sb + (r * p.nck + cj[j]) * CB + l * (CB / 8);
-                        uint4 a;
-                        if (Q4) {
-                            asm volatile("ld.shared.v2.u32 {%0,%1}, [%2];" : "=r"(a.x), "=r"(a.y) : "r"(at));
-                            a.z = a.w = 0u;
-                        } else {
-                            asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
-                                         : "=r"(a.x), "=r"(a.y), "=r"(a.z), "=r"(a.w)
-                                         : "r"(at));
-                        }
-                        unsigned long long b01, b23;
-                        chunk_block_sums<Q4>(a, xp[j], nz, b01, b23);
-                        sts_u64x2(sb + bs_off + ((r * p.nck + cj[j]) * 8 + l) * 16, b01, b23);
+                    const uint32_t la = vj[j] ? sb + r * rs_ld + loff[j] : dummy;
+                    if (Q4) {
+                        asm volatile("ld.shared.v2.u32 {%0,%1}, [%2];" : "=r"(cw[r][j].x), "=r"(cw[r][j].y) : "r"(la));
+                        cw[r][j].z = cw[r][j].w = 0u;
+                    } else {
+                        asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
+                                     : "=r"(cw[r][j].x), "=r"(cw[r][j].y), "=r"(cw[r][j].z), "=r"(cw[r][j].w)
+                                     : "r"(la));
                     }
+                }
+            };
+#pragma unroll
+            for (int r = 0; r < PRE; ++r) load_row(r);
+#pragma unroll
+            for (int r = 0; r < 4; ++r) {
+                if (r + PRE < 4) load_row(r + PRE);
+#pragma unroll
+                for (int j = 0; j < CPT; ++j) {
+                    const uint32_t sa = vj[j] ? sb + r * (Q4 ? rs_st : rs_ld) + (Q4 ? soff[j] : loff[j]) : dummy;
+                    unsigned long long b01, b23;
+                    chunk_block_sums<Q4>(cw[r][j], xp[j], nz, b01, b23);
+                    sts_u64x2(sa, b01, b23);
                 }
             }
             // This slot's next writer is the copy engine (after the chain warp
@@ -250,12 +278,11 @@ __global__ void __launch_bounds__(CPT == 1 ? 512 : 384, 2) gemv_dec_kernel(const
         row0 = (g - W->gbase) * 4;
         nr = min(4, W->rows - row0);
     };
-    // Codes and scales of group i into its slot (lane 0 only).
-    auto issue = [&](int i) {
+    // Codes and scales of group i into pipe slot `slot` (lane 0 only).
+    auto issue = [&](int i, int slot) {
         const DecWeight* W;
         int row0, nr;
         group_rows(i, W, row0, nr);
-        const int slot = pp * p.D + i % p.D;
         uint8_t* sb = slots + (size_t)slot * p.slot_bytes;
         const uint32_t cbytes = (uint32_t)(nr * p.row_bytes), sbytes = (uint32_t)(nr * p.nb_pad * 4);
         const uint32_t bar = landed0 + slot * 8;
@@ -274,7 +301,7 @@ __global__ void __launch_bounds__(CPT == 1 ? 512 : 384, 2) gemv_dec_kernel(const
     // Before the dependency wait: fill the ring (group i by chain warp i % C)
     // and ask L2 for the groups after it.
     if (lane32 == 0) {
-        for (int i = cc; i < n && i < p.D; i += p.C) issue(i);
+        for (int i = cc; i < n && i < p.D; i += p.C) issue(i, pp * p.D + i);
         for (int i = p.D + cc; i < n && i < p.D + p.ahead; i += p.C) prefetch(i);
     }
     pdl_launch_dependents();
@@ -282,9 +309,19 @@ __global__ void __launch_bounds__(CPT == 1 ? 512 : 384, 2) gemv_dec_kernel(const
     const int nbf = p.k / kBlock;  // full blocks
     const int cfull = nbf / 4;     // chunks of four full blocks
     const int rem_blocks = nbf - cfull * 4;
+    // This warp's groups i = cc, cc + C, ... sit in slots i % D (D is a
+    // multiple of C), phase (i / D) & 1; tracked incrementally.
+    int si = cc;
+    uint32_t par = 0;
     for (int i = cc; i < n; i += p.C) {
-        const int slot = pp * p.D + i % p.D;
-        const bool ok = mbar_wait(full0 + slot * 8, (uint32_t)((i / p.D) & 1), abort_flag, kDecWaitBudget);
+        const int slot = pp * p.D + si;
+        const uint32_t this_par = par;
+        si += p.C;
+        if (si >= p.D) {
+            si -= p.D;
+            par ^= 1u;
+        }
+        const bool ok = mbar_wait(full0 + slot * 8, this_par, abort_flag, kDecWaitBudget);
         if (!__all_sync(0xffffffffu, ok)) {
             *abort_flag = 1;
             if (lane32 == 0 && p.status) atomicCAS(p.status, 0, kDecStatusTimeout);
@@ -313,7 +350,7 @@ __global__ void __launch_bounds__(CPT == 1 ? 512 : 384, 2) gemv_dec_kernel(const
         fence_proxy_async_smem();
         __syncwarp();
         if (lane32 == 0) {
-            if (i + p.D < n) issue(i + p.D);
+            if (i + p.D < n) issue(i + p.D, slot);
             if (i + p.D + p.ahead < n) prefetch(i + p.D + p.ahead);
         }
         t = __fadd_rn(t, __shfl_xor_sync(0xffffffffu, t, 4));
@@ -404,7 +441,7 @@ bool dec_plan(int groups, int k, bool q4, int sm_count, DecPlan* pl) {
     if (pl->C > D) pl->C = D;
     D -= D % pl->C;
     pl->D = D;
-    pl->smem = P * D * (pl->slot_bytes + 24) + 16;
+    pl->smem = P * D * (pl->slot_bytes + 24) + 16 + P * S * 512 + 16;
     if (pl->smem > 220 * 1024) return false;
     pl->threads = P * (S + pl->C) * 32;
     pl->ahead = D + 3;

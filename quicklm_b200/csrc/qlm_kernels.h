@@ -121,6 +121,11 @@ bool gemv_decode_supported(int rows_total, int nw, int k, int sm_count, bool q4)
 cudaError_t launch_gemv_decode(const float* x, const GemvWeight* ws, int nw, int k, int* status, int sm_count,
                                cudaStream_t stream, bool pdl, bool q4);
 
+// math::rms_norm (zero-centred gain) on rows of `size` floats spaced `ld` apart
+// (qlm_layer.cu).
+cudaError_t launch_rms_norm_strided(const float* x, const float* w, float* y, int rows, int size, int64_t ld,
+                                    float eps, cudaStream_t stream);
+
 // ---- tensor-core prefill GEMM (qlm_gemm_tc.cu) ----
 struct TcMaps {
     alignas(64) CUtensorMap w;  // packed int8 rows, 128 x 128-byte boxes

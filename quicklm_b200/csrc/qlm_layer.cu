@@ -99,12 +99,14 @@ __device__ __forceinline__ void apply_zc(const float* in, const float* __restric
 // One CTA per row. Rows up to kStageFloats are first staged in shared memory
 // with coalesced loads, so the ordered accumulation chains read on-chip data.
 // ZC: zero-centred gain (1 + w) as math::rms_norm; else the plain gain w.
+// ld: row stride of x and y in floats (>= size; the rows' first `size` values
+// are normalized, the rest untouched).
 template <bool ZC>
 __global__ void __launch_bounds__(kThreads) rms_norm_kernel(const float* x, const float* __restrict__ w, float* y,
-                                                            int size, float eps) {
+                                                            int size, float eps, int64_t ld) {
     extern __shared__ float stage[];
     __shared__ float s_scale;
-    const float* xr = x + (int64_t)blockIdx.x * size;
+    const float* xr = x + (int64_t)blockIdx.x * ld;
     if (size <= kStageFloats) {
         for (int i = threadIdx.x; i < size; i += blockDim.x) stage[i] = xr[i];
         __syncthreads();
@@ -115,7 +117,7 @@ __global__ void __launch_bounds__(kThreads) rms_norm_kernel(const float* x, cons
         if (threadIdx.x == 0) s_scale = rms_scale(ss, size, eps);
     }
     __syncthreads();
-    apply_zc<ZC>(xr, w, y + (int64_t)blockIdx.x * size, s_scale, size);
+    apply_zc<ZC>(xr, w, y + (int64_t)blockIdx.x * ld, s_scale, size);
 }
 
 // One CTA per row: residual += delta (stored), then out = rms_norm(residual).
@@ -518,13 +520,24 @@ int launched(const char* what) {
 
 }  // namespace
 
+namespace qlm {
+// math::rms_norm on `rows` rows of `size` floats spaced `ld` apart (in place
+// when x == y): the per-head QK-norm of a query laid out [query | gate].
+cudaError_t launch_rms_norm_strided(const float* x, const float* w, float* y, int rows, int size, int64_t ld,
+                                    float eps, cudaStream_t stream) {
+    const size_t smem = size <= kStageFloats ? (size_t)size * sizeof(float) : 0;
+    rms_norm_kernel<true><<<rows, kThreads, smem, stream>>>(x, w, y, size, eps, ld);
+    return cudaGetLastError();
+}
+}  // namespace qlm
+
 extern "C" {
 
 int qlm_rms_norm(const float* x, const float* w, float* y, int rows, int size, float eps, void* stream) {
     if (!x || !w || !y) return layer_fail(QLM_ERR_INVALID_ARG, "NULL argument");
     if (rows <= 0 || size <= 0) return layer_fail(QLM_ERR_INVALID_ARG, "rows and size must be positive");
     const size_t smem = size <= qlm::kStageFloats ? (size_t)size * sizeof(float) : 0;
-    qlm::rms_norm_kernel<true><<<rows, qlm::kThreads, smem, static_cast<cudaStream_t>(stream)>>>(x, w, y, size, eps);
+    qlm::rms_norm_kernel<true><<<rows, qlm::kThreads, smem, static_cast<cudaStream_t>(stream)>>>(x, w, y, size, eps, size);
     return launched("rms_norm launch");
 }
 
@@ -532,7 +545,7 @@ int qlm_rms_norm_gain(const float* x, const float* w, float* y, int rows, int si
     if (!x || !w || !y) return layer_fail(QLM_ERR_INVALID_ARG, "NULL argument");
     if (rows <= 0 || size <= 0) return layer_fail(QLM_ERR_INVALID_ARG, "rows and size must be positive");
     const size_t smem = size <= qlm::kStageFloats ? (size_t)size * sizeof(float) : 0;
-    qlm::rms_norm_kernel<false><<<rows, qlm::kThreads, smem, static_cast<cudaStream_t>(stream)>>>(x, w, y, size, eps);
+    qlm::rms_norm_kernel<false><<<rows, qlm::kThreads, smem, static_cast<cudaStream_t>(stream)>>>(x, w, y, size, eps, size);
     return launched("rms_norm_gain launch");
 }
 
