@@ -557,7 +557,7 @@ def main():
             out = [None] * world
             dist.all_gather_object(out, h)
             return out
-        comm = qlm.Comm(local, rank, world, n_total, exchange)
+        comm = qlm.Comm(local, rank, world, max(n_total, max(n for n, _, _ in SHARDED)), exchange)
 
     def step():
         for i in range(STACK):

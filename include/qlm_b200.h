@@ -232,12 +232,23 @@ int qlm_gqa_attend(const float* q, int q_stride, const float* k_cache, const flo
  *                     (optional HOST pointer, vocab floats) receives them.
  *                     Prefill = one call per prompt token, pos 0, 1, ...
  *                     (the reference's chunked prefill computes the same).
- *   qlm_model_info:   vocab (lm_head rows), hidden size, layers, max_seq. */
+ *   qlm_model_info:   vocab (lm_head rows), hidden size, layers, max_seq,
+ *                     batch (any output pointer may be NULL).
+ * Batched decode (no counterpart in the reference, which decodes one sequence
+ * per DecoderModel): qlm_model_load_batch keeps `batch` independent sequences
+ * (own KV caches, conv and recurrent states) that advance in lockstep, one
+ * position for all; qlm_model_decode_batch takes their `batch` input tokens
+ * (host array) and returns their greedy choices, logits [batch][vocab]
+ * optional. Every op is row- or head-independent, so each sequence's logits
+ * are bit-identical to decoding it alone. qlm_model_load / qlm_model_decode
+ * are the batch = 1 forms. */
 typedef struct qlm_model qlm_model;
 int qlm_model_load(const char* dir, int device, int max_seq, qlm_model** out);
+int qlm_model_load_batch(const char* dir, int device, int max_seq, int batch, qlm_model** out);
 int qlm_model_reset(qlm_model* m);
 int qlm_model_decode(qlm_model* m, int token, int pos, int* next_token, float* logits);
-int qlm_model_info(const qlm_model* m, int* vocab, int* hidden, int* layers, int* max_seq);
+int qlm_model_decode_batch(qlm_model* m, const int* tokens, int pos, int* next_tokens, float* logits);
+int qlm_model_info(const qlm_model* m, int* vocab, int* hidden, int* layers, int* max_seq, int* batch);
 void qlm_model_free(qlm_model* m);
 
 /* Release a handle and its device memory (NULL is a no-op). */

@@ -51,7 +51,7 @@ int main(int argc, char** argv) {
     next = prompt.back();
     const char* dump = std::getenv("QLM_DUMP_LOGITS");  // first decode step's logits, raw float32
     int vocab = 0;
-    qlm_model_info(m, &vocab, nullptr, nullptr, nullptr);
+    qlm_model_info(m, &vocab, nullptr, nullptr, nullptr, nullptr);
     std::vector<float> first(dump && *dump ? (size_t)vocab : 0);
     for (int i = 0; i < n_new; ++i) {
         int tok = 0;

@@ -26,7 +26,7 @@ import numpy as np
 __all__ = ["QlmError", "Int8Weight", "matmul", "matmul_grouped", "argmax", "load", "LIB_PATH", "EXACT", "TENSOR", "HOST_IO", "SYNC",
            "BLOCK", "Comm", "exchange_handles", "shard_rows", "matmul_allgather", "save", "store_info", "rms_norm", "add_rms_norm",
            "silu_mul", "rope_neox", "rope_neox_tables", "silu", "conv1d_update_tapmajor", "l2norm_heads",
-           "gdn_gates", "gdn_recurrence", "rms_norm_gain", "gqa_attend"]
+           "gdn_gates", "gdn_recurrence", "rms_norm_gain", "gqa_attend", "Model"]
 
 LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "lib", "libqlm_b200.so")
 BLOCK = 32
@@ -44,7 +44,7 @@ ABI_SYMBOLS = (
     "qlm_add_rms_norm", "qlm_silu_mul", "qlm_rope_neox", "qlm_rope_neox_tables", "qlm_silu",
     "qlm_conv1d_update_tapmajor", "qlm_l2norm_heads", "qlm_gdn_gates", "qlm_gdn_recurrence", "qlm_rms_norm_gain",
     "qlm_gqa_attend", "qlm_comm_set_timeout_us", "qlm_comm_status", "qlm_model_load", "qlm_model_reset",
-    "qlm_model_decode", "qlm_model_info", "qlm_model_free",
+    "qlm_model_decode", "qlm_model_info", "qlm_model_free", "qlm_model_load_batch", "qlm_model_decode_batch",
 )
 
 _STATUS = {0: "OK", 1: "INVALID_ARG", 2: "CUDA", 3: "OUT_OF_MEMORY", 4: "UNSUPPORTED", 5: "TIMEOUT", 6: "NCCL",
@@ -115,7 +115,9 @@ def load(path: str = LIB_PATH):
     lib.qlm_model_load.argtypes = [ctypes.c_char_p, I, I, ctypes.POINTER(P)]
     lib.qlm_model_reset.argtypes = [P]
     lib.qlm_model_decode.argtypes = [P, I, I, ctypes.POINTER(I), P]
-    lib.qlm_model_info.argtypes = [P] + [ctypes.POINTER(I)] * 4
+    lib.qlm_model_info.argtypes = [P] + [ctypes.POINTER(I)] * 5
+    lib.qlm_model_load_batch.argtypes = [ctypes.c_char_p, I, I, I, ctypes.POINTER(P)]
+    lib.qlm_model_decode_batch.argtypes = [P, P, I, P, P]
     lib.qlm_model_free.argtypes = [P]
     lib.qlm_model_free.restype = None
     lib.qlm_comm_status.argtypes = [P]
@@ -637,3 +639,54 @@ def matmul_grouped(x, weights, ys=None, flags: int = 0, stream=None):
     _check(lib.qlm_linear_int8_grouped(a2.data_ptr(), a2.shape[0], a2.shape[1], a2.stride(0), hs, n, yp, ld, flags,
                                        st))
     return ys
+
+
+class Model:
+    """A QuickLM Qwen3.5-hybrid checkpoint decoded on the device (qlm_model_*):
+    every activation stays in HBM; ``decode`` returns the greedy next token of
+    each sequence (DecoderModel::forward + sample(logits, 0, 0),
+    src/model/model.cpp:151-199, 259-272). ``batch`` sequences advance in
+    lockstep (one position for all); each one's logits are bit-identical to
+    decoding it alone."""
+
+    def __init__(self, path: str, device: int = 0, max_seq: int = 2048, batch: int = 1):
+        lib = load()
+        h = ctypes.c_void_p()
+        _check(lib.qlm_model_load_batch(os.fsencode(path), device, max_seq, batch, ctypes.byref(h)))
+        self._h = h
+        vals = [ctypes.c_int() for _ in range(5)]
+        _check(lib.qlm_model_info(self._h, *[ctypes.byref(v) for v in vals]))
+        self.vocab, self.hidden, self.layers, self.max_seq, self.batch = (v.value for v in vals)
+
+    @property
+    def handle(self):
+        if not self._h:
+            raise QlmError(1, "model already freed")
+        return self._h
+
+    def decode(self, tokens, pos: int, logits: bool = False):
+        """One step at position ``pos``: tokens (``batch`` ints) in, the greedy
+        next tokens out (and the logits [batch, vocab] when asked)."""
+        toks = np.ascontiguousarray(np.asarray(tokens, np.int32).reshape(-1))
+        if toks.size != self.batch:
+            raise QlmError(1, f"{toks.size} tokens for a batch of {self.batch}")
+        nxt = np.empty(self.batch, np.int32)
+        lg = np.empty((self.batch, self.vocab), np.float32) if logits else None
+        _check(load().qlm_model_decode_batch(self.handle, toks.ctypes.data, int(pos), nxt.ctypes.data,
+                                             lg.ctypes.data if lg is not None else None))
+        return (nxt, lg) if logits else nxt
+
+    def reset(self) -> None:
+        """Clear the KV caches and recurrent states (DecoderModel::reset_states)."""
+        _check(load().qlm_model_reset(self.handle))
+
+    def free(self) -> None:
+        if self._h:
+            load().qlm_model_free(self._h)
+            self._h = ctypes.c_void_p()
+
+    def __del__(self):
+        try:
+            self.free()
+        except Exception:
+            pass

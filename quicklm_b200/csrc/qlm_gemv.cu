@@ -226,9 +226,11 @@ __global__ void __launch_bounds__(MM == 1 ? 384 : 512, MM == 1 ? 2 : 1)
     // plan requests 128 spare bytes).
     uint8_t* smem = smem_raw + ((128u - (sm100::smem_u32(smem_raw) & 127u)) & 127u);
     using namespace sm100;
-    // A communicator whose bounded wait gave up is failed: do nothing (the
-    // host reports QLM_ERR_TIMEOUT until it is freed and recreated).
-    if (GATHER && *reinterpret_cast<volatile const int*>(p.status) != 0) return;
+    // A communicator whose bounded wait gave up is failed: such a call does
+    // nothing (the host reports QLM_ERR_TIMEOUT until the communicator is
+    // freed and recreated). The word is loaded here and looked at after the
+    // dependency wait, so the load's latency overlaps the weight copies.
+    const int comm_failed = GATHER ? ld_relaxed_sys_i32(p.status) : 0;
     const int warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5, lane32 = threadIdx.x & 31;
     const int lane = threadIdx.x & 7;                // reference lane l
     const int rsub = ((threadIdx.x >> 3) & 3) * R;   // first of the thread's R rows within the unit
@@ -299,6 +301,13 @@ __global__ void __launch_bounds__(MM == 1 ? 384 : 512, MM == 1 ? 2 : 1)
     // thread's loads are issued before its first store, so staging costs one
     // L2 round trip per 8 elements per thread, not one per element.
     pdl_wait();
+    if (GATHER && comm_failed) {
+        // Let this warp's copies land before leaving (bounded).
+        if (lane32 == 0)
+            for (int j = 0; j < p.d && j < items; ++j)
+                mbar_wait(bars + j * 8, 0u, nullptr, kWaitBudget);
+        return;
+    }
     // Gather: this call's epoch (the previous call's kernel, which advanced
     // it, has completed) and the exchange half it selects.
     int g_epoch = 0;

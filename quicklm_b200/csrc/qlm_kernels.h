@@ -126,6 +126,11 @@ cudaError_t launch_gemv_decode(const float* x, const GemvWeight* ws, int nw, int
 cudaError_t launch_rms_norm_strided(const float* x, const float* w, float* y, int rows, int size, int64_t ld,
                                     float eps, cudaStream_t stream);
 
+// The gated-delta-net gates of qlm_gdn_gates for `heads` heads of several
+// sequences in a row, A_log / dt_bias repeating every `per` heads (qlm_layer.cu).
+cudaError_t launch_gdn_gates(const float* a_raw, const float* b_raw, const float* A_log, const float* dt_bias,
+                             float* decay, float* beta, int heads, int per, cudaStream_t stream);
+
 // ---- tensor-core prefill GEMM (qlm_gemm_tc.cu) ----
 struct TcMaps {
     alignas(64) CUtensorMap w;  // packed int8 rows, 128 x 128-byte boxes

@@ -472,12 +472,14 @@ __global__ void __launch_bounds__(32) gqa_v_kernel(const float* __restrict__ pro
 // a correctly rounded float function would.
 __global__ void gdn_gates_kernel(const float* __restrict__ a_raw, const float* __restrict__ b_raw,
                                  const float* __restrict__ A_log, const float* __restrict__ dt_bias,
-                                 float* __restrict__ dec, float* __restrict__ beta, int heads) {
+                                 float* __restrict__ dec, float* __restrict__ beta, int heads, int per) {
+    // heads of several sequences in a row: the per-head parameters repeat every `per` heads
     const int h = blockIdx.x * blockDim.x + threadIdx.x;
     if (h >= heads) return;
-    const float dt_in = __fadd_rn(a_raw[h], dt_bias[h]);
+    const int hp = h % per;
+    const float dt_in = __fadd_rn(a_raw[h], dt_bias[hp]);
     const float sp = dt_in > 20.0f ? dt_in : (float)log1p((double)(float)exp((double)dt_in));
-    const float alpha = __fmul_rn(-(float)exp((double)A_log[h]), sp);
+    const float alpha = __fmul_rn(-(float)exp((double)A_log[hp]), sp);
     dec[h] = (float)exp((double)alpha);
     beta[h] = __fdiv_rn(1.0f, __fadd_rn(1.0f, (float)exp(-(double)b_raw[h])));
 }
@@ -521,6 +523,14 @@ int launched(const char* what) {
 }  // namespace
 
 namespace qlm {
+// The gated-delta-net gates for `heads` heads of several sequences in a row,
+// the per-head parameters (A_log, dt_bias) repeating every `per` heads.
+cudaError_t launch_gdn_gates(const float* a_raw, const float* b_raw, const float* A_log, const float* dt_bias,
+                             float* decay, float* beta, int heads, int per, cudaStream_t stream) {
+    gdn_gates_kernel<<<(heads + 127) / 128, 128, 0, stream>>>(a_raw, b_raw, A_log, dt_bias, decay, beta, heads, per);
+    return cudaGetLastError();
+}
+
 // math::rms_norm on `rows` rows of `size` floats spaced `ld` apart (in place
 // when x == y): the per-head QK-norm of a query laid out [query | gate].
 cudaError_t launch_rms_norm_strided(const float* x, const float* w, float* y, int rows, int size, int64_t ld,
@@ -612,8 +622,8 @@ int qlm_gdn_gates(const float* a_raw, const float* b_raw, const float* A_log, co
                   float* beta, int heads, void* stream) {
     if (!a_raw || !b_raw || !A_log || !dt_bias || !decay || !beta) return layer_fail(QLM_ERR_INVALID_ARG, "NULL argument");
     if (heads <= 0) return layer_fail(QLM_ERR_INVALID_ARG, "heads must be positive");
-    qlm::gdn_gates_kernel<<<(heads + 127) / 128, 128, 0, static_cast<cudaStream_t>(stream)>>>(a_raw, b_raw, A_log,
-                                                                                            dt_bias, decay, beta, heads);
+    qlm::gdn_gates_kernel<<<(heads + 127) / 128, 128, 0, static_cast<cudaStream_t>(stream)>>>(
+        a_raw, b_raw, A_log, dt_bias, decay, beta, heads, heads);
     return launched("gdn_gates launch");
 }
 

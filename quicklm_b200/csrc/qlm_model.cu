@@ -55,16 +55,69 @@ namespace {
 
 constexpr int kEmbThreads = 256;
 
-// x[i] = the embedding row of `token` (BF16 upcast exactly, or F32 copied).
-__global__ void embed_row_kernel(const void* table, int bf16, const int* token_dev, int token, int hidden, float* x) {
-    const int t = token_dev ? *token_dev : token;
+// x[b][i] = the embedding row of tokens[b] (BF16 upcast exactly, or F32
+// copied); one CTA row per sequence b.
+__global__ void embed_rows_kernel(const void* table, int bf16, const int* __restrict__ tokens, int hidden, float* x) {
+    const int t = tokens[blockIdx.y];
+    float* xr = x + (int64_t)blockIdx.y * hidden;
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < hidden; i += gridDim.x * blockDim.x) {
         if (bf16) {
             const uint16_t h = static_cast<const uint16_t*>(table)[(int64_t)t * hidden + i];
-            x[i] = __uint_as_float((uint32_t)h << 16);
+            xr[i] = __uint_as_float((uint32_t)h << 16);
         } else {
-            x[i] = static_cast<const float*>(table)[(int64_t)t * hidden + i];
+            xr[i] = static_cast<const float*>(table)[(int64_t)t * hidden + i];
         }
+    }
+}
+
+// DecoderModel::sample(logits, 0, 0) (src/model/model.cpp:259-272) for each
+// of the rows: the scan keeps the first strictly larger logit starting from
+// logit 0, i.e. 0 if logit 0 is NaN, else the lowest index of the largest
+// non-NaN logit (0 when no other logit is a number). One CTA per row.
+__global__ void __launch_bounds__(1024) greedy_rows_kernel(const float* __restrict__ logits, int n, int* out) {
+    const float* l = logits + (int64_t)blockIdx.x * n;
+    float best = 0.0f;
+    int bi = -1;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+        const float v = l[i];
+        if (v == v && (bi < 0 || v > best)) {  // indices ascend per thread: ties keep the first
+            best = v;
+            bi = i;
+        }
+    }
+    __shared__ float sv[32];
+    __shared__ int si[32];
+    auto better = [](float v, int i, float bv, int b) {  // (v, i) beats (bv, b)?
+        if (i < 0) return false;
+        if (b < 0) return true;
+        return v > bv || (v == bv && i < b);
+    };
+    for (int o = 16; o > 0; o >>= 1) {
+        const float v = __shfl_xor_sync(0xffffffffu, best, o);
+        const int i = __shfl_xor_sync(0xffffffffu, bi, o);
+        if (better(v, i, best, bi)) {
+            best = v;
+            bi = i;
+        }
+    }
+    const int w = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+    if (lane == 0) {
+        sv[w] = best;
+        si[w] = bi;
+    }
+    __syncthreads();
+    if (w == 0) {
+        best = lane < nw ? sv[lane] : 0.0f;
+        bi = lane < nw ? si[lane] : -1;
+        for (int o = 16; o > 0; o >>= 1) {
+            const float v = __shfl_xor_sync(0xffffffffu, best, o);
+            const int i = __shfl_xor_sync(0xffffffffu, bi, o);
+            if (better(v, i, best, bi)) {
+                best = v;
+                bi = i;
+            }
+        }
+        if (lane == 0) out[blockIdx.x] = (l[0] != l[0] || bi < 0) ? 0 : bi;
     }
 }
 
@@ -98,20 +151,24 @@ int fail(int code, const char* fmt, ...) {
 
 struct Layer {
     bool full_attn = false;
+    // gated delta net, batched: in_proj_qkv as three row ranges (q, k, v), so
+    // each part of every sequence is contiguous ([part][B][lin]); the conv runs
+    // over those 3*B*lin channels with its kernel replicated per sequence
+    qlm_w8 *qkv_q = nullptr, *qkv_k = nullptr, *qkv_v = nullptr;
     float* in_norm = nullptr;    // input_layernorm [hidden] (zero-centred)
     float* post_norm = nullptr;  // post_attention_layernorm [hidden]
     qlm_w8 *gate = nullptr, *up = nullptr, *down = nullptr;
     // gated GQA
     qlm_w8 *q = nullptr, *k = nullptr, *v = nullptr, *o = nullptr;
     float *q_norm = nullptr, *k_norm = nullptr;  // [head_dim] each
-    float *k_cache = nullptr, *v_cache = nullptr;  // [max_seq][kv_heads][head_dim]
+    float *k_cache = nullptr, *v_cache = nullptr;  // [max_seq][B][kv_heads][head_dim]
     // gated delta net
-    qlm_w8 *qkv = nullptr, *z = nullptr, *b = nullptr, *a = nullptr, *out = nullptr;
-    float* conv_wt = nullptr;     // [kernel][conv_dim] (tap-major)
-    float* conv_state = nullptr;  // [kernel - 1][conv_dim]
+    qlm_w8 *z = nullptr, *b = nullptr, *a = nullptr, *out = nullptr;
+    float* conv_wt = nullptr;     // [kernel][3][B][lin] (tap-major, replicated per sequence)
+    float* conv_state = nullptr;  // [kernel - 1][3][B][lin]
     int conv_ring = 0;
     float *gdn_norm = nullptr, *A_log = nullptr, *dt_bias = nullptr;
-    float* rstate = nullptr;      // [lin_heads][lin_dim][lin_dim]
+    float* rstate = nullptr;      // [B][lin_heads][lin_dim][lin_dim]
 };
 
 }  // namespace
@@ -121,6 +178,7 @@ struct qlm_model {
     // configuration (src/model/config.hpp, parsed as src/arch/qwen3_5.cpp:11-72)
     int vocab = 0, hidden = 0, inter = 0, layers_n = 0, heads = 0, kv_heads = 0, head_dim = 0;
     int lin_heads = 0, lin_dim = 0, rotary_dim = 0, conv_kernel = 0, max_seq = 0;
+    int batch = 1;  // sequences decoded in lockstep (one position for all)
     float eps = 1e-6f, rope_theta = 1000000.0f;
     std::vector<Layer> layers;
     void* embed = nullptr;  // [vocab][hidden], BF16 or F32 as stored
@@ -132,9 +190,8 @@ struct qlm_model {
     float *x = nullptr, *h = nullptr, *t1 = nullptr, *t2 = nullptr, *t3 = nullptr, *t4 = nullptr, *t5 = nullptr;
     float *gate_buf = nullptr, *up_buf = nullptr, *logits = nullptr, *scores = nullptr;
     float *decay = nullptr, *beta = nullptr;
-    int* d_token = nullptr;
-    float* d_val = nullptr;
-    int* h_token = nullptr;  // pinned
+    int* d_tokens = nullptr;  // [B] the step's input tokens, then its greedy choices
+    int* h_tokens = nullptr;  // [B] pinned
     cudaStream_t stream = nullptr;
     std::vector<void*> allocs;
     std::vector<qlm_w8*> weights;
@@ -227,6 +284,25 @@ struct Loader {
         }
         return t;
     }
+    // The values on the host only (BF16 upcast exactly).
+    int host_f32(const std::string& name, size_t numel, std::vector<float>& h) {
+        const qlm_st::Store* st = nullptr;
+        const qlm_st::TensorRef* t = tensor(name, &st, numel);
+        if (!t) return QLM_ERR_INVALID_ARG;
+        h.resize(numel);
+        const uint8_t* src = static_cast<const uint8_t*>(st->m.base) + t->begin;
+        if (t->dtype == "F32") {
+            std::memcpy(h.data(), src, numel * 4);
+        } else {
+            for (size_t i = 0; i < numel; ++i) {
+                uint16_t b;
+                std::memcpy(&b, src + 2 * i, 2);
+                const uint32_t bits = (uint32_t)b << 16;
+                std::memcpy(&h[i], &bits, 4);
+            }
+        }
+        return QLM_OK;
+    }
     // An F32 copy on the device (ModelWeights::get_tensor: BF16 upcast exactly).
     int f32(const std::string& name, size_t numel, float** out, std::vector<float>* host = nullptr) {
         const qlm_st::Store* st = nullptr;
@@ -251,17 +327,19 @@ struct Loader {
             return fail(QLM_ERR_CUDA, "upload of '%s' failed", name.c_str());
         return QLM_OK;
     }
-    // An int8 matmul weight [rows, k], quantized on the device from the mapped
-    // bytes (ModelWeights::get_weight at Precision::Int8 -> get_tensor_keep_int8).
-    int weight(const std::string& name, int rows, int k, qlm_w8** out) {
+    // Rows [rb, re) (all when re < 0) of an int8 matmul weight [rows, k],
+    // quantized on the device from the mapped bytes (ModelWeights::get_weight
+    // at Precision::Int8 -> get_tensor_keep_int8; the quantizer is row-local,
+    // so a row range holds exactly those rows' bytes and scales).
+    int weight(const std::string& name, int rows, int k, qlm_w8** out, int rb = 0, int re = -1) {
         const qlm_st::Store* st = nullptr;
         const qlm_st::TensorRef* t = tensor(name, &st, (size_t)rows * k);
         if (!t) return QLM_ERR_INVALID_ARG;
         if (t->shape.size() != 2 || t->shape[0] != rows || t->shape[1] != k)
             return fail(QLM_ERR_INVALID_ARG, "weight '%s' is not [%d, %d]", name.c_str(), rows, k);
         const void* src = static_cast<const uint8_t*>(st->m.base) + t->begin;
-        const int rc = qlm_weight_quantize_upload(src, t->dtype == "F32" ? QLM_SRC_F32 : QLM_SRC_BF16, k, rows, k, 0,
-                                                  rows, m->device, s, out);
+        const int rc = qlm_weight_quantize_upload(src, t->dtype == "F32" ? QLM_SRC_F32 : QLM_SRC_BF16, k, rows, k, rb,
+                                                  re < 0 ? rows : re, m->device, s, out);
         if (rc == QLM_OK) m->weights.push_back(*out);
         return rc;
     }
@@ -409,13 +487,16 @@ int load_all(const std::string& dir, qlm_model* m) {
                 return fail(QLM_ERR_UNSUPPORTED, "attention without QK-norm is not supported");
             QLM_TRY(L.f32(p + "self_attn.q_norm.weight", hd, &ly.q_norm));
             QLM_TRY(L.f32(p + "self_attn.k_norm.weight", hd, &ly.k_norm));
-            QLM_TRY(L.zeros(&ly.k_cache, (size_t)m->max_seq * m->kv_heads * hd));
-            QLM_TRY(L.zeros(&ly.v_cache, (size_t)m->max_seq * m->kv_heads * hd));
+            QLM_TRY(L.zeros(&ly.k_cache, (size_t)m->max_seq * m->batch * m->kv_heads * hd));
+            QLM_TRY(L.zeros(&ly.v_cache, (size_t)m->max_seq * m->batch * m->kv_heads * hd));
         } else {
             const int lin = m->lin_heads * m->lin_dim;
             if (lin <= 0) return fail(QLM_ERR_INVALID_ARG, "linear-attention layer %d without linear head sizes", i);
             const int conv_dim = 3 * lin;
-            QLM_TRY(L.weight(p + "linear_attn.in_proj_qkv.weight", conv_dim, H, &ly.qkv));
+            const std::string qkv = p + "linear_attn.in_proj_qkv.weight";
+            QLM_TRY(L.weight(qkv, conv_dim, H, &ly.qkv_q, 0, lin));
+            QLM_TRY(L.weight(qkv, conv_dim, H, &ly.qkv_k, lin, 2 * lin));
+            QLM_TRY(L.weight(qkv, conv_dim, H, &ly.qkv_v, 2 * lin, 3 * lin));
             QLM_TRY(L.weight(p + "linear_attn.in_proj_z.weight", lin, H, &ly.z));
             QLM_TRY(L.weight(p + "linear_attn.in_proj_b.weight", m->lin_heads, H, &ly.b));
             QLM_TRY(L.weight(p + "linear_attn.in_proj_a.weight", m->lin_heads, H, &ly.a));
@@ -428,19 +509,24 @@ int load_all(const std::string& dir, qlm_model* m) {
             if (m->conv_kernel && m->conv_kernel != kernel) return fail(QLM_ERR_UNSUPPORTED, "conv kernels differ");
             m->conv_kernel = kernel;
             std::vector<float> w;
-            float* tmp = nullptr;
-            QLM_TRY(L.f32(p + "linear_attn.conv1d.weight", (size_t)conv_dim * kernel, &tmp, &w));
-            std::vector<float> wt((size_t)conv_dim * kernel);
-            for (int c = 0; c < conv_dim; ++c)
-                for (int k = 0; k < kernel; ++k) wt[(size_t)k * conv_dim + c] = w[(size_t)c * kernel + k];
-            if (cudaMemcpy(tmp, wt.data(), wt.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess)
+            QLM_TRY(L.host_f32(p + "linear_attn.conv1d.weight", (size_t)conv_dim * kernel, w));
+            // tap-major (attention.cpp:402-407), channels ordered [part][sequence][c]
+            const int B = m->batch;
+            std::vector<float> wt((size_t)kernel * 3 * B * lin);
+            for (int k = 0; k < kernel; ++k)
+                for (int part = 0; part < 3; ++part)
+                    for (int b = 0; b < B; ++b)
+                        for (int c = 0; c < lin; ++c)
+                            wt[(size_t)k * 3 * B * lin + ((size_t)part * B + b) * lin + c] =
+                                w[(size_t)(part * lin + c) * kernel + k];
+            QLM_TRY(L.dev_alloc(reinterpret_cast<void**>(&ly.conv_wt), wt.size() * 4));
+            if (cudaMemcpy(ly.conv_wt, wt.data(), wt.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess)
                 return fail(QLM_ERR_CUDA, "conv weight upload failed");
-            ly.conv_wt = tmp;  // same size: reuse the buffer for the tap-major copy
-            QLM_TRY(L.zeros(&ly.conv_state, (size_t)(kernel - 1) * conv_dim));
+            QLM_TRY(L.zeros(&ly.conv_state, (size_t)(kernel - 1) * 3 * B * lin));
             QLM_TRY(L.f32(p + "linear_attn.norm.weight", m->lin_dim, &ly.gdn_norm));
             QLM_TRY(L.f32(p + "linear_attn.A_log", m->lin_heads, &ly.A_log));
             QLM_TRY(L.f32(p + "linear_attn.dt_bias", m->lin_heads, &ly.dt_bias));
-            QLM_TRY(L.zeros(&ly.rstate, (size_t)m->lin_heads * m->lin_dim * m->lin_dim));
+            QLM_TRY(L.zeros(&ly.rstate, (size_t)m->batch * m->lin_heads * m->lin_dim * m->lin_dim));
             conv_dim_max = conv_dim > conv_dim_max ? conv_dim : conv_dim_max;
         }
     }
@@ -468,18 +554,18 @@ int load_all(const std::string& dir, qlm_model* m) {
     const size_t cands[] = {(size_t)conv_dim_max, (size_t)2 * m->heads * m->head_dim, (size_t)m->inter,
                             (size_t)m->lin_heads * m->lin_dim, (size_t)2 * m->lin_heads + 16};
     for (size_t c : cands) big = c > big ? c : big;
+    const size_t B = (size_t)m->batch;
     float** bufs[] = {&m->x, &m->h, &m->t1, &m->t2, &m->t3, &m->t4, &m->t5};
-    for (float** b : bufs) QLM_TRY(L.zeros(b, big));
-    QLM_TRY(L.zeros(&m->gate_buf, (size_t)m->inter));
-    QLM_TRY(L.zeros(&m->up_buf, (size_t)m->inter));
-    QLM_TRY(L.zeros(&m->logits, (size_t)m->vocab));
-    QLM_TRY(L.zeros(&m->scores, (size_t)m->heads * m->max_seq));
-    QLM_TRY(L.zeros(&m->decay, (size_t)m->lin_heads + 1));
-    QLM_TRY(L.zeros(&m->beta, (size_t)m->lin_heads + 1));
-    QLM_TRY(L.zeros(&m->d_token, 1));
-    QLM_TRY(L.zeros(&m->d_val, 1));
-    if (cudaMallocHost(reinterpret_cast<void**>(&m->h_token), sizeof(int)) != cudaSuccess)
-        return fail(QLM_ERR_OUT_OF_MEMORY, "pinned host word");
+    for (float** b : bufs) QLM_TRY(L.zeros(b, B * big));
+    QLM_TRY(L.zeros(&m->gate_buf, B * m->inter));
+    QLM_TRY(L.zeros(&m->up_buf, B * m->inter));
+    QLM_TRY(L.zeros(&m->logits, B * m->vocab));
+    QLM_TRY(L.zeros(&m->scores, B * m->heads * m->max_seq));
+    QLM_TRY(L.zeros(&m->decay, B * m->lin_heads + 1));
+    QLM_TRY(L.zeros(&m->beta, B * m->lin_heads + 1));
+    QLM_TRY(L.zeros(&m->d_tokens, B));
+    if (cudaMallocHost(reinterpret_cast<void**>(&m->h_tokens), B * sizeof(int)) != cudaSuccess)
+        return fail(QLM_ERR_OUT_OF_MEMORY, "pinned host words");
     if (cudaStreamSynchronize(m->stream) != cudaSuccess) return fail(QLM_ERR_CUDA, "load synchronize failed");
     return QLM_OK;
 }
@@ -490,7 +576,7 @@ void release(qlm_model* m) {
     if (m->stream) cudaStreamSynchronize(m->stream);
     for (qlm_w8* w : m->weights) qlm_weight_free(w);
     for (void* p : m->allocs) cudaFree(p);
-    if (m->h_token) cudaFreeHost(m->h_token);
+    if (m->h_tokens) cudaFreeHost(m->h_tokens);
     if (m->stream) cudaStreamDestroy(m->stream);
     delete m;
 }
@@ -500,59 +586,68 @@ void release(qlm_model* m) {
 namespace {
 
 // One layer's gated-delta-net step (Qwen3_5GatedDeltaNet::forward,
-// src/model/attention.cpp:414-591) on m->h; result in m->t5.
+// src/model/attention.cpp:414-591) for the B sequences on m->h [B][hidden];
+// result in m->t5 [B][hidden]. Heads of all sequences run as B * lin_heads heads.
 int gdn_step(qlm_model* m, Layer& ly) {
     cudaStream_t s = m->stream;
-    const int H = m->hidden, lh = m->lin_heads, ld = m->lin_dim, lin = lh * ld, conv_dim = 3 * lin;
-    float* qkv = m->t1;
-    float* conv = m->t2;
-    float* z = m->t3;
-    float* b_raw = m->t4;
-    float* a_raw = m->t4 + lh;
-    const qlm_w8* ws[4] = {ly.qkv, ly.z, ly.b, ly.a};
-    float* ys[4] = {qkv, z, b_raw, a_raw};
-    const int64_t lds[4] = {conv_dim, lin, lh, lh};
-    QLM_TRY(qlm_linear_int8_grouped(m->h, 1, H, H, ws, 4, ys, lds, 0, s));                 // 1. projections
-    QLM_TRY(qlm_conv1d_update_tapmajor(qkv, ly.conv_state, ly.conv_ring, ly.conv_wt, conv, conv_dim,
-                                       m->conv_kernel, s));                                  // 2. conv step
+    const int B = m->batch, H = m->hidden, lh = m->lin_heads, ld = m->lin_dim, lin = lh * ld;
+    const int channels = 3 * B * lin;  // conv channels: [part][sequence][c]
+    float* qkv = m->t1;                // [3][B][lin]
+    float* conv = m->t2;               // same layout, after the conv
+    float* z = m->t3;                  // [B][lin]
+    float* b_raw = m->t4;              // [B][lh]
+    float* a_raw = m->t4 + (size_t)B * lh;
+    const qlm_w8* ws[6] = {ly.qkv_q, ly.qkv_k, ly.qkv_v, ly.z, ly.b, ly.a};
+    float* ys[6] = {qkv, qkv + (size_t)B * lin, qkv + (size_t)2 * B * lin, z, b_raw, a_raw};
+    const int64_t lds[6] = {lin, lin, lin, lin, lh, lh};
+    QLM_TRY(qlm_linear_int8_grouped(m->h, B, H, H, ws, 6, ys, lds, 0, s));                      // 1. projections
+    QLM_TRY(qlm_conv1d_update_tapmajor(qkv, ly.conv_state, ly.conv_ring, ly.conv_wt, conv, channels,
+                                       m->conv_kernel, s));                                       // 2. conv step
     ly.conv_ring = (ly.conv_ring + 1) % (m->conv_kernel - 1);
-    QLM_TRY(qlm_silu(conv, conv_dim, s));                                                    // 4. SiLU
-    float *q = conv, *k = conv + lin, *v = conv + 2 * lin;
-    QLM_TRY(qlm_l2norm_heads(q, lh, ld, 1e-6f, s));                                          // 5. L2 norms
-    QLM_TRY(qlm_l2norm_heads(k, lh, ld, 1e-6f, s));
-    QLM_TRY(qlm_gdn_gates(a_raw, b_raw, ly.A_log, ly.dt_bias, m->decay, m->beta, lh, s));  // 6. gates
+    QLM_TRY(qlm_silu(conv, channels, s));                                                         // 4. SiLU
+    float *q = conv, *k = conv + (size_t)B * lin, *v = conv + (size_t)2 * B * lin;
+    QLM_TRY(qlm_l2norm_heads(q, B * lh, ld, 1e-6f, s));                                           // 5. L2 norms
+    QLM_TRY(qlm_l2norm_heads(k, B * lh, ld, 1e-6f, s));
+    if (qlm::launch_gdn_gates(a_raw, b_raw, ly.A_log, ly.dt_bias, m->decay, m->beta, B * lh, lh, s) != cudaSuccess)
+        return launch_ok("gates");                                                                // 6. gates
     float* out = qkv;  // the projections are consumed
-    QLM_TRY(qlm_gdn_recurrence(ly.rstate, q, k, v, m->decay, m->beta, out, lh, ld, s));    // 7. delta rule
-    QLM_TRY(qlm_rms_norm_gain(out, ly.gdn_norm, out, lh, ld, 1e-6f, s));                    // 8. head norm
-    QLM_TRY(qlm_silu_mul(z, out, lin, s));                                                   // 9. z = SiLU(z) * out
-    return qlm_linear_int8(z, 1, lin, lin, ly.out, m->t5, H, 0, s);                          // 10. out_proj
+    QLM_TRY(qlm_gdn_recurrence(ly.rstate, q, k, v, m->decay, m->beta, out, B * lh, ld, s));     // 7. delta rule
+    QLM_TRY(qlm_rms_norm_gain(out, ly.gdn_norm, out, B * lh, ld, 1e-6f, s));                     // 8. head norm
+    QLM_TRY(qlm_silu_mul(z, out, (int64_t)B * lin, s));                                           // 9. SiLU(z) * out
+    return qlm_linear_int8(z, B, lin, lin, ly.out, m->t5, H, 0, s);                               // 10. out_proj
 }
 
 // One layer's gated GQA step (Qwen3_5Attention::forward,
-// src/model/attention.cpp:138-235) at position pos on m->h; result in m->t5.
+// src/model/attention.cpp:138-235) at position pos for the B sequences;
+// result in m->t5. Sequence b's query head h is head b * heads + h, its KV
+// head b * kv_heads + h / group: the cache [T][B][kv_heads][d] reads as
+// B * kv_heads heads.
 int attn_step(qlm_model* m, Layer& ly, int pos) {
     cudaStream_t s = m->stream;
-    const int H = m->hidden, hd = m->head_dim, qd = 2 * hd, nh = m->heads, kvh = m->kv_heads, kv = kvh * hd;
+    const int B = m->batch, H = m->hidden, hd = m->head_dim, qd = 2 * hd, nh = m->heads, kvh = m->kv_heads;
+    const int kv = kvh * hd;
     float *q = m->t1, *k = m->t2, *v = m->t3, *att = m->t4;
     const qlm_w8* ws[3] = {ly.q, ly.k, ly.v};
     float* ys[3] = {q, k, v};
     const int64_t lds[3] = {(int64_t)nh * qd, kv, kv};
-    QLM_TRY(qlm_linear_int8_grouped(m->h, 1, H, H, ws, 3, ys, lds, 0, s));        // 1. projections
-    if (qlm::launch_rms_norm_strided(q, ly.q_norm, q, nh, hd, qd, 1e-6f, s) != cudaSuccess)  // 2. QK-norm
+    QLM_TRY(qlm_linear_int8_grouped(m->h, B, H, H, ws, 3, ys, lds, 0, s));                // 1. projections
+    if (qlm::launch_rms_norm_strided(q, ly.q_norm, q, B * nh, hd, qd, 1e-6f, s) != cudaSuccess)  // 2. QK-norm
         return launch_ok("QK-norm");
-    QLM_TRY(qlm_rms_norm(k, ly.k_norm, k, kvh, hd, 1e-6f, s));
-    const int half = m->rotary_dim / 2;                                              // 3. partial RoPE
+    QLM_TRY(qlm_rms_norm(k, ly.k_norm, k, B * kvh, hd, 1e-6f, s));
+    const int half = m->rotary_dim / 2;                                                      // 3. partial RoPE
     const float* cs = m->rope_cos + (size_t)pos * half;
     const float* sn = m->rope_sin + (size_t)pos * half;
-    QLM_TRY(qlm_rope_neox(k, 1, kvh, hd, m->rotary_dim, cs, sn, s));
-    QLM_TRY(qlm_rope_neox(q, 1, nh, qd, m->rotary_dim, cs, sn, s));  // the query half of each [query | gate] row
-    if (cudaMemcpyAsync(ly.k_cache + (size_t)pos * kv, k, kv * 4, cudaMemcpyDeviceToDevice, s) != cudaSuccess ||
-        cudaMemcpyAsync(ly.v_cache + (size_t)pos * kv, v, kv * 4, cudaMemcpyDeviceToDevice, s) != cudaSuccess)
-        return fail(QLM_ERR_CUDA, "KV cache write failed");                          // 4. cache
-    QLM_TRY(qlm_gqa_attend(q, qd, ly.k_cache, ly.v_cache, att, pos, nh, kvh, hd, m->scores, s));  // 5. attention
-    sigmoid_gate_kernel<<<(nh * hd + kEmbThreads - 1) / kEmbThreads, kEmbThreads, 0, s>>>(att, q, nh, hd);  // 6.
+    QLM_TRY(qlm_rope_neox(k, 1, B * kvh, hd, m->rotary_dim, cs, sn, s));
+    QLM_TRY(qlm_rope_neox(q, 1, B * nh, qd, m->rotary_dim, cs, sn, s));  // the query half of each [query | gate] row
+    const size_t row = (size_t)B * kv;
+    if (cudaMemcpyAsync(ly.k_cache + (size_t)pos * row, k, row * 4, cudaMemcpyDeviceToDevice, s) != cudaSuccess ||
+        cudaMemcpyAsync(ly.v_cache + (size_t)pos * row, v, row * 4, cudaMemcpyDeviceToDevice, s) != cudaSuccess)
+        return fail(QLM_ERR_CUDA, "KV cache write failed");                                  // 4. cache
+    QLM_TRY(qlm_gqa_attend(q, qd, ly.k_cache, ly.v_cache, att, pos, B * nh, B * kvh, hd, m->scores, s));  // 5.
+    const int n = B * nh * hd;
+    sigmoid_gate_kernel<<<(n + kEmbThreads - 1) / kEmbThreads, kEmbThreads, 0, s>>>(att, q, B * nh, hd);  // 6.
     QLM_TRY(launch_ok("output gate"));
-    return qlm_linear_int8(att, 1, nh * hd, nh * hd, ly.o, m->t5, H, 0, s);         // 7. o_proj
+    return qlm_linear_int8(att, B, nh * hd, nh * hd, ly.o, m->t5, H, 0, s);                 // 7. o_proj
 }
 
 int add_into(qlm_model* m, float* x, const float* d, int n) {
@@ -562,16 +657,67 @@ int add_into(qlm_model* m, float* x, const float* d, int n) {
 
 }  // namespace
 
+namespace {
+
+int decode_step(qlm_model* m, const int* tokens, int pos, int* next_tokens, float* logits) {
+    const int B = m->batch;
+    for (int b = 0; b < B; ++b)
+        if (tokens[b] < 0 || tokens[b] >= m->vocab)
+            return fail(QLM_ERR_INVALID_ARG, "token %d (sequence %d) not in [0, %d)", tokens[b], b, m->vocab);
+    if (pos < 0 || pos >= m->max_seq)
+        return fail(QLM_ERR_INVALID_ARG, "position %d not in [0, max_seq %d)", pos, m->max_seq);
+    Dev g(m->device);
+    if (!g.ok) return fail(QLM_ERR_CUDA, "cudaSetDevice(%d) failed", m->device);
+    cudaStream_t s = m->stream;
+    const int H = m->hidden;
+    std::memcpy(m->h_tokens, tokens, (size_t)B * sizeof(int));
+    if (cudaMemcpyAsync(m->d_tokens, m->h_tokens, (size_t)B * sizeof(int), cudaMemcpyHostToDevice, s) != cudaSuccess)
+        return fail(QLM_ERR_CUDA, "token upload failed");
+    embed_rows_kernel<<<dim3((H + kEmbThreads - 1) / kEmbThreads, B), kEmbThreads, 0, s>>>(m->embed, m->embed_bf16,
+                                                                                           m->d_tokens, H, m->x);
+    QLM_TRY(launch_ok("embedding"));
+    for (Layer& ly : m->layers) {
+        QLM_TRY(qlm_rms_norm(m->x, ly.in_norm, m->h, B, H, m->eps, s));
+        QLM_TRY(ly.full_attn ? attn_step(m, ly, pos) : gdn_step(m, ly));
+        QLM_TRY(add_into(m, m->x, m->t5, B * H));
+        QLM_TRY(qlm_rms_norm(m->x, ly.post_norm, m->h, B, H, m->eps, s));
+        const qlm_w8* ws[2] = {ly.gate, ly.up};
+        float* ys[2] = {m->gate_buf, m->up_buf};
+        const int64_t lds[2] = {m->inter, m->inter};
+        QLM_TRY(qlm_linear_int8_grouped(m->h, B, H, H, ws, 2, ys, lds, 0, s));
+        QLM_TRY(qlm_silu_mul(m->gate_buf, m->up_buf, (int64_t)B * m->inter, s));
+        QLM_TRY(qlm_linear_int8(m->gate_buf, B, m->inter, m->inter, ly.down, m->t5, H, 0, s));
+        QLM_TRY(add_into(m, m->x, m->t5, B * H));
+    }
+    QLM_TRY(qlm_rms_norm(m->x, m->final_norm, m->h, B, H, m->eps, s));
+    QLM_TRY(qlm_linear_int8(m->h, B, H, H, m->lm_head, m->logits, m->vocab, 0, s));
+    greedy_rows_kernel<<<B, 1024, 0, s>>>(m->logits, m->vocab, m->d_tokens);
+    QLM_TRY(launch_ok("greedy choice"));
+    if (cudaMemcpyAsync(m->h_tokens, m->d_tokens, (size_t)B * sizeof(int), cudaMemcpyDeviceToHost, s) != cudaSuccess)
+        return fail(QLM_ERR_CUDA, "token read-back failed");
+    if (logits &&
+        cudaMemcpyAsync(logits, m->logits, (size_t)B * m->vocab * 4, cudaMemcpyDeviceToHost, s) != cudaSuccess)
+        return fail(QLM_ERR_CUDA, "logits read-back failed");
+    if (cudaStreamSynchronize(s) != cudaSuccess) return launch_ok("decode step");
+    QLM_TRY(qlm_device_status(m->device, 1));
+    std::memcpy(next_tokens, m->h_tokens, (size_t)B * sizeof(int));
+    return QLM_OK;
+}
+
+}  // namespace
+
 extern "C" {
 
-int qlm_model_load(const char* dir, int device, int max_seq, qlm_model** out) {
+int qlm_model_load_batch(const char* dir, int device, int max_seq, int batch, qlm_model** out) {
     if (!dir || !out) return fail(QLM_ERR_INVALID_ARG, "NULL argument");
     *out = nullptr;
     if (max_seq < 1 || max_seq > (1 << 20)) return fail(QLM_ERR_INVALID_ARG, "max_seq %d not in [1, 2^20]", max_seq);
+    if (batch < 1 || batch > 1024) return fail(QLM_ERR_INVALID_ARG, "batch %d not in [1, 1024]", batch);
     qlm_model* m = new (std::nothrow) qlm_model();
     if (!m) return fail(QLM_ERR_OUT_OF_MEMORY, "host allocation failed");
     m->device = device;
     m->max_seq = max_seq;
+    m->batch = batch;
     int rc = parse_config(dir, m);
     Dev g(device);
     if (rc == QLM_OK && !g.ok) rc = fail(QLM_ERR_CUDA, "cudaSetDevice(%d) failed", device);
@@ -586,20 +732,25 @@ int qlm_model_load(const char* dir, int device, int max_seq, qlm_model** out) {
     return QLM_OK;
 }
 
+int qlm_model_load(const char* dir, int device, int max_seq, qlm_model** out) {
+    return qlm_model_load_batch(dir, device, max_seq, 1, out);
+}
+
 int qlm_model_reset(qlm_model* m) {
     if (!m) return fail(QLM_ERR_INVALID_ARG, "NULL model");
     Dev g(m->device);
     if (!g.ok) return fail(QLM_ERR_CUDA, "cudaSetDevice(%d) failed", m->device);
+    const size_t B = (size_t)m->batch;
     for (Layer& ly : m->layers) {
-        const size_t kv = (size_t)m->max_seq * m->kv_heads * m->head_dim * 4;
+        const size_t kv = (size_t)m->max_seq * B * m->kv_heads * m->head_dim * 4;
         const size_t lin = (size_t)m->lin_heads * m->lin_dim;
         cudaError_t e = cudaSuccess;
         if (ly.full_attn) {
             e = cudaMemsetAsync(ly.k_cache, 0, kv, m->stream);
             if (e == cudaSuccess) e = cudaMemsetAsync(ly.v_cache, 0, kv, m->stream);
         } else {
-            e = cudaMemsetAsync(ly.conv_state, 0, (size_t)(m->conv_kernel - 1) * 3 * lin * 4, m->stream);
-            if (e == cudaSuccess) e = cudaMemsetAsync(ly.rstate, 0, lin * m->lin_dim * 4, m->stream);
+            e = cudaMemsetAsync(ly.conv_state, 0, (size_t)(m->conv_kernel - 1) * 3 * B * lin * 4, m->stream);
+            if (e == cudaSuccess) e = cudaMemsetAsync(ly.rstate, 0, B * lin * m->lin_dim * 4, m->stream);
             ly.conv_ring = 0;
         }
         if (e != cudaSuccess) return fail(QLM_ERR_CUDA, "state reset failed");
@@ -607,52 +758,25 @@ int qlm_model_reset(qlm_model* m) {
     return cudaStreamSynchronize(m->stream) == cudaSuccess ? QLM_OK : fail(QLM_ERR_CUDA, "synchronize failed");
 }
 
-int qlm_model_info(const qlm_model* m, int* vocab, int* hidden, int* layers, int* max_seq) {
+int qlm_model_info(const qlm_model* m, int* vocab, int* hidden, int* layers, int* max_seq, int* batch) {
     if (!m) return fail(QLM_ERR_INVALID_ARG, "NULL model");
     if (vocab) *vocab = m->vocab;
     if (hidden) *hidden = m->hidden;
     if (layers) *layers = m->layers_n;
     if (max_seq) *max_seq = m->max_seq;
+    if (batch) *batch = m->batch;
     return QLM_OK;
 }
 
 int qlm_model_decode(qlm_model* m, int token, int pos, int* next_token, float* logits) {
     if (!m || !next_token) return fail(QLM_ERR_INVALID_ARG, "NULL argument");
-    if (token < 0 || token >= m->vocab) return fail(QLM_ERR_INVALID_ARG, "token %d not in [0, %d)", token, m->vocab);
-    if (pos < 0 || pos >= m->max_seq)
-        return fail(QLM_ERR_INVALID_ARG, "position %d not in [0, max_seq %d)", pos, m->max_seq);
-    Dev g(m->device);
-    if (!g.ok) return fail(QLM_ERR_CUDA, "cudaSetDevice(%d) failed", m->device);
-    cudaStream_t s = m->stream;
-    const int H = m->hidden;
-    embed_row_kernel<<<(H + kEmbThreads - 1) / kEmbThreads, kEmbThreads, 0, s>>>(m->embed, m->embed_bf16, nullptr,
-                                                                                   token, H, m->x);
-    QLM_TRY(launch_ok("embedding"));
-    for (Layer& ly : m->layers) {
-        QLM_TRY(qlm_rms_norm(m->x, ly.in_norm, m->h, 1, H, m->eps, s));
-        QLM_TRY(ly.full_attn ? attn_step(m, ly, pos) : gdn_step(m, ly));
-        QLM_TRY(add_into(m, m->x, m->t5, H));
-        QLM_TRY(qlm_rms_norm(m->x, ly.post_norm, m->h, 1, H, m->eps, s));
-        const qlm_w8* ws[2] = {ly.gate, ly.up};
-        float* ys[2] = {m->gate_buf, m->up_buf};
-        const int64_t lds[2] = {m->inter, m->inter};
-        QLM_TRY(qlm_linear_int8_grouped(m->h, 1, H, H, ws, 2, ys, lds, 0, s));
-        QLM_TRY(qlm_silu_mul(m->gate_buf, m->up_buf, m->inter, s));
-        QLM_TRY(qlm_linear_int8(m->gate_buf, 1, m->inter, m->inter, ly.down, m->t5, H, 0, s));
-        QLM_TRY(add_into(m, m->x, m->t5, H));
-    }
-    QLM_TRY(qlm_rms_norm(m->x, m->final_norm, m->h, 1, H, m->eps, s));
-    QLM_TRY(qlm_linear_int8(m->h, 1, H, H, m->lm_head, m->logits, m->vocab, 0, s));
-    QLM_TRY(qlm_argmax_f32(m->logits, m->vocab, 0, nullptr, m->d_token, m->d_val, 0, s));
-    if (cudaMemcpyAsync(m->h_token, m->d_token, sizeof(int), cudaMemcpyDeviceToHost, s) != cudaSuccess)
-        return fail(QLM_ERR_CUDA, "token read-back failed");
-    if (logits && cudaMemcpyAsync(logits, m->logits, (size_t)m->vocab * 4, cudaMemcpyDeviceToHost, s) != cudaSuccess)
-        return fail(QLM_ERR_CUDA, "logits read-back failed");
-    if (cudaStreamSynchronize(s) != cudaSuccess) return launch_ok("decode step");
-    QLM_TRY(qlm_device_status(m->device, 1));
-    // DecoderModel::sample(logits, 0, 0) answers 0 when no logit is a number
-    *next_token = *m->h_token < 0 ? 0 : *m->h_token;
-    return QLM_OK;
+    if (m->batch != 1) return fail(QLM_ERR_INVALID_ARG, "the model decodes %d sequences: use qlm_model_decode_batch", m->batch);
+    return decode_step(m, &token, pos, next_token, logits);
+}
+
+int qlm_model_decode_batch(qlm_model* m, const int* tokens, int pos, int* next_tokens, float* logits) {
+    if (!m || !tokens || !next_tokens) return fail(QLM_ERR_INVALID_ARG, "NULL argument");
+    return decode_step(m, tokens, pos, next_tokens, logits);
 }
 
 void qlm_model_free(qlm_model* m) { release(m); }
