@@ -22,6 +22,8 @@ one GEMV each; the step is captured once as a CUDA graph and replayed.
            at M=1, row-sharded over the N ranks (strong scaling), each checked
            against the reference output hash, the fused NVLink gather timed
            beside the GEMV + NCCL all-gather
+* cfg5:    configuration 5, 64 sequences decoded data-parallel over the N
+           GPUs with the device-resident step, aggregate tok/s (every N)
 * decode:  configuration 3 greedy decode tok/s with the whole step on the
            GPU (activations in HBM), beside QuickLM's own model code with only
            the int8 matmuls on the GPU and QuickLM on the host cores; token
@@ -369,6 +371,96 @@ def decode_leg(n_new=128, seed=7, prompt_len=64):
         shutil.rmtree(d, ignore_errors=True)
 
 
+# Configuration 5: the configuration-3 architecture widened (other sizes as configuration 3).
+CFG5 = {"hidden": 2560, "layers": 36, "inter": 9728}
+
+
+def cfg5_leg(qlm, torch, dist, world, rank, local, n_seq=64, prompt_len=128, n_new=256, seed=5):
+    """Configuration 5: whole-box batched greedy decode. 64 independent
+    sequences (prompts of 128 uniform random token ids) of the configuration-3
+    architecture widened to hidden 2560, 36 layers, intermediate 9728 (3.9B
+    parameters, int8), 256 new tokens each. The sequences are spread data-
+    parallel: each of the N ranks holds the whole int8 model (4.4 GB) and
+    decodes 64/N of them in lockstep with the device-resident step (every
+    activation in HBM), so nothing crosses NVLink during decode. Timed with CUDA
+    events on the model's stream, max over ranks; value = 64 * 256 tokens /
+    decode time. Parity: the batched logits are bit-identical to decoding a
+    sequence alone (checked on rank 0's first sequence, tokens compared), and
+    the single-sequence step is pinned to QuickLM's own CPU decode by
+    tests/test_gpu_model.py and tests/test_gpu_e2e.py. The checkpoint is
+    written once per run from torch's seeded GPU generator (same format and
+    N(0, 0.02^2) distribution as integration/make_checkpoint.py's numpy draw)."""
+    import shutil
+    import tempfile
+    sys.path.insert(0, os.path.join(ROOT, "integration"))
+    from make_checkpoint import build as build_ckpt
+    base = "/dev/shm" if os.path.isdir("/dev/shm") and shutil.disk_usage("/dev/shm").free > 12e9 \
+        else tempfile.gettempdir()
+    tag = os.environ.get("MASTER_PORT", str(os.getpid())) if world > 1 else str(os.getpid())
+    d = os.path.join(base, f"qlm_cfg5_{tag}")
+    out = {"metric": "aggregate greedy decode tok/s (cfg5: 64 sequences, 128-token prompts, 256 new tokens)",
+           "unit": "tok/s", "n_gpus": world, "sequences_per_gpu": n_seq // world, "prompt_len": prompt_len,
+           "new_tokens": n_new, "parallelism": f"data-parallel x{world}, whole int8 model on every GPU"}
+    try:
+        t0 = time.perf_counter()
+        if rank == 0:
+            build_ckpt(d, seed=seed, prompt_len=2, device_rng=True, **CFG5)
+        if dist is not None:
+            dist.barrier()
+        out["checkpoint_write_s"] = round(time.perf_counter() - t0, 2)
+        B = n_seq // world
+        prompts = np.random.default_rng(seed + 100).integers(0, 151936, size=(n_seq, prompt_len))
+        mine = prompts[rank * B:(rank + 1) * B]
+        t0 = time.perf_counter()
+        m = qlm.Model(d, device=local, max_seq=prompt_len + n_new, batch=B)
+        out["load_s"] = round(time.perf_counter() - t0, 2)
+        stream = torch.cuda.ExternalStream(m.stream)
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+        ev[0].record(stream)
+        for i in range(prompt_len - 1):
+            m.decode(mine[:, i], i)
+        ev[1].record(stream)
+        cur = mine[:, -1]
+        toks = []
+        if dist is not None:
+            dist.barrier()
+        ev[2].record(stream)
+        for j in range(n_new):
+            cur = m.decode(cur, prompt_len - 1 + j)
+            toks.append(cur)
+        ev[3].record(stream)
+        torch.cuda.synchronize()
+        t = torch.tensor([ev[0].elapsed_time(ev[1]), ev[2].elapsed_time(ev[3])], device="cuda")
+        if dist is not None:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        prefill_ms, decode_ms = float(t[0]), float(t[1])
+        m.free()
+        ok = True
+        if rank == 0:
+            m1 = qlm.Model(d, device=local, max_seq=prompt_len + n_new, batch=1)
+            for i in range(prompt_len - 1):
+                m1.decode(mine[:1, i], i)
+            c1 = mine[:1, -1]
+            alone = []
+            for j in range(n_new):
+                c1 = m1.decode(c1, prompt_len - 1 + j)
+                alone.append(int(c1[0]))
+            m1.free()
+            ok = alone == [int(s[0]) for s in toks]
+        out.update({"value": round(n_seq * n_new / (decode_ms / 1000.0), 2), "decode_s": round(decode_ms / 1000, 3),
+                    "prefill_s": round(prefill_ms / 1000, 3),
+                    "ms_per_step": round(decode_ms / n_new, 3),
+                    "parity": "sequence 0 batched == alone" if ok else "MISMATCH: batched != alone"})
+    except Exception as exc:  # reported, never hidden
+        out["error"] = f"{type(exc).__name__}: {exc}"
+    finally:
+        if dist is not None:
+            dist.barrier()
+        if rank == 0:
+            shutil.rmtree(d, ignore_errors=True)
+    return out
+
+
 def physical_cores(cpus):
     """Physical cores among the logical CPUs `cpus` (from /proc/cpuinfo)."""
     try:
@@ -515,6 +607,7 @@ def main():
     ap.add_argument("--m", type=int, default=1)
     ap.add_argument("--no-decode", action="store_true", help="skip the configuration-3 decode leg")
     ap.add_argument("--no-sharded", action="store_true", help="skip the configuration-4 sharded-shape table")
+    ap.add_argument("--no-cfg5", action="store_true", help="skip the configuration-5 batched decode")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.impl == "reference":
@@ -693,6 +786,10 @@ def main():
     if not args.no_sharded:
         sharded, sharded_ok = sharded_leg(qlm, torch, dist, comm, world, rank, local)
 
+    cfg5 = None
+    if not args.no_cfg5:
+        cfg5 = cfg5_leg(qlm, torch, dist, world, rank, local)
+
     prefill = None
     if world == 1 and not args.no_prefill:
         try:
@@ -711,7 +808,8 @@ def main():
             decode = decode_leg()
         except Exception as exc:  # reported, never hidden
             decode = {"error": f"{type(exc).__name__}: {exc}"}
-    all_ok = parity_ok and sharded_ok and (decode is None or decode.get("tokens_identical", True))
+    all_ok = parity_ok and sharded_ok and (decode is None or decode.get("tokens_identical", True)) and \
+        (cfg5 is None or not str(cfg5.get("parity", "")).startswith("MISMATCH"))
 
     used_graph = graph is not None
     graph = None
@@ -747,6 +845,7 @@ def main():
                           "sharded shapes vs the reference output hashes",
             "sharded": sharded,
             "decode": decode,
+            "cfg5": cfg5,
         }
         print(json.dumps(line), flush=True)
     for w in weights:

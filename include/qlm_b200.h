@@ -249,6 +249,8 @@ int qlm_model_reset(qlm_model* m);
 int qlm_model_decode(qlm_model* m, int token, int pos, int* next_token, float* logits);
 int qlm_model_decode_batch(qlm_model* m, const int* tokens, int pos, int* next_tokens, float* logits);
 int qlm_model_info(const qlm_model* m, int* vocab, int* hidden, int* layers, int* max_seq, int* batch);
+/* The cudaStream_t every step of the model runs on (for timing with events). */
+void* qlm_model_stream(const qlm_model* m);
 void qlm_model_free(qlm_model* m);
 
 /* Release a handle and its device memory (NULL is a no-op). */

@@ -30,9 +30,16 @@ def to_bf16(a: np.ndarray) -> np.ndarray:
 
 def build(out_dir: str, seed: int = 7, hidden: int = 1024, layers: int = 24, inter: int = 3584,
           vocab: int = 151936, heads: int = 16, kv_heads: int = 4, head_dim: int = 64, lin_heads: int = 16,
-          lin_dim: int = 128, prompt_len: int = 64) -> dict:
+          lin_dim: int = 128, prompt_len: int = 64, device_rng: bool = False) -> dict:
+    """device_rng: draw the N(0, 0.02^2) weights with torch's generator on the
+    GPU (seeded; the same distribution, other numbers) — for the multi-GB
+    configuration-5 checkpoint, which numpy would take minutes to draw."""
     os.makedirs(out_dir, exist_ok=True)
     rng = np.random.default_rng(seed)
+    gen = None
+    if device_rng:
+        import torch
+        gen = torch.Generator(device="cuda").manual_seed(seed)
     layer_types = ["full_attention" if i % 4 == 3 else "linear_attention" for i in range(layers)]
     cfg = {"model_type": "qwen3_5_text", "vocab_size": vocab, "hidden_size": hidden, "intermediate_size": inter,
            "num_hidden_layers": layers, "num_attention_heads": heads, "num_key_value_heads": kv_heads,
@@ -84,16 +91,21 @@ def build(out_dir: str, seed: int = 7, hidden: int = 1024, layers: int = 24, int
     with open(os.path.join(out_dir, "model.safetensors"), "wb") as f:
         f.write(struct.pack("<Q", len(hjson)))
         f.write(hjson)
-        for name, shape, gen in tensors:
+        for name, shape, kind in tensors:
             n = int(np.prod(shape))
-            if gen == "normal":
+            if kind == "normal":
                 left, step = n, 1 << 24
                 while left:
                     k = min(left, step)
-                    f.write(to_bf16(rng.standard_normal(k) * 0.02).tobytes())
+                    if gen is not None:
+                        import torch
+                        t = (torch.randn(k, device="cuda", generator=gen) * 0.02).to(torch.bfloat16)
+                        f.write(t.view(torch.int16).cpu().numpy().tobytes())
+                    else:
+                        f.write(to_bf16(rng.standard_normal(k) * 0.02).tobytes())
                     left -= k
             else:
-                f.write(to_bf16(np.full(n, gen, np.float32)).tobytes())
+                f.write(to_bf16(np.full(n, kind, np.float32)).tobytes())
     with open(os.path.join(out_dir, "config.json"), "w") as f:
         json.dump(cfg, f, indent=1)
     prompt = np.random.default_rng(seed + 1).integers(0, vocab, size=prompt_len)

@@ -44,7 +44,7 @@ ABI_SYMBOLS = (
     "qlm_add_rms_norm", "qlm_silu_mul", "qlm_rope_neox", "qlm_rope_neox_tables", "qlm_silu",
     "qlm_conv1d_update_tapmajor", "qlm_l2norm_heads", "qlm_gdn_gates", "qlm_gdn_recurrence", "qlm_rms_norm_gain",
     "qlm_gqa_attend", "qlm_comm_set_timeout_us", "qlm_comm_status", "qlm_model_load", "qlm_model_reset",
-    "qlm_model_decode", "qlm_model_info", "qlm_model_free", "qlm_model_load_batch", "qlm_model_decode_batch",
+    "qlm_model_decode", "qlm_model_info", "qlm_model_free", "qlm_model_load_batch", "qlm_model_decode_batch", "qlm_model_stream",
 )
 
 _STATUS = {0: "OK", 1: "INVALID_ARG", 2: "CUDA", 3: "OUT_OF_MEMORY", 4: "UNSUPPORTED", 5: "TIMEOUT", 6: "NCCL",
@@ -118,6 +118,8 @@ def load(path: str = LIB_PATH):
     lib.qlm_model_info.argtypes = [P] + [ctypes.POINTER(I)] * 5
     lib.qlm_model_load_batch.argtypes = [ctypes.c_char_p, I, I, I, ctypes.POINTER(P)]
     lib.qlm_model_decode_batch.argtypes = [P, P, I, P, P]
+    lib.qlm_model_stream.argtypes = [P]
+    lib.qlm_model_stream.restype = P
     lib.qlm_model_free.argtypes = [P]
     lib.qlm_model_free.restype = None
     lib.qlm_comm_status.argtypes = [P]
@@ -675,6 +677,11 @@ class Model:
         _check(load().qlm_model_decode_batch(self.handle, toks.ctypes.data, int(pos), nxt.ctypes.data,
                                              lg.ctypes.data if lg is not None else None))
         return (nxt, lg) if logits else nxt
+
+    @property
+    def stream(self) -> int:
+        """The cudaStream_t (as an integer) every step runs on."""
+        return int(load().qlm_model_stream(self.handle) or 0)
 
     def reset(self) -> None:
         """Clear the KV caches and recurrent states (DecoderModel::reset_states)."""

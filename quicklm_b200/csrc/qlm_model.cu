@@ -779,6 +779,8 @@ int qlm_model_decode_batch(qlm_model* m, const int* tokens, int pos, int* next_t
     return decode_step(m, tokens, pos, next_tokens, logits);
 }
 
+void* qlm_model_stream(const qlm_model* m) { return m ? static_cast<void*>(m->stream) : nullptr; }
+
 void qlm_model_free(qlm_model* m) { release(m); }
 
 }  // extern "C"
