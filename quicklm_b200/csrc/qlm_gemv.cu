@@ -217,7 +217,7 @@ __device__ __forceinline__ void chunk_update(const float* __restrict__ xs_chunk,
 // kernel's CTA can start its weight copies while this one finishes.
 // TMA: fill slots by TMA (GemvGroup::mq/ms) instead of per-row bulk copies.
 template <int MM, int R, bool GATHER, bool Q4, bool TMA>
-__global__ void __launch_bounds__(MM == 1 ? 384 : 512, MM == 1 ? 2 : 1)
+__global__ void __launch_bounds__(MM == 1 || R == 2 ? 384 : 512, MM == 1 ? 2 : 1)
     gemv_kernel(const __grid_constant__ GemvParams p) {
     constexpr int CB = Q4 ? 64 : 128;  // weight bytes per row per 128-element chunk
     constexpr int kRowChunkBytes = row_chunk_bytes<Q4>();
@@ -495,8 +495,17 @@ struct Plan {
 // 12.1 us); below that R = 1 keeps enough warps per SM and two CTAs per SM
 // (config 1, 6144 x 2048: 5.5 us vs 8.2 us at R = 2). R = 4 was slower than
 // R = 2 everywhere. M > 1 keeps R = 1.
+// M > 1: two rows per thread halve the activations' shared-memory traffic,
+// which bounds the one-row form (per activation row and 128-element chunk a
+// warp issues ~22 instructions against four 128-bit activation loads, 16
+// shared-memory wavefronts). QLM_GEMV_R2=0 keeps one row per thread (for
+// comparisons).
 int pick_rows_per_thread(int mm, int rows, int sm_count) {
-    if (mm > 1) return 1;
+    static const bool r2_multi = [] {
+        const char* e = std::getenv("QLM_GEMV_R2");
+        return !(e && e[0] == '0');
+    }();
+    if (mm > 1 && !r2_multi) return 1;
     return rows / sm_count >= 48 ? 2 : 1;
 }
 
@@ -505,7 +514,7 @@ int pick_rows_per_thread(int mm, int rows, int sm_count) {
 bool make_plan(int mm, int rows, int k, int sm_count, Plan* pl, int force_r = 0, bool q4 = false) {
     const int k_pad = packed_k(k);
     const int nck = k_pad / kChunk;
-    const int max_warps = mm == 1 ? 12 : 16;
+    const int max_warps = mm == 1 ? 12 : (force_r == 2 || pick_rows_per_thread(mm, rows, sm_count) == 2 ? 12 : 16);
     pl->mm = mm;
     pl->r = force_r ? force_r : pick_rows_per_thread(mm, rows, sm_count);
     const int unit_rows = 4 * pl->r;
@@ -605,13 +614,13 @@ template <bool Q4>
 cudaError_t launch_mm_any(int mm, const GemvParams& p, const Plan& pl, cudaStream_t stream, bool pdl) {
     switch (mm) {
         case 1: return pl.r == 2 ? launch_mm<1, 2, Q4>(p, pl, stream, pdl) : launch_mm<1, 1, Q4>(p, pl, stream, pdl);
-        case 2: return launch_mm<2, 1, Q4>(p, pl, stream, pdl);
-        case 3: return launch_mm<3, 1, Q4>(p, pl, stream, pdl);
-        case 4: return launch_mm<4, 1, Q4>(p, pl, stream, pdl);
-        case 5: return launch_mm<5, 1, Q4>(p, pl, stream, pdl);
-        case 6: return launch_mm<6, 1, Q4>(p, pl, stream, pdl);
-        case 7: return launch_mm<7, 1, Q4>(p, pl, stream, pdl);
-        case 8: return launch_mm<8, 1, Q4>(p, pl, stream, pdl);
+        case 2: return pl.r == 2 ? launch_mm<2, 2, Q4>(p, pl, stream, pdl) : launch_mm<2, 1, Q4>(p, pl, stream, pdl);
+        case 3: return pl.r == 2 ? launch_mm<3, 2, Q4>(p, pl, stream, pdl) : launch_mm<3, 1, Q4>(p, pl, stream, pdl);
+        case 4: return pl.r == 2 ? launch_mm<4, 2, Q4>(p, pl, stream, pdl) : launch_mm<4, 1, Q4>(p, pl, stream, pdl);
+        case 5: return pl.r == 2 ? launch_mm<5, 2, Q4>(p, pl, stream, pdl) : launch_mm<5, 1, Q4>(p, pl, stream, pdl);
+        case 6: return pl.r == 2 ? launch_mm<6, 2, Q4>(p, pl, stream, pdl) : launch_mm<6, 1, Q4>(p, pl, stream, pdl);
+        case 7: return pl.r == 2 ? launch_mm<7, 2, Q4>(p, pl, stream, pdl) : launch_mm<7, 1, Q4>(p, pl, stream, pdl);
+        case 8: return pl.r == 2 ? launch_mm<8, 2, Q4>(p, pl, stream, pdl) : launch_mm<8, 1, Q4>(p, pl, stream, pdl);
         default: return cudaErrorInvalidValue;
     }
 }
