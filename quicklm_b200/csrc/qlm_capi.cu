@@ -72,6 +72,8 @@ struct DeviceState {
     int* ea = nullptr;       // tensor-core path: activation row exponents
     size_t ea_cap = 0;
     int* status = nullptr;   // device status word written by kernels on a timeout
+    void* xpair = nullptr;   // exact small-M product: activations in its pair layout
+    size_t xpair_cap = 0;
 };
 DeviceState g_dev[kMaxDevices];
 std::mutex g_dev_mu;
@@ -106,6 +108,18 @@ int ensure_buf(T** buf, size_t* cap, size_t bytes) {
     *cap = bytes;
     return QLM_OK;
 }
+
+// The exact product for 9..64 activation rows per launch streams W once
+// (qlm_gemm_exact.cu); QLM_GEMM_EXACT=0 runs such M as launches of up to 8
+// rows instead (for comparisons).
+bool exact_gemm_enabled() {
+    static const bool on = [] {
+        const char* e = std::getenv("QLM_GEMM_EXACT");
+        return !(e && e[0] == '0');
+    }();
+    return on;
+}
+constexpr int kExactGemmMin = 9;  // from this M on, one launch per 64 rows
 
 bool pdl_enabled() {
     static const bool on = [] {
@@ -477,6 +491,24 @@ int qlm_linear_int8(const float* x, int M, int k, int64_t ldx, const qlm_w8* w, 
         QLM_CUDA(qlm::launch_gemm_tc(*w->maps, w->ew, w->rows, k, dx, dldx, M, st->x16, st->ea, dy, dldy, st->status,
                                      s, pdl_enabled()),
                  "tensor-core GEMM launch");
+    } else if (M >= kExactGemmMin && exact_gemm_enabled()) {
+        {
+            std::lock_guard<std::mutex> lk(g_dev_mu);
+            if ((rc = ensure_buf(&st->xpair, &st->xpair_cap, qlm::gemm_exact_scratch_bytes(64, k)))) return rc;
+        }
+        for (int m0 = 0; m0 < M; m0 += 64) {
+            const int g_rows = (M - m0) < 64 ? (M - m0) : 64;
+            if (g_rows >= 2) {
+                QLM_CUDA(qlm::launch_gemm_exact(dx + (int64_t)m0 * dldx, dldx, g_rows, w->q, w->s, w->rows, k, q4,
+                                                dy + (int64_t)m0 * dldy, dldy, st->xpair, s),
+                         "exact small-M launch");
+            } else {
+                QLM_CUDA(qlm::launch_gemv_exact(dx + (int64_t)m0 * dldx, dldx, 1, w->q, w->s, w->gmaps, w->rows, k,
+                                                dy + (int64_t)m0 * dldy, dldy, st->status, st->sm_count, s,
+                                                pdl_enabled(), nullptr, q4),
+                         "gemv launch");
+            }
+        }
     } else {
         for (int m0 = 0; m0 < M; m0 += mm) {
             const int g_rows = (M - m0) < mm ? (M - m0) : mm;
@@ -528,6 +560,33 @@ int qlm_linear_int8_grouped(const float* x, int M, int k, int64_t ldx, const qlm
     while (mm > 1 && !qlm::gemv_supported(mm, rows_total, k, st->sm_count, q4)) --mm;
     if (!qlm::gemv_supported(mm, rows_total, k, st->sm_count, q4))
         return set_err(QLM_ERR_UNSUPPORTED, "k=%d exceeds the exact path's shared-memory staging limit", k);
+    if (M >= kExactGemmMin && exact_gemm_enabled()) {
+        // one exact small-M launch per weight and 64 activation rows
+        {
+            std::lock_guard<std::mutex> lk(g_dev_mu);
+            if ((rc = ensure_buf(&st->xpair, &st->xpair_cap, qlm::gemm_exact_scratch_bytes(64, k)))) return rc;
+        }
+        for (int m0 = 0; m0 < M; m0 += 64) {
+            const int g_rows = (M - m0) < 64 ? (M - m0) : 64;
+            for (int g = 0; g < nw; ++g) {
+                if (g_rows >= 2) {
+                    QLM_CUDA(qlm::launch_gemm_exact(x + (int64_t)m0 * ldx, ldx, g_rows, gw[g].q, gw[g].s, gw[g].rows,
+                                                    k, q4, gw[g].y + (int64_t)m0 * gw[g].ldy, gw[g].ldy, st->xpair, s),
+                             "exact small-M launch");
+                } else {
+                    QLM_CUDA(qlm::launch_gemv_exact(x + (int64_t)m0 * ldx, ldx, 1, gw[g].q, gw[g].s, *gw[g].maps,
+                                                    gw[g].rows, k, gw[g].y + (int64_t)m0 * gw[g].ldy, gw[g].ldy,
+                                                    st->status, st->sm_count, s, pdl_enabled(), nullptr, q4),
+                             "gemv launch");
+                }
+            }
+        }
+        if (flags & QLM_LINEAR_SYNC) {
+            QLM_CUDA(cudaStreamSynchronize(s), "stream synchronize");
+            return qlm_device_status(ws[0]->device, 1);
+        }
+        return QLM_OK;
+    }
     for (int m0 = 0; m0 < M; m0 += mm) {
         const int rows_m = (M - m0) < mm ? (M - m0) : mm;
         qlm::GemvWeight gm[qlm::kMaxGroup];

@@ -131,6 +131,15 @@ cudaError_t launch_rms_norm_strided(const float* x, const float* w, float* y, in
 cudaError_t launch_gdn_gates(const float* a_raw, const float* b_raw, const float* A_log, const float* dt_bias,
                              float* decay, float* beta, int heads, int per, cudaStream_t stream);
 
+// Bit-exact y[m][0:rows] = x[m][0:k] . W^T for 2 <= M <= 64 activation rows
+// in one launch that streams W once (qlm_gemm_exact.cu): a pre-pass writes the
+// activations into `scratch` (gemm_exact_scratch_bytes) in the kernel's pair
+// layout. Outputs bit-identical to the GEMV for every m.
+bool gemm_exact_supported(int M, int k);
+size_t gemm_exact_scratch_bytes(int M, int k);
+cudaError_t launch_gemm_exact(const float* x, int64_t ldx, int M, const uint8_t* q, const float* s, int rows, int k,
+                              bool q4, float* y, int64_t ldy, void* scratch, cudaStream_t stream);
+
 // ---- tensor-core prefill GEMM (qlm_gemm_tc.cu) ----
 struct TcMaps {
     alignas(64) CUtensorMap w;  // packed int8 rows, 128 x 128-byte boxes
