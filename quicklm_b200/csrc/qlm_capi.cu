@@ -120,6 +120,11 @@ bool exact_gemm_enabled() {
     return on;
 }
 constexpr int kExactGemmMin = 9;  // from this M on, one launch per 64 rows
+// ... for matrices up to this many rows: each 32-row CTA of that kernel reads
+// all activation rows, which outweighs the single weight stream for a
+// vocabulary head (lm_head [151936, 2560] at M = 64: 2.35 ms vs 2.11 ms as
+// launches of 8 rows; [2560, 9728]: 0.27 vs 1.29 ms).
+constexpr int kExactGemmMaxRows = 65536;
 
 bool pdl_enabled() {
     static const bool on = [] {
@@ -491,7 +496,7 @@ int qlm_linear_int8(const float* x, int M, int k, int64_t ldx, const qlm_w8* w, 
         QLM_CUDA(qlm::launch_gemm_tc(*w->maps, w->ew, w->rows, k, dx, dldx, M, st->x16, st->ea, dy, dldy, st->status,
                                      s, pdl_enabled()),
                  "tensor-core GEMM launch");
-    } else if (M >= kExactGemmMin && exact_gemm_enabled()) {
+    } else if (M >= kExactGemmMin && exact_gemm_enabled() && w->rows <= kExactGemmMaxRows) {
         {
             std::lock_guard<std::mutex> lk(g_dev_mu);
             if ((rc = ensure_buf(&st->xpair, &st->xpair_cap, qlm::gemm_exact_scratch_bytes(64, k)))) return rc;
