@@ -367,6 +367,37 @@ int qlm_device_status(int device, int reset);
 /* Block until all work queued on `stream` is done (reports async errors). */
 int qlm_stream_sync(void* stream);
 
+/* ---- Per-matmul timing (replaces QUICKLM_PROF's matmul accumulator) -------
+ * Replaces math::get_matmul_ms / reset_matmul_ms (src/ops/math_ops.hpp:85-87;
+ * accumulation at src/ops/math_ops.cpp:151-159, 821-823, 896-899; the total is
+ * printed by src/main.cpp:706-709). On when QUICKLM_PROF or QLM_PROF is set in
+ * the environment, or after qlm_prof_enable(1). While on, qlm_linear_int8,
+ * qlm_linear_int8_grouped and qlm_linear_int8_allgather record two CUDA events
+ * on their stream around their work (host copies included for
+ * QLM_LINEAR_HOST_IO), so the figure is device time and adds no
+ * synchronisation; calls issued while their stream is being captured into a
+ * CUDA graph are not timed. qlm_linear_int8_tc_noalloc is never timed (event
+ * pools allocate). Every linear entry point, qlm_model_decode and
+ * qlm_model_decode_batch also open an NVTX range named after the entry point,
+ * whether or not timing is on.
+ *
+ * qlm_prof_enable: on = 1 / 0 switches timing on / off, -1 only asks; returns
+ * the state before the call (1 on, 0 off). */
+int qlm_prof_enable(int on);
+
+/* Cumulative device milliseconds and number of timed calls since the last
+ * reset (waits for the calls still in flight). Either pointer may be NULL. */
+int qlm_prof_matmul_ms(double* ms, int64_t* calls);
+
+/* Zero the totals (waits for calls still in flight). */
+int qlm_prof_reset(void);
+
+/* Per-(entry point, M, N, K) totals as text, one line each, largest total
+ * first: "<entry>\t<M>\t<N>\t<K>\t<calls>\t<ms>\n". Writes at most cap bytes
+ * (always NUL-terminated when cap > 0) and sets *needed to the full size
+ * including the NUL. */
+int qlm_prof_report(char* buf, int64_t cap, int64_t* needed);
+
 #ifdef __cplusplus
 }
 #endif

@@ -9,9 +9,13 @@
 //
 //   decode_main MODEL_DIR PROMPT_IDS_FILE N_NEW THREADS [PRECISION]
 //
-// PROMPT_IDS_FILE: whitespace-separated token ids.
+// PROMPT_IDS_FILE: whitespace-separated token ids. With QUICKLM_PROF set, the
+// cumulative matmul time is printed to stderr as the reference CLI does.
 #include "math_ops.hpp"
 #include "model.hpp"
+#ifdef QLM_DROPIN
+#include "qlm_b200.h"
+#endif
 
 #include <chrono>
 #include <cstdio>
@@ -88,6 +92,17 @@ int main(int argc, char** argv) {
         std::printf("], \"prompt_len\": %zu, \"load_s\": %.3f, \"prefill_s\": %.4f, \"decode_s\": %.4f, "
                     "\"decode_tok_s\": %.3f, \"threads\": %d}\n",
                     prompt.size(), load_s, prefill_s, decode_s, n_new / decode_s, threads);
+        if (std::getenv("QUICKLM_PROF")) {  // as src/main.cpp:706-709
+            std::fprintf(stderr, "[prof] cumulative matmul: %g ms\n", math::get_matmul_ms());
+#ifdef QLM_DROPIN
+            // The line above counts the matmuls left on the CPU; the int8 ones ran on the device.
+            double ms = 0.0;
+            int64_t calls = 0;
+            if (qlm_prof_matmul_ms(&ms, &calls) == QLM_OK)
+                std::fprintf(stderr, "[prof] cumulative int8 matmul (device): %g ms over %lld calls\n", ms,
+                             (long long)calls);
+#endif
+        }
         return 0;
     } catch (const std::exception& e) {
         std::fprintf(stderr, "error: %s\n", e.what());

@@ -77,6 +77,12 @@ int main(int argc, char** argv) {
     std::printf("], \"prompt_len\": %zu, \"load_s\": %.3f, \"prefill_s\": %.4f, \"decode_s\": %.4f, "
                 "\"decode_tok_s\": %.3f, \"threads\": 0}\n",
                 prompt.size(), load_s, prefill_s, decode_s, n_new / decode_s);
+    if (std::getenv("QUICKLM_PROF")) {  // as src/main.cpp:706-709, device time of the linear calls
+        double ms = 0.0;
+        int64_t calls = 0;
+        if (qlm_prof_matmul_ms(&ms, &calls) == QLM_OK)
+            std::fprintf(stderr, "[prof] cumulative matmul (device): %g ms over %lld calls\n", ms, (long long)calls);
+    }
     qlm_model_free(m);
     return 0;
 }

@@ -45,6 +45,7 @@ ABI_SYMBOLS = (
     "qlm_conv1d_update_tapmajor", "qlm_l2norm_heads", "qlm_gdn_gates", "qlm_gdn_recurrence", "qlm_rms_norm_gain",
     "qlm_gqa_attend", "qlm_comm_set_timeout_us", "qlm_comm_status", "qlm_model_load", "qlm_model_reset",
     "qlm_model_decode", "qlm_model_info", "qlm_model_free", "qlm_model_load_batch", "qlm_model_decode_batch", "qlm_model_stream",
+    "qlm_prof_enable", "qlm_prof_matmul_ms", "qlm_prof_reset", "qlm_prof_report",
 )
 
 _STATUS = {0: "OK", 1: "INVALID_ARG", 2: "CUDA", 3: "OUT_OF_MEMORY", 4: "UNSUPPORTED", 5: "TIMEOUT", 6: "NCCL",
@@ -126,6 +127,9 @@ def load(path: str = LIB_PATH):
     lib.qlm_linear_int8_allgather.argtypes = [P, I, I, L, P, P, P, L, I, P]
     lib.qlm_argmax_f32.argtypes = [P, I, L, P, P, P, I, P]
     lib.qlm_linear_int8_grouped.argtypes = [P, I, I, L, P, I, P, P, I, P]
+    lib.qlm_prof_enable.argtypes = [I]
+    lib.qlm_prof_matmul_ms.argtypes = [ctypes.POINTER(ctypes.c_double), ctypes.POINTER(L)]
+    lib.qlm_prof_report.argtypes = [ctypes.c_char_p, L, ctypes.POINTER(L)]
     if lib.qlm_abi_version() != 1:
         raise QlmError(7, "ABI version mismatch")
     _lib = lib
@@ -355,6 +359,40 @@ def matmul(A, B: Int8Weight, C=None, transpose_B: bool = True, flags: int = EXAC
     _check(lib.qlm_linear_int8(a2.ctypes.data, M, K, a2.strides[0] // 4, B.handle, c2.ctypes.data,
                                c2.strides[0] // 4, flags | HOST_IO, _stream_ptr(stream)))
     return C
+
+
+def prof_enable(on: bool | None = None) -> bool:
+    """Switch per-matmul device timing on or off (None: only ask); returns the
+    state before the call. The counterpart of QuickLM's QUICKLM_PROF switch
+    (src/ops/math_ops.cpp:821-823), which also turns it on here."""
+    return bool(load().qlm_prof_enable(-1 if on is None else int(bool(on))))
+
+
+def prof_matmul_ms() -> tuple[float, int]:
+    """(cumulative device ms, timed calls) of the linear entry points since the
+    last reset — math::get_matmul_ms (src/ops/math_ops.hpp:85-87)."""
+    ms, n = ctypes.c_double(), ctypes.c_int64()
+    _check(load().qlm_prof_matmul_ms(ctypes.byref(ms), ctypes.byref(n)))
+    return ms.value, n.value
+
+
+def prof_reset() -> None:
+    """Zero the totals — math::reset_matmul_ms (src/ops/math_ops.hpp:87)."""
+    _check(load().qlm_prof_reset())
+
+
+def prof_report() -> list[dict]:
+    """Per-(entry point, M, N, K) totals, largest total first."""
+    lib = load()
+    need = ctypes.c_int64()
+    _check(lib.qlm_prof_report(None, 0, ctypes.byref(need)))
+    buf = ctypes.create_string_buffer(int(need.value) + 256)
+    _check(lib.qlm_prof_report(buf, len(buf), ctypes.byref(need)))
+    rows = []
+    for line in buf.value.decode().splitlines():
+        kind, m, n, k, calls, ms = line.split("\t")
+        rows.append({"entry": kind, "M": int(m), "N": int(n), "K": int(k), "calls": int(calls), "ms": float(ms)})
+    return rows
 
 
 def shard_rows(n: int, nranks: int, rank: int):

@@ -9,6 +9,7 @@
 #include "qlm_device.cuh"
 #include "qlm_handle.h"
 #include "qlm_kernels.h"
+#include "qlm_prof.h"
 
 #include <cstdarg>
 #include <cstdio>
@@ -453,6 +454,7 @@ int qlm_linear_int8(const float* x, int M, int k, int64_t ldx, const qlm_w8* w, 
     DeviceGuard g(w->device);
     if (!g.ok) return set_err(QLM_ERR_CUDA, "cudaSetDevice(%d) failed", w->device);
     cudaStream_t s = static_cast<cudaStream_t>(stream);
+    qlm_internal::ProfScope prof("qlm_linear_int8", M, w->rows, k, s);
 
     // Exact path: rows of x per launch (all activations of a launch live in
     // shared memory next to the weight slots).
@@ -528,6 +530,7 @@ int qlm_linear_int8(const float* x, int M, int k, int64_t ldx, const qlm_w8* w, 
                                    (size_t)w->rows * sizeof(float), M, cudaMemcpyDeviceToHost, s),
                  "copy y to host");
     }
+    prof.stop();
     if (host_io || (flags & QLM_LINEAR_SYNC)) {
         QLM_CUDA(cudaStreamSynchronize(s), "stream synchronize");
         if (tensor || (flags & QLM_LINEAR_SYNC)) return qlm_device_status(w->device, 1);
@@ -560,6 +563,7 @@ int qlm_linear_int8_grouped(const float* x, int M, int k, int64_t ldx, const qlm
     DeviceGuard g(ws[0]->device);
     if (!g.ok) return set_err(QLM_ERR_CUDA, "cudaSetDevice(%d) failed", ws[0]->device);
     cudaStream_t s = static_cast<cudaStream_t>(stream);
+    qlm_internal::ProfScope prof("qlm_linear_int8_grouped", M, rows_total, k, s);
     int mm = 8;
     const bool q4 = ws[0]->bits == 4;
     while (mm > 1 && !qlm::gemv_supported(mm, rows_total, k, st->sm_count, q4)) --mm;
@@ -586,6 +590,7 @@ int qlm_linear_int8_grouped(const float* x, int M, int k, int64_t ldx, const qlm
                 }
             }
         }
+        prof.stop();
         if (flags & QLM_LINEAR_SYNC) {
             QLM_CUDA(cudaStreamSynchronize(s), "stream synchronize");
             return qlm_device_status(ws[0]->device, 1);
@@ -603,6 +608,7 @@ int qlm_linear_int8_grouped(const float* x, int M, int k, int64_t ldx, const qlm
                                           pdl_enabled(), nullptr, q4),
                  "grouped gemv launch");
     }
+    prof.stop();
     if (flags & QLM_LINEAR_SYNC) {
         QLM_CUDA(cudaStreamSynchronize(s), "stream synchronize");
         return qlm_device_status(ws[0]->device, 1);

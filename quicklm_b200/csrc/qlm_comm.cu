@@ -21,6 +21,7 @@
 #include "qlm_device.cuh"
 #include "qlm_handle.h"
 #include "qlm_kernels.h"
+#include "qlm_prof.h"
 
 #include <cstdarg>
 #include <cstdio>
@@ -181,6 +182,7 @@ int qlm_linear_int8_allgather(const float* x, int M, int k, int64_t ldx, const q
     Dev g(c->device);
     if (!g.ok) return fail(QLM_ERR_CUDA, "cudaSetDevice(%d) failed", c->device);
     cudaStream_t s = static_cast<cudaStream_t>(stream);
+    qlm_internal::ProfScope prof("qlm_linear_int8_allgather", M, w->n_total, k, s);
 
     qlm::GatherArgs ga{};
     ga.wait_ns = c->wait_ns;
@@ -197,6 +199,7 @@ int qlm_linear_int8_allgather(const float* x, int M, int k, int64_t ldx, const q
     cudaError_t e = qlm::launch_gemv_exact(x, ldx, 1, w->q, w->s, w->gmaps, w->rows, k, y, ldy, c->state + 2,
                                            c->sm_count, s, true, &ga, w->bits == 4);
     if (e != cudaSuccess) return cuda_fail(e, "fused GEMV + all-gather launch");
+    prof.stop();
     if (flags & QLM_LINEAR_SYNC) {
         e = cudaStreamSynchronize(s);
         if (e != cudaSuccess) return cuda_fail(e, "stream synchronize");

@@ -48,9 +48,6 @@ struct MtParams {
     float zero_neg;    // -0.0f: the product addend (see qlm_gemv.cu)
 };
 
-__device__ __forceinline__ void cp_async4(uint32_t dst, const void* src, bool valid) {
-    asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(dst), "l"(src), "r"(valid ? 4 : 0) : "memory");
-}
 __device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, bool valid) {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(valid ? 16 : 0) : "memory");
 }

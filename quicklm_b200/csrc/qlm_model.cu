@@ -45,6 +45,7 @@
 #include "qlm_device.cuh"
 #include "qlm_handle.h"
 #include "qlm_kernels.h"
+#include "qlm_prof.h"
 #include "qlm_safetensors.h"
 
 namespace qlm_internal {
@@ -771,11 +772,13 @@ int qlm_model_info(const qlm_model* m, int* vocab, int* hidden, int* layers, int
 int qlm_model_decode(qlm_model* m, int token, int pos, int* next_token, float* logits) {
     if (!m || !next_token) return fail(QLM_ERR_INVALID_ARG, "NULL argument");
     if (m->batch != 1) return fail(QLM_ERR_INVALID_ARG, "the model decodes %d sequences: use qlm_model_decode_batch", m->batch);
+    qlm_internal::NvtxRange range("qlm_model_decode");
     return decode_step(m, &token, pos, next_token, logits);
 }
 
 int qlm_model_decode_batch(qlm_model* m, const int* tokens, int pos, int* next_tokens, float* logits) {
     if (!m || !tokens || !next_tokens) return fail(QLM_ERR_INVALID_ARG, "NULL argument");
+    qlm_internal::NvtxRange range("qlm_model_decode_batch");
     return decode_step(m, tokens, pos, next_tokens, logits);
 }
 

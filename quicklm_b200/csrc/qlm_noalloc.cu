@@ -22,6 +22,7 @@
 #include "qlm_device.cuh"
 #include "qlm_handle.h"
 #include "qlm_kernels.h"
+#include "qlm_prof.h"
 
 #include <atomic>
 #include <cstdarg>
@@ -93,6 +94,7 @@ cudaError_t noalloc_status(int device, int reset, int* code) {
 
 extern "C" int qlm_linear_int8_tc_noalloc(const float* x, int M, int k, int64_t ldx, const qlm_w8* w, float* y,
                                           int64_t ldy, int flags, void* stream) {
+    qlm_internal::NvtxRange range("qlm_linear_int8_tc_noalloc");
     int rc = QLM_OK;
     do {
         if (!x || !y || !w) {
