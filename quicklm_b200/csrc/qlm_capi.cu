@@ -507,7 +507,7 @@ int qlm_linear_int8(const float* x, int M, int k, int64_t ldx, const qlm_w8* w, 
             const int g_rows = (M - m0) < 64 ? (M - m0) : 64;
             if (g_rows >= 2) {
                 QLM_CUDA(qlm::launch_gemm_exact(dx + (int64_t)m0 * dldx, dldx, g_rows, w->q, w->s, w->rows, k, q4,
-                                                dy + (int64_t)m0 * dldy, dldy, st->xpair, s),
+                                                dy + (int64_t)m0 * dldy, dldy, st->xpair, st->sm_count, s),
                          "exact small-M launch");
             } else {
                 QLM_CUDA(qlm::launch_gemv_exact(dx + (int64_t)m0 * dldx, dldx, 1, w->q, w->s, w->gmaps, w->rows, k,
@@ -580,7 +580,7 @@ int qlm_linear_int8_grouped(const float* x, int M, int k, int64_t ldx, const qlm
             for (int g = 0; g < nw; ++g) {
                 if (g_rows >= 2) {
                     QLM_CUDA(qlm::launch_gemm_exact(x + (int64_t)m0 * ldx, ldx, g_rows, gw[g].q, gw[g].s, gw[g].rows,
-                                                    k, q4, gw[g].y + (int64_t)m0 * gw[g].ldy, gw[g].ldy, st->xpair, s),
+                                                    k, q4, gw[g].y + (int64_t)m0 * gw[g].ldy, gw[g].ldy, st->xpair, st->sm_count, s),
                              "exact small-M launch");
                 } else {
                     QLM_CUDA(qlm::launch_gemv_exact(x + (int64_t)m0 * ldx, ldx, 1, gw[g].q, gw[g].s, *gw[g].maps,

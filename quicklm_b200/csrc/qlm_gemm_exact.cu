@@ -19,20 +19,24 @@
 // 128-bit load gives two ready pairs and the 8 lanes of a quarter warp read
 // 128 consecutive bytes. That layout is written once per call by a small
 // pre-pass (xpair_kernel) into scratch, so each CTA fills a stage with plain
-// 16-byte copies. A warp is 8 lanes x 4 activation-row sets (32 activation
-// rows) of 4 weight rows; a CTA holds 32 weight rows and all M activation
-// rows. Codes, scales and activations of a chunk arrive by cp.async in a
-// 3-stage ring, so chunk c+2 is in flight while chunk c computes.
+// 16-byte copies. M is staged in buckets of 16, 32 or 64 rows (MS = 2, 4, 8
+// sets of 8); a CTA's 64 groups of 8 lanes cover the MS sets of 256 / MS x 4
+// weight rows per pass. The grid is one CTA per SM, each owning a balanced
+// contiguous range of weight rows that it works in passes, so no SM idles
+// while another runs a last wave. Codes, scales and activations of an item
+// (pass, chunk) arrive by cp.async in a 3-stage ring that runs across passes,
+// so item i+2 is in flight while item i computes.
 #include "qlm_device.cuh"
 #include "qlm_kernels.h"
+
+#include <algorithm>
 
 namespace qlm {
 namespace {
 
 constexpr int kMtStages = 3;
-constexpr int kMtRows = 32;     // weight rows per CTA
 constexpr int kMtMaxM = 64;     // activation rows per launch
-constexpr int kMtThreads = 512; // 8 row groups x 2 halves of 32 activation rows
+constexpr int kMtThreads = 512; // 64 groups of the 8 reference lanes
 
 struct MtParams {
     const float* x;
@@ -43,7 +47,8 @@ struct MtParams {
     float* y;
     int64_t ldy;
     int rows, k, nb_pad, nck, row_bytes;
-    int m_alloc;       // activation rows staged: 32 or 64
+    int m_alloc;       // activation rows staged: 16, 32 or 64
+    int row_q, row_r;  // rows per CTA: CTA b owns [b*q + min(b, r), +q + (b < r))
     const float* xp;   // the activations in the pair-interleaved chunk layout
     float zero_neg;    // -0.0f: the product addend (see qlm_gemv.cu)
 };
@@ -66,17 +71,24 @@ __device__ __forceinline__ uint32_t lds_u32(uint32_t a) {
     return v;
 }
 
-// Stage layout (bytes): activations [M/2 pairs][4 blocks][2 halves][8 lanes]
-// float4 (32 KB at M = 64), then codes [kMtRows][128 or 64], then scales
-// [kMtRows][4]. The scratch holds the same activation layout per chunk.
-template <bool Q4>
+// Rows of W per pass: each group of 8 threads (the reference lanes) runs 4
+// weight rows x 8 activation rows, and the 64 groups of a CTA cover all
+// MS x 8 staged activation rows: 32 rows per pass at MS = 8 (M <= 64), 64 at
+// MS = 4 (M <= 32), 128 at MS = 2 (M <= 16).
+template <int MS>
+__host__ __device__ constexpr int pass_rows() { return 4 * (kMtThreads / 8) / MS; }
+
+// Stage layout (bytes): activations [MS*4 pairs][4 blocks][2 halves][8 lanes]
+// float4 (MS * 4 KB), then codes [pass rows][128 or 64], then scales
+// [pass rows][4]. The scratch holds the same activation layout per chunk.
+template <int MS, bool Q4>
 struct MtStage {
-    static constexpr int kX = kMtMaxM / 2 * 4 * 2 * 8 * 16;
-    static constexpr int kCodes = kMtRows * (Q4 ? 64 : 128);
-    static constexpr int kScales = kMtRows * 16;
+    static constexpr int kX = MS * 8 * kChunk * 4;
+    static constexpr int kRows = pass_rows<MS>();
+    static constexpr int kCodes = kRows * (Q4 ? 64 : 128);
+    static constexpr int kScales = kRows * 16;
     static constexpr int kBytes = kX + kCodes + kScales;
 };
-
 
 // xp[c][mp][b][h][l] = float4(x[2mp][k], x[2mp+1][k], x[2mp][k+8], x[2mp+1][k+8])
 // with k = c*128 + 32b + 16h + l: the activation pairs of lane l, block b,
@@ -96,48 +108,58 @@ __global__ void xpair_kernel(const float* __restrict__ x, int64_t ldx, int M, in
     }
 }
 
-template <bool Q4>
+template <int MS, bool Q4>
 __global__ void __launch_bounds__(kMtThreads, 1) gemm_exact_kernel(const __grid_constant__ MtParams p) {
     extern __shared__ __align__(128) uint8_t smem[];
     constexpr int CB = Q4 ? 64 : 128;
-    using St = MtStage<Q4>;
-    const int tid = threadIdx.x, warp = tid >> 5, lane32 = tid & 31;
-    const int l = lane32 & 7, ms = lane32 >> 3;
-    const int rg = warp & 7, mh = warp >> 3;
-    const int mbase = mh * 32 + ms * 8;  // this thread's 8 activation rows
-    const int row0 = blockIdx.x * kMtRows;
-    const int xbytes = p.m_alloc * kChunk * 4;  // activation bytes per chunk
+    constexpr int PR = pass_rows<MS>();
+    using St = MtStage<MS, Q4>;
+    const int tid = threadIdx.x, l = tid & 7, oct = tid >> 3;
+    const int ms = oct % MS, rq = oct / MS;  // activation set, row quad of the pass
+    const int mbase = ms * 8;                // this thread's 8 activation rows
     const uint32_t sbase = __cvta_generic_to_shared(smem);
+    // Balanced contiguous row range of this CTA, worked in passes of PR rows;
+    // groups whose 4 rows lie past the range skip the arithmetic, so a short
+    // last pass costs little more than its activation copies.
+    const int b = (int)blockIdx.x;
+    const int r_begin = b * p.row_q + min(b, p.row_r);
+    const int r_end = r_begin + p.row_q + (b < p.row_r ? 1 : 0);
+    const int npass = (r_end - r_begin + PR - 1) / PR;
 
-    // Fill stage st with chunk c: activations (contiguous in the scratch), the
-    // 32 rows' code bytes and scales of the chunk. Zero past the weight's rows.
-    auto issue = [&](int c, int st) {
+    const int nbf = p.k / kBlock;  // full blocks
+    const int cfull = nbf / 4;
+    const int rem_blocks = nbf - cfull * 4;
+    // Chunks holding full blocks; one (empty) item per pass when K < 32, so
+    // the pass still ends in the ragged tail and the stores.
+    const int nchunks = max(1, cfull + (rem_blocks ? 1 : 0));
+    const int items = npass * nchunks;  // (pass, chunk), chunk fastest
+
+    // Fill stage st with item it: the chunk's activations (contiguous in the
+    // scratch), the pass rows' code bytes and scales. Zero past the range.
+    auto issue = [&](int it, int st) {
+        const int pass = it / nchunks, c = it - pass * nchunks;
+        const int row0 = r_begin + pass * PR;
         const uint32_t dst = sbase + st * St::kBytes;
-        const uint8_t* xs = reinterpret_cast<const uint8_t*>(p.xp) + (int64_t)c * xbytes;
-        for (int o = tid * 16; o < xbytes; o += blockDim.x * 16) cp_async16(dst + o, xs + o, true);
-        const int nq = kMtRows * (CB / 16);  // 16-byte pieces of codes
-        for (int i = tid; i < nq + kMtRows; i += blockDim.x) {
+        const uint8_t* xs = reinterpret_cast<const uint8_t*>(p.xp) + (int64_t)c * St::kX;
+        for (int o = tid * 16; o < St::kX; o += kMtThreads * 16) cp_async16(dst + o, xs + o, true);
+        constexpr int nq = PR * (CB / 16);  // 16-byte pieces of codes
+        for (int i = tid; i < nq + PR; i += kMtThreads) {
             if (i < nq) {
                 const int r = i / (CB / 16), piece = i % (CB / 16);
-                const bool ok = row0 + r < p.rows;
+                const bool ok = row0 + r < r_end;
                 cp_async16(dst + St::kX + r * CB + piece * 16,
                            ok ? p.q + (int64_t)(row0 + r) * p.row_bytes + (int64_t)c * CB + piece * 16 : p.q, ok);
             } else {
                 const int r = i - nq;
-                const bool ok = row0 + r < p.rows;
+                const bool ok = row0 + r < r_end;
                 cp_async16(dst + St::kX + St::kCodes + r * 16, ok ? p.s + (int64_t)(row0 + r) * p.nb_pad + c * 4 : p.s,
                            ok);
             }
         }
     };
 
-    const int nbf = p.k / kBlock;  // full blocks
-    const int cfull = nbf / 4;
-    const int rem_blocks = nbf - cfull * 4;
-    const int nchunks = cfull + (rem_blocks ? 1 : 0);  // chunks holding full blocks
-
     for (int i = 0; i < kMtStages - 1; ++i) {
-        if (i < nchunks) issue(i, i);
+        if (i < items) issue(i, i);
         cp_async_commit();
     }
     const unsigned long long nz = f2pack(p.zero_neg, p.zero_neg);
@@ -148,15 +170,18 @@ __global__ void __launch_bounds__(kMtThreads, 1) gemm_exact_kernel(const __grid_
 #pragma unroll
         for (int i = 0; i < 4; ++i) t[r][i] = 0ull;  // (+0, +0)
 
-    for (int c = 0; c < nchunks; ++c) {
-        const int nxt = c + kMtStages - 1;
-        if (nxt < nchunks) issue(nxt, nxt % kMtStages);
+    int c = 0, pass = 0;
+    for (int it = 0; it < items; ++it) {
+        const int nxt = it + kMtStages - 1;
+        if (nxt < items) issue(nxt, nxt % kMtStages);
         cp_async_commit();
         cp_async_wait<kMtStages - 1>();
         __syncthreads();
-        const uint32_t sb = sbase + (c % kMtStages) * St::kBytes;
+        const uint32_t sb = sbase + (it % kMtStages) * St::kBytes;
         const int nblk = c < cfull ? 4 : rem_blocks;
-        if (mbase < p.m_alloc) {
+        const int row0 = r_begin + pass * PR;
+        const bool active = row0 + 4 * rq < r_end && mbase < p.M;
+        if (active) {
             for (int bb = 0; bb < nblk; ++bb) {
                 unsigned long long xq[4][4];  // [pair][step]
 #pragma unroll
@@ -171,7 +196,7 @@ __global__ void __launch_bounds__(kMtThreads, 1) gemm_exact_kernel(const __grid_
                 }
 #pragma unroll
                 for (int r = 0; r < 4; ++r) {
-                    const int rr = rg * 4 + r;
+                    const int rr = rq * 4 + r;
                     uint32_t w;
                     if (Q4) {
                         w = lds_u32(sb + St::kX + rr * 64 + l * 8 + (bb >> 1) * 4);
@@ -198,55 +223,64 @@ __global__ void __launch_bounds__(kMtThreads, 1) gemm_exact_kernel(const __grid_
                 }
             }
         }
-        __syncthreads();  // the stage is read: chunk c + kMtStages may refill it
-    }
-    cp_async_wait<0>();
-
-    // 8 -> 1 tree over the lanes of each quarter warp, then the ragged tail.
+        __syncthreads();  // the stage is read: item it + kMtStages may refill it
+        if (++c < nchunks) continue;
+        // Pass done: 8 -> 1 tree over the lanes of each group (every lane of
+        // the warp takes part in the shuffles), then the ragged tail and the
+        // stores of the group's valid rows.
 #pragma unroll
-    for (int r = 0; r < 4; ++r)
-#pragma unroll
-        for (int pi = 0; pi < 4; ++pi) {
-            float a, b2;
-            f2unpack(t[r][pi], a, b2);
-            a = __fadd_rn(a, __shfl_xor_sync(0xffffffffu, a, 4));
-            b2 = __fadd_rn(b2, __shfl_xor_sync(0xffffffffu, b2, 4));
-            a = __fadd_rn(a, __shfl_xor_sync(0xffffffffu, a, 1));
-            b2 = __fadd_rn(b2, __shfl_xor_sync(0xffffffffu, b2, 1));
-            a = __fadd_rn(a, __shfl_xor_sync(0xffffffffu, a, 2));
-            b2 = __fadd_rn(b2, __shfl_xor_sync(0xffffffffu, b2, 2));
-            t[r][pi] = f2pack(a, b2);
-        }
-    if (l == 0 && mbase < p.M) {
-#pragma unroll
-        for (int r = 0; r < 4; ++r) {
-            const int row = row0 + rg * 4 + r;
-            if (row >= p.rows) break;
-            const uint8_t* qr = p.q + (int64_t)row * p.row_bytes;
+        for (int r = 0; r < 4; ++r)
 #pragma unroll
             for (int pi = 0; pi < 4; ++pi) {
-                float v[2];
-                f2unpack(t[r][pi], v[0], v[1]);
+                float a, b2;
+                f2unpack(t[r][pi], a, b2);
+                a = __fadd_rn(a, __shfl_xor_sync(0xffffffffu, a, 4));
+                b2 = __fadd_rn(b2, __shfl_xor_sync(0xffffffffu, b2, 4));
+                a = __fadd_rn(a, __shfl_xor_sync(0xffffffffu, a, 1));
+                b2 = __fadd_rn(b2, __shfl_xor_sync(0xffffffffu, b2, 1));
+                a = __fadd_rn(a, __shfl_xor_sync(0xffffffffu, a, 2));
+                b2 = __fadd_rn(b2, __shfl_xor_sync(0xffffffffu, b2, 2));
+                t[r][pi] = f2pack(a, b2);
+            }
+        if (l == 0 && active) {
 #pragma unroll
-                for (int e = 0; e < 2; ++e) {
-                    const int m = mbase + 2 * pi + e;
-                    if (m >= p.M) continue;
-                    float y = v[e];
-                    if (p.k > nbf * kBlock) {
-                        // ragged tail: sequential scalar sum times the last block's scale
-                        float acc = 0.0f;
-                        for (int kk = nbf * kBlock; kk < p.k; ++kk) {
-                            const float qf = Q4 ? (float)((int)((qr[packed_offset_q4(kk)] >> packed_shift_q4(kk)) & 0xF) - 8)
-                                                : (float)(int8_t)qr[packed_offset(kk)];
-                            acc = __fadd_rn(acc, __fmul_rn(__ldg(p.x + (int64_t)m * p.ldx + kk), qf));
+            for (int r = 0; r < 4; ++r) {
+                const int row = row0 + rq * 4 + r;
+                if (row >= r_end) break;
+                const uint8_t* qr = p.q + (int64_t)row * p.row_bytes;
+#pragma unroll
+                for (int pi = 0; pi < 4; ++pi) {
+                    float v[2];
+                    f2unpack(t[r][pi], v[0], v[1]);
+#pragma unroll
+                    for (int e = 0; e < 2; ++e) {
+                        const int m = mbase + 2 * pi + e;
+                        if (m >= p.M) continue;
+                        float y = v[e];
+                        if (p.k > nbf * kBlock) {
+                            // ragged tail: sequential scalar sum times the last block's scale
+                            float acc = 0.0f;
+                            for (int kk = nbf * kBlock; kk < p.k; ++kk) {
+                                const float qf =
+                                    Q4 ? (float)((int)((qr[packed_offset_q4(kk)] >> packed_shift_q4(kk)) & 0xF) - 8)
+                                       : (float)(int8_t)qr[packed_offset(kk)];
+                                acc = __fadd_rn(acc, __fmul_rn(__ldg(p.x + (int64_t)m * p.ldx + kk), qf));
+                            }
+                            y = __fadd_rn(y, __fmul_rn(acc, p.s[(int64_t)row * p.nb_pad + nbf]));
                         }
-                        y = __fadd_rn(y, __fmul_rn(acc, p.s[(int64_t)row * p.nb_pad + nbf]));
+                        p.y[(int64_t)m * p.ldy + row] = y;
                     }
-                    p.y[(int64_t)m * p.ldy + row] = y;
                 }
             }
         }
+#pragma unroll
+        for (int r = 0; r < 4; ++r)
+#pragma unroll
+            for (int i = 0; i < 4; ++i) t[r][i] = 0ull;
+        c = 0;
+        ++pass;
     }
+    cp_async_wait<0>();
 }
 
 }  // namespace
@@ -254,13 +288,33 @@ __global__ void __launch_bounds__(kMtThreads, 1) gemm_exact_kernel(const __grid_
 bool gemm_exact_supported(int M, int k) { return M >= 2 && M <= kMtMaxM && k >= 1; }
 
 size_t gemm_exact_scratch_bytes(int M, int k) {
-    const int m_alloc = M <= 32 ? 32 : kMtMaxM;
+    const int m_alloc = M <= 16 ? 16 : M <= 32 ? 32 : kMtMaxM;
     return (size_t)(packed_k(k) / kChunk) * m_alloc * kChunk * 4;
 }
 
+namespace {
+template <int MS, bool Q4>
+cudaError_t launch_ms(const MtParams& p, int ctas, cudaStream_t stream) {
+    static bool attr[64] = {};
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+    const size_t smem = (size_t)kMtStages * MtStage<MS, Q4>::kBytes;
+    if (!attr[dev]) {
+        if ((e = cudaFuncSetAttribute(gemm_exact_kernel<MS, Q4>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      (int)smem)) != cudaSuccess)
+            return e;
+        attr[dev] = true;
+    }
+    gemm_exact_kernel<MS, Q4><<<ctas, kMtThreads, smem, stream>>>(p);
+    return cudaGetLastError();
+}
+}  // namespace
+
 cudaError_t launch_gemm_exact(const float* x, int64_t ldx, int M, const uint8_t* q, const float* s, int rows, int k,
-                              bool q4, float* y, int64_t ldy, void* scratch, cudaStream_t stream) {
-    if (!gemm_exact_supported(M, k) || rows < 1) return cudaErrorInvalidValue;
+                              bool q4, float* y, int64_t ldy, void* scratch, int sm_count, cudaStream_t stream) {
+    if (!gemm_exact_supported(M, k) || rows < 1 || sm_count < 1) return cudaErrorInvalidValue;
     MtParams p{};
     p.x = x;
     p.ldx = ldx;
@@ -275,30 +329,23 @@ cudaError_t launch_gemm_exact(const float* x, int64_t ldx, int M, const uint8_t*
     p.nb_pad = k_pad / kBlock;
     p.nck = k_pad / kChunk;
     p.row_bytes = q4 ? k_pad / 2 : k_pad;
-    p.m_alloc = M <= 32 ? 32 : kMtMaxM;
+    p.m_alloc = M <= 16 ? 16 : M <= 32 ? 32 : kMtMaxM;
     p.xp = static_cast<const float*>(scratch);
     p.zero_neg = -0.0f;
+    // One CTA per SM (fewer for matrices of fewer than 4 rows per SM).
+    const int ctas = std::min(sm_count, (rows + 3) / 4);
+    p.row_q = rows / ctas;
+    p.row_r = rows % ctas;
     const int64_t n4 = (int64_t)p.nck * (p.m_alloc / 2) * 64;
     xpair_kernel<<<(int)((n4 + 255) / 256), 256, 0, stream>>>(x, ldx, M, k, p.m_alloc, p.nck,
                                                               static_cast<float4*>(scratch));
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
-    const int stage = q4 ? MtStage<true>::kBytes : MtStage<false>::kBytes;
-    // The stage keeps room for 64 activation rows; a 32-row launch uses the first half.
-    const size_t smem = (size_t)kMtStages * stage;
-    static bool attr[2][64] = {};
-    int dev = 0;
-    if ((e = cudaGetDevice(&dev)) != cudaSuccess) return e;
-    if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
-    auto kern = q4 ? gemm_exact_kernel<true> : gemm_exact_kernel<false>;
-    if (!attr[q4][dev]) {
-        if ((e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)) != cudaSuccess)
-            return e;
-        attr[q4][dev] = true;
+    switch (p.m_alloc) {
+        case 16: return q4 ? launch_ms<2, true>(p, ctas, stream) : launch_ms<2, false>(p, ctas, stream);
+        case 32: return q4 ? launch_ms<4, true>(p, ctas, stream) : launch_ms<4, false>(p, ctas, stream);
+        default: return q4 ? launch_ms<8, true>(p, ctas, stream) : launch_ms<8, false>(p, ctas, stream);
     }
-    const int threads = p.m_alloc == 32 ? kMtThreads / 2 : kMtThreads;
-    kern<<<(rows + kMtRows - 1) / kMtRows, threads, smem, stream>>>(p);
-    return cudaGetLastError();
 }
 
 }  // namespace qlm

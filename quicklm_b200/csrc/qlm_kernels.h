@@ -131,14 +131,32 @@ cudaError_t launch_rms_norm_strided(const float* x, const float* w, float* y, in
 cudaError_t launch_gdn_gates(const float* a_raw, const float* b_raw, const float* A_log, const float* dt_bias,
                              float* decay, float* beta, int heads, int per, cudaStream_t stream);
 
+// Decode-step forms that read the position (and the conv ring position) from
+// device memory, so one captured step replays at every position
+// (qlm_layer.cu). launch_gqa_attend_dev: the three-launch attention with grids
+// and shared memory sized for positions up to max_pos; scratch holds
+// heads * (max_pos + 1) floats; gqa_v_kernel takes gqa_dev_smem_bytes(max_pos)
+// of shared memory (at most 200 KB).
+cudaError_t launch_conv1d_dev(const float* input, float* state, const int* d_oldest, const float* weight_t,
+                              float* output, int conv_dim, int kernel_size, cudaStream_t stream);
+cudaError_t launch_rope_dev(float* t, int heads, int head_dim, int rotary_dim, const float* cos_all,
+                            const float* sin_all, const int* d_pos, cudaStream_t stream);
+cudaError_t launch_kv_append(const float* k, const float* v, float* k_cache, float* v_cache, const int* d_pos,
+                             int row, cudaStream_t stream);
+size_t gqa_dev_smem_bytes(int max_pos);
+cudaError_t launch_gqa_attend_dev(const float* q, int q_stride, const float* k_cache, const float* v_cache,
+                                  float* out, const int* d_pos, int max_pos, int heads, int kv_heads, int head_dim,
+                                  float* scratch, cudaStream_t stream);
+
 // Bit-exact y[m][0:rows] = x[m][0:k] . W^T for 2 <= M <= 64 activation rows
 // in one launch that streams W once (qlm_gemm_exact.cu): a pre-pass writes the
 // activations into `scratch` (gemm_exact_scratch_bytes) in the kernel's pair
-// layout. Outputs bit-identical to the GEMV for every m.
+// layout; one CTA per SM (sm_count) works a balanced range of rows. Outputs
+// bit-identical to the GEMV for every m.
 bool gemm_exact_supported(int M, int k);
 size_t gemm_exact_scratch_bytes(int M, int k);
 cudaError_t launch_gemm_exact(const float* x, int64_t ldx, int M, const uint8_t* q, const float* s, int rows, int k,
-                              bool q4, float* y, int64_t ldy, void* scratch, cudaStream_t stream);
+                              bool q4, float* y, int64_t ldy, void* scratch, int sm_count, cudaStream_t stream);
 
 // ---- tensor-core prefill GEMM (qlm_gemm_tc.cu) ----
 struct TcMaps {
