@@ -241,7 +241,13 @@ int qlm_gqa_attend(const float* q, int q_stride, const float* k_cache, const flo
  * (host array) and returns their greedy choices, logits [batch][vocab]
  * optional. Every op is row- or head-independent, so each sequence's logits
  * are bit-identical to decoding it alone. qlm_model_load / qlm_model_decode
- * are the batch = 1 forms. */
+ * are the batch = 1 forms.
+ * Execution: the first step runs eagerly; the next one captures the step into
+ * a CUDA graph (the position and conv ring position travel in device memory
+ * with the tokens) that every later step replays, with the same results.
+ * QLM_MODEL_GRAPH=0 in the environment at load keeps every step eager.
+ * max_seq * 4 bytes must fit the attention kernels' 200 KB of shared memory
+ * (max_seq <= 51200) when the model has attention layers. */
 typedef struct qlm_model qlm_model;
 int qlm_model_load(const char* dir, int device, int max_seq, qlm_model** out);
 int qlm_model_load_batch(const char* dir, int device, int max_seq, int batch, qlm_model** out);
@@ -376,7 +382,8 @@ int qlm_stream_sync(void* stream);
  * on their stream around their work (host copies included for
  * QLM_LINEAR_HOST_IO), so the figure is device time and adds no
  * synchronisation; calls issued while their stream is being captured into a
- * CUDA graph are not timed. qlm_linear_int8_tc_noalloc is never timed (event
+ * CUDA graph are not timed (qlm_model_decode[_batch] therefore runs its step
+ * eagerly while timing is on). qlm_linear_int8_tc_noalloc is never timed (event
  * pools allocate). Every linear entry point, qlm_model_decode and
  * qlm_model_decode_batch also open an NVTX range named after the entry point,
  * whether or not timing is on.

@@ -166,11 +166,15 @@ __global__ void __launch_bounds__(kThreads) silu_kernel(float* __restrict__ x, i
 // row (oldest + j) % ntaps is the j-th oldest tap; weight_t [ntaps + 1][conv_dim]):
 // out[c] = (((0 + s_0 w_0) + s_1 w_1) + ...) + in w_last, products and sums
 // rounded separately; the oldest row then takes the input. One thread per channel.
+// d_oldest: when set, the ring position is read from device memory (a
+// captured decode step replays at every position).
 __global__ void __launch_bounds__(kThreads) conv1d_tapmajor_kernel(const float* __restrict__ in, float* state,
-                                                                   int oldest, const float* __restrict__ wt,
+                                                                   int oldest, const int* __restrict__ d_oldest,
+                                                                   const float* __restrict__ wt,
                                                                    float* __restrict__ out, int conv_dim, int ntaps) {
     const int c = blockIdx.x * blockDim.x + threadIdx.x;
     if (c >= conv_dim) return;
+    if (d_oldest) oldest = *d_oldest;
     float sum = 0.0f;
     for (int j = 0; j < ntaps; ++j) {
         const int row = (oldest + j) % ntaps;
@@ -356,10 +360,15 @@ __global__ void __launch_bounds__(256) gqa_attend_kernel(const float* __restrict
 // Position-parallel form of gqa_attend_kernel for long contexts, in three
 // launches with the same arithmetic. Scores: CTA (head, block of 64 positions),
 // 16-thread groups as above, into scratch [heads][pos + 1].
+// d_pos: when set, the position is read from device memory and the grid
+// covers the longest context (CTAs past the position return at once).
 __global__ void __launch_bounds__(256) gqa_scores_kernel(const float* __restrict__ q, int q_stride,
                                                          const float* __restrict__ kc, float* __restrict__ scores,
-                                                         int pos, int heads, int kv_heads, int d) {
+                                                         int pos, const int* __restrict__ d_pos, int heads,
+                                                         int kv_heads, int d) {
     extern __shared__ float qs[];
+    if (d_pos) pos = *d_pos;
+    if ((int)blockIdx.y * 64 > pos) return;
     const int h = blockIdx.x, tid = threadIdx.x;
     const int kv_size = kv_heads * d, off = (h / (heads / kv_heads)) * d;
     for (int i = tid; i < d; i += blockDim.x) qs[i] = q[(int64_t)h * q_stride + i];
@@ -402,8 +411,10 @@ __global__ void __launch_bounds__(256) gqa_scores_kernel(const float* __restrict
 
 // Softmax of one head's scores in place, one CTA per head: max with the NaN
 // rule, exp in double, the sum in position order, the division.
-__global__ void __launch_bounds__(256) gqa_softmax_kernel(float* __restrict__ scores, int pos) {
+__global__ void __launch_bounds__(256) gqa_softmax_kernel(float* __restrict__ scores, int pos,
+                                                          const int* __restrict__ d_pos) {
     __shared__ float red[34];
+    if (d_pos) pos = *d_pos;
     float* sc = scores + (int64_t)blockIdx.x * (pos + 1);
     const int tid = threadIdx.x;
     float m = -INFINITY;
@@ -439,8 +450,10 @@ __global__ void __launch_bounds__(256) gqa_softmax_kernel(float* __restrict__ sc
 // staged in shared memory, then each lane accumulates its output element over
 // the positions in order.
 __global__ void __launch_bounds__(32) gqa_v_kernel(const float* __restrict__ probs, const float* __restrict__ vc,
-                                                   float* __restrict__ out, int pos, int heads, int kv_heads, int d) {
+                                                   float* __restrict__ out, int pos, const int* __restrict__ d_pos,
+                                                   int heads, int kv_heads, int d) {
     extern __shared__ float pr[];  // [pos + 1]
+    if (d_pos) pos = *d_pos;
     const int h = blockIdx.x, lane = threadIdx.x;
     const int kv_size = kv_heads * d, off = (h / (heads / kv_heads)) * d;
     const float* src = probs + (int64_t)h * (pos + 1);
@@ -485,10 +498,16 @@ __global__ void gdn_gates_kernel(const float* __restrict__ a_raw, const float* _
 }
 
 // t [tokens][heads][head_dim]; cos/sin [tokens][rotary_dim / 2].
+// d_pos: when set, one token whose table row is *d_pos (the tables then hold
+// every position).
 __global__ void __launch_bounds__(kThreads) rope_neox_kernel(float* __restrict__ t, const float* __restrict__ ct,
                                                              const float* __restrict__ st, int heads, int head_dim,
-                                                             int half) {
+                                                             int half, const int* __restrict__ d_pos) {
     const int tok = blockIdx.y;
+    if (d_pos) {
+        ct += (int64_t)*d_pos * half;
+        st += (int64_t)*d_pos * half;
+    }
     const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (idx >= (int64_t)heads * half) return;
     const int h = (int)(idx / half), i = (int)(idx % half);
@@ -497,6 +516,17 @@ __global__ void __launch_bounds__(kThreads) rope_neox_kernel(float* __restrict__
     const float x1 = hd[i], x2 = hd[i + half];
     hd[i] = __fsub_rn(__fmul_rn(x1, c), __fmul_rn(x2, s));
     hd[i + half] = __fadd_rn(__fmul_rn(x2, c), __fmul_rn(x1, s));
+}
+
+// The decode token's keys and values into row *d_pos of the caches ([T][row]).
+__global__ void __launch_bounds__(kThreads) kv_append_kernel(const float* __restrict__ k, const float* __restrict__ v,
+                                                             float* __restrict__ kc, float* __restrict__ vc,
+                                                             const int* __restrict__ d_pos, int row) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= row) return;
+    const int64_t o = (int64_t)*d_pos * row + i;
+    kc[o] = k[i];
+    vc[o] = v[i];
 }
 
 }  // namespace
@@ -537,6 +567,58 @@ cudaError_t launch_rms_norm_strided(const float* x, const float* w, float* y, in
                                     float eps, cudaStream_t stream) {
     const size_t smem = size <= kStageFloats ? (size_t)size * sizeof(float) : 0;
     rms_norm_kernel<true><<<rows, kThreads, smem, stream>>>(x, w, y, size, eps, ld);
+    return cudaGetLastError();
+}
+
+// Position-from-device forms for a decode step that is captured once and
+// replayed at every position (same kernels and arithmetic as the C ABI's).
+cudaError_t launch_conv1d_dev(const float* input, float* state, const int* d_oldest, const float* weight_t,
+                              float* output, int conv_dim, int kernel_size, cudaStream_t stream) {
+    conv1d_tapmajor_kernel<<<(conv_dim + kThreads - 1) / kThreads, kThreads, 0, stream>>>(
+        input, state, 0, d_oldest, weight_t, output, conv_dim, kernel_size - 1);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_rope_dev(float* t, int heads, int head_dim, int rotary_dim, const float* cos_all,
+                            const float* sin_all, const int* d_pos, cudaStream_t stream) {
+    const int half = rotary_dim / 2;
+    const int64_t n = (int64_t)heads * half;
+    rope_neox_kernel<<<dim3((unsigned)((n + kThreads - 1) / kThreads), 1), kThreads, 0, stream>>>(
+        t, cos_all, sin_all, heads, head_dim, half, d_pos);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_kv_append(const float* k, const float* v, float* k_cache, float* v_cache, const int* d_pos,
+                             int row, cudaStream_t stream) {
+    kv_append_kernel<<<(row + kThreads - 1) / kThreads, kThreads, 0, stream>>>(k, v, k_cache, v_cache, d_pos, row);
+    return cudaGetLastError();
+}
+
+size_t gqa_dev_smem_bytes(int max_pos) { return (size_t)(max_pos + 1) * sizeof(float); }
+
+cudaError_t launch_gqa_attend_dev(const float* q, int q_stride, const float* k_cache, const float* v_cache,
+                                  float* out, const int* d_pos, int max_pos, int heads, int kv_heads, int head_dim,
+                                  float* scratch, cudaStream_t stream) {
+    static bool attr_set[64] = {};
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+    if (!attr_set[dev]) {
+        if ((e = cudaFuncSetAttribute(gqa_v_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024)) !=
+            cudaSuccess)
+            return e;
+        attr_set[dev] = true;
+    }
+    const dim3 g1((unsigned)heads, (unsigned)((max_pos + 64) / 64));
+    gqa_scores_kernel<<<g1, 256, (size_t)head_dim * sizeof(float), stream>>>(q, q_stride, k_cache, scratch, 0, d_pos,
+                                                                             heads, kv_heads, head_dim);
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    gqa_softmax_kernel<<<heads, 256, 0, stream>>>(scratch, 0, d_pos);
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    const dim3 g2((unsigned)heads, (unsigned)((head_dim + 31) / 32));
+    gqa_v_kernel<<<g2, 32, gqa_dev_smem_bytes(max_pos), stream>>>(scratch, v_cache, out, 0, d_pos, heads, kv_heads,
+                                                                  head_dim);
     return cudaGetLastError();
 }
 }  // namespace qlm
@@ -606,15 +688,15 @@ int qlm_gqa_attend(const float* q, int q_stride, const float* k_cache, const flo
         return launched("gqa_attend launch");
     }
     const dim3 g1((unsigned)heads, (unsigned)((pos + 64) / 64));
-    qlm::gqa_scores_kernel<<<g1, 256, (size_t)head_dim * sizeof(float), s>>>(q, q_stride, k_cache, scratch, pos, heads,
-                                                                            kv_heads, head_dim);
+    qlm::gqa_scores_kernel<<<g1, 256, (size_t)head_dim * sizeof(float), s>>>(q, q_stride, k_cache, scratch, pos,
+                                                                            nullptr, heads, kv_heads, head_dim);
     int rc = launched("gqa_scores launch");
     if (rc) return rc;
-    qlm::gqa_softmax_kernel<<<heads, 256, 0, s>>>(scratch, pos);
+    qlm::gqa_softmax_kernel<<<heads, 256, 0, s>>>(scratch, pos, nullptr);
     if ((rc = launched("gqa_softmax launch"))) return rc;
     const dim3 g2((unsigned)heads, (unsigned)((head_dim + 31) / 32));
-    qlm::gqa_v_kernel<<<g2, 32, (size_t)(pos + 1) * sizeof(float), s>>>(scratch, v_cache, out, pos, heads, kv_heads,
-                                                                        head_dim);
+    qlm::gqa_v_kernel<<<g2, 32, (size_t)(pos + 1) * sizeof(float), s>>>(scratch, v_cache, out, pos, nullptr, heads,
+                                                                        kv_heads, head_dim);
     return launched("gqa_v launch");
 }
 
@@ -656,7 +738,8 @@ int qlm_rope_neox(float* t, int num_tokens, int num_heads, int head_dim, int rot
     const int64_t per_tok = (int64_t)num_heads * half;
     const dim3 grid((unsigned)((per_tok + qlm::kThreads - 1) / qlm::kThreads), (unsigned)num_tokens);
     qlm::rope_neox_kernel<<<grid, qlm::kThreads, 0, static_cast<cudaStream_t>(stream)>>>(t, cos_tab, sin_tab,
-                                                                                       num_heads, head_dim, half);
+                                                                                       num_heads, head_dim, half,
+                                                                                       nullptr);
     return launched("rope_neox launch");
 }
 
@@ -675,8 +758,8 @@ int qlm_conv1d_update_tapmajor(const float* input, float* state, int oldest_tap,
     if (conv_dim <= 0 || kernel_size < 2 || oldest_tap < 0 || oldest_tap >= kernel_size - 1)
         return layer_fail(QLM_ERR_INVALID_ARG, "bad conv1d shape or ring position");
     qlm::conv1d_tapmajor_kernel<<<(conv_dim + qlm::kThreads - 1) / qlm::kThreads, qlm::kThreads, 0,
-                                  static_cast<cudaStream_t>(stream)>>>(input, state, oldest_tap, weight_t, output,
-                                                                       conv_dim, kernel_size - 1);
+                                  static_cast<cudaStream_t>(stream)>>>(input, state, oldest_tap, nullptr, weight_t,
+                                                                       output, conv_dim, kernel_size - 1);
     return launched("conv1d launch");
 }
 

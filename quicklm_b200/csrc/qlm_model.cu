@@ -167,7 +167,6 @@ struct Layer {
     qlm_w8 *z = nullptr, *b = nullptr, *a = nullptr, *out = nullptr;
     float* conv_wt = nullptr;     // [kernel][3][B][lin] (tap-major, replicated per sequence)
     float* conv_state = nullptr;  // [kernel - 1][3][B][lin]
-    int conv_ring = 0;
     float *gdn_norm = nullptr, *A_log = nullptr, *dt_bias = nullptr;
     float* rstate = nullptr;      // [B][lin_heads][lin_dim][lin_dim]
 };
@@ -191,8 +190,17 @@ struct qlm_model {
     float *x = nullptr, *h = nullptr, *t1 = nullptr, *t2 = nullptr, *t3 = nullptr, *t4 = nullptr, *t5 = nullptr;
     float *gate_buf = nullptr, *up_buf = nullptr, *logits = nullptr, *scores = nullptr;
     float *decay = nullptr, *beta = nullptr;
-    int* d_tokens = nullptr;  // [B] the step's input tokens, then its greedy choices
-    int* h_tokens = nullptr;  // [B] pinned
+    // The step's control words [B tokens][position][conv ring position],
+    // uploaded with one copy; the greedy choices come back in the token words.
+    int* d_tokens = nullptr;  // device [B + 2]
+    int* h_tokens = nullptr;  // pinned host [B + 2]
+    int ring = 0;             // oldest tap of every gated-delta-net conv ring (all advance together)
+    // The step captured once as a CUDA graph (after one eager step has sized
+    // every scratch buffer) and replayed at every position.
+    bool use_graph = true;
+    int eager_steps = 0;
+    cudaGraph_t graph = nullptr;
+    cudaGraphExec_t graph_exec = nullptr;
     cudaStream_t stream = nullptr;
     std::vector<void*> allocs;
     std::vector<qlm_w8*> weights;
@@ -564,9 +572,17 @@ int load_all(const std::string& dir, qlm_model* m) {
     QLM_TRY(L.zeros(&m->scores, B * m->heads * m->max_seq));
     QLM_TRY(L.zeros(&m->decay, B * m->lin_heads + 1));
     QLM_TRY(L.zeros(&m->beta, B * m->lin_heads + 1));
-    QLM_TRY(L.zeros(&m->d_tokens, B));
-    if (cudaMallocHost(reinterpret_cast<void**>(&m->h_tokens), B * sizeof(int)) != cudaSuccess)
+    QLM_TRY(L.zeros(&m->d_tokens, B + 2));
+    if (cudaMallocHost(reinterpret_cast<void**>(&m->h_tokens), (B + 2) * sizeof(int)) != cudaSuccess)
         return fail(QLM_ERR_OUT_OF_MEMORY, "pinned host words");
+    bool any_attn = false;
+    for (const Layer& ly : m->layers) any_attn = any_attn || ly.full_attn;
+    if (any_attn && qlm::gqa_dev_smem_bytes(m->max_seq - 1) > 200 * 1024)
+        return fail(QLM_ERR_UNSUPPORTED, "max_seq %d too long for the attention kernels", m->max_seq);
+    {
+        const char* e = std::getenv("QLM_MODEL_GRAPH");
+        m->use_graph = !(e && e[0] == '0');
+    }
     if (cudaStreamSynchronize(m->stream) != cudaSuccess) return fail(QLM_ERR_CUDA, "load synchronize failed");
     return QLM_OK;
 }
@@ -575,6 +591,8 @@ void release(qlm_model* m) {
     if (!m) return;
     Dev g(m->device >= 0 ? m->device : 0);
     if (m->stream) cudaStreamSynchronize(m->stream);
+    if (m->graph_exec) cudaGraphExecDestroy(m->graph_exec);
+    if (m->graph) cudaGraphDestroy(m->graph);
     for (qlm_w8* w : m->weights) qlm_weight_free(w);
     for (void* p : m->allocs) cudaFree(p);
     if (m->h_tokens) cudaFreeHost(m->h_tokens);
@@ -602,9 +620,9 @@ int gdn_step(qlm_model* m, Layer& ly) {
     float* ys[6] = {qkv, qkv + (size_t)B * lin, qkv + (size_t)2 * B * lin, z, b_raw, a_raw};
     const int64_t lds[6] = {lin, lin, lin, lin, lh, lh};
     QLM_TRY(qlm_linear_int8_grouped(m->h, B, H, H, ws, 6, ys, lds, 0, s));                      // 1. projections
-    QLM_TRY(qlm_conv1d_update_tapmajor(qkv, ly.conv_state, ly.conv_ring, ly.conv_wt, conv, channels,
-                                       m->conv_kernel, s));                                       // 2. conv step
-    ly.conv_ring = (ly.conv_ring + 1) % (m->conv_kernel - 1);
+    if (qlm::launch_conv1d_dev(qkv, ly.conv_state, m->d_tokens + B + 1, ly.conv_wt, conv, channels, m->conv_kernel,
+                               s) != cudaSuccess)
+        return launch_ok("conv step");                                                            // 2. conv step
     QLM_TRY(qlm_silu(conv, channels, s));                                                         // 4. SiLU
     float *q = conv, *k = conv + (size_t)B * lin, *v = conv + (size_t)2 * B * lin;
     QLM_TRY(qlm_l2norm_heads(q, B * lh, ld, 1e-6f, s));                                           // 5. L2 norms
@@ -619,11 +637,12 @@ int gdn_step(qlm_model* m, Layer& ly) {
 }
 
 // One layer's gated GQA step (Qwen3_5Attention::forward,
-// src/model/attention.cpp:138-235) at position pos for the B sequences;
-// result in m->t5. Sequence b's query head h is head b * heads + h, its KV
-// head b * kv_heads + h / group: the cache [T][B][kv_heads][d] reads as
-// B * kv_heads heads.
-int attn_step(qlm_model* m, Layer& ly, int pos) {
+// src/model/attention.cpp:138-235) for the B sequences at the position held
+// in the step's control words (device memory, so a captured step replays at
+// every position); result in m->t5. Sequence b's query head h is head
+// b * heads + h, its KV head b * kv_heads + h / group: the cache
+// [T][B][kv_heads][d] reads as B * kv_heads heads.
+int attn_step(qlm_model* m, Layer& ly) {
     cudaStream_t s = m->stream;
     const int B = m->batch, H = m->hidden, hd = m->head_dim, qd = 2 * hd, nh = m->heads, kvh = m->kv_heads;
     const int kv = kvh * hd;
@@ -635,16 +654,15 @@ int attn_step(qlm_model* m, Layer& ly, int pos) {
     if (qlm::launch_rms_norm_strided(q, ly.q_norm, q, B * nh, hd, qd, 1e-6f, s) != cudaSuccess)  // 2. QK-norm
         return launch_ok("QK-norm");
     QLM_TRY(qlm_rms_norm(k, ly.k_norm, k, B * kvh, hd, 1e-6f, s));
-    const int half = m->rotary_dim / 2;                                                      // 3. partial RoPE
-    const float* cs = m->rope_cos + (size_t)pos * half;
-    const float* sn = m->rope_sin + (size_t)pos * half;
-    QLM_TRY(qlm_rope_neox(k, 1, B * kvh, hd, m->rotary_dim, cs, sn, s));
-    QLM_TRY(qlm_rope_neox(q, 1, B * nh, qd, m->rotary_dim, cs, sn, s));  // the query half of each [query | gate] row
-    const size_t row = (size_t)B * kv;
-    if (cudaMemcpyAsync(ly.k_cache + (size_t)pos * row, k, row * 4, cudaMemcpyDeviceToDevice, s) != cudaSuccess ||
-        cudaMemcpyAsync(ly.v_cache + (size_t)pos * row, v, row * 4, cudaMemcpyDeviceToDevice, s) != cudaSuccess)
-        return fail(QLM_ERR_CUDA, "KV cache write failed");                                  // 4. cache
-    QLM_TRY(qlm_gqa_attend(q, qd, ly.k_cache, ly.v_cache, att, pos, B * nh, B * kvh, hd, m->scores, s));  // 5.
+    const int* d_pos = m->d_tokens + B;                                                    // 3. partial RoPE
+    if (qlm::launch_rope_dev(k, B * kvh, hd, m->rotary_dim, m->rope_cos, m->rope_sin, d_pos, s) != cudaSuccess ||
+        qlm::launch_rope_dev(q, B * nh, qd, m->rotary_dim, m->rope_cos, m->rope_sin, d_pos, s) != cudaSuccess)
+        return launch_ok("RoPE");  // q: the query half of each [query | gate] row
+    if (qlm::launch_kv_append(k, v, ly.k_cache, ly.v_cache, d_pos, B * kv, s) != cudaSuccess)  // 4. cache
+        return launch_ok("KV cache write");
+    if (qlm::launch_gqa_attend_dev(q, qd, ly.k_cache, ly.v_cache, att, d_pos, m->max_seq - 1, B * nh, B * kvh, hd,
+                                   m->scores, s) != cudaSuccess)                             // 5. attention
+        return launch_ok("attention");
     const int n = B * nh * hd;
     sigmoid_gate_kernel<<<(n + kEmbThreads - 1) / kEmbThreads, kEmbThreads, 0, s>>>(att, q, B * nh, hd);  // 6.
     QLM_TRY(launch_ok("output gate"));
@@ -660,26 +678,22 @@ int add_into(qlm_model* m, float* x, const float* d, int n) {
 
 namespace {
 
-int decode_step(qlm_model* m, const int* tokens, int pos, int* next_tokens, float* logits) {
+// The step's device work, from the upload of the control words to the
+// read-back of the greedy choices (DecoderModel::forward + sample,
+// src/model/model.cpp:151-199, 259-272). Enqueued eagerly or into a capture.
+int enqueue_step(qlm_model* m) {
     const int B = m->batch;
-    for (int b = 0; b < B; ++b)
-        if (tokens[b] < 0 || tokens[b] >= m->vocab)
-            return fail(QLM_ERR_INVALID_ARG, "token %d (sequence %d) not in [0, %d)", tokens[b], b, m->vocab);
-    if (pos < 0 || pos >= m->max_seq)
-        return fail(QLM_ERR_INVALID_ARG, "position %d not in [0, max_seq %d)", pos, m->max_seq);
-    Dev g(m->device);
-    if (!g.ok) return fail(QLM_ERR_CUDA, "cudaSetDevice(%d) failed", m->device);
     cudaStream_t s = m->stream;
     const int H = m->hidden;
-    std::memcpy(m->h_tokens, tokens, (size_t)B * sizeof(int));
-    if (cudaMemcpyAsync(m->d_tokens, m->h_tokens, (size_t)B * sizeof(int), cudaMemcpyHostToDevice, s) != cudaSuccess)
+    if (cudaMemcpyAsync(m->d_tokens, m->h_tokens, (size_t)(B + 2) * sizeof(int), cudaMemcpyHostToDevice, s) !=
+        cudaSuccess)
         return fail(QLM_ERR_CUDA, "token upload failed");
     embed_rows_kernel<<<dim3((H + kEmbThreads - 1) / kEmbThreads, B), kEmbThreads, 0, s>>>(m->embed, m->embed_bf16,
                                                                                            m->d_tokens, H, m->x);
     QLM_TRY(launch_ok("embedding"));
     for (Layer& ly : m->layers) {
         QLM_TRY(qlm_rms_norm(m->x, ly.in_norm, m->h, B, H, m->eps, s));
-        QLM_TRY(ly.full_attn ? attn_step(m, ly, pos) : gdn_step(m, ly));
+        QLM_TRY(ly.full_attn ? attn_step(m, ly) : gdn_step(m, ly));
         QLM_TRY(add_into(m, m->x, m->t5, B * H));
         QLM_TRY(qlm_rms_norm(m->x, ly.post_norm, m->h, B, H, m->eps, s));
         const qlm_w8* ws[2] = {ly.gate, ly.up};
@@ -696,10 +710,60 @@ int decode_step(qlm_model* m, const int* tokens, int pos, int* next_tokens, floa
     QLM_TRY(launch_ok("greedy choice"));
     if (cudaMemcpyAsync(m->h_tokens, m->d_tokens, (size_t)B * sizeof(int), cudaMemcpyDeviceToHost, s) != cudaSuccess)
         return fail(QLM_ERR_CUDA, "token read-back failed");
+    return QLM_OK;
+}
+
+// Captures the step into m->graph_exec; on any failure the model stays on
+// eager steps (the result is the same, only slower).
+void capture_step(qlm_model* m) {
+    cudaStream_t s = m->stream;
+    if (cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal) != cudaSuccess) {
+        cudaGetLastError();
+        m->use_graph = false;
+        return;
+    }
+    const int rc = enqueue_step(m);
+    cudaGraph_t g = nullptr;
+    const cudaError_t e = cudaStreamEndCapture(s, &g);
+    if (rc != QLM_OK || e != cudaSuccess || !g ||
+        cudaGraphInstantiate(&m->graph_exec, g, 0) != cudaSuccess) {
+        cudaGetLastError();
+        if (g) cudaGraphDestroy(g);
+        m->graph_exec = nullptr;
+        m->use_graph = false;
+        return;
+    }
+    m->graph = g;
+}
+
+int decode_step(qlm_model* m, const int* tokens, int pos, int* next_tokens, float* logits) {
+    const int B = m->batch;
+    for (int b = 0; b < B; ++b)
+        if (tokens[b] < 0 || tokens[b] >= m->vocab)
+            return fail(QLM_ERR_INVALID_ARG, "token %d (sequence %d) not in [0, %d)", tokens[b], b, m->vocab);
+    if (pos < 0 || pos >= m->max_seq)
+        return fail(QLM_ERR_INVALID_ARG, "position %d not in [0, max_seq %d)", pos, m->max_seq);
+    Dev g(m->device);
+    if (!g.ok) return fail(QLM_ERR_CUDA, "cudaSetDevice(%d) failed", m->device);
+    cudaStream_t s = m->stream;
+    std::memcpy(m->h_tokens, tokens, (size_t)B * sizeof(int));
+    m->h_tokens[B] = pos;
+    m->h_tokens[B + 1] = m->ring;
+    // While per-matmul timing is on the step runs eagerly, so every linear
+    // call is timed (calls replayed inside a graph are not).
+    const bool graph = m->use_graph && !qlm_internal::prof_on();
+    if (graph && !m->graph_exec && m->eager_steps > 0) capture_step(m);
+    if (graph && m->graph_exec) {
+        if (cudaGraphLaunch(m->graph_exec, s) != cudaSuccess) return launch_ok("decode step graph");
+    } else {
+        QLM_TRY(enqueue_step(m));
+        ++m->eager_steps;
+    }
     if (logits &&
         cudaMemcpyAsync(logits, m->logits, (size_t)B * m->vocab * 4, cudaMemcpyDeviceToHost, s) != cudaSuccess)
         return fail(QLM_ERR_CUDA, "logits read-back failed");
     if (cudaStreamSynchronize(s) != cudaSuccess) return launch_ok("decode step");
+    if (m->conv_kernel > 1) m->ring = (m->ring + 1) % (m->conv_kernel - 1);
     QLM_TRY(qlm_device_status(m->device, 1));
     std::memcpy(next_tokens, m->h_tokens, (size_t)B * sizeof(int));
     return QLM_OK;
@@ -752,10 +816,10 @@ int qlm_model_reset(qlm_model* m) {
         } else {
             e = cudaMemsetAsync(ly.conv_state, 0, (size_t)(m->conv_kernel - 1) * 3 * B * lin * 4, m->stream);
             if (e == cudaSuccess) e = cudaMemsetAsync(ly.rstate, 0, B * lin * m->lin_dim * 4, m->stream);
-            ly.conv_ring = 0;
         }
         if (e != cudaSuccess) return fail(QLM_ERR_CUDA, "state reset failed");
     }
+    m->ring = 0;
     return cudaStreamSynchronize(m->stream) == cudaSuccess ? QLM_OK : fail(QLM_ERR_CUDA, "synchronize failed");
 }
 

@@ -80,3 +80,31 @@ def test_single_matches_reference_decode(qlm_lib, cuda_device, small_checkpoint)
     toks, _ = _decode(m, [prompt], n_new)
     m.free()
     assert list(toks[0]) == ref
+
+
+def test_graph_replay_equals_eager(qlm_lib, cuda_device, small_checkpoint):
+    """Steps replayed from the captured graph (position and conv ring position
+    read from device memory) give exactly the eager steps' logits, also after
+    a reset."""
+    import quicklm_b200 as q
+    rng = np.random.default_rng(9)
+    prompts = [list(rng.integers(0, SMALL["vocab"], 6)) for _ in range(2)]
+    old = os.environ.get("QLM_MODEL_GRAPH")
+    os.environ["QLM_MODEL_GRAPH"] = "0"
+    try:
+        me = q.Model(small_checkpoint, max_seq=64, batch=2)
+    finally:
+        if old is None:
+            del os.environ["QLM_MODEL_GRAPH"]
+        else:
+            os.environ["QLM_MODEL_GRAPH"] = old
+    mg = q.Model(small_checkpoint, max_seq=64, batch=2)
+    for _ in range(2):
+        te, le = _decode(me, prompts, 12)
+        tg, lg = _decode(mg, prompts, 12)
+        assert np.array_equal(te, tg)
+        assert np.array_equal(le.view(np.uint32), lg.view(np.uint32))
+        me.reset()
+        mg.reset()
+    me.free()
+    mg.free()
