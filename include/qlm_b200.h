@@ -152,6 +152,12 @@ int qlm_store_info(const char* path, const char* name, int* bits, int64_t* rows,
  *                     x and y may be the same buffer. Bit-identical.
  *   qlm_add_rms_norm  residual += delta; out = rms_norm(residual):
  *                     math::add_rms_norm (math_ops.cpp:1133-1174). Bit-identical.
+ *   qlm_add_then_rms_norm  the decoder layer's unfused residual step
+ *                     (src/model/modules.hpp:228-231, 239-240, the default):
+ *                     math::elementwise_add(residual, delta), then
+ *                     math::rms_norm(residual) into out, in one launch;
+ *                     bit-identical to the two (whose accumulation order
+ *                     differs from math::add_rms_norm's).
  *   qlm_silu_mul      a = silu(a) * b: math::silu_mul (math_ops.cpp:1122-1131);
  *                     within 2 ulp (exp in double, rounded once, vs host expf).
  *   qlm_rope_neox     partial NeoX RoPE of t [num_tokens][num_heads][head_dim]
@@ -194,6 +200,8 @@ int qlm_store_info(const char* path, const char* name, int* bits, int64_t* rows,
 int qlm_rms_norm(const float* x, const float* w, float* y, int rows, int size, float eps, void* stream);
 int qlm_add_rms_norm(float* residual, const float* delta, const float* w, float* out, int rows, int size, float eps,
                      void* stream);
+int qlm_add_then_rms_norm(float* residual, const float* delta, const float* w, float* out, int rows, int size,
+                          float eps, void* stream);
 int qlm_silu_mul(float* a, const float* b, int64_t n, void* stream);
 int qlm_rope_neox(float* t, int num_tokens, int num_heads, int head_dim, int rotary_dim, const float* cos_tab,
                   const float* sin_tab, void* stream);

@@ -41,7 +41,7 @@ ABI_SYMBOLS = (
     "qlm_comm_create", "qlm_comm_connect", "qlm_comm_free", "qlm_linear_int8_allgather", "qlm_argmax_f32",
     "qlm_linear_int8_grouped", "qlm_weight_quantize_upload_q4", "qlm_weight_export_int4", "qlm_weight_bits",
     "qlm_weight_import_int4", "qlm_store_save", "qlm_store_load", "qlm_store_info", "qlm_rms_norm",
-    "qlm_add_rms_norm", "qlm_silu_mul", "qlm_rope_neox", "qlm_rope_neox_tables", "qlm_silu",
+    "qlm_add_rms_norm", "qlm_add_then_rms_norm", "qlm_silu_mul", "qlm_rope_neox", "qlm_rope_neox_tables", "qlm_silu",
     "qlm_conv1d_update_tapmajor", "qlm_l2norm_heads", "qlm_gdn_gates", "qlm_gdn_recurrence", "qlm_rms_norm_gain",
     "qlm_gqa_attend", "qlm_comm_set_timeout_us", "qlm_comm_status", "qlm_model_load", "qlm_model_reset",
     "qlm_model_decode", "qlm_model_info", "qlm_model_free", "qlm_model_load_batch", "qlm_model_decode_batch", "qlm_model_stream",
@@ -88,6 +88,7 @@ def load(path: str = LIB_PATH):
     F = ctypes.c_float
     lib.qlm_rms_norm.argtypes = [P, P, P, I, I, F, P]
     lib.qlm_add_rms_norm.argtypes = [P, P, P, P, I, I, F, P]
+    lib.qlm_add_then_rms_norm.argtypes = [P, P, P, P, I, I, F, P]
     lib.qlm_silu_mul.argtypes = [P, P, L, P]
     lib.qlm_rope_neox.argtypes = [P, I, I, I, I, P, P, P]
     lib.qlm_rope_neox_tables.argtypes = [I, I, F, I, P, P]
@@ -538,6 +539,20 @@ def add_rms_norm(residual, delta, w, eps: float, out=None, stream=None):
     out = residual.new_empty(residual.shape) if out is None else _dev_f32(out, "out")
     _check(load().qlm_add_rms_norm(residual.data_ptr(), delta.data_ptr(), w.data_ptr(), out.data_ptr(),
                                    residual.numel() // size, size, eps, _torch_stream(stream)))
+    return out
+
+
+def add_then_rms_norm(residual, delta, w, eps: float, out=None, stream=None):
+    """The decoder layer's unfused residual step (modules.hpp:228-231):
+    math::elementwise_add(residual, delta) in place, then returns
+    math::rms_norm(residual) — one launch, the bits of the two."""
+    _dev_f32(residual, "residual"), _dev_f32(delta, "delta"), _dev_f32(w, "w")
+    size = w.numel()
+    if residual.numel() % size or delta.numel() != residual.numel():
+        raise QlmError(1, "residual/delta shapes do not match w")
+    out = residual.new_empty(residual.shape) if out is None else _dev_f32(out, "out")
+    _check(load().qlm_add_then_rms_norm(residual.data_ptr(), delta.data_ptr(), w.data_ptr(), out.data_ptr(),
+                                        residual.numel() // size, size, eps, _torch_stream(stream)))
     return out
 
 

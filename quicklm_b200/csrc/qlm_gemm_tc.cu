@@ -463,6 +463,8 @@ __global__ void __launch_bounds__(256) act_to_f16_kernel(const float* __restrict
                                                          __half* __restrict__ x16, int* __restrict__ ea) {
     __shared__ float red[8];
     pdl_wait();  // x comes from the previous kernel; x16/ea may still be read by the previous GEMM
+    // x is read through L2 (ld.global.cg): under programmatic launch its producer may
+    // still be running when this kernel starts, so the read-only path is not safe.
     const int m = blockIdx.x;
     const float* xr = x + (int64_t)m * ldx;
     float mx = 0.0f;
@@ -472,7 +474,7 @@ __global__ void __launch_bounds__(256) act_to_f16_kernel(const float* __restrict
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
             const int k = base + i * (int)blockDim.x + (int)threadIdx.x;
-            v[i] = k < K ? fabsf(__ldg(xr + k)) : 0.0f;
+            v[i] = k < K ? fabsf(__ldcg(xr + k)) : 0.0f;
         }
 #pragma unroll
         for (int i = 0; i < 8; ++i)
@@ -495,8 +497,8 @@ __global__ void __launch_bounds__(256) act_to_f16_kernel(const float* __restrict
         for (int i = 0; i < 4; ++i) {
             const int l = l0 + (i >> 1), pp = i & 1;  // output pair i = positions 2i, 2i+1: h = 0, 1
             const int k0 = base + 32 * bl + 8 * pp + l, k1 = k0 + 16;
-            const float a = k0 < K ? __ldg(xr + k0) : 0.0f;
-            const float b = k1 < K ? __ldg(xr + k1) : 0.0f;
+            const float a = k0 < K ? __ldcg(xr + k0) : 0.0f;
+            const float b = k1 < K ? __ldcg(xr + k1) : 0.0f;
             const __half2 v = __halves2half2(__float2half_rn(scale_pow2(a, e)), __float2half_rn(scale_pow2(b, e)));
             hw[i] = h2_bits(v);
         }

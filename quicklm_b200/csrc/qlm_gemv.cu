@@ -299,7 +299,11 @@ __global__ void __launch_bounds__(MM == 1 || R == 2 ? 384 : 512, MM == 1 ? 2 : 1
     pdl_launch_dependents();
     // Activations are produced by the previous kernel in the stream. All of a
     // thread's loads are issued before its first store, so staging costs one
-    // L2 round trip per 8 elements per thread, not one per element.
+    // L2 round trip per 8 elements per thread, not one per element. They are
+    // L2 loads (ld.global.cg), never the non-coherent read-only path: under
+    // programmatic launch this kernel starts while its producer still writes
+    // x, so x is not read-only for this kernel's lifetime and an L1/texture
+    // line of an earlier read of the buffer could be served stale.
     pdl_wait();
     if (GATHER && comm_failed) {
         // Let this warp's copies land before leaving (bounded).
@@ -325,7 +329,7 @@ __global__ void __launch_bounds__(MM == 1 || R == 2 ? 384 : 512, MM == 1 ? 2 : 1
 #pragma unroll
             for (int i = 0; i < 8; ++i) {
                 const int kk = base + (int)threadIdx.x + i * (int)blockDim.x;
-                v[i] = kk < p.k ? __ldg(xr + kk) : 0.0f;
+                v[i] = kk < p.k ? __ldcg(xr + kk) : 0.0f;
             }
 #pragma unroll
             for (int i = 0; i < 8; ++i) {

@@ -194,6 +194,8 @@ __global__ void __launch_bounds__(CPT == 1 ? 512 : 384, 2) gemv_dec_kernel(const
         const uint32_t dummy = smem_u32(dummy_base) + (uint32_t)(warp * 512 + lane32 * 16);
         pdl_launch_dependents();
         pdl_wait();
+        // L2 loads of x, not the read-only path: this kernel may start while
+        // its producer still writes x (see the staging in qlm_gemv.cu).
         unsigned long long xp[CPT][2][4];
 #pragma unroll
         for (int j = 0; j < CPT; ++j)
@@ -202,8 +204,8 @@ __global__ void __launch_bounds__(CPT == 1 ? 512 : 384, 2) gemv_dec_kernel(const
 #pragma unroll
                 for (int jj = 0; jj < 4; ++jj) {
                     const int k0 = cj[j] * kChunk + (2 * h) * kBlock + jj * 8 + l, k1 = k0 + kBlock;
-                    const float x0 = vj[j] && k0 < p.k ? __ldg(p.x + k0) : 0.0f;
-                    const float x1 = vj[j] && k1 < p.k ? __ldg(p.x + k1) : 0.0f;
+                    const float x0 = vj[j] && k0 < p.k ? __ldcg(p.x + k0) : 0.0f;
+                    const float x1 = vj[j] && k1 < p.k ? __ldcg(p.x + k1) : 0.0f;
                     xp[j][h][jj] = f2pack(x0, x1);
                 }
         const unsigned long long nz = f2pack(p.zero_neg, p.zero_neg);
@@ -369,7 +371,7 @@ __global__ void __launch_bounds__(CPT == 1 ? 512 : 384, 2) gemv_dec_kernel(const
                     for (int kk = nbf * kBlock; kk < p.k; ++kk) {
                         const float qf = Q4 ? (float)((int)((qr[packed_offset_q4(kk)] >> packed_shift_q4(kk)) & 0xF) - 8)
                                             : (float)(int8_t)qr[packed_offset(kk)];
-                        acc = __fadd_rn(acc, __fmul_rn(__ldg(p.x + kk), qf));
+                        acc = __fadd_rn(acc, __fmul_rn(__ldcg(p.x + kk), qf));
                     }
                     t = __fadd_rn(t, __fmul_rn(acc, W->s[(int64_t)row * p.nb_pad + nbf]));
                 }

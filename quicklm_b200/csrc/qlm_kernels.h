@@ -131,6 +131,12 @@ cudaError_t launch_rms_norm_strided(const float* x, const float* w, float* y, in
 cudaError_t launch_gdn_gates(const float* a_raw, const float* b_raw, const float* A_log, const float* dt_bias,
                              float* decay, float* beta, int heads, int per, cudaStream_t stream);
 
+// x += delta (stored), then y = rms_norm(x) with rms_norm's own accumulation
+// order (zero-centred gain): the decoder layer's unfused residual add and the
+// next norm in one launch, bit-identical to the two (qlm_layer.cu).
+cudaError_t launch_add_then_rms_norm(float* x, const float* delta, const float* w, float* y, int rows, int size,
+                                     float eps, cudaStream_t stream);
+
 // Decode-step forms that read the position (and the conv ring position) from
 // device memory, so one captured step replays at every position
 // (qlm_layer.cu). launch_gqa_attend_dev: the three-launch attention with grids

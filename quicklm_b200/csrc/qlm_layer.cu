@@ -101,11 +101,16 @@ __device__ __forceinline__ void apply_zc(const float* in, const float* __restric
 // ZC: zero-centred gain (1 + w) as math::rms_norm; else the plain gain w.
 // ld: row stride of x and y in floats (>= size; the rows' first `size` values
 // are normalized, the rest untouched).
+// This kernel and silu_mul_kernel usually precede a GEMV launched with
+// programmatic stream serialization: they let it start at once, so its weight
+// copies overlap them (the GEMV reads its activations only after its
+// dependency wait, which still waits for this kernel to complete).
 template <bool ZC>
 __global__ void __launch_bounds__(kThreads) rms_norm_kernel(const float* x, const float* __restrict__ w, float* y,
                                                             int size, float eps, int64_t ld) {
     extern __shared__ float stage[];
     __shared__ float s_scale;
+    pdl_launch_dependents();
     const float* xr = x + (int64_t)blockIdx.x * ld;
     if (size <= kStageFloats) {
         for (int i = threadIdx.x; i < size; i += blockDim.x) stage[i] = xr[i];
@@ -118,6 +123,35 @@ __global__ void __launch_bounds__(kThreads) rms_norm_kernel(const float* x, cons
     }
     __syncthreads();
     apply_zc<ZC>(xr, w, y + (int64_t)blockIdx.x * ld, s_scale, size);
+}
+
+// The decoder layer's unfused residual step (src/model/modules.hpp:228-231,
+// 239-240 with the next layer's norm1): x += delta (stored, one rounding per
+// element, math::elementwise_add), then y = math::rms_norm(x) in rms_norm's
+// own accumulation order — the same bits as the two separate kernels, in one
+// launch. One CTA per row; lets a following GEMV start (see rms_norm_kernel).
+__global__ void __launch_bounds__(kThreads) add_then_rms_norm_kernel(float* x, const float* __restrict__ delta,
+                                                                     const float* __restrict__ w, float* y, int size,
+                                                                     float eps) {
+    extern __shared__ float stage[];
+    __shared__ float s_scale;
+    pdl_launch_dependents();
+    float* xr = x + (int64_t)blockIdx.x * size;
+    const float* dr = delta + (int64_t)blockIdx.x * size;
+    const bool staged = size <= kStageFloats;
+    for (int i = threadIdx.x; i < size; i += blockDim.x) {
+        const float v = __fadd_rn(xr[i], dr[i]);
+        xr[i] = v;
+        if (staged) stage[i] = v;
+    }
+    __syncthreads();  // the row's sums are visible to warp 0
+    const float* v = staged ? stage : xr;
+    if (threadIdx.x < 32) {
+        const float ss = sumsq_ref(v, size);
+        if (threadIdx.x == 0) s_scale = rms_scale(ss, size, eps);
+    }
+    __syncthreads();
+    apply_zc<true>(v, w, y + (int64_t)blockIdx.x * size, s_scale, size);
 }
 
 // One CTA per row: residual += delta (stored), then out = rms_norm(residual).
@@ -147,6 +181,7 @@ __global__ void __launch_bounds__(kThreads) add_rms_norm_kernel(float* res, cons
 // a = (x / (1 + exp(-x))) * b with exp evaluated in double and rounded once.
 __global__ void __launch_bounds__(kThreads) silu_mul_kernel(float* __restrict__ a, const float* __restrict__ b,
                                                             int64_t n) {
+    pdl_launch_dependents();
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
         const float x = a[i];
         const float e = (float)exp(-(double)x);
@@ -570,6 +605,13 @@ cudaError_t launch_rms_norm_strided(const float* x, const float* w, float* y, in
     return cudaGetLastError();
 }
 
+cudaError_t launch_add_then_rms_norm(float* x, const float* delta, const float* w, float* y, int rows, int size,
+                                     float eps, cudaStream_t stream) {
+    const size_t smem = size <= kStageFloats ? (size_t)size * sizeof(float) : 0;
+    add_then_rms_norm_kernel<<<rows, kThreads, smem, stream>>>(x, delta, w, y, size, eps);
+    return cudaGetLastError();
+}
+
 // Position-from-device forms for a decode step that is captured once and
 // replayed at every position (same kernels and arithmetic as the C ABI's).
 cudaError_t launch_conv1d_dev(const float* input, float* state, const int* d_oldest, const float* weight_t,
@@ -707,6 +749,14 @@ int qlm_gdn_gates(const float* a_raw, const float* b_raw, const float* A_log, co
     qlm::gdn_gates_kernel<<<(heads + 127) / 128, 128, 0, static_cast<cudaStream_t>(stream)>>>(
         a_raw, b_raw, A_log, dt_bias, decay, beta, heads, heads);
     return launched("gdn_gates launch");
+}
+
+int qlm_add_then_rms_norm(float* residual, const float* delta, const float* w, float* out, int rows, int size,
+                          float eps, void* stream) {
+    if (!residual || !delta || !w || !out) return layer_fail(QLM_ERR_INVALID_ARG, "NULL argument");
+    if (rows <= 0 || size <= 0) return layer_fail(QLM_ERR_INVALID_ARG, "rows and size must be positive");
+    qlm::launch_add_then_rms_norm(residual, delta, w, out, rows, size, eps, static_cast<cudaStream_t>(stream));
+    return launched("add_then_rms_norm launch");
 }
 
 int qlm_add_rms_norm(float* residual, const float* delta, const float* w, float* out, int rows, int size, float eps,

@@ -122,15 +122,13 @@ __global__ void __launch_bounds__(1024) greedy_rows_kernel(const float* __restri
     }
 }
 
-// x[i] += d[i] (math::elementwise_add, one rounding per element).
-__global__ void add_kernel(float* __restrict__ x, const float* __restrict__ d, int n) {
-    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) x[i] = __fadd_rn(x[i], d[i]);
-}
-
 // The gated attention's output gate (src/model/attention.cpp:216-226):
 // out[h][d] *= 1 / (1 + exp(-gate[h][d])), gate = q[h][head_dim + d] of the
 // [query | gate] projection; exp in double, rounded once.
+// Precedes o_proj's GEMV: lets it start its weight copies at once (see
+// rms_norm_kernel).
 __global__ void sigmoid_gate_kernel(float* __restrict__ out, const float* __restrict__ q, int heads, int head_dim) {
+    qlm::pdl_launch_dependents();
     const int n = heads * head_dim;
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
         const int h = i / head_dim, d = i - h * head_dim;
@@ -669,11 +667,6 @@ int attn_step(qlm_model* m, Layer& ly) {
     return qlm_linear_int8(att, B, nh * hd, nh * hd, ly.o, m->t5, H, 0, s);                 // 7. o_proj
 }
 
-int add_into(qlm_model* m, float* x, const float* d, int n) {
-    add_kernel<<<(n + kEmbThreads - 1) / kEmbThreads, kEmbThreads, 0, m->stream>>>(x, d, n);
-    return launch_ok("residual add");
-}
-
 }  // namespace
 
 namespace {
@@ -691,20 +684,26 @@ int enqueue_step(qlm_model* m) {
     embed_rows_kernel<<<dim3((H + kEmbThreads - 1) / kEmbThreads, B), kEmbThreads, 0, s>>>(m->embed, m->embed_bf16,
                                                                                            m->d_tokens, H, m->x);
     QLM_TRY(launch_ok("embedding"));
-    for (Layer& ly : m->layers) {
-        QLM_TRY(qlm_rms_norm(m->x, ly.in_norm, m->h, B, H, m->eps, s));
+    // Each residual add is fused with the norm that follows it (post-attention
+    // norm, the next layer's input norm, the final norm): same bits as
+    // elementwise_add + rms_norm (modules.hpp:228-231, 239-240).
+    const size_t nl = m->layers.size();
+    QLM_TRY(qlm_rms_norm(m->x, nl ? m->layers[0].in_norm : m->final_norm, m->h, B, H, m->eps, s));
+    for (size_t l = 0; l < nl; ++l) {
+        Layer& ly = m->layers[l];
         QLM_TRY(ly.full_attn ? attn_step(m, ly) : gdn_step(m, ly));
-        QLM_TRY(add_into(m, m->x, m->t5, B * H));
-        QLM_TRY(qlm_rms_norm(m->x, ly.post_norm, m->h, B, H, m->eps, s));
+        if (qlm::launch_add_then_rms_norm(m->x, m->t5, ly.post_norm, m->h, B, H, m->eps, s) != cudaSuccess)
+            return launch_ok("residual add + post-attention norm");
         const qlm_w8* ws[2] = {ly.gate, ly.up};
         float* ys[2] = {m->gate_buf, m->up_buf};
         const int64_t lds[2] = {m->inter, m->inter};
         QLM_TRY(qlm_linear_int8_grouped(m->h, B, H, H, ws, 2, ys, lds, 0, s));
         QLM_TRY(qlm_silu_mul(m->gate_buf, m->up_buf, (int64_t)B * m->inter, s));
         QLM_TRY(qlm_linear_int8(m->gate_buf, B, m->inter, m->inter, ly.down, m->t5, H, 0, s));
-        QLM_TRY(add_into(m, m->x, m->t5, B * H));
+        const float* next_norm = l + 1 < nl ? m->layers[l + 1].in_norm : m->final_norm;
+        if (qlm::launch_add_then_rms_norm(m->x, m->t5, next_norm, m->h, B, H, m->eps, s) != cudaSuccess)
+            return launch_ok("residual add + norm");
     }
-    QLM_TRY(qlm_rms_norm(m->x, m->final_norm, m->h, B, H, m->eps, s));
     QLM_TRY(qlm_linear_int8(m->h, B, H, H, m->lm_head, m->logits, m->vocab, 0, s));
     greedy_rows_kernel<<<B, 1024, 0, s>>>(m->logits, m->vocab, m->d_tokens);
     QLM_TRY(launch_ok("greedy choice"));

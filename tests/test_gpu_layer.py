@@ -68,6 +68,26 @@ def test_add_rms_norm_bit_exact(q, refcpu, size, rows, special):
     assert bits_equal(o.cpu().numpy(), o_ref)
 
 
+@pytest.mark.parametrize("size", SIZES)
+@pytest.mark.parametrize("rows", [1, 5])
+@pytest.mark.parametrize("special", [None, "scaled", "nan"])
+def test_add_then_rms_norm_bit_exact(q, refcpu, size, rows, special):
+    """elementwise_add then math::rms_norm (the decoder layer's default
+    residual step), fused in one launch: the reference's two calls' bits."""
+    import torch
+    rng = np.random.default_rng(size * 13 + rows)
+    r = _rows(rng, rows, size, special)
+    d = rng.standard_normal((rows, size)).astype(np.float32)
+    w = (rng.standard_normal(size) * 0.1).astype(np.float32)
+    eps = 1e-6
+    s_ref = r + d  # IEEE single-precision add, as math::elementwise_add
+    o_ref = refcpu.rms_norm(s_ref, w, eps)
+    rd = torch.from_numpy(r).cuda()
+    o = q.add_then_rms_norm(rd, torch.from_numpy(d).cuda(), torch.from_numpy(w).cuda(), eps)
+    assert bits_equal(rd.cpu().numpy(), s_ref)
+    assert bits_equal(o.cpu().numpy(), o_ref)
+
+
 def _ulp_diff(a, b):
     ai = a.view(np.int32).astype(np.int64)
     bi = b.view(np.int32).astype(np.int64)
