@@ -603,15 +603,15 @@ bool gemv_supported(int mm, int rows, int k, int sm_count, bool q4) {
 
 namespace {
 
-// QLM_GEMV_DECODE=0 selects the single-role kernel for every M = 1 launch
-// (for comparisons); by default the producer/consumer form takes the small
-// matrices (below).
-bool decode_form_enabled() {
-    static const bool on = [] {
+// QLM_GEMV_DECODE=0 selects the single-role kernel for every M = 1 launch,
+// =2 the producer/consumer form wherever its plan fits (for comparisons); by
+// default the producer/consumer form takes the small matrices (below).
+int decode_form_mode() {
+    static const int mode = [] {
         const char* e = std::getenv("QLM_GEMV_DECODE");
-        return !(e && e[0] == '0');
+        return e && e[0] == '0' ? 0 : e && e[0] == '2' ? 2 : 1;
     }();
-    return on;
+    return mode;
 }
 
 template <bool Q4>
@@ -646,7 +646,8 @@ cudaError_t launch_gemv_grouped(const float* x, int64_t ldx, int mm, const GemvW
     // [2560,9728] 12.0 vs 16.1 us, [1024,3584] 3.6 vs 7.0 us, while from ~40 rows
     // per SM the single-role kernel is faster (config 1 [6144,2048] 5.6 vs
     // 6.9 us, lm_head [151936,2560] 76 vs 107 us).
-    if (mm == 1 && !gather && decode_form_enabled() && rows_total < 32 * sm_count &&
+    const int dmode = decode_form_mode();
+    if (mm == 1 && !gather && dmode != 0 && (dmode == 2 || rows_total < 32 * sm_count) &&
         gemv_decode_supported(rows_total, nw, k, sm_count, q4))
         return launch_gemv_decode(x, ws, nw, k, status, sm_count, stream, pdl, q4);
     const int r = pick_rows_per_thread(mm, rows_total, sm_count);
