@@ -121,16 +121,6 @@ bool gemv_decode_supported(int rows_total, int nw, int k, int sm_count, bool q4)
 cudaError_t launch_gemv_decode(const float* x, const GemvWeight* ws, int nw, int k, int* status, int sm_count,
                                cudaStream_t stream, bool pdl, bool q4);
 
-// math::rms_norm (zero-centred gain) on rows of `size` floats spaced `ld` apart
-// (qlm_layer.cu).
-cudaError_t launch_rms_norm_strided(const float* x, const float* w, float* y, int rows, int size, int64_t ld,
-                                    float eps, cudaStream_t stream);
-
-// The gated-delta-net gates of qlm_gdn_gates for `heads` heads of several
-// sequences in a row, A_log / dt_bias repeating every `per` heads (qlm_layer.cu).
-cudaError_t launch_gdn_gates(const float* a_raw, const float* b_raw, const float* A_log, const float* dt_bias,
-                             float* decay, float* beta, int heads, int per, cudaStream_t stream);
-
 // x += delta (stored), then y = rms_norm(x) with rms_norm's own accumulation
 // order (zero-centred gain): the decoder layer's unfused residual add and the
 // next norm in one launch, bit-identical to the two (qlm_layer.cu).
@@ -142,17 +132,40 @@ cudaError_t launch_add_then_rms_norm(float* x, const float* delta, const float* 
 // (qlm_layer.cu). launch_gqa_attend_dev: the three-launch attention with grids
 // and shared memory sized for positions up to max_pos; scratch holds
 // heads * (max_pos + 1) floats; gqa_v_kernel takes gqa_dev_smem_bytes(max_pos)
-// of shared memory (at most 200 KB).
-cudaError_t launch_conv1d_dev(const float* input, float* state, const int* d_oldest, const float* weight_t,
-                              float* output, int conv_dim, int kernel_size, cudaStream_t stream);
-cudaError_t launch_rope_dev(float* t, int heads, int head_dim, int rotary_dim, const float* cos_all,
-                            const float* sin_all, const int* d_pos, cudaStream_t stream);
-cudaError_t launch_kv_append(const float* k, const float* v, float* k_cache, float* v_cache, const int* d_pos,
-                             int row, cudaStream_t stream);
+// of shared memory (at most 200 KB); gate (optional, row stride gate_ld): the
+// sigmoid output gate applied to each output in the same launch.
+// The conv step followed by SiLU on every output channel, in one launch.
+cudaError_t launch_conv1d_silu_dev(const float* input, float* state, const int* d_oldest, const float* weight_t,
+                                   float* output, int conv_dim, int kernel_size, cudaStream_t stream);
+// Partial NeoX RoPE of nq query heads (in place, head stride q_ld) and nk key
+// heads at position *d_pos, the rotated keys and the values written to row
+// *d_pos of the caches ([T][nk * head_dim]); one launch, the arithmetic of
+// the separate RoPE and append.
+cudaError_t launch_rope_append(float* q, int q_ld, int nq, const float* k, const float* v, int nk, int head_dim,
+                               int rotary_dim, const float* cos_all, const float* sin_all, const int* d_pos,
+                               float* k_cache, float* v_cache, cudaStream_t stream);
+// The attention's q and k head norms (zero-centred gain) in one launch, in
+// place: nq query rows of stride q_ld with wq, nk key rows of stride k_ld with
+// wk; bit-identical to the two separate rms_norm launches.
+cudaError_t launch_qk_norm(float* q, int q_ld, const float* wq, int nq, float* k, int k_ld, const float* wk, int nk,
+                           int size, float eps, cudaStream_t stream);
+// Per head row: o = rms_norm with plain gain w (not stored), then
+// z = silu(z) * o — the gated-delta-net's head norm and output gate in one
+// launch, bit-identical to qlm_rms_norm_gain + qlm_silu_mul.
+cudaError_t launch_head_norm_gate(const float* x, const float* w, float* z, int rows, int size, float eps,
+                                  cudaStream_t stream);
+// The delta-rule recurrence with the gates step folded in: each head's decay
+// and beta computed in the recurrence's CTAs from the raw gate inputs, the
+// parameters repeating every `per` heads (same arithmetic as the separate
+// gates kernel).
+cudaError_t launch_gdn_recurrence_gates(float* state, const float* q, const float* k, const float* v,
+                                        const float* a_raw, const float* b_raw, const float* A_log,
+                                        const float* dt_bias, int per, float* out, int heads, int head_dim,
+                                        cudaStream_t stream);
 size_t gqa_dev_smem_bytes(int max_pos);
 cudaError_t launch_gqa_attend_dev(const float* q, int q_stride, const float* k_cache, const float* v_cache,
                                   float* out, const int* d_pos, int max_pos, int heads, int kv_heads, int head_dim,
-                                  float* scratch, cudaStream_t stream);
+                                  float* scratch, const float* gate, int gate_ld, cudaStream_t stream);
 
 // Bit-exact y[m][0:rows] = x[m][0:k] . W^T for 2 <= M <= 64 activation rows
 // in one launch that streams W once (qlm_gemm_exact.cu): a pre-pass writes the

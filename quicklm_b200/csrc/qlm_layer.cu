@@ -154,6 +154,61 @@ __global__ void __launch_bounds__(kThreads) add_then_rms_norm_kernel(float* x, c
     apply_zc<true>(v, w, y + (int64_t)blockIdx.x * size, s_scale, size);
 }
 
+// The gated attention's QK-norm (attention.cpp:166-178) in one launch: CTA r
+// < nq normalizes query head r (row stride q_ld, the query half of each
+// [query | gate] row) with wq, the others key head r - nq (row stride k_ld)
+// with wk; rms_norm_kernel<true>'s arithmetic, in place.
+__global__ void __launch_bounds__(kThreads) qk_norm_kernel(float* q, int q_ld, const float* __restrict__ wq,
+                                                           float* k, int k_ld, const float* __restrict__ wk, int nq,
+                                                           int size, float eps) {
+    extern __shared__ float stage[];
+    __shared__ float s_scale;
+    const bool isq = (int)blockIdx.x < nq;
+    float* xr = isq ? q + (int64_t)blockIdx.x * q_ld : k + (int64_t)(blockIdx.x - nq) * k_ld;
+    const float* w = isq ? wq : wk;
+    const float* src = xr;
+    if (size <= kStageFloats) {
+        for (int i = threadIdx.x; i < size; i += blockDim.x) stage[i] = xr[i];
+        __syncthreads();
+        src = stage;
+    }
+    if (threadIdx.x < 32) {
+        const float ss = sumsq_ref(src, size);
+        if (threadIdx.x == 0) s_scale = rms_scale(ss, size, eps);
+    }
+    __syncthreads();
+    apply_zc<true>(src, w, xr, s_scale, size);
+}
+
+// Gated-delta-net steps 8-9 (attention.cpp:573-584) in one launch, one CTA per
+// head row: o = (x * s) * w with s from rms_norm's accumulation order (the
+// arithmetic of rms_norm_kernel<false>), then z = silu(z) * o (that of
+// silu_mul_kernel); o itself is not stored. Precedes out_proj's GEMV.
+__global__ void __launch_bounds__(kThreads) head_norm_gate_kernel(const float* x, const float* __restrict__ w,
+                                                                  float* __restrict__ z, int size, float eps) {
+    extern __shared__ float stage[];
+    __shared__ float s_scale;
+    pdl_launch_dependents();
+    const float* xr = x + (int64_t)blockIdx.x * size;
+    if (size <= kStageFloats) {
+        for (int i = threadIdx.x; i < size; i += blockDim.x) stage[i] = xr[i];
+        __syncthreads();
+        xr = stage;
+    }
+    if (threadIdx.x < 32) {
+        const float ss = sumsq_ref(xr, size);
+        if (threadIdx.x == 0) s_scale = rms_scale(ss, size, eps);
+    }
+    __syncthreads();
+    float* zr = z + (int64_t)blockIdx.x * size;
+    for (int i = threadIdx.x; i < size; i += blockDim.x) {
+        const float o = __fmul_rn(__fmul_rn(xr[i], s_scale), w[i]);
+        const float zx = zr[i];
+        const float e = (float)exp(-(double)zx);
+        zr[i] = __fmul_rn(__fdiv_rn(zx, __fadd_rn(1.0f, e)), o);
+    }
+}
+
 // One CTA per row: residual += delta (stored), then out = rms_norm(residual).
 __global__ void __launch_bounds__(kThreads) add_rms_norm_kernel(float* res, const float* __restrict__ delta,
                                                                 const float* __restrict__ w, float* out, int size,
@@ -202,7 +257,10 @@ __global__ void __launch_bounds__(kThreads) silu_kernel(float* __restrict__ x, i
 // out[c] = (((0 + s_0 w_0) + s_1 w_1) + ...) + in w_last, products and sums
 // rounded separately; the oldest row then takes the input. One thread per channel.
 // d_oldest: when set, the ring position is read from device memory (a
-// captured decode step replays at every position).
+// captured decode step replays at every position). SILU: the output then goes
+// through silu_kernel's arithmetic (the gated-delta-net's next step,
+// attention.cpp:452-457) in the same launch.
+template <bool SILU>
 __global__ void __launch_bounds__(kThreads) conv1d_tapmajor_kernel(const float* __restrict__ in, float* state,
                                                                    int oldest, const int* __restrict__ d_oldest,
                                                                    const float* __restrict__ wt,
@@ -216,7 +274,9 @@ __global__ void __launch_bounds__(kThreads) conv1d_tapmajor_kernel(const float* 
         sum = __fadd_rn(sum, __fmul_rn(state[(int64_t)row * conv_dim + c], wt[(int64_t)j * conv_dim + c]));
     }
     const float x = in[c];
-    out[c] = __fadd_rn(sum, __fmul_rn(x, wt[(int64_t)ntaps * conv_dim + c]));
+    float y = __fadd_rn(sum, __fmul_rn(x, wt[(int64_t)ntaps * conv_dim + c]));
+    if (SILU) y = __fdiv_rn(y, __fadd_rn(1.0f, (float)exp(-(double)y)));
+    out[c] = y;
     state[(int64_t)oldest * conv_dim + c] = x;
 }
 
@@ -231,6 +291,19 @@ __global__ void __launch_bounds__(kThreads) l2norm_heads_kernel(float* x, int he
     for (int i = threadIdx.x & 31; i < head_dim; i += 32) xh[i] = __fdiv_rn(xh[i], n);
 }
 
+// The gated-delta-net gates of one head (attention.cpp:472-482): softplus,
+// decay = exp(-exp(A_log) * softplus), beta = sigmoid(b); each libm call
+// evaluated in double and rounded once, as a correctly rounded float function
+// would. Shared by gdn_gates_kernel and the recurrence that folds it in.
+__device__ __forceinline__ void gdn_gate(float a_raw, float b_raw, float A_log, float dt_bias, float& dec,
+                                         float& beta) {
+    const float dt_in = __fadd_rn(a_raw, dt_bias);
+    const float sp = dt_in > 20.0f ? dt_in : (float)log1p((double)(float)exp((double)dt_in));
+    const float alpha = __fmul_rn(-(float)exp((double)A_log), sp);
+    dec = (float)exp((double)alpha);
+    beta = __fdiv_rn(1.0f, __fadd_rn(1.0f, (float)exp(-(double)b_raw)));
+}
+
 // The delta-rule recurrence; CTA (head h, block of 32 state columns), one
 // thread per column j: S = dec * S; kv = k . S; S += (beta k) outer (v - kv);
 // out = (q . S) / sqrt(d). The reference's 8-wide body (j < d - d % 8) uses
@@ -239,12 +312,18 @@ __global__ void __launch_bounds__(kThreads) l2norm_heads_kernel(float* x, int he
 // touch only that column, so fusing the update and output passes changes no
 // rounding. The CTA's [d][32] slice of the state is loaded into shared memory
 // with independent coalesced loads (128 bytes per row), updated there, and
-// written back.
+// written back. GATES: the head's decay and beta are computed here from the
+// raw gate inputs (gdn_gate, parameters repeating every `per` heads) instead
+// of being read from dec / beta — the gates step folded into this launch.
+template <bool GATES>
 __global__ void __launch_bounds__(32) gdn_recurrence_kernel(float* __restrict__ state, const float* __restrict__ q,
                                                             const float* __restrict__ k, const float* __restrict__ v,
                                                             const float* __restrict__ dec,
                                                             const float* __restrict__ beta, float* __restrict__ out,
-                                                            int d) {
+                                                            int d, const float* __restrict__ a_raw,
+                                                            const float* __restrict__ b_raw,
+                                                            const float* __restrict__ A_log,
+                                                            const float* __restrict__ dt_bias, int per) {
     extern __shared__ float sh[];  // q_h [d], k_h [d], slice [d][32]
     const int h = blockIdx.x, lane = threadIdx.x, j = blockIdx.y * 32 + lane;
     float* qs = sh;
@@ -261,7 +340,13 @@ __global__ void __launch_bounds__(32) gdn_recurrence_kernel(float* __restrict__ 
     __syncwarp();
     if (live) {
         const bool body = j < d - d % 8;
-        const float dh = dec[h], bh = beta[h];
+        float dh, bh;
+        if (GATES) {
+            gdn_gate(a_raw[h], b_raw[h], A_log[h % per], dt_bias[h % per], dh, bh);
+        } else {
+            dh = dec[h];
+            bh = beta[h];
+        }
         float kv = 0.0f;
 #pragma unroll 8
         for (int i = 0; i < d; ++i) {
@@ -484,10 +569,15 @@ __global__ void __launch_bounds__(256) gqa_softmax_kernel(float* __restrict__ sc
 // V: CTA (head, block of 32 output elements), one warp; the head's weights are
 // staged in shared memory, then each lane accumulates its output element over
 // the positions in order.
+// gate: when set, each output is multiplied by the gated attention's sigmoid
+// output gate (attention.cpp:216-226) of its element, gate[h * gate_ld + i]
+// (exp in double, rounded once), so the gate needs no launch of its own.
 __global__ void __launch_bounds__(32) gqa_v_kernel(const float* __restrict__ probs, const float* __restrict__ vc,
                                                    float* __restrict__ out, int pos, const int* __restrict__ d_pos,
-                                                   int heads, int kv_heads, int d) {
+                                                   int heads, int kv_heads, int d, const float* __restrict__ gate,
+                                                   int gate_ld) {
     extern __shared__ float pr[];  // [pos + 1]
+    pdl_launch_dependents();  // usually precedes o_proj's GEMV (see rms_norm_kernel)
     if (d_pos) pos = *d_pos;
     const int h = blockIdx.x, lane = threadIdx.x;
     const int kv_size = kv_heads * d, off = (h / (heads / kv_heads)) * d;
@@ -513,6 +603,10 @@ __global__ void __launch_bounds__(32) gqa_v_kernel(const float* __restrict__ pro
                 o = body ? __fmaf_rn(w, vv[u], o) : __fadd_rn(o, __fmul_rn(w, vv[u]));
             }
     }
+    if (gate) {
+        const float e = (float)exp(-(double)gate[(int64_t)h * gate_ld + i]);
+        o = __fmul_rn(o, __fdiv_rn(1.0f, __fadd_rn(1.0f, e)));
+    }
     out[(int64_t)h * d + i] = o;
 }
 
@@ -525,24 +619,14 @@ __global__ void gdn_gates_kernel(const float* __restrict__ a_raw, const float* _
     const int h = blockIdx.x * blockDim.x + threadIdx.x;
     if (h >= heads) return;
     const int hp = h % per;
-    const float dt_in = __fadd_rn(a_raw[h], dt_bias[hp]);
-    const float sp = dt_in > 20.0f ? dt_in : (float)log1p((double)(float)exp((double)dt_in));
-    const float alpha = __fmul_rn(-(float)exp((double)A_log[hp]), sp);
-    dec[h] = (float)exp((double)alpha);
-    beta[h] = __fdiv_rn(1.0f, __fadd_rn(1.0f, (float)exp(-(double)b_raw[h])));
+    gdn_gate(a_raw[h], b_raw[h], A_log[hp], dt_bias[hp], dec[h], beta[h]);
 }
 
 // t [tokens][heads][head_dim]; cos/sin [tokens][rotary_dim / 2].
-// d_pos: when set, one token whose table row is *d_pos (the tables then hold
-// every position).
 __global__ void __launch_bounds__(kThreads) rope_neox_kernel(float* __restrict__ t, const float* __restrict__ ct,
                                                              const float* __restrict__ st, int heads, int head_dim,
-                                                             int half, const int* __restrict__ d_pos) {
+                                                             int half) {
     const int tok = blockIdx.y;
-    if (d_pos) {
-        ct += (int64_t)*d_pos * half;
-        st += (int64_t)*d_pos * half;
-    }
     const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (idx >= (int64_t)heads * half) return;
     const int h = (int)(idx / half), i = (int)(idx % half);
@@ -553,16 +637,51 @@ __global__ void __launch_bounds__(kThreads) rope_neox_kernel(float* __restrict__
     hd[i + half] = __fadd_rn(__fmul_rn(x2, c), __fmul_rn(x1, s));
 }
 
-// The decode token's keys and values into row *d_pos of the caches ([T][row]).
-__global__ void __launch_bounds__(kThreads) kv_append_kernel(const float* __restrict__ k, const float* __restrict__ v,
-                                                             float* __restrict__ kc, float* __restrict__ vc,
-                                                             const int* __restrict__ d_pos, int row) {
-    const int i = blockIdx.x * blockDim.x + threadIdx.x;
-    if (i >= row) return;
-    const int64_t o = (int64_t)*d_pos * row + i;
-    kc[o] = k[i];
-    vc[o] = v[i];
+// Steps 3-4 of the gated attention's decode (attention.cpp:183-187 RoPE,
+// 190-200 cache append) in one launch, at the position *d_pos: thread i <
+// nq * half rotates query pair i in place (rope_neox_kernel's arithmetic, head
+// stride q_ld); the next nk * head_dim threads each write one element of the
+// rotated keys straight into the key cache row (the rotated value of its
+// pair, or the element itself past rotary_dim), the last nk * head_dim copy
+// the values into the value cache. The keys themselves are not rewritten.
+__global__ void __launch_bounds__(kThreads) rope_append_kernel(float* __restrict__ q, int q_ld, int nq,
+                                                               const float* __restrict__ k,
+                                                               const float* __restrict__ v, int nk, int head_dim,
+                                                               int half, const float* __restrict__ cos_all,
+                                                               const float* __restrict__ sin_all,
+                                                               const int* __restrict__ d_pos, float* __restrict__ kc,
+                                                               float* __restrict__ vc) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    const int pos = *d_pos;
+    const float* ct = cos_all + (int64_t)pos * half;
+    const float* st = sin_all + (int64_t)pos * half;
+    const int64_t nqp = (int64_t)nq * half, nke = (int64_t)nk * head_dim;
+    if (i < nqp) {
+        const int h = (int)(i / half), e = (int)(i % half);
+        float* hd = q + (int64_t)h * q_ld;
+        const float c = ct[e], sn = st[e];
+        const float x1 = hd[e], x2 = hd[e + half];
+        hd[e] = __fsub_rn(__fmul_rn(x1, c), __fmul_rn(x2, sn));
+        hd[e + half] = __fadd_rn(__fmul_rn(x2, c), __fmul_rn(x1, sn));
+    } else if (i < nqp + nke) {
+        const int64_t j = i - nqp;
+        const int h = (int)(j / head_dim), e = (int)(j % head_dim);
+        const float* hd = k + (int64_t)h * head_dim;
+        float r;
+        if (e < half) {
+            r = __fsub_rn(__fmul_rn(hd[e], ct[e]), __fmul_rn(hd[e + half], st[e]));
+        } else if (e < 2 * half) {
+            r = __fadd_rn(__fmul_rn(hd[e], ct[e - half]), __fmul_rn(hd[e - half], st[e - half]));
+        } else {
+            r = hd[e];
+        }
+        kc[(int64_t)pos * nke + j] = r;
+    } else if (i < nqp + 2 * nke) {
+        const int64_t j = i - nqp - nke;
+        vc[(int64_t)pos * nke + j] = v[j];
+    }
 }
+
 
 }  // namespace
 }  // namespace qlm
@@ -588,23 +707,9 @@ int launched(const char* what) {
 }  // namespace
 
 namespace qlm {
-// The gated-delta-net gates for `heads` heads of several sequences in a row,
-// the per-head parameters (A_log, dt_bias) repeating every `per` heads.
-cudaError_t launch_gdn_gates(const float* a_raw, const float* b_raw, const float* A_log, const float* dt_bias,
-                             float* decay, float* beta, int heads, int per, cudaStream_t stream) {
-    gdn_gates_kernel<<<(heads + 127) / 128, 128, 0, stream>>>(a_raw, b_raw, A_log, dt_bias, decay, beta, heads, per);
-    return cudaGetLastError();
-}
 
 // math::rms_norm on `rows` rows of `size` floats spaced `ld` apart (in place
 // when x == y): the per-head QK-norm of a query laid out [query | gate].
-cudaError_t launch_rms_norm_strided(const float* x, const float* w, float* y, int rows, int size, int64_t ld,
-                                    float eps, cudaStream_t stream) {
-    const size_t smem = size <= kStageFloats ? (size_t)size * sizeof(float) : 0;
-    rms_norm_kernel<true><<<rows, kThreads, smem, stream>>>(x, w, y, size, eps, ld);
-    return cudaGetLastError();
-}
-
 cudaError_t launch_add_then_rms_norm(float* x, const float* delta, const float* w, float* y, int rows, int size,
                                      float eps, cudaStream_t stream) {
     const size_t smem = size <= kStageFloats ? (size_t)size * sizeof(float) : 0;
@@ -614,25 +719,57 @@ cudaError_t launch_add_then_rms_norm(float* x, const float* delta, const float* 
 
 // Position-from-device forms for a decode step that is captured once and
 // replayed at every position (same kernels and arithmetic as the C ABI's).
-cudaError_t launch_conv1d_dev(const float* input, float* state, const int* d_oldest, const float* weight_t,
-                              float* output, int conv_dim, int kernel_size, cudaStream_t stream) {
-    conv1d_tapmajor_kernel<<<(conv_dim + kThreads - 1) / kThreads, kThreads, 0, stream>>>(
+cudaError_t launch_conv1d_silu_dev(const float* input, float* state, const int* d_oldest, const float* weight_t,
+                                   float* output, int conv_dim, int kernel_size, cudaStream_t stream) {
+    conv1d_tapmajor_kernel<true><<<(conv_dim + kThreads - 1) / kThreads, kThreads, 0, stream>>>(
         input, state, 0, d_oldest, weight_t, output, conv_dim, kernel_size - 1);
     return cudaGetLastError();
 }
 
-cudaError_t launch_rope_dev(float* t, int heads, int head_dim, int rotary_dim, const float* cos_all,
-                            const float* sin_all, const int* d_pos, cudaStream_t stream) {
+cudaError_t launch_rope_append(float* q, int q_ld, int nq, const float* k, const float* v, int nk, int head_dim,
+                               int rotary_dim, const float* cos_all, const float* sin_all, const int* d_pos,
+                               float* k_cache, float* v_cache, cudaStream_t stream) {
     const int half = rotary_dim / 2;
-    const int64_t n = (int64_t)heads * half;
-    rope_neox_kernel<<<dim3((unsigned)((n + kThreads - 1) / kThreads), 1), kThreads, 0, stream>>>(
-        t, cos_all, sin_all, heads, head_dim, half, d_pos);
+    const int64_t n = (int64_t)nq * half + 2 * (int64_t)nk * head_dim;
+    rope_append_kernel<<<(unsigned)((n + kThreads - 1) / kThreads), kThreads, 0, stream>>>(
+        q, q_ld, nq, k, v, nk, head_dim, half, cos_all, sin_all, d_pos, k_cache, v_cache);
     return cudaGetLastError();
 }
 
-cudaError_t launch_kv_append(const float* k, const float* v, float* k_cache, float* v_cache, const int* d_pos,
-                             int row, cudaStream_t stream) {
-    kv_append_kernel<<<(row + kThreads - 1) / kThreads, kThreads, 0, stream>>>(k, v, k_cache, v_cache, d_pos, row);
+cudaError_t launch_qk_norm(float* q, int q_ld, const float* wq, int nq, float* k, int k_ld, const float* wk, int nk,
+                           int size, float eps, cudaStream_t stream) {
+    const size_t smem = size <= kStageFloats ? (size_t)size * sizeof(float) : 0;
+    qk_norm_kernel<<<nq + nk, kThreads, smem, stream>>>(q, q_ld, wq, k, k_ld, wk, nq, size, eps);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_head_norm_gate(const float* x, const float* w, float* z, int rows, int size, float eps,
+                                  cudaStream_t stream) {
+    const size_t smem = size <= kStageFloats ? (size_t)size * sizeof(float) : 0;
+    head_norm_gate_kernel<<<rows, kThreads, smem, stream>>>(x, w, z, size, eps);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_gdn_recurrence_gates(float* state, const float* q, const float* k, const float* v,
+                                        const float* a_raw, const float* b_raw, const float* A_log,
+                                        const float* dt_bias, int per, float* out, int heads, int head_dim,
+                                        cudaStream_t stream) {
+    if (heads <= 0 || head_dim <= 0 || head_dim > 1024 || per <= 0) return cudaErrorInvalidValue;
+    static bool attr_set[64] = {};
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+    if (!attr_set[dev]) {
+        if ((e = cudaFuncSetAttribute(gdn_recurrence_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      (2 + 32) * 1024 * (int)sizeof(float))) != cudaSuccess)
+            return e;
+        attr_set[dev] = true;
+    }
+    const dim3 grid((unsigned)heads, (unsigned)((head_dim + 31) / 32));
+    const size_t smem = (size_t)(2 + 32) * head_dim * sizeof(float);
+    gdn_recurrence_kernel<true><<<grid, 32, smem, stream>>>(state, q, k, v, nullptr, nullptr, out, head_dim, a_raw,
+                                                            b_raw, A_log, dt_bias, per);
     return cudaGetLastError();
 }
 
@@ -640,7 +777,7 @@ size_t gqa_dev_smem_bytes(int max_pos) { return (size_t)(max_pos + 1) * sizeof(f
 
 cudaError_t launch_gqa_attend_dev(const float* q, int q_stride, const float* k_cache, const float* v_cache,
                                   float* out, const int* d_pos, int max_pos, int heads, int kv_heads, int head_dim,
-                                  float* scratch, cudaStream_t stream) {
+                                  float* scratch, const float* gate, int gate_ld, cudaStream_t stream) {
     static bool attr_set[64] = {};
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
@@ -660,7 +797,7 @@ cudaError_t launch_gqa_attend_dev(const float* q, int q_stride, const float* k_c
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
     const dim3 g2((unsigned)heads, (unsigned)((head_dim + 31) / 32));
     gqa_v_kernel<<<g2, 32, gqa_dev_smem_bytes(max_pos), stream>>>(scratch, v_cache, out, 0, d_pos, heads, kv_heads,
-                                                                  head_dim);
+                                                                  head_dim, gate, gate_ld);
     return cudaGetLastError();
 }
 }  // namespace qlm
@@ -694,13 +831,13 @@ int qlm_gdn_recurrence(float* state, const float* q, const float* k, const float
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return layer_fail(QLM_ERR_CUDA, "cudaGetDevice");
     if (!attr_set[dev]) {
-        if (cudaFuncSetAttribute(qlm::gdn_recurrence_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        if (cudaFuncSetAttribute(qlm::gdn_recurrence_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  (2 + 32) * 1024 * (int)sizeof(float)) != cudaSuccess)
             return launched("gdn_recurrence attribute");
         attr_set[dev] = true;
     }
-    qlm::gdn_recurrence_kernel<<<grid, 32, smem, static_cast<cudaStream_t>(stream)>>>(state, q, k, v, decay, beta,
-                                                                                     out, head_dim);
+    qlm::gdn_recurrence_kernel<false><<<grid, 32, smem, static_cast<cudaStream_t>(stream)>>>(
+        state, q, k, v, decay, beta, out, head_dim, nullptr, nullptr, nullptr, nullptr, 1);
     return launched("gdn_recurrence launch");
 }
 
@@ -738,7 +875,7 @@ int qlm_gqa_attend(const float* q, int q_stride, const float* k_cache, const flo
     if ((rc = launched("gqa_softmax launch"))) return rc;
     const dim3 g2((unsigned)heads, (unsigned)((head_dim + 31) / 32));
     qlm::gqa_v_kernel<<<g2, 32, (size_t)(pos + 1) * sizeof(float), s>>>(scratch, v_cache, out, pos, nullptr, heads,
-                                                                        kv_heads, head_dim);
+                                                                        kv_heads, head_dim, nullptr, 0);
     return launched("gqa_v launch");
 }
 
@@ -788,8 +925,7 @@ int qlm_rope_neox(float* t, int num_tokens, int num_heads, int head_dim, int rot
     const int64_t per_tok = (int64_t)num_heads * half;
     const dim3 grid((unsigned)((per_tok + qlm::kThreads - 1) / qlm::kThreads), (unsigned)num_tokens);
     qlm::rope_neox_kernel<<<grid, qlm::kThreads, 0, static_cast<cudaStream_t>(stream)>>>(t, cos_tab, sin_tab,
-                                                                                       num_heads, head_dim, half,
-                                                                                       nullptr);
+                                                                                       num_heads, head_dim, half);
     return launched("rope_neox launch");
 }
 
@@ -807,7 +943,7 @@ int qlm_conv1d_update_tapmajor(const float* input, float* state, int oldest_tap,
     if (!input || !state || !weight_t || !output) return layer_fail(QLM_ERR_INVALID_ARG, "NULL argument");
     if (conv_dim <= 0 || kernel_size < 2 || oldest_tap < 0 || oldest_tap >= kernel_size - 1)
         return layer_fail(QLM_ERR_INVALID_ARG, "bad conv1d shape or ring position");
-    qlm::conv1d_tapmajor_kernel<<<(conv_dim + qlm::kThreads - 1) / qlm::kThreads, qlm::kThreads, 0,
+    qlm::conv1d_tapmajor_kernel<false><<<(conv_dim + qlm::kThreads - 1) / qlm::kThreads, qlm::kThreads, 0,
                                   static_cast<cudaStream_t>(stream)>>>(input, state, oldest_tap, nullptr, weight_t,
                                                                        output, conv_dim, kernel_size - 1);
     return launched("conv1d launch");

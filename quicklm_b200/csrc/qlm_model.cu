@@ -122,22 +122,6 @@ __global__ void __launch_bounds__(1024) greedy_rows_kernel(const float* __restri
     }
 }
 
-// The gated attention's output gate (src/model/attention.cpp:216-226):
-// out[h][d] *= 1 / (1 + exp(-gate[h][d])), gate = q[h][head_dim + d] of the
-// [query | gate] projection; exp in double, rounded once.
-// Precedes o_proj's GEMV: lets it start its weight copies at once (see
-// rms_norm_kernel).
-__global__ void sigmoid_gate_kernel(float* __restrict__ out, const float* __restrict__ q, int heads, int head_dim) {
-    qlm::pdl_launch_dependents();
-    const int n = heads * head_dim;
-    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
-        const int h = i / head_dim, d = i - h * head_dim;
-        const float g = q[(int64_t)h * 2 * head_dim + head_dim + d];
-        const float e = (float)exp(-(double)g);
-        out[i] = __fmul_rn(out[i], __fdiv_rn(1.0f, __fadd_rn(1.0f, e)));
-    }
-}
-
 int fail(int code, const char* fmt, ...) {
     char buf[512];
     va_list ap;
@@ -187,7 +171,6 @@ struct qlm_model {
     // activations and scratch (device)
     float *x = nullptr, *h = nullptr, *t1 = nullptr, *t2 = nullptr, *t3 = nullptr, *t4 = nullptr, *t5 = nullptr;
     float *gate_buf = nullptr, *up_buf = nullptr, *logits = nullptr, *scores = nullptr;
-    float *decay = nullptr, *beta = nullptr;
     // The step's control words [B tokens][position][conv ring position],
     // uploaded with one copy; the greedy choices come back in the token words.
     int* d_tokens = nullptr;  // device [B + 2]
@@ -568,8 +551,6 @@ int load_all(const std::string& dir, qlm_model* m) {
     QLM_TRY(L.zeros(&m->up_buf, B * m->inter));
     QLM_TRY(L.zeros(&m->logits, B * m->vocab));
     QLM_TRY(L.zeros(&m->scores, B * m->heads * m->max_seq));
-    QLM_TRY(L.zeros(&m->decay, B * m->lin_heads + 1));
-    QLM_TRY(L.zeros(&m->beta, B * m->lin_heads + 1));
     QLM_TRY(L.zeros(&m->d_tokens, B + 2));
     if (cudaMallocHost(reinterpret_cast<void**>(&m->h_tokens), (B + 2) * sizeof(int)) != cudaSuccess)
         return fail(QLM_ERR_OUT_OF_MEMORY, "pinned host words");
@@ -618,19 +599,17 @@ int gdn_step(qlm_model* m, Layer& ly) {
     float* ys[6] = {qkv, qkv + (size_t)B * lin, qkv + (size_t)2 * B * lin, z, b_raw, a_raw};
     const int64_t lds[6] = {lin, lin, lin, lin, lh, lh};
     QLM_TRY(qlm_linear_int8_grouped(m->h, B, H, H, ws, 6, ys, lds, 0, s));                      // 1. projections
-    if (qlm::launch_conv1d_dev(qkv, ly.conv_state, m->d_tokens + B + 1, ly.conv_wt, conv, channels, m->conv_kernel,
-                               s) != cudaSuccess)
-        return launch_ok("conv step");                                                            // 2. conv step
-    QLM_TRY(qlm_silu(conv, channels, s));                                                         // 4. SiLU
+    if (qlm::launch_conv1d_silu_dev(qkv, ly.conv_state, m->d_tokens + B + 1, ly.conv_wt, conv, channels,
+                                    m->conv_kernel, s) != cudaSuccess)
+        return launch_ok("conv step + SiLU");                                                     // 2.-4. conv, SiLU
     float *q = conv, *k = conv + (size_t)B * lin, *v = conv + (size_t)2 * B * lin;
-    QLM_TRY(qlm_l2norm_heads(q, B * lh, ld, 1e-6f, s));                                           // 5. L2 norms
-    QLM_TRY(qlm_l2norm_heads(k, B * lh, ld, 1e-6f, s));
-    if (qlm::launch_gdn_gates(a_raw, b_raw, ly.A_log, ly.dt_bias, m->decay, m->beta, B * lh, lh, s) != cudaSuccess)
-        return launch_ok("gates");                                                                // 6. gates
+    QLM_TRY(qlm_l2norm_heads(q, 2 * B * lh, ld, 1e-6f, s));  // 5. L2 norms: the k heads follow the q heads
     float* out = qkv;  // the projections are consumed
-    QLM_TRY(qlm_gdn_recurrence(ly.rstate, q, k, v, m->decay, m->beta, out, B * lh, ld, s));     // 7. delta rule
-    QLM_TRY(qlm_rms_norm_gain(out, ly.gdn_norm, out, B * lh, ld, 1e-6f, s));                     // 8. head norm
-    QLM_TRY(qlm_silu_mul(z, out, (int64_t)B * lin, s));                                           // 9. SiLU(z) * out
+    if (qlm::launch_gdn_recurrence_gates(ly.rstate, q, k, v, a_raw, b_raw, ly.A_log, ly.dt_bias, lh, out, B * lh, ld,
+                                         s) != cudaSuccess)
+        return launch_ok("gates + delta rule");                                                   // 6.-7.
+    if (qlm::launch_head_norm_gate(out, ly.gdn_norm, z, B * lh, ld, 1e-6f, s) != cudaSuccess)
+        return launch_ok("head norm + output gate");                                              // 8.-9.
     return qlm_linear_int8(z, B, lin, lin, ly.out, m->t5, H, 0, s);                               // 10. out_proj
 }
 
@@ -649,21 +628,15 @@ int attn_step(qlm_model* m, Layer& ly) {
     float* ys[3] = {q, k, v};
     const int64_t lds[3] = {(int64_t)nh * qd, kv, kv};
     QLM_TRY(qlm_linear_int8_grouped(m->h, B, H, H, ws, 3, ys, lds, 0, s));                // 1. projections
-    if (qlm::launch_rms_norm_strided(q, ly.q_norm, q, B * nh, hd, qd, 1e-6f, s) != cudaSuccess)  // 2. QK-norm
-        return launch_ok("QK-norm");
-    QLM_TRY(qlm_rms_norm(k, ly.k_norm, k, B * kvh, hd, 1e-6f, s));
-    const int* d_pos = m->d_tokens + B;                                                    // 3. partial RoPE
-    if (qlm::launch_rope_dev(k, B * kvh, hd, m->rotary_dim, m->rope_cos, m->rope_sin, d_pos, s) != cudaSuccess ||
-        qlm::launch_rope_dev(q, B * nh, qd, m->rotary_dim, m->rope_cos, m->rope_sin, d_pos, s) != cudaSuccess)
-        return launch_ok("RoPE");  // q: the query half of each [query | gate] row
-    if (qlm::launch_kv_append(k, v, ly.k_cache, ly.v_cache, d_pos, B * kv, s) != cudaSuccess)  // 4. cache
-        return launch_ok("KV cache write");
+    if (qlm::launch_qk_norm(q, qd, ly.q_norm, B * nh, k, hd, ly.k_norm, B * kvh, hd, 1e-6f, s) != cudaSuccess)
+        return launch_ok("QK-norm");                                                          // 2. QK-norm
+    const int* d_pos = m->d_tokens + B;  // q: the query half of each [query | gate] row
+    if (qlm::launch_rope_append(q, qd, B * nh, k, v, B * kvh, hd, m->rotary_dim, m->rope_cos, m->rope_sin, d_pos,
+                                ly.k_cache, ly.v_cache, s) != cudaSuccess)
+        return launch_ok("RoPE + KV cache write");                                           // 3.-4.
     if (qlm::launch_gqa_attend_dev(q, qd, ly.k_cache, ly.v_cache, att, d_pos, m->max_seq - 1, B * nh, B * kvh, hd,
-                                   m->scores, s) != cudaSuccess)                             // 5. attention
-        return launch_ok("attention");
-    const int n = B * nh * hd;
-    sigmoid_gate_kernel<<<(n + kEmbThreads - 1) / kEmbThreads, kEmbThreads, 0, s>>>(att, q, B * nh, hd);  // 6.
-    QLM_TRY(launch_ok("output gate"));
+                                   m->scores, q + hd, qd, s) != cudaSuccess)                 // 5.-6. attention,
+        return launch_ok("attention");                                                       // output gate
     return qlm_linear_int8(att, B, nh * hd, nh * hd, ly.o, m->t5, H, 0, s);                 // 7. o_proj
 }
 
