@@ -11,6 +11,7 @@
 #include "qlm_kernels.h"
 #include "qlm_prof.h"
 
+#include <chrono>
 #include <cstdarg>
 #include <cstdio>
 #include <cstdlib>
@@ -75,6 +76,7 @@ struct DeviceState {
     int* status = nullptr;   // device status word written by kernels on a timeout
     void* xpair = nullptr;   // exact small-M product: activations in its pair layout
     size_t xpair_cap = 0;
+    cudaEvent_t done = nullptr;  // HOST_IO: marks the end of a call's work on its stream
 };
 DeviceState g_dev[kMaxDevices];
 std::mutex g_dev_mu;
@@ -91,12 +93,61 @@ int device_state(int dev, DeviceState** out) {
         QLM_CUDA(cudaSetDevice(dev), "cudaSetDevice");
         cudaError_t e = cudaMalloc(&st.status, sizeof(int));
         if (e == cudaSuccess) e = cudaMemset(st.status, 0, sizeof(int));
+        if (e == cudaSuccess) e = cudaEventCreateWithFlags(&st.done, cudaEventDisableTiming);
         cudaSetDevice(prev);
         if (e != cudaSuccess) return cuda_err(e, "device status word");
         st.sm_count = sms;
     }
     *out = &st;
     return QLM_OK;
+}
+
+// QLM_HOSTIO_SPIN=0 makes synchronous host-buffer calls block in
+// cudaStreamSynchronize instead of polling their completion event (for
+// comparisons).
+bool hostio_spin() {
+    static const bool on = [] {
+        const char* e = std::getenv("QLM_HOSTIO_SPIN");
+        return !(e && e[0] == '0');
+    }();
+    return on;
+}
+
+// Device address of a pinned, mapped host buffer (nullptr for any other
+// memory). A small output of a synchronous host-buffer call is stored there by
+// the kernel itself, which saves a device-to-host copy and its dependency gap.
+float* mapped_host_ptr(void* p) {
+    cudaPointerAttributes a{};
+    if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+        cudaGetLastError();  // an unregistered pointer is an answer here, not an error
+        return nullptr;
+    }
+    return a.type == cudaMemoryTypeHost ? static_cast<float*>(a.devicePointer) : nullptr;
+}
+constexpr size_t kZeroCopyMaxBytes = 1 << 20;
+
+// Waits for the work queued on s so far. The synchronous host-buffer call
+// (math::matmul's contract) returns as soon as its copy-out lands: polling an
+// event avoids the wake-up latency of a blocking synchronisation, which is
+// several microseconds against a kernel of a few. After ~50 ms of polling it
+// falls back to the blocking wait, so a long queue costs no more CPU than that.
+cudaError_t wait_stream(cudaStream_t s, cudaEvent_t ev) {
+    if (!hostio_spin() || !ev) return cudaStreamSynchronize(s);
+    cudaError_t e = cudaEventRecord(ev, s);
+    if (e != cudaSuccess) return e;
+    const auto t0 = std::chrono::steady_clock::now();
+    for (;;) {
+        e = cudaEventQuery(ev);
+        if (e != cudaErrorNotReady) break;
+        if (std::chrono::steady_clock::now() - t0 > std::chrono::milliseconds(50)) {
+            e = cudaEventSynchronize(ev);
+            break;
+        }
+    }
+    // "not ready" is an answer, not an error: leave no trace of it for the
+    // launch checks that read the runtime's last error.
+    if (cudaPeekAtLastError() == cudaErrorNotReady) cudaGetLastError();
+    return e;
 }
 
 template <typename T>
@@ -482,17 +533,29 @@ int qlm_linear_int8(const float* x, int M, int k, int64_t ldx, const qlm_w8* w, 
     float* dy = y;
     int64_t dldx = ldx, dldy = ldy;
     const bool host_io = (flags & QLM_LINEAR_HOST_IO) != 0;
+    bool y_direct = false;
     if (host_io) {
         std::lock_guard<std::mutex> lk(g_dev_mu);
         if ((rc = ensure_buf(&st->x_buf, &st->x_cap, (size_t)M * k * sizeof(float)))) return rc;
         if ((rc = ensure_buf(&st->y_buf, &st->y_cap, (size_t)M * w->rows * sizeof(float)))) return rc;
-        QLM_CUDA(cudaMemcpy2DAsync(st->x_buf, (size_t)k * sizeof(float), x, (size_t)ldx * sizeof(float),
-                                   (size_t)k * sizeof(float), M, cudaMemcpyHostToDevice, s),
-                 "copy x to device");
+        if (ldx == k || M == 1)
+            QLM_CUDA(cudaMemcpyAsync(st->x_buf, x, (size_t)M * k * sizeof(float), cudaMemcpyHostToDevice, s),
+                     "copy x to device");
+        else
+            QLM_CUDA(cudaMemcpy2DAsync(st->x_buf, (size_t)k * sizeof(float), x, (size_t)ldx * sizeof(float),
+                                       (size_t)k * sizeof(float), M, cudaMemcpyHostToDevice, s),
+                     "copy x to device");
         dx = st->x_buf;
-        dy = st->y_buf;
         dldx = k;
-        dldy = w->rows;
+        float* my = (size_t)M * ldy * sizeof(float) <= kZeroCopyMaxBytes ? mapped_host_ptr(y) : nullptr;
+        if (my) {
+            dy = my;  // the kernel stores into the caller's pinned buffer
+            dldy = ldy;
+            y_direct = true;
+        } else {
+            dy = st->y_buf;
+            dldy = w->rows;
+        }
     }
     if (tensor) {
         QLM_CUDA(qlm::launch_gemm_tc(*w->maps, w->ew, w->rows, k, dx, dldx, M, st->x16, st->ea, dy, dldy, st->status,
@@ -525,14 +588,18 @@ int qlm_linear_int8(const float* x, int M, int k, int64_t ldx, const qlm_w8* w, 
                      "gemv launch");
         }
     }
-    if (host_io) {
-        QLM_CUDA(cudaMemcpy2DAsync(y, (size_t)ldy * sizeof(float), dy, (size_t)w->rows * sizeof(float),
-                                   (size_t)w->rows * sizeof(float), M, cudaMemcpyDeviceToHost, s),
-                 "copy y to host");
+    if (host_io && !y_direct) {
+        if (ldy == w->rows || M == 1)
+            QLM_CUDA(cudaMemcpyAsync(y, dy, (size_t)M * w->rows * sizeof(float), cudaMemcpyDeviceToHost, s),
+                     "copy y to host");
+        else
+            QLM_CUDA(cudaMemcpy2DAsync(y, (size_t)ldy * sizeof(float), dy, (size_t)w->rows * sizeof(float),
+                                       (size_t)w->rows * sizeof(float), M, cudaMemcpyDeviceToHost, s),
+                     "copy y to host");
     }
     prof.stop();
     if (host_io || (flags & QLM_LINEAR_SYNC)) {
-        QLM_CUDA(cudaStreamSynchronize(s), "stream synchronize");
+        QLM_CUDA(host_io ? wait_stream(s, st->done) : cudaStreamSynchronize(s), "stream synchronize");
         if (tensor || (flags & QLM_LINEAR_SYNC)) return qlm_device_status(w->device, 1);
     }
     return QLM_OK;
