@@ -126,6 +126,22 @@ float* mapped_host_ptr(void* p) {
 }
 constexpr size_t kZeroCopyMaxBytes = 1 << 20;
 
+// The input rows of a synchronous call from a pinned, mapped host buffer into
+// device memory, read by the device itself. It lets the GEMV that follows (a
+// programmatic-launch secondary) start at once, so the GEMV's weight copies
+// from HBM overlap the transfer of x; the GEMV reads x after its dependency
+// wait, when this kernel has completed.
+__global__ void __launch_bounds__(256) host_rows_in_kernel(const float* __restrict__ src, int64_t lds, int M, int k,
+                                                          float* __restrict__ dst) {
+    qlm::pdl_launch_dependents();
+    const int64_t n = (int64_t)M * k;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t m = i / k, c = i - m * k;
+        dst[i] = src[m * lds + c];
+    }
+}
+constexpr size_t kHostReadMaxBytes = 64 << 10;
+
 // Waits for the work queued on s so far. The synchronous host-buffer call
 // (math::matmul's contract) returns as soon as its copy-out lands: polling an
 // event avoids the wake-up latency of a blocking synchronisation, which is
@@ -538,7 +554,14 @@ int qlm_linear_int8(const float* x, int M, int k, int64_t ldx, const qlm_w8* w, 
         std::lock_guard<std::mutex> lk(g_dev_mu);
         if ((rc = ensure_buf(&st->x_buf, &st->x_cap, (size_t)M * k * sizeof(float)))) return rc;
         if ((rc = ensure_buf(&st->y_buf, &st->y_cap, (size_t)M * w->rows * sizeof(float)))) return rc;
-        if (ldx == k || M == 1)
+        const float* mx =
+            (size_t)M * k * sizeof(float) <= kHostReadMaxBytes ? mapped_host_ptr(const_cast<float*>(x)) : nullptr;
+        if (mx) {
+            const int64_t n = (int64_t)M * k;
+            // one element per thread: every read is in flight at once
+            host_rows_in_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(mx, ldx, M, k, st->x_buf);
+            QLM_CUDA(cudaGetLastError(), "read x from the pinned host buffer");
+        } else if (ldx == k || M == 1)
             QLM_CUDA(cudaMemcpyAsync(st->x_buf, x, (size_t)M * k * sizeof(float), cudaMemcpyHostToDevice, s),
                      "copy x to device");
         else
