@@ -459,9 +459,14 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__
 // by 2^ea[m] so the row's largest finite magnitude lands in [2^13, 2^14);
 // zeros past k. One CTA per row; each thread writes 8 consecutive positions
 // (16 bytes), reading their sources back from L1.
+// early: every row's CTA is resident from the start (few rows), so the GEMM
+// may launch at once: its set-up and first weight chunks then overlap this
+// kernel (it waits for x16 and ea before reading them). Otherwise the trigger
+// comes last, since an early GEMM CTA would hold an SM this grid still needs.
 __global__ void __launch_bounds__(256) act_to_f16_kernel(const float* __restrict__ x, int64_t ldx, int K, int k_pad,
-                                                         __half* __restrict__ x16, int* __restrict__ ea) {
+                                                         __half* __restrict__ x16, int* __restrict__ ea, int early) {
     __shared__ float red[8];
+    if (early) pdl_launch_dependents();
     pdl_wait();  // x comes from the previous kernel; x16/ea may still be read by the previous GEMM
     // x is read through L2 (ld.global.cg): under programmatic launch its producer may
     // still be running when this kernel starts, so the read-only path is not safe.
@@ -505,8 +510,7 @@ __global__ void __launch_bounds__(256) act_to_f16_kernel(const float* __restrict
         dst[pos0 >> 3] = make_uint4(hw[0], hw[1], hw[2], hw[3]);
     }
     if (threadIdx.x == 0) ea[m] = e;
-    // Only now: a GEMM launched early would hold the SMs this grid still needs.
-    pdl_launch_dependents();
+    if (!early) pdl_launch_dependents();
 }
 
 // Per weight row: ew so that 127 * max(finite block scale) * 2^ew is in
@@ -630,8 +634,10 @@ cudaError_t launch_gemm_tc(const TcMaps& maps, const int* ew, int rows, int k, c
         attr[0].val.programmaticStreamSerializationAllowed = 1;
         cfg.attrs = attr;
         cfg.numAttrs = pdl ? 1 : 0;
+        // at most 4 of its 256-thread CTAs per SM: all resident at once
+        const int early = pdl && M <= 4 * sm_count_of_current_device() ? 1 : 0;
         cudaError_t e = cudaLaunchKernelEx(&cfg, act_to_f16_kernel, x, ldx, k, k_pad,
-                                           static_cast<__half*>(x16_scratch), ea_scratch);
+                                           static_cast<__half*>(x16_scratch), ea_scratch, early);
         if (e != cudaSuccess) return e;
     }
     CUtensorMap tm_x;
