@@ -5,7 +5,8 @@
 //   * SafetensorsLoader::get_tensor_keep_int8 (src/io/safetensors.cpp:517-585):
 //     quantizes and packs the weight on the GPU straight from the memory-mapped
 //     F32/BF16 bytes (bit-identical bytes and scales) and keeps it resident in
-//     HBM; the returned Tensor carries a host key that maps to the device handle.
+//     HBM; the returned Tensor's int8 storage holds the device handle itself
+//     (a tag and the handle pointer; its deleter frees the device weight).
 //   * math::matmul (src/ops/math_ops.hpp:92, src/ops/math_ops.cpp:820-900):
 //     int8 B operands run on the device through the C ABI (bit-identical by
 //     default); every other operand type goes to the reference's own code.
@@ -34,9 +35,10 @@ void qlm_reference_matmul_cpu(const Tensor& A, const Tensor& B, Tensor& C, bool 
 
 namespace {
 
+// Weights quantized on the CPU, imported once: host address -> device weight.
 struct Registry {
     std::mutex mu;
-    std::unordered_map<const int8_t*, qlm_w8*> handles;  // host key -> device weight
+    std::unordered_map<const int8_t*, qlm_w8*> handles;
     ~Registry() {
         for (auto& kv : handles) qlm_weight_free(kv.second);
     }
@@ -67,9 +69,36 @@ int tensor_min_m() {
     throw std::runtime_error(std::string(what) + ": " + qlm_last_error());
 }
 
-// Device handle for an int8 B: registered at load, or imported once from the
-// reference's host int8 layout if the Tensor was quantized on the CPU.
+// A device-resident weight travels in the Tensor's own int8 storage (the
+// reference Tensor has no field for it, and its sources stay unchanged): 8
+// tag bytes, then the handle pointer. The storage's deleter frees the weight.
+constexpr char kDeviceTag[8] = {'q', 'l', 'm', 'b', '2', '0', '0', 'w'};
+
+std::shared_ptr<std::vector<int8_t>> device_storage(qlm_w8* h) {
+    auto* v = new std::vector<int8_t>(sizeof(kDeviceTag) + sizeof(qlm_w8*));
+    std::memcpy(v->data(), kDeviceTag, sizeof(kDeviceTag));
+    std::memcpy(v->data() + sizeof(kDeviceTag), &h, sizeof(h));
+    return std::shared_ptr<std::vector<int8_t>>(v, [h](std::vector<int8_t>* p) {
+        qlm_weight_free(h);
+        delete p;
+    });
+}
+
+qlm_w8* stored_handle(const Tensor& B) {
+    const std::vector<int8_t>* v = B.int8_owner.get();
+    if (!v || v->size() != sizeof(kDeviceTag) + sizeof(qlm_w8*) || B.int8_data != v->data() ||
+        std::memcmp(v->data(), kDeviceTag, sizeof(kDeviceTag)) != 0)
+        return nullptr;
+    qlm_w8* h = nullptr;
+    std::memcpy(&h, v->data() + sizeof(kDeviceTag), sizeof(h));
+    return h;
+}
+
+// Device handle for an int8 B: carried by the Tensor (quantized on the device
+// at load), or imported once from the reference's host int8 layout if the
+// Tensor was quantized on the CPU (kept in a registry by host address).
 qlm_w8* device_weight(const Tensor& B, int N, int K) {
+    if (qlm_w8* h = stored_handle(B)) return h;
     Registry& r = registry();
     std::lock_guard<std::mutex> lk(r.mu);
     auto it = r.handles.find(B.int8_data);
@@ -108,16 +137,10 @@ Tensor SafetensorsLoader::get_tensor_keep_int8(const std::string& name) {
     Tensor t;
     t.shape = info.shape;
     t.compute_strides();
-    // A small host allocation is the key the model code carries around; the
-    // int8 bytes themselves live only in HBM.
-    t.int8_owner = std::make_shared<std::vector<int8_t>>(64, 0);
+    // The int8 codes and scales live only in HBM; the Tensor carries the handle.
+    t.int8_owner = device_storage(h);
     t.int8_data = t.int8_owner->data();
     t.int8_scales = std::make_shared<std::vector<float>>(1, 0.0f);
-    {
-        Registry& r = registry();
-        std::lock_guard<std::mutex> lk(r.mu);
-        r.handles.emplace(t.int8_data, h);
-    }
     return t;
 }
 
