@@ -77,6 +77,10 @@ struct DeviceState {
     void* xpair = nullptr;   // exact small-M product: activations in its pair layout
     size_t xpair_cap = 0;
     cudaEvent_t done = nullptr;  // HOST_IO: marks the end of a call's work on its stream
+    float* pin_x = nullptr;      // HOST_IO: pinned, mapped staging of small pageable inputs
+    size_t pin_x_cap = 0;
+    float* pin_y = nullptr;      // ... and outputs
+    size_t pin_y_cap = 0;
 };
 DeviceState g_dev[kMaxDevices];
 std::mutex g_dev_mu;
@@ -164,6 +168,17 @@ cudaError_t wait_stream(cudaStream_t s, cudaEvent_t ev) {
     // launch checks that read the runtime's last error.
     if (cudaPeekAtLastError() == cudaErrorNotReady) cudaGetLastError();
     return e;
+}
+
+// Pinned, mapped host staging (cudaHostAlloc), grown on demand.
+int ensure_pinned(float** buf, size_t* cap, size_t bytes) {
+    if (*cap >= bytes) return QLM_OK;
+    if (*buf) cudaFreeHost(*buf);
+    *buf = nullptr;
+    *cap = 0;
+    QLM_CUDA(cudaHostAlloc(reinterpret_cast<void**>(buf), bytes, cudaHostAllocMapped), "cudaHostAlloc(staging)");
+    *cap = bytes;
+    return QLM_OK;
 }
 
 template <typename T>
@@ -549,17 +564,27 @@ int qlm_linear_int8(const float* x, int M, int k, int64_t ldx, const qlm_w8* w, 
     float* dy = y;
     int64_t dldx = ldx, dldy = ldy;
     const bool host_io = (flags & QLM_LINEAR_HOST_IO) != 0;
-    bool y_direct = false;
+    bool y_direct = false, y_staged = false;
     if (host_io) {
         std::lock_guard<std::mutex> lk(g_dev_mu);
         if ((rc = ensure_buf(&st->x_buf, &st->x_cap, (size_t)M * k * sizeof(float)))) return rc;
         if ((rc = ensure_buf(&st->y_buf, &st->y_cap, (size_t)M * w->rows * sizeof(float)))) return rc;
-        const float* mx =
-            (size_t)M * k * sizeof(float) <= kHostReadMaxBytes ? mapped_host_ptr(const_cast<float*>(x)) : nullptr;
+        const bool small_x = (size_t)M * k * sizeof(float) <= kHostReadMaxBytes;
+        const float* mx = small_x ? mapped_host_ptr(const_cast<float*>(x)) : nullptr;
+        int64_t mldx = ldx;
+        if (small_x && !mx) {
+            // A small pageable input (QuickLM's own activations): a host copy
+            // into pinned staging, which the device then reads itself.
+            if ((rc = ensure_pinned(&st->pin_x, &st->pin_x_cap, (size_t)M * k * sizeof(float)))) return rc;
+            for (int m = 0; m < M; ++m)
+                std::memcpy(st->pin_x + (size_t)m * k, x + (size_t)m * ldx, (size_t)k * sizeof(float));
+            mx = mapped_host_ptr(st->pin_x);
+            mldx = k;
+        }
         if (mx) {
             const int64_t n = (int64_t)M * k;
             // one element per thread: every read is in flight at once
-            host_rows_in_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(mx, ldx, M, k, st->x_buf);
+            host_rows_in_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(mx, mldx, M, k, st->x_buf);
             QLM_CUDA(cudaGetLastError(), "read x from the pinned host buffer");
         } else if (ldx == k || M == 1)
             QLM_CUDA(cudaMemcpyAsync(st->x_buf, x, (size_t)M * k * sizeof(float), cudaMemcpyHostToDevice, s),
@@ -570,12 +595,21 @@ int qlm_linear_int8(const float* x, int M, int k, int64_t ldx, const qlm_w8* w, 
                      "copy x to device");
         dx = st->x_buf;
         dldx = k;
-        float* my = (size_t)M * ldy * sizeof(float) <= kZeroCopyMaxBytes ? mapped_host_ptr(y) : nullptr;
+        const bool small_y = (size_t)M * ldy * sizeof(float) <= kZeroCopyMaxBytes;
+        float* my = small_y ? mapped_host_ptr(y) : nullptr;
         if (my) {
             dy = my;  // the kernel stores into the caller's pinned buffer
             dldy = ldy;
             y_direct = true;
+        } else if (small_y && (rc = ensure_pinned(&st->pin_y, &st->pin_y_cap,
+                                                  (size_t)M * w->rows * sizeof(float))) == QLM_OK &&
+                   (my = mapped_host_ptr(st->pin_y)) != nullptr) {
+            dy = my;  // pinned staging, copied into the caller's pageable buffer after the wait
+            dldy = w->rows;
+            y_direct = true;
+            y_staged = true;
         } else {
+            if (rc) return rc;
             dy = st->y_buf;
             dldy = w->rows;
         }
@@ -623,6 +657,9 @@ int qlm_linear_int8(const float* x, int M, int k, int64_t ldx, const qlm_w8* w, 
     prof.stop();
     if (host_io || (flags & QLM_LINEAR_SYNC)) {
         QLM_CUDA(host_io ? wait_stream(s, st->done) : cudaStreamSynchronize(s), "stream synchronize");
+        if (y_staged)
+            for (int m = 0; m < M; ++m)
+                std::memcpy(y + (size_t)m * ldy, st->pin_y + (size_t)m * w->rows, (size_t)w->rows * sizeof(float));
         if (tensor || (flags & QLM_LINEAR_SYNC)) return qlm_device_status(w->device, 1);
     }
     return QLM_OK;
