@@ -183,4 +183,25 @@ __device__ __forceinline__ long long globaltimer_ns() {
 __device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 
+// Launch `kern` in stream s; with pdl, as a programmatic-dependent secondary
+// of the previous kernel in the stream: it may start while that kernel still
+// runs, so it must call pdl_wait() before touching data another kernel writes,
+// and read such data through L2 (its L1 may hold lines from before the
+// producer's stores).
+template <typename... P, typename... A>
+inline cudaError_t launch_pdl(bool pdl, void (*kern)(P...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                              A&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, kern, static_cast<A&&>(args)...);
+}
+
 }  // namespace qlm

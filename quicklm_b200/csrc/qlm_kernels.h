@@ -125,10 +125,16 @@ cudaError_t launch_gemv_decode(const float* x, const GemvWeight* ws, int nw, int
 // order (zero-centred gain): the decoder layer's unfused residual add and the
 // next norm in one launch, bit-identical to the two (qlm_layer.cu).
 cudaError_t launch_add_then_rms_norm(float* x, const float* delta, const float* w, float* y, int rows, int size,
-                                     float eps, cudaStream_t stream);
+                                     float eps, cudaStream_t stream, bool pdl);
+// math::rms_norm (zero-centred gain) and math::silu_mul, launched from the
+// decode step (qlm_layer.cu).
+cudaError_t launch_rms_norm(const float* x, const float* w, float* y, int rows, int size, float eps,
+                            cudaStream_t stream, bool pdl);
+cudaError_t launch_silu_mul(float* a, const float* b, int64_t n, cudaStream_t stream, bool pdl);
 
-// Decode-step forms that read the position (and the conv ring position) from
-// device memory, so one captured step replays at every position
+// Decode-step forms (pdl: launched as programmatic-dependent secondaries; the
+// kernels wait and read through L2) that read the position (and the conv ring
+// position) from device memory, so one captured step replays at every position
 // (qlm_layer.cu). launch_gqa_attend_dev: the three-launch attention with grids
 // and shared memory sized for positions up to max_pos; scratch holds
 // heads * (max_pos + 1) floats; gqa_v_kernel takes gqa_dev_smem_bytes(max_pos)
@@ -136,36 +142,37 @@ cudaError_t launch_add_then_rms_norm(float* x, const float* delta, const float* 
 // sigmoid output gate applied to each output in the same launch.
 // The conv step followed by SiLU on every output channel, in one launch.
 cudaError_t launch_conv1d_silu_dev(const float* input, float* state, const int* d_oldest, const float* weight_t,
-                                   float* output, int conv_dim, int kernel_size, cudaStream_t stream);
+                                   float* output, int conv_dim, int kernel_size, cudaStream_t stream, bool pdl);
 // Partial NeoX RoPE of nq query heads (in place, head stride q_ld) and nk key
 // heads at position *d_pos, the rotated keys and the values written to row
 // *d_pos of the caches ([T][nk * head_dim]); one launch, the arithmetic of
 // the separate RoPE and append.
 cudaError_t launch_rope_append(float* q, int q_ld, int nq, const float* k, const float* v, int nk, int head_dim,
                                int rotary_dim, const float* cos_all, const float* sin_all, const int* d_pos,
-                               float* k_cache, float* v_cache, cudaStream_t stream);
+                               float* k_cache, float* v_cache, cudaStream_t stream, bool pdl);
 // The attention's q and k head norms (zero-centred gain) in one launch, in
 // place: nq query rows of stride q_ld with wq, nk key rows of stride k_ld with
 // wk; bit-identical to the two separate rms_norm launches.
 cudaError_t launch_qk_norm(float* q, int q_ld, const float* wq, int nq, float* k, int k_ld, const float* wk, int nk,
-                           int size, float eps, cudaStream_t stream);
+                           int size, float eps, cudaStream_t stream, bool pdl);
 // Per head row: o = rms_norm with plain gain w (not stored), then
 // z = silu(z) * o — the gated-delta-net's head norm and output gate in one
 // launch, bit-identical to qlm_rms_norm_gain + qlm_silu_mul.
 cudaError_t launch_head_norm_gate(const float* x, const float* w, float* z, int rows, int size, float eps,
-                                  cudaStream_t stream);
-// The delta-rule recurrence with the gates step folded in: each head's decay
-// and beta computed in the recurrence's CTAs from the raw gate inputs, the
-// parameters repeating every `per` heads (same arithmetic as the separate
-// gates kernel).
-cudaError_t launch_gdn_recurrence_gates(float* state, const float* q, const float* k, const float* v,
+                                  cudaStream_t stream, bool pdl);
+// The delta-rule recurrence with the gates and the q/k L2 norms folded in:
+// each head's decay and beta computed in the recurrence's CTAs from the raw
+// gate inputs (parameters repeating every `per` heads), q and k normalized in
+// shared memory (eps norm_eps); the separate steps' arithmetic. pdl: launched
+// as a programmatic-dependent secondary.
+cudaError_t launch_gdn_recurrence_fused(float* state, const float* q, const float* k, const float* v,
                                         const float* a_raw, const float* b_raw, const float* A_log,
-                                        const float* dt_bias, int per, float* out, int heads, int head_dim,
-                                        cudaStream_t stream);
+                                        const float* dt_bias, int per, float norm_eps, float* out, int heads,
+                                        int head_dim, cudaStream_t stream, bool pdl);
 size_t gqa_dev_smem_bytes(int max_pos);
 cudaError_t launch_gqa_attend_dev(const float* q, int q_stride, const float* k_cache, const float* v_cache,
                                   float* out, const int* d_pos, int max_pos, int heads, int kv_heads, int head_dim,
-                                  float* scratch, const float* gate, int gate_ld, cudaStream_t stream);
+                                  float* scratch, const float* gate, int gate_ld, cudaStream_t stream, bool pdl);
 
 // Bit-exact y[m][0:rows] = x[m][0:k] . W^T for 2 <= M <= 64 activation rows
 // in one launch that streams W once (qlm_gemm_exact.cu): a pre-pass writes the

@@ -101,19 +101,25 @@ __device__ __forceinline__ void apply_zc(const float* in, const float* __restric
 // ZC: zero-centred gain (1 + w) as math::rms_norm; else the plain gain w.
 // ld: row stride of x and y in floats (>= size; the rows' first `size` values
 // are normalized, the rest untouched).
-// This kernel and silu_mul_kernel usually precede a GEMV launched with
-// programmatic stream serialization: they let it start at once, so its weight
-// copies overlap them (the GEMV reads its activations only after its
-// dependency wait, which still waits for this kernel to complete).
+// Programmatic launch: the decode step launches this kernel and the others it
+// runs (qlm_model.cu) as secondaries of the kernel before them. Each waits for
+// its predecessor first (pdl_wait), reads data other kernels wrote through L2,
+// and then lets its own successor start — usually a GEMV whose weight copies
+// then overlap it (the GEMV reads its activations only after its own wait).
+// Triggering after the wait keeps the stream at most one kernel ahead: a
+// trigger before it let later GEMVs launch while an earlier one still ran
+// (620 vs 662-673 tok/s on configuration 3). Launched plainly (the C ABI), the
+// wait and the trigger do nothing.
 template <bool ZC>
 __global__ void __launch_bounds__(kThreads) rms_norm_kernel(const float* x, const float* __restrict__ w, float* y,
                                                             int size, float eps, int64_t ld) {
     extern __shared__ float stage[];
     __shared__ float s_scale;
+    pdl_wait();
     pdl_launch_dependents();
     const float* xr = x + (int64_t)blockIdx.x * ld;
     if (size <= kStageFloats) {
-        for (int i = threadIdx.x; i < size; i += blockDim.x) stage[i] = xr[i];
+        for (int i = threadIdx.x; i < size; i += blockDim.x) stage[i] = __ldcg(xr + i);
         __syncthreads();
         xr = stage;
     }
@@ -135,12 +141,13 @@ __global__ void __launch_bounds__(kThreads) add_then_rms_norm_kernel(float* x, c
                                                                      float eps) {
     extern __shared__ float stage[];
     __shared__ float s_scale;
+    pdl_wait();
     pdl_launch_dependents();
     float* xr = x + (int64_t)blockIdx.x * size;
     const float* dr = delta + (int64_t)blockIdx.x * size;
     const bool staged = size <= kStageFloats;
     for (int i = threadIdx.x; i < size; i += blockDim.x) {
-        const float v = __fadd_rn(xr[i], dr[i]);
+        const float v = __fadd_rn(__ldcg(xr + i), __ldcg(dr + i));
         xr[i] = v;
         if (staged) stage[i] = v;
     }
@@ -163,12 +170,14 @@ __global__ void __launch_bounds__(kThreads) qk_norm_kernel(float* q, int q_ld, c
                                                            int size, float eps) {
     extern __shared__ float stage[];
     __shared__ float s_scale;
+    pdl_wait();
+    pdl_launch_dependents();
     const bool isq = (int)blockIdx.x < nq;
     float* xr = isq ? q + (int64_t)blockIdx.x * q_ld : k + (int64_t)(blockIdx.x - nq) * k_ld;
     const float* w = isq ? wq : wk;
     const float* src = xr;
     if (size <= kStageFloats) {
-        for (int i = threadIdx.x; i < size; i += blockDim.x) stage[i] = xr[i];
+        for (int i = threadIdx.x; i < size; i += blockDim.x) stage[i] = __ldcg(xr + i);
         __syncthreads();
         src = stage;
     }
@@ -188,10 +197,11 @@ __global__ void __launch_bounds__(kThreads) head_norm_gate_kernel(const float* x
                                                                   float* __restrict__ z, int size, float eps) {
     extern __shared__ float stage[];
     __shared__ float s_scale;
+    pdl_wait();
     pdl_launch_dependents();
     const float* xr = x + (int64_t)blockIdx.x * size;
     if (size <= kStageFloats) {
-        for (int i = threadIdx.x; i < size; i += blockDim.x) stage[i] = xr[i];
+        for (int i = threadIdx.x; i < size; i += blockDim.x) stage[i] = __ldcg(xr + i);
         __syncthreads();
         xr = stage;
     }
@@ -203,7 +213,7 @@ __global__ void __launch_bounds__(kThreads) head_norm_gate_kernel(const float* x
     float* zr = z + (int64_t)blockIdx.x * size;
     for (int i = threadIdx.x; i < size; i += blockDim.x) {
         const float o = __fmul_rn(__fmul_rn(xr[i], s_scale), w[i]);
-        const float zx = zr[i];
+        const float zx = __ldcg(zr + i);
         const float e = (float)exp(-(double)zx);
         zr[i] = __fmul_rn(__fdiv_rn(zx, __fadd_rn(1.0f, e)), o);
     }
@@ -236,11 +246,12 @@ __global__ void __launch_bounds__(kThreads) add_rms_norm_kernel(float* res, cons
 // a = (x / (1 + exp(-x))) * b with exp evaluated in double and rounded once.
 __global__ void __launch_bounds__(kThreads) silu_mul_kernel(float* __restrict__ a, const float* __restrict__ b,
                                                             int64_t n) {
+    pdl_wait();
     pdl_launch_dependents();
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
-        const float x = a[i];
+        const float x = __ldcg(a + i);
         const float e = (float)exp(-(double)x);
-        a[i] = __fmul_rn(__fdiv_rn(x, __fadd_rn(1.0f, e)), b[i]);
+        a[i] = __fmul_rn(__fdiv_rn(x, __fadd_rn(1.0f, e)), __ldcg(b + i));
     }
 }
 
@@ -265,15 +276,17 @@ __global__ void __launch_bounds__(kThreads) conv1d_tapmajor_kernel(const float* 
                                                                    int oldest, const int* __restrict__ d_oldest,
                                                                    const float* __restrict__ wt,
                                                                    float* __restrict__ out, int conv_dim, int ntaps) {
+    pdl_wait();
+    pdl_launch_dependents();
     const int c = blockIdx.x * blockDim.x + threadIdx.x;
     if (c >= conv_dim) return;
-    if (d_oldest) oldest = *d_oldest;
+    if (d_oldest) oldest = __ldcg(d_oldest);
     float sum = 0.0f;
     for (int j = 0; j < ntaps; ++j) {
         const int row = (oldest + j) % ntaps;
-        sum = __fadd_rn(sum, __fmul_rn(state[(int64_t)row * conv_dim + c], wt[(int64_t)j * conv_dim + c]));
+        sum = __fadd_rn(sum, __fmul_rn(__ldcg(state + (int64_t)row * conv_dim + c), wt[(int64_t)j * conv_dim + c]));
     }
-    const float x = in[c];
+    const float x = __ldcg(in + c);
     float y = __fadd_rn(sum, __fmul_rn(x, wt[(int64_t)ntaps * conv_dim + c]));
     if (SILU) y = __fdiv_rn(y, __fadd_rn(1.0f, (float)exp(-(double)y)));
     out[c] = y;
@@ -315,7 +328,10 @@ __device__ __forceinline__ void gdn_gate(float a_raw, float b_raw, float A_log, 
 // written back. GATES: the head's decay and beta are computed here from the
 // raw gate inputs (gdn_gate, parameters repeating every `per` heads) instead
 // of being read from dec / beta — the gates step folded into this launch.
-template <bool GATES>
+// NORM: q and k are L2-normalized here, in their shared-memory copies, with
+// l2norm_heads_kernel's arithmetic (sumsq in the reference's order,
+// sqrt(ss + eps), one division per element) — that step folded in as well.
+template <bool GATES, bool NORM = false>
 __global__ void __launch_bounds__(32) gdn_recurrence_kernel(float* __restrict__ state, const float* __restrict__ q,
                                                             const float* __restrict__ k, const float* __restrict__ v,
                                                             const float* __restrict__ dec,
@@ -323,26 +339,39 @@ __global__ void __launch_bounds__(32) gdn_recurrence_kernel(float* __restrict__ 
                                                             int d, const float* __restrict__ a_raw,
                                                             const float* __restrict__ b_raw,
                                                             const float* __restrict__ A_log,
-                                                            const float* __restrict__ dt_bias, int per) {
+                                                            const float* __restrict__ dt_bias, int per,
+                                                            float norm_eps) {
     extern __shared__ float sh[];  // q_h [d], k_h [d], slice [d][32]
+    pdl_wait();
+    pdl_launch_dependents();
     const int h = blockIdx.x, lane = threadIdx.x, j = blockIdx.y * 32 + lane;
     float* qs = sh;
     float* ks = sh + d;
     float* tile = sh + 2 * d;
     for (int i = lane; i < d; i += 32) {
-        qs[i] = q[(int64_t)h * d + i];
-        ks[i] = k[(int64_t)h * d + i];
+        qs[i] = __ldcg(q + (int64_t)h * d + i);
+        ks[i] = __ldcg(k + (int64_t)h * d + i);
+    }
+    if (NORM) {
+        __syncwarp();
+        const float nq = __fsqrt_rn(__fadd_rn(sumsq_ref(qs, d), norm_eps));
+        const float nk = __fsqrt_rn(__fadd_rn(sumsq_ref(ks, d), norm_eps));
+        __syncwarp();
+        for (int i = lane; i < d; i += 32) {
+            qs[i] = __fdiv_rn(qs[i], nq);
+            ks[i] = __fdiv_rn(ks[i], nk);
+        }
     }
     float* S = state + (int64_t)h * d * d + j;
     const bool live = j < d;
 #pragma unroll 8
-    for (int i = 0; i < d; ++i) tile[i * 32 + lane] = live ? S[(int64_t)i * d] : 0.0f;
+    for (int i = 0; i < d; ++i) tile[i * 32 + lane] = live ? __ldcg(S + (int64_t)i * d) : 0.0f;
     __syncwarp();
     if (live) {
         const bool body = j < d - d % 8;
         float dh, bh;
         if (GATES) {
-            gdn_gate(a_raw[h], b_raw[h], A_log[h % per], dt_bias[h % per], dh, bh);
+            gdn_gate(__ldcg(a_raw + h), __ldcg(b_raw + h), A_log[h % per], dt_bias[h % per], dh, bh);
         } else {
             dh = dec[h];
             bh = beta[h];
@@ -354,7 +383,7 @@ __global__ void __launch_bounds__(32) gdn_recurrence_kernel(float* __restrict__ 
             tile[i * 32 + lane] = r;
             kv = body ? __fmaf_rn(ks[i], r, kv) : __fadd_rn(kv, __fmul_rn(ks[i], r));
         }
-        const float delta = __fsub_rn(v[(int64_t)h * d + j], kv);
+        const float delta = __fsub_rn(__ldcg(v + (int64_t)h * d + j), kv);
         float o = 0.0f;
 #pragma unroll 8
         for (int i = 0; i < d; ++i) {
@@ -487,11 +516,13 @@ __global__ void __launch_bounds__(256) gqa_scores_kernel(const float* __restrict
                                                          int pos, const int* __restrict__ d_pos, int heads,
                                                          int kv_heads, int d) {
     extern __shared__ float qs[];
-    if (d_pos) pos = *d_pos;
+    pdl_wait();
+    pdl_launch_dependents();
+    if (d_pos) pos = __ldcg(d_pos);
     if ((int)blockIdx.y * 64 > pos) return;
     const int h = blockIdx.x, tid = threadIdx.x;
     const int kv_size = kv_heads * d, off = (h / (heads / kv_heads)) * d;
-    for (int i = tid; i < d; i += blockDim.x) qs[i] = q[(int64_t)h * q_stride + i];
+    for (int i = tid; i < d; i += blockDim.x) qs[i] = __ldcg(q + (int64_t)h * q_stride + i);
     __syncthreads();
     const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)d));
     const int g = tid >> 4, a = tid & 15;
@@ -506,14 +537,14 @@ __global__ void __launch_bounds__(256) gqa_scores_kernel(const float* __restrict
             float kk[8];
 #pragma unroll
             for (int u = 0; u < 8; ++u)
-                if (c0 + u < n16) kk[u] = kp[16 * (c0 + u) + a];
+                if (c0 + u < n16) kk[u] = __ldcg(kp + (16 * (c0 + u) + a));
 #pragma unroll
             for (int u = 0; u < 8; ++u)
                 if (c0 + u < n16) acc = __fmaf_rn(qs[16 * (c0 + u) + a], kk[u], acc);
         }
         int tail = i8;
         if (i8 + 8 <= d) {
-            if (a < 8) acc = __fmaf_rn(qs[i8 + a], kp[i8 + a], acc);
+            if (a < 8) acc = __fmaf_rn(qs[i8 + a], __ldcg(kp + (i8 + a)), acc);
             tail = i8 + 8;
         }
         const float s = __fadd_rn(acc, __shfl_down_sync(0xffffffffu, acc, 8, 16));
@@ -523,7 +554,7 @@ __global__ void __launch_bounds__(256) gqa_scores_kernel(const float* __restrict
         const float l3 = __shfl_down_sync(0xffffffffu, lo, 3, 16);
         if (a == 0 && pw <= pos) {
             float r = __fadd_rn(__fadd_rn(lo, l1), __fadd_rn(l2, l3));
-            for (int i = tail; i < d; ++i) r = __fadd_rn(r, __fmul_rn(qs[i], kp[i]));
+            for (int i = tail; i < d; ++i) r = __fadd_rn(r, __fmul_rn(qs[i], __ldcg(kp + (i))));
             scores[(int64_t)h * (pos + 1) + p] = __fmul_rn(r, scale);
         }
     }
@@ -534,12 +565,14 @@ __global__ void __launch_bounds__(256) gqa_scores_kernel(const float* __restrict
 __global__ void __launch_bounds__(256) gqa_softmax_kernel(float* __restrict__ scores, int pos,
                                                           const int* __restrict__ d_pos) {
     __shared__ float red[34];
-    if (d_pos) pos = *d_pos;
+    pdl_wait();
+    pdl_launch_dependents();
+    if (d_pos) pos = __ldcg(d_pos);
     float* sc = scores + (int64_t)blockIdx.x * (pos + 1);
     const int tid = threadIdx.x;
     float m = -INFINITY;
     for (int p = tid; p <= pos; p += blockDim.x)
-        if (sc[p] > m) m = sc[p];
+        if (__ldcg(sc + p) > m) m = __ldcg(sc + p);
     for (int o = 16; o; o >>= 1) {
         const float t = __shfl_xor_sync(0xffffffffu, m, o);
         m = t > m ? t : m;
@@ -549,21 +582,22 @@ __global__ void __launch_bounds__(256) gqa_softmax_kernel(float* __restrict__ sc
     if (tid == 0) {
         float mm = red[0];
         for (int w = 1; w < (int)(blockDim.x >> 5); ++w) mm = red[w] > mm ? red[w] : mm;
-        red[32] = isnan(sc[0]) ? sc[0] : mm;
+        const float s0 = __ldcg(sc);
+        red[32] = isnan(s0) ? s0 : mm;
     }
     __syncthreads();
     m = red[32];
-    for (int p = tid; p <= pos; p += blockDim.x) sc[p] = (float)exp((double)__fsub_rn(sc[p], m));
+    for (int p = tid; p <= pos; p += blockDim.x) sc[p] = (float)exp((double)__fsub_rn(__ldcg(sc + p), m));
     __syncthreads();
     if (tid == 0) {
         float sum = 0.0f;
 #pragma unroll 8
-        for (int p = 0; p <= pos; ++p) sum = __fadd_rn(sum, sc[p]);
+        for (int p = 0; p <= pos; ++p) sum = __fadd_rn(sum, __ldcg(sc + p));
         red[33] = sum;
     }
     __syncthreads();
     const float sum = red[33];
-    for (int p = tid; p <= pos; p += blockDim.x) sc[p] = __fdiv_rn(sc[p], sum);
+    for (int p = tid; p <= pos; p += blockDim.x) sc[p] = __fdiv_rn(__ldcg(sc + p), sum);
 }
 
 // V: CTA (head, block of 32 output elements), one warp; the head's weights are
@@ -577,12 +611,13 @@ __global__ void __launch_bounds__(32) gqa_v_kernel(const float* __restrict__ pro
                                                    int heads, int kv_heads, int d, const float* __restrict__ gate,
                                                    int gate_ld) {
     extern __shared__ float pr[];  // [pos + 1]
+    pdl_wait();
     pdl_launch_dependents();  // usually precedes o_proj's GEMV (see rms_norm_kernel)
-    if (d_pos) pos = *d_pos;
+    if (d_pos) pos = __ldcg(d_pos);
     const int h = blockIdx.x, lane = threadIdx.x;
     const int kv_size = kv_heads * d, off = (h / (heads / kv_heads)) * d;
     const float* src = probs + (int64_t)h * (pos + 1);
-    for (int p = lane; p <= pos; p += 32) pr[p] = src[p];
+    for (int p = lane; p <= pos; p += 32) pr[p] = __ldcg(src + p);
     __syncwarp();
     const int i = blockIdx.y * 32 + lane;
     if (i >= d) return;
@@ -595,7 +630,7 @@ __global__ void __launch_bounds__(32) gqa_v_kernel(const float* __restrict__ pro
         float vv[kVBatch];
 #pragma unroll
         for (int u = 0; u < kVBatch; ++u)
-            if (u < n) vv[u] = vp[(int64_t)(p0 + u) * kv_size];
+            if (u < n) vv[u] = __ldcg(vp + (int64_t)(p0 + u) * kv_size);
 #pragma unroll
         for (int u = 0; u < kVBatch; ++u)
             if (u < n) {
@@ -604,7 +639,7 @@ __global__ void __launch_bounds__(32) gqa_v_kernel(const float* __restrict__ pro
             }
     }
     if (gate) {
-        const float e = (float)exp(-(double)gate[(int64_t)h * gate_ld + i]);
+        const float e = (float)exp(-(double)__ldcg(gate + (int64_t)h * gate_ld + i));
         o = __fmul_rn(o, __fdiv_rn(1.0f, __fadd_rn(1.0f, e)));
     }
     out[(int64_t)h * d + i] = o;
@@ -651,8 +686,10 @@ __global__ void __launch_bounds__(kThreads) rope_append_kernel(float* __restrict
                                                                const float* __restrict__ sin_all,
                                                                const int* __restrict__ d_pos, float* __restrict__ kc,
                                                                float* __restrict__ vc) {
+    pdl_wait();
+    pdl_launch_dependents();
     const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-    const int pos = *d_pos;
+    const int pos = __ldcg(d_pos);
     const float* ct = cos_all + (int64_t)pos * half;
     const float* st = sin_all + (int64_t)pos * half;
     const int64_t nqp = (int64_t)nq * half, nke = (int64_t)nk * head_dim;
@@ -660,7 +697,7 @@ __global__ void __launch_bounds__(kThreads) rope_append_kernel(float* __restrict
         const int h = (int)(i / half), e = (int)(i % half);
         float* hd = q + (int64_t)h * q_ld;
         const float c = ct[e], sn = st[e];
-        const float x1 = hd[e], x2 = hd[e + half];
+        const float x1 = __ldcg(hd + e), x2 = __ldcg(hd + e + half);
         hd[e] = __fsub_rn(__fmul_rn(x1, c), __fmul_rn(x2, sn));
         hd[e + half] = __fadd_rn(__fmul_rn(x2, c), __fmul_rn(x1, sn));
     } else if (i < nqp + nke) {
@@ -669,16 +706,16 @@ __global__ void __launch_bounds__(kThreads) rope_append_kernel(float* __restrict
         const float* hd = k + (int64_t)h * head_dim;
         float r;
         if (e < half) {
-            r = __fsub_rn(__fmul_rn(hd[e], ct[e]), __fmul_rn(hd[e + half], st[e]));
+            r = __fsub_rn(__fmul_rn(__ldcg(hd + e), ct[e]), __fmul_rn(__ldcg(hd + e + half), st[e]));
         } else if (e < 2 * half) {
-            r = __fadd_rn(__fmul_rn(hd[e], ct[e - half]), __fmul_rn(hd[e - half], st[e - half]));
+            r = __fadd_rn(__fmul_rn(__ldcg(hd + e), ct[e - half]), __fmul_rn(__ldcg(hd + e - half), st[e - half]));
         } else {
-            r = hd[e];
+            r = __ldcg(hd + e);
         }
         kc[(int64_t)pos * nke + j] = r;
     } else if (i < nqp + 2 * nke) {
         const int64_t j = i - nqp - nke;
-        vc[(int64_t)pos * nke + j] = v[j];
+        vc[(int64_t)pos * nke + j] = __ldcg(v + j);
     }
 }
 
@@ -710,50 +747,64 @@ namespace qlm {
 
 // math::rms_norm on `rows` rows of `size` floats spaced `ld` apart (in place
 // when x == y): the per-head QK-norm of a query laid out [query | gate].
+// The internal launchers below launch as programmatic-dependent secondaries
+// when pdl is set; the norm kernels only when their rows are staged in shared
+// memory (their unstaged form reads the row again through L1).
 cudaError_t launch_add_then_rms_norm(float* x, const float* delta, const float* w, float* y, int rows, int size,
-                                     float eps, cudaStream_t stream) {
-    const size_t smem = size <= kStageFloats ? (size_t)size * sizeof(float) : 0;
-    add_then_rms_norm_kernel<<<rows, kThreads, smem, stream>>>(x, delta, w, y, size, eps);
-    return cudaGetLastError();
+                                     float eps, cudaStream_t stream, bool pdl) {
+    const bool staged = size <= kStageFloats;
+    return launch_pdl(pdl && staged, add_then_rms_norm_kernel, dim3(rows), dim3(kThreads),
+                      staged ? (size_t)size * sizeof(float) : 0, stream, x, delta, w, y, size, eps);
+}
+
+cudaError_t launch_rms_norm(const float* x, const float* w, float* y, int rows, int size, float eps,
+                            cudaStream_t stream, bool pdl) {
+    const bool staged = size <= kStageFloats;
+    return launch_pdl(pdl && staged, rms_norm_kernel<true>, dim3(rows), dim3(kThreads),
+                      staged ? (size_t)size * sizeof(float) : 0, stream, x, w, y, size, eps, (int64_t)size);
+}
+
+cudaError_t launch_silu_mul(float* a, const float* b, int64_t n, cudaStream_t stream, bool pdl) {
+    int64_t blocks = (n + kThreads - 1) / kThreads;
+    if (blocks > 148 * 64) blocks = 148 * 64;
+    return launch_pdl(pdl, silu_mul_kernel, dim3((unsigned)blocks), dim3(kThreads), 0, stream, a, b, n);
 }
 
 // Position-from-device forms for a decode step that is captured once and
 // replayed at every position (same kernels and arithmetic as the C ABI's).
 cudaError_t launch_conv1d_silu_dev(const float* input, float* state, const int* d_oldest, const float* weight_t,
-                                   float* output, int conv_dim, int kernel_size, cudaStream_t stream) {
-    conv1d_tapmajor_kernel<true><<<(conv_dim + kThreads - 1) / kThreads, kThreads, 0, stream>>>(
-        input, state, 0, d_oldest, weight_t, output, conv_dim, kernel_size - 1);
-    return cudaGetLastError();
+                                   float* output, int conv_dim, int kernel_size, cudaStream_t stream, bool pdl) {
+    return launch_pdl(pdl, conv1d_tapmajor_kernel<true>, dim3((conv_dim + kThreads - 1) / kThreads), dim3(kThreads), 0,
+                      stream, input, state, 0, d_oldest, weight_t, output, conv_dim, kernel_size - 1);
 }
 
 cudaError_t launch_rope_append(float* q, int q_ld, int nq, const float* k, const float* v, int nk, int head_dim,
                                int rotary_dim, const float* cos_all, const float* sin_all, const int* d_pos,
-                               float* k_cache, float* v_cache, cudaStream_t stream) {
+                               float* k_cache, float* v_cache, cudaStream_t stream, bool pdl) {
     const int half = rotary_dim / 2;
     const int64_t n = (int64_t)nq * half + 2 * (int64_t)nk * head_dim;
-    rope_append_kernel<<<(unsigned)((n + kThreads - 1) / kThreads), kThreads, 0, stream>>>(
-        q, q_ld, nq, k, v, nk, head_dim, half, cos_all, sin_all, d_pos, k_cache, v_cache);
-    return cudaGetLastError();
+    return launch_pdl(pdl, rope_append_kernel, dim3((unsigned)((n + kThreads - 1) / kThreads)), dim3(kThreads), 0,
+                      stream, q, q_ld, nq, k, v, nk, head_dim, half, cos_all, sin_all, d_pos, k_cache, v_cache);
 }
 
 cudaError_t launch_qk_norm(float* q, int q_ld, const float* wq, int nq, float* k, int k_ld, const float* wk, int nk,
-                           int size, float eps, cudaStream_t stream) {
-    const size_t smem = size <= kStageFloats ? (size_t)size * sizeof(float) : 0;
-    qk_norm_kernel<<<nq + nk, kThreads, smem, stream>>>(q, q_ld, wq, k, k_ld, wk, nq, size, eps);
-    return cudaGetLastError();
+                           int size, float eps, cudaStream_t stream, bool pdl) {
+    const bool staged = size <= kStageFloats;
+    return launch_pdl(pdl && staged, qk_norm_kernel, dim3(nq + nk), dim3(kThreads),
+                      staged ? (size_t)size * sizeof(float) : 0, stream, q, q_ld, wq, k, k_ld, wk, nq, size, eps);
 }
 
 cudaError_t launch_head_norm_gate(const float* x, const float* w, float* z, int rows, int size, float eps,
-                                  cudaStream_t stream) {
-    const size_t smem = size <= kStageFloats ? (size_t)size * sizeof(float) : 0;
-    head_norm_gate_kernel<<<rows, kThreads, smem, stream>>>(x, w, z, size, eps);
-    return cudaGetLastError();
+                                  cudaStream_t stream, bool pdl) {
+    const bool staged = size <= kStageFloats;
+    return launch_pdl(pdl && staged, head_norm_gate_kernel, dim3(rows), dim3(kThreads),
+                      staged ? (size_t)size * sizeof(float) : 0, stream, x, w, z, size, eps);
 }
 
-cudaError_t launch_gdn_recurrence_gates(float* state, const float* q, const float* k, const float* v,
+cudaError_t launch_gdn_recurrence_fused(float* state, const float* q, const float* k, const float* v,
                                         const float* a_raw, const float* b_raw, const float* A_log,
-                                        const float* dt_bias, int per, float* out, int heads, int head_dim,
-                                        cudaStream_t stream) {
+                                        const float* dt_bias, int per, float norm_eps, float* out, int heads,
+                                        int head_dim, cudaStream_t stream, bool pdl) {
     if (heads <= 0 || head_dim <= 0 || head_dim > 1024 || per <= 0) return cudaErrorInvalidValue;
     static bool attr_set[64] = {};
     int dev = 0;
@@ -761,23 +812,23 @@ cudaError_t launch_gdn_recurrence_gates(float* state, const float* q, const floa
     if (e != cudaSuccess) return e;
     if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
     if (!attr_set[dev]) {
-        if ((e = cudaFuncSetAttribute(gdn_recurrence_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        if ((e = cudaFuncSetAttribute(gdn_recurrence_kernel<true, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                       (2 + 32) * 1024 * (int)sizeof(float))) != cudaSuccess)
             return e;
         attr_set[dev] = true;
     }
     const dim3 grid((unsigned)heads, (unsigned)((head_dim + 31) / 32));
     const size_t smem = (size_t)(2 + 32) * head_dim * sizeof(float);
-    gdn_recurrence_kernel<true><<<grid, 32, smem, stream>>>(state, q, k, v, nullptr, nullptr, out, head_dim, a_raw,
-                                                            b_raw, A_log, dt_bias, per);
-    return cudaGetLastError();
+    return launch_pdl(pdl, gdn_recurrence_kernel<true, true>, grid, dim3(32), smem, stream, state, q, k, v,
+                      (const float*)nullptr, (const float*)nullptr, out, head_dim, a_raw, b_raw, A_log, dt_bias, per,
+                      norm_eps);
 }
 
 size_t gqa_dev_smem_bytes(int max_pos) { return (size_t)(max_pos + 1) * sizeof(float); }
 
 cudaError_t launch_gqa_attend_dev(const float* q, int q_stride, const float* k_cache, const float* v_cache,
                                   float* out, const int* d_pos, int max_pos, int heads, int kv_heads, int head_dim,
-                                  float* scratch, const float* gate, int gate_ld, cudaStream_t stream) {
+                                  float* scratch, const float* gate, int gate_ld, cudaStream_t stream, bool pdl) {
     static bool attr_set[64] = {};
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
@@ -790,15 +841,14 @@ cudaError_t launch_gqa_attend_dev(const float* q, int q_stride, const float* k_c
         attr_set[dev] = true;
     }
     const dim3 g1((unsigned)heads, (unsigned)((max_pos + 64) / 64));
-    gqa_scores_kernel<<<g1, 256, (size_t)head_dim * sizeof(float), stream>>>(q, q_stride, k_cache, scratch, 0, d_pos,
-                                                                             heads, kv_heads, head_dim);
-    if ((e = cudaGetLastError()) != cudaSuccess) return e;
-    gqa_softmax_kernel<<<heads, 256, 0, stream>>>(scratch, 0, d_pos);
-    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    if ((e = launch_pdl(pdl, gqa_scores_kernel, g1, dim3(256), (size_t)head_dim * sizeof(float), stream, q, q_stride,
+                        k_cache, scratch, 0, d_pos, heads, kv_heads, head_dim)) != cudaSuccess)
+        return e;
+    if ((e = launch_pdl(pdl, gqa_softmax_kernel, dim3(heads), dim3(256), 0, stream, scratch, 0, d_pos)) != cudaSuccess)
+        return e;
     const dim3 g2((unsigned)heads, (unsigned)((head_dim + 31) / 32));
-    gqa_v_kernel<<<g2, 32, gqa_dev_smem_bytes(max_pos), stream>>>(scratch, v_cache, out, 0, d_pos, heads, kv_heads,
-                                                                  head_dim, gate, gate_ld);
-    return cudaGetLastError();
+    return launch_pdl(pdl, gqa_v_kernel, g2, dim3(32), gqa_dev_smem_bytes(max_pos), stream, (const float*)scratch,
+                      v_cache, out, 0, d_pos, heads, kv_heads, head_dim, gate, gate_ld);
 }
 }  // namespace qlm
 
@@ -837,7 +887,7 @@ int qlm_gdn_recurrence(float* state, const float* q, const float* k, const float
         attr_set[dev] = true;
     }
     qlm::gdn_recurrence_kernel<false><<<grid, 32, smem, static_cast<cudaStream_t>(stream)>>>(
-        state, q, k, v, decay, beta, out, head_dim, nullptr, nullptr, nullptr, nullptr, 1);
+        state, q, k, v, decay, beta, out, head_dim, nullptr, nullptr, nullptr, nullptr, 1, 0.0f);
     return launched("gdn_recurrence launch");
 }
 
@@ -892,7 +942,9 @@ int qlm_add_then_rms_norm(float* residual, const float* delta, const float* w, f
                           float eps, void* stream) {
     if (!residual || !delta || !w || !out) return layer_fail(QLM_ERR_INVALID_ARG, "NULL argument");
     if (rows <= 0 || size <= 0) return layer_fail(QLM_ERR_INVALID_ARG, "rows and size must be positive");
-    qlm::launch_add_then_rms_norm(residual, delta, w, out, rows, size, eps, static_cast<cudaStream_t>(stream));
+    const cudaError_t e =
+        qlm::launch_add_then_rms_norm(residual, delta, w, out, rows, size, eps, static_cast<cudaStream_t>(stream), false);
+    if (e != cudaSuccess) return layer_fail(QLM_ERR_CUDA, cudaGetErrorString(e));
     return launched("add_then_rms_norm launch");
 }
 

@@ -76,11 +76,12 @@ __global__ void embed_rows_kernel(const void* table, int bf16, const int* __rest
 // logit 0, i.e. 0 if logit 0 is NaN, else the lowest index of the largest
 // non-NaN logit (0 when no other logit is a number). One CTA per row.
 __global__ void __launch_bounds__(1024) greedy_rows_kernel(const float* __restrict__ logits, int n, int* out) {
+    qlm::pdl_wait();  // the logits come from the lm_head GEMV (read through L2)
     const float* l = logits + (int64_t)blockIdx.x * n;
     float best = 0.0f;
     int bi = -1;
     for (int i = threadIdx.x; i < n; i += blockDim.x) {
-        const float v = l[i];
+        const float v = __ldcg(l + i);
         if (v == v && (bi < 0 || v > best)) {  // indices ascend per thread: ties keep the first
             best = v;
             bi = i;
@@ -118,7 +119,10 @@ __global__ void __launch_bounds__(1024) greedy_rows_kernel(const float* __restri
                 bi = i;
             }
         }
-        if (lane == 0) out[blockIdx.x] = (l[0] != l[0] || bi < 0) ? 0 : bi;
+        if (lane == 0) {
+            const float l0 = __ldcg(l);
+            out[blockIdx.x] = (l0 != l0 || bi < 0) ? 0 : bi;
+        }
     }
 }
 
@@ -179,6 +183,7 @@ struct qlm_model {
     // The step captured once as a CUDA graph (after one eager step has sized
     // every scratch buffer) and replayed at every position.
     bool use_graph = true;
+    bool pdl = true;  // step kernels launched as programmatic-dependent secondaries (QLM_PDL=0: not)
     int eager_steps = 0;
     cudaGraph_t graph = nullptr;
     cudaGraphExec_t graph_exec = nullptr;
@@ -561,6 +566,8 @@ int load_all(const std::string& dir, qlm_model* m) {
     {
         const char* e = std::getenv("QLM_MODEL_GRAPH");
         m->use_graph = !(e && e[0] == '0');
+        const char* p = std::getenv("QLM_PDL");
+        m->pdl = !(p && p[0] == '0');
     }
     if (cudaStreamSynchronize(m->stream) != cudaSuccess) return fail(QLM_ERR_CUDA, "load synchronize failed");
     return QLM_OK;
@@ -600,15 +607,14 @@ int gdn_step(qlm_model* m, Layer& ly) {
     const int64_t lds[6] = {lin, lin, lin, lin, lh, lh};
     QLM_TRY(qlm_linear_int8_grouped(m->h, B, H, H, ws, 6, ys, lds, 0, s));                      // 1. projections
     if (qlm::launch_conv1d_silu_dev(qkv, ly.conv_state, m->d_tokens + B + 1, ly.conv_wt, conv, channels,
-                                    m->conv_kernel, s) != cudaSuccess)
+                                    m->conv_kernel, s, m->pdl) != cudaSuccess)
         return launch_ok("conv step + SiLU");                                                     // 2.-4. conv, SiLU
     float *q = conv, *k = conv + (size_t)B * lin, *v = conv + (size_t)2 * B * lin;
-    QLM_TRY(qlm_l2norm_heads(q, 2 * B * lh, ld, 1e-6f, s));  // 5. L2 norms: the k heads follow the q heads
     float* out = qkv;  // the projections are consumed
-    if (qlm::launch_gdn_recurrence_gates(ly.rstate, q, k, v, a_raw, b_raw, ly.A_log, ly.dt_bias, lh, out, B * lh, ld,
-                                         s) != cudaSuccess)
-        return launch_ok("gates + delta rule");                                                   // 6.-7.
-    if (qlm::launch_head_norm_gate(out, ly.gdn_norm, z, B * lh, ld, 1e-6f, s) != cudaSuccess)
+    if (qlm::launch_gdn_recurrence_fused(ly.rstate, q, k, v, a_raw, b_raw, ly.A_log, ly.dt_bias, lh, 1e-6f, out,
+                                         B * lh, ld, s, m->pdl) != cudaSuccess)
+        return launch_ok("L2 norms + gates + delta rule");                                        // 5.-7.
+    if (qlm::launch_head_norm_gate(out, ly.gdn_norm, z, B * lh, ld, 1e-6f, s, m->pdl) != cudaSuccess)
         return launch_ok("head norm + output gate");                                              // 8.-9.
     return qlm_linear_int8(z, B, lin, lin, ly.out, m->t5, H, 0, s);                               // 10. out_proj
 }
@@ -628,14 +634,15 @@ int attn_step(qlm_model* m, Layer& ly) {
     float* ys[3] = {q, k, v};
     const int64_t lds[3] = {(int64_t)nh * qd, kv, kv};
     QLM_TRY(qlm_linear_int8_grouped(m->h, B, H, H, ws, 3, ys, lds, 0, s));                // 1. projections
-    if (qlm::launch_qk_norm(q, qd, ly.q_norm, B * nh, k, hd, ly.k_norm, B * kvh, hd, 1e-6f, s) != cudaSuccess)
+    if (qlm::launch_qk_norm(q, qd, ly.q_norm, B * nh, k, hd, ly.k_norm, B * kvh, hd, 1e-6f, s, m->pdl) !=
+        cudaSuccess)
         return launch_ok("QK-norm");                                                          // 2. QK-norm
     const int* d_pos = m->d_tokens + B;  // q: the query half of each [query | gate] row
     if (qlm::launch_rope_append(q, qd, B * nh, k, v, B * kvh, hd, m->rotary_dim, m->rope_cos, m->rope_sin, d_pos,
-                                ly.k_cache, ly.v_cache, s) != cudaSuccess)
+                                ly.k_cache, ly.v_cache, s, m->pdl) != cudaSuccess)
         return launch_ok("RoPE + KV cache write");                                           // 3.-4.
     if (qlm::launch_gqa_attend_dev(q, qd, ly.k_cache, ly.v_cache, att, d_pos, m->max_seq - 1, B * nh, B * kvh, hd,
-                                   m->scores, q + hd, qd, s) != cudaSuccess)                 // 5.-6. attention,
+                                   m->scores, q + hd, qd, s, m->pdl) != cudaSuccess)                 // 5.-6. attention,
         return launch_ok("attention");                                                       // output gate
     return qlm_linear_int8(att, B, nh * hd, nh * hd, ly.o, m->t5, H, 0, s);                 // 7. o_proj
 }
@@ -661,25 +668,29 @@ int enqueue_step(qlm_model* m) {
     // norm, the next layer's input norm, the final norm): same bits as
     // elementwise_add + rms_norm (modules.hpp:228-231, 239-240).
     const size_t nl = m->layers.size();
-    QLM_TRY(qlm_rms_norm(m->x, nl ? m->layers[0].in_norm : m->final_norm, m->h, B, H, m->eps, s));
+    if (qlm::launch_rms_norm(m->x, nl ? m->layers[0].in_norm : m->final_norm, m->h, B, H, m->eps, s, m->pdl) !=
+        cudaSuccess)
+        return launch_ok("input norm");
     for (size_t l = 0; l < nl; ++l) {
         Layer& ly = m->layers[l];
         QLM_TRY(ly.full_attn ? attn_step(m, ly) : gdn_step(m, ly));
-        if (qlm::launch_add_then_rms_norm(m->x, m->t5, ly.post_norm, m->h, B, H, m->eps, s) != cudaSuccess)
+        if (qlm::launch_add_then_rms_norm(m->x, m->t5, ly.post_norm, m->h, B, H, m->eps, s, m->pdl) != cudaSuccess)
             return launch_ok("residual add + post-attention norm");
         const qlm_w8* ws[2] = {ly.gate, ly.up};
         float* ys[2] = {m->gate_buf, m->up_buf};
         const int64_t lds[2] = {m->inter, m->inter};
         QLM_TRY(qlm_linear_int8_grouped(m->h, B, H, H, ws, 2, ys, lds, 0, s));
-        QLM_TRY(qlm_silu_mul(m->gate_buf, m->up_buf, (int64_t)B * m->inter, s));
+        if (qlm::launch_silu_mul(m->gate_buf, m->up_buf, (int64_t)B * m->inter, s, m->pdl) != cudaSuccess)
+            return launch_ok("SiLU * up");
         QLM_TRY(qlm_linear_int8(m->gate_buf, B, m->inter, m->inter, ly.down, m->t5, H, 0, s));
         const float* next_norm = l + 1 < nl ? m->layers[l + 1].in_norm : m->final_norm;
-        if (qlm::launch_add_then_rms_norm(m->x, m->t5, next_norm, m->h, B, H, m->eps, s) != cudaSuccess)
+        if (qlm::launch_add_then_rms_norm(m->x, m->t5, next_norm, m->h, B, H, m->eps, s, m->pdl) != cudaSuccess)
             return launch_ok("residual add + norm");
     }
     QLM_TRY(qlm_linear_int8(m->h, B, H, H, m->lm_head, m->logits, m->vocab, 0, s));
-    greedy_rows_kernel<<<B, 1024, 0, s>>>(m->logits, m->vocab, m->d_tokens);
-    QLM_TRY(launch_ok("greedy choice"));
+    if (qlm::launch_pdl(m->pdl, greedy_rows_kernel, dim3(B), dim3(1024), 0, s, (const float*)m->logits, m->vocab,
+                        m->d_tokens) != cudaSuccess)
+        return launch_ok("greedy choice");
     if (cudaMemcpyAsync(m->h_tokens, m->d_tokens, (size_t)B * sizeof(int), cudaMemcpyDeviceToHost, s) != cudaSuccess)
         return fail(QLM_ERR_CUDA, "token read-back failed");
     return QLM_OK;
