@@ -317,6 +317,16 @@ def store_info(path: str, name: str):
     return b.value, r.value, k.value
 
 
+def _host_addr(a) -> int:
+    """Address of a numpy array's first element. A writable C-contiguous array
+    exports it through the buffer protocol in ~0.5 us; `.ctypes.data` builds
+    an object (1.3-2.2 us), which is the fallback for any other array."""
+    try:
+        return ctypes.addressof(ctypes.c_char.from_buffer(a))
+    except (TypeError, ValueError, BufferError):
+        return a.ctypes.data
+
+
 def matmul(A, B: Int8Weight, C=None, transpose_B: bool = True, flags: int = EXACT, stream=None):
     """C = A . B^T for an int8 or int4 B (``math::matmul`` with transpose_B=true).
 
@@ -357,7 +367,7 @@ def matmul(A, B: Int8Weight, C=None, transpose_B: bool = True, flags: int = EXAC
     c2 = C if C.ndim == 2 else C.reshape(1, -1)
     if c2.dtype != np.float32 or c2.strides[1] != 4 or c2.shape != (M, B.rows):
         raise QlmError(1, "C must be float32 [M, N] with unit column stride")
-    _check(lib.qlm_linear_int8(a2.ctypes.data, M, K, a2.strides[0] // 4, B.handle, c2.ctypes.data,
+    _check(lib.qlm_linear_int8(_host_addr(a2), M, K, a2.strides[0] // 4, B.handle, _host_addr(c2),
                                c2.strides[0] // 4, flags | HOST_IO, _stream_ptr(stream)))
     return C
 
