@@ -745,7 +745,9 @@ def main():
 
     launches = args.steps * STACK
     total_weight = launches * weight_bytes() * world
-    kernels_per_gemv = 1  # the all-gather (N > 1) is fused into the GEMV kernel
+    # N > 1: the GEMV stores its rows into every rank's buffer over NVLink and
+    # a small collect kernel waits for the peers' rows and writes y
+    kernels_per_gemv = 2 if world > 1 else 1
     value = total_weight / (ms / 1000.0) / 1e9
     mean_launch_s = (ms / 1000.0) / launches
     peak, peak_kind = measured_peaks()

@@ -353,9 +353,11 @@ int qlm_comm_status(qlm_comm* c);
 
 /* y[0, 0:n_total] = x[0, 0:k] . W^T for a row-sharded W: this rank's shard w
  * (rows [row_begin, row_end) of n_total) is computed and stored into every
- * rank's exchange buffer over NVLink by the GEMV kernel itself; a bounded wait
- * then copies the gathered row into y (device pointer, n_total floats).
- * M must be 1 (decode). All ranks must make the same sequence of calls. */
+ * rank's exchange buffer over NVLink by the GEMV kernel itself; a second,
+ * small kernel then waits (bounded) for the other ranks' rows and copies the
+ * gathered row into y (device pointer, n_total floats), while the next kernel
+ * in the stream already starts its weight copies. M must be 1 (decode). All
+ * ranks must make the same sequence of calls. */
 int qlm_linear_int8_allgather(const float* x, int M, int k, int64_t ldx, const qlm_w8* w, qlm_comm* c, float* y,
                               int64_t ldy, int flags, void* stream);
 

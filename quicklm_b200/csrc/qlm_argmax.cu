@@ -97,7 +97,7 @@ __global__ void __launch_bounds__(kThreads) argmax_kernel(const float* __restric
     }
     // A failed communicator (a bounded wait gave up earlier): do nothing.
     if (a.status && *reinterpret_cast<volatile const int*>(a.status) != 0) return;
-    const int e = *reinterpret_cast<volatile const int*>(a.epoch) + 1;
+    const int e = *reinterpret_cast<volatile const int*>(a.epochs) + 1;
     const unsigned long long* mine = a.peer_words[a.rank] + (e & 1) * kMaxRanks;
     if (threadIdx.x == 0) {
         const uint32_t idx = first_nan ? kIdxFirstNan : (c.i < 0 ? kIdxNone : (uint32_t)(col0 + c.i));
@@ -141,7 +141,8 @@ __global__ void __launch_bounds__(kThreads) argmax_kernel(const float* __restric
             *out_idx = best.i;
             *out_val = best.i < 0 ? __int_as_float(0x7fc00000) : best.v;
         }
-        if (*reinterpret_cast<volatile const int*>(a.status) == 0) *const_cast<volatile int*>(a.epoch) = e;
+        if (*reinterpret_cast<volatile const int*>(a.status) == 0)
+            for (int s = 0; s < a.nepochs; ++s) reinterpret_cast<volatile int*>(a.epochs)[s] = e;
     }
 }
 

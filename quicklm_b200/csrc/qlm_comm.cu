@@ -48,6 +48,11 @@ void set_last_error(const std::string& msg);
 namespace {
 
 constexpr size_t kHeaderBytes = 256;  // greedy-choice words; keeps the gathered words 256-byte aligned
+// Device state words: [2] the sticky status, [8, 8 + kEpochWords) the epoch
+// words (qlm::GatherArgs), one per CTA index of a gather launch (at most one
+// CTA per SM).
+constexpr int kEpochOffset = 8;
+constexpr int kEpochWords = 256;
 static_assert(2 * qlm::kMaxRanks * sizeof(unsigned long long) <= kHeaderBytes, "argmax words fit the header");
 
 int fail(int code, const char* fmt, ...) {
@@ -100,8 +105,9 @@ int qlm_comm_create(int device, int rank, int nranks, int64_t max_out, qlm_comm*
     const size_t bytes = kHeaderBytes + 2 * (size_t)c->stride * sizeof(unsigned long long);
     if (e == cudaSuccess) e = cudaMalloc(&c->base, bytes);
     if (e == cudaSuccess) e = cudaMemset(c->base, 0, bytes);
-    if (e == cudaSuccess) e = cudaMalloc(&c->state, 4 * sizeof(int));
-    if (e == cudaSuccess) e = cudaMemset(c->state, 0, 4 * sizeof(int));
+    if (e == cudaSuccess && c->sm_count > kEpochWords) e = cudaErrorNotSupported;
+    if (e == cudaSuccess) e = cudaMalloc(&c->state, (kEpochOffset + kEpochWords) * sizeof(int));
+    if (e == cudaSuccess) e = cudaMemset(c->state, 0, (kEpochOffset + kEpochWords) * sizeof(int));
     cudaIpcMemHandle_t h;
     if (e == cudaSuccess) e = cudaIpcGetMemHandle(&h, c->base);
     if (e != cudaSuccess) {
@@ -189,8 +195,8 @@ int qlm_linear_int8_allgather(const float* x, int M, int k, int64_t ldx, const q
     for (int r = 0; r < c->nranks; ++r) {
         ga.peer_slots[r] = reinterpret_cast<unsigned long long*>(c->peers[r] + kHeaderBytes);
     }
-    ga.counter = c->state;
-    ga.epoch = c->state + 1;
+    ga.epochs = c->state + kEpochOffset;
+    ga.nepochs = kEpochWords;
     ga.out_stride = c->stride;
     ga.nranks = c->nranks;
     ga.rank = c->rank;
@@ -199,6 +205,8 @@ int qlm_linear_int8_allgather(const float* x, int M, int k, int64_t ldx, const q
     cudaError_t e = qlm::launch_gemv_exact(x, ldx, 1, w->q, w->s, w->gmaps, w->rows, k, y, ldy, c->state + 2,
                                            c->sm_count, s, true, &ga, w->bits == 4);
     if (e != cudaSuccess) return cuda_fail(e, "fused GEMV + all-gather launch");
+    e = qlm::launch_gather_collect(ga, y, c->state + 2, c->sm_count, s, true);
+    if (e != cudaSuccess) return cuda_fail(e, "all-gather collect launch");
     prof.stop();
     if (flags & QLM_LINEAR_SYNC) {
         e = cudaStreamSynchronize(s);
@@ -230,7 +238,8 @@ int qlm_argmax_f32(const float* logits, int n, int64_t col0, qlm_comm* c, int* o
         if (c->failed) return fail(QLM_ERR_TIMEOUT, "the communicator failed earlier (a peer did not answer); free and recreate it");
         for (int r = 0; r < c->nranks; ++r) a.peer_words[r] = reinterpret_cast<unsigned long long*>(c->peers[r]);
         a.wait_ns = c->wait_ns;
-        a.epoch = c->state + 1;
+        a.epochs = c->state + kEpochOffset;
+        a.nepochs = kEpochWords;
         a.status = c->state + 2;
         a.nranks = c->nranks;
         a.rank = c->rank;

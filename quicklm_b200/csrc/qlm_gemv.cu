@@ -226,11 +226,6 @@ __global__ void __launch_bounds__(MM == 1 || R == 2 ? 384 : 512, MM == 1 ? 2 : 1
     // plan requests 128 spare bytes).
     uint8_t* smem = smem_raw + ((128u - (sm100::smem_u32(smem_raw) & 127u)) & 127u);
     using namespace sm100;
-    // A communicator whose bounded wait gave up is failed: such a call does
-    // nothing (the host reports QLM_ERR_TIMEOUT until the communicator is
-    // freed and recreated). The word is loaded here and looked at after the
-    // dependency wait, so the load's latency overlaps the weight copies.
-    const int comm_failed = GATHER ? ld_relaxed_sys_i32(p.status) : 0;
     const int warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5, lane32 = threadIdx.x & 31;
     const int lane = threadIdx.x & 7;                // reference lane l
     const int rsub = ((threadIdx.x >> 3) & 3) * R;   // first of the thread's R rows within the unit
@@ -305,19 +300,19 @@ __global__ void __launch_bounds__(MM == 1 || R == 2 ? 384 : 512, MM == 1 ? 2 : 1
     // x, so x is not read-only for this kernel's lifetime and an L1/texture
     // line of an earlier read of the buffer could be served stale.
     pdl_wait();
-    if (GATHER && comm_failed) {
-        // Let this warp's copies land before leaving (bounded).
-        if (lane32 == 0)
-            for (int j = 0; j < p.d && j < items; ++j)
-                mbar_wait(bars + j * 8, 0u, nullptr, kWaitBudget);
-        return;
-    }
-    // Gather: this call's epoch (the previous call's kernel, which advanced
-    // it, has completed) and the exchange half it selects.
+    // Gather: a communicator whose bounded wait gave up is failed, and such a
+    // call does nothing (the host reports QLM_ERR_TIMEOUT until the
+    // communicator is freed and recreated). The status word is read after the
+    // dependency wait, so it includes the previous call's collect kernel; one
+    // thread reads it and the CTA decides together after the staging barrier.
+    // Then this call's epoch (the previous call's collect kernel, which
+    // advanced it, has completed) and the exchange half it selects.
+    __shared__ int comm_failed;
     int g_epoch = 0;
     long long g_half = 0;
     if (GATHER) {
-        g_epoch = *reinterpret_cast<volatile const int*>(p.ga.epoch) + 1;
+        if (threadIdx.x == 0) comm_failed = ld_relaxed_sys_i32(p.status);
+        g_epoch = *reinterpret_cast<volatile const int*>(p.ga.epochs + blockIdx.x) + 1;
         g_half = (long long)(g_epoch & 1) * p.ga.out_stride;
     }
 #pragma unroll 1
@@ -339,6 +334,13 @@ __global__ void __launch_bounds__(MM == 1 || R == 2 ? 384 : 512, MM == 1 ? 2 : 1
         }
     }
     __syncthreads();
+    if (GATHER && comm_failed) {
+        // Let this warp's copies land before leaving (bounded).
+        if (lane32 == 0)
+            for (int j = 0; j < p.d && j < items; ++j)
+                mbar_wait(bars + j * 8, 0u, nullptr, kWaitBudget);
+        return;
+    }
 
     const int nbf = p.k / kBlock;  // full blocks
     const int cfull = nbf / 4;     // chunks of 4 full blocks
@@ -452,42 +454,6 @@ __global__ void __launch_bounds__(MM == 1 || R == 2 ? 384 : 512, MM == 1 ? 2 : 1
     if (lane32 == 0)
         for (int j = stop; j < stop + p.d && j < items; ++j)
             mbar_wait(bars + (j % p.d) * 8, (uint32_t)((j / p.d) & 1), nullptr, kWaitBudget);
-    if (GATHER) {
-        // Completion, by every CTA: wait (bounded) until every word of this
-        // CTA's slice of the gathered row carries this call's epoch, and copy
-        // the values into y. The last CTA to finish resets the counter and
-        // records the epoch (every CTA read it before counting itself).
-        __shared__ int is_last;
-        const int per = (p.ga.n_total + (int)gridDim.x - 1) / (int)gridDim.x;
-        const int c0 = min((int)blockIdx.x * per, p.ga.n_total), c1 = min(c0 + per, p.ga.n_total);
-        const unsigned long long* mine = p.ga.peer_slots[p.ga.rank] + g_half;
-        const long long t0 = globaltimer_ns();
-        for (int i = c0 + (int)threadIdx.x; i < c1; i += blockDim.x) {
-            unsigned long long v = ld_relaxed_sys_u64(mine + i);
-            while ((int)(v >> 32) != g_epoch) {
-                if (globaltimer_ns() - t0 > p.ga.wait_ns) {
-                    if (p.status) atomicCAS(p.status, 0, kStatusGatherTimeout);
-                    break;
-                }
-                __nanosleep(32);
-                v = ld_relaxed_sys_u64(mine + i);
-            }
-            if ((int)(v >> 32) == g_epoch) p.grp[0].y[i] = __uint_as_float((uint32_t)v);
-        }
-        __syncthreads();
-        if (threadIdx.x == 0) {
-            __threadfence();
-            is_last = atomicAdd(p.ga.counter, 1) == (int)gridDim.x - 1;
-            if (is_last) {
-                __threadfence();
-                *p.ga.counter = 0;
-                // After a give-up the communicator is failed: its epoch stays
-                // where it was and every later call returns at entry.
-                if (*reinterpret_cast<volatile int*>(p.status) == 0)
-                    *const_cast<volatile int*>(p.ga.epoch) = g_epoch;
-            }
-        }
-    }
 }
 
 struct Plan {
@@ -724,6 +690,83 @@ cudaError_t gemv_make_maps(const uint8_t* q, const float* s, int rows, int k, bo
         out->dev = nullptr;
     }
     return e;
+}
+
+namespace {
+
+constexpr int kCollectThreads = 256;
+
+// Second half of the fused all-gather: the GEMV of a call stores its rows'
+// words into every rank's exchange buffer and ends; this kernel, next in the
+// stream, waits (bounded) until every word of the gathered row in this rank's
+// buffer carries the call's epoch, copies the values into y and advances the
+// epoch words, so no GEMV ends in a cross-GPU barrier. The trigger comes
+// first: the next kernel (typically the next GEMV, which waits for this one's
+// completion before it reads anything) can then take an SM beside this call's
+// GEMV and issue its weight copies during that GEMV's compute and this
+// kernel's wait, as consecutive GEMVs do on one GPU.
+__global__ void __launch_bounds__(kCollectThreads) gather_collect_kernel(const __grid_constant__ GatherArgs ga,
+                                                                         float* __restrict__ y, int* status) {
+    using namespace sm100;
+    constexpr int kBatch = 4;  // words of a thread in flight at once
+    pdl_launch_dependents();
+    pdl_wait();  // this call's GEMV has completed (its own stores are issued)
+    const int failed = ld_relaxed_sys_i32(status);
+    const int e = *reinterpret_cast<volatile const int*>(ga.epochs + blockIdx.x) + 1;
+    if (failed) return;  // the GEMV returned at entry; nothing was stored
+    const unsigned long long* mine = ga.peer_slots[ga.rank] + (long long)(e & 1) * ga.out_stride;
+    const long long t0 = globaltimer_ns();
+    const int stride = (int)(gridDim.x * blockDim.x);
+    for (int base = (int)(blockIdx.x * blockDim.x + threadIdx.x); base < ga.n_total; base += kBatch * stride) {
+        unsigned long long v[kBatch];
+#pragma unroll
+        for (int u = 0; u < kBatch; ++u) {
+            const int i = base + u * stride;
+            v[u] = i < ga.n_total ? ld_relaxed_sys_u64(mine + i) : 0ull;
+        }
+#pragma unroll
+        for (int u = 0; u < kBatch; ++u) {
+            const int i = base + u * stride;
+            if (i >= ga.n_total) break;
+            while ((int)(v[u] >> 32) != e) {
+                if (globaltimer_ns() - t0 > ga.wait_ns) {
+                    atomicCAS(status, 0, kStatusGatherTimeout);
+                    break;
+                }
+                __nanosleep(32);
+                v[u] = ld_relaxed_sys_u64(mine + i);
+            }
+            if ((int)(v[u] >> 32) == e) y[i] = __uint_as_float((uint32_t)v[u]);
+        }
+    }
+    __syncthreads();  // every thread's wait has ended (or recorded a give-up)
+    // CTA b advances words b, b + grid, ... (see GatherArgs). After a give-up
+    // the communicator is failed and its epoch words are not used again.
+    if (threadIdx.x == 0 && ld_relaxed_sys_i32(status) == 0)
+        for (int sl = (int)blockIdx.x; sl < ga.nepochs; sl += (int)gridDim.x)
+            reinterpret_cast<volatile int*>(ga.epochs)[sl] = e;
+}
+
+}  // namespace
+
+cudaError_t launch_gather_collect(const GatherArgs& ga, float* y, int* status, int sm_count, cudaStream_t stream,
+                                  bool pdl) {
+    if (ga.nranks <= 0 || ga.n_total <= 0 || !status || !ga.epochs) return cudaErrorInvalidValue;
+    int ctas = (ga.n_total + kCollectThreads - 1) / kCollectThreads;
+    if (ctas > sm_count) ctas = sm_count;
+    if (ctas > ga.nepochs) ctas = ga.nepochs;
+    if (ctas < 1) ctas = 1;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)ctas);
+    cfg.blockDim = dim3((unsigned)kCollectThreads);
+    cfg.dynamicSmemBytes = 0;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, gather_collect_kernel, ga, y, status);
 }
 
 }  // namespace qlm

@@ -34,12 +34,16 @@ constexpr int kMaxRanks = 8;
 // rank r's exchange area: two halves of out_stride 64-bit words, picked by
 // the parity of the call's epoch; a word holds (epoch << 32) | float bits of
 // one gathered output, so a reader knows from the word alone whether it
-// belongs to the current call. Device-resident state of this rank: counter
-// (CTA completions, starts at 0) and epoch (last completed call).
+// belongs to the current call. Device-resident state of this rank: the
+// communicator's last completed call (its epoch), kept in nepochs equal
+// words, one per CTA index. The GEMV's CTA b reads word b; the collect
+// kernel's CTA b reads word b and, at its end, writes the new epoch into words
+// b, b + grid, b + 2 grid, ..., so every word advances once per call for any
+// grid size, with no cross-CTA counter.
 struct GatherArgs {
     unsigned long long* peer_slots[kMaxRanks];
-    int* counter;
-    const int* epoch;
+    int* epochs;
+    int nepochs;
     long long out_stride;
     int n_total; // gathered width copied into y
     int nranks;  // 0 = no gather
@@ -53,7 +57,8 @@ struct GatherArgs {
 // launch reduces its logits alone.
 struct ArgmaxArgs {
     unsigned long long* peer_words[kMaxRanks];
-    const int* epoch;
+    int* epochs;        // the communicator's epoch words (GatherArgs); this one-CTA launch advances all
+    int nepochs;
     int* status;        // the communicator's: non-zero = failed, the kernel does nothing
     int nranks;
     int rank;
@@ -87,10 +92,18 @@ cudaError_t gemv_make_maps(const uint8_t* q, const float* s, int rows, int k, bo
 // Bit-exact y[m][0:rows] = x[m][0:k] . W^T for m < mm (1..8), W packed.
 // status: device int set non-zero if a bounded wait gave up. With gather
 // (mm == 1 only) the rows are stored into every rank's exchange buffer
-// instead of y.
+// instead of y, and launch_gather_collect, next in the stream, completes the
+// call.
 cudaError_t launch_gemv_exact(const float* x, int64_t ldx, int mm, const uint8_t* q, const float* s,
                               const GemvMaps& maps, int rows, int k, float* y, int64_t ldy, int* status, int sm_count,
                               cudaStream_t stream, bool pdl, const GatherArgs* gather = nullptr, bool q4 = false);
+
+// Completes a gather call: waits (bounded, ga.wait_ns; status 0x202 on a
+// give-up) for every rank's words of the call in this rank's exchange buffer,
+// writes y[0:ga.n_total] and advances the epoch words. Does nothing when
+// *status is non-zero.
+cudaError_t launch_gather_collect(const GatherArgs& ga, float* y, int* status, int sm_count, cudaStream_t stream,
+                                  bool pdl);
 
 // One weight of a grouped exact launch (packed q, scales, their descriptors,
 // rows, output).

@@ -126,6 +126,28 @@ def _worker(rank, world, port, result_dir):
                 got = q.argmax(loc, comm2, col0=b2)
                 if msg == "ok" and got[0] != greedy_argmax(v):
                     msg = f"sharded argmax case: {got} != {greedy_argmax(v)}"
+            # gathers of different grid sizes (126 and 13 CTAs) and the
+            # one-CTA argmax interleaved on one communicator: every CTA index
+            # must see the call's epoch
+            _, ws_ = synth_case(1, 100, 300, 6)
+            wsd = torch.from_numpy(ws_).cuda()
+            b3, e3 = q.shard_rows(100, world, rank)
+            shard3 = q.Int8Weight.quantize(wsd, device=rank, row_begin=b3, row_end=e3)
+            full3 = q.Int8Weight.quantize(wsd, device=rank)
+            y3_ref = q.matmul(xod, full3, flags=q.SYNC)
+            for i, which in enumerate((3, 2, 3, 3, "a", 2, 3, 2)):
+                if which == "a":
+                    loc = torch.from_numpy(cases[0][b2:e2].copy()).cuda()
+                    got = q.argmax(loc, comm2, col0=b2)
+                    ok = got[0] == greedy_argmax(cases[0])
+                elif which == 3:
+                    ok = torch.equal(q.matmul_allgather(xod, shard3, comm2, flags=q.SYNC).view(torch.int32),
+                                     y3_ref.view(torch.int32))
+                else:
+                    ok = torch.equal(q.matmul_allgather(xod, shard2, comm2, flags=q.SYNC).view(torch.int32),
+                                     y_ref.view(torch.int32))
+                if msg == "ok" and not ok:
+                    msg = f"interleaved grid sizes, call {i} ({which}): result differs"
             torch.cuda.synchronize()
             dist.barrier()
             comm2.free()
