@@ -194,19 +194,23 @@ int ensure_buf(T** buf, size_t* cap, size_t bytes) {
 
 // The exact product for 9..64 activation rows per launch streams W once
 // (qlm_gemm_exact.cu); QLM_GEMM_EXACT=0 runs such M as launches of up to 8
-// rows instead (for comparisons).
-bool exact_gemm_enabled() {
-    static const bool on = [] {
+// rows instead, =2 uses the one-launch kernel whatever the row count (both
+// for comparisons).
+int exact_gemm_mode() {
+    static const int mode = [] {
         const char* e = std::getenv("QLM_GEMM_EXACT");
-        return !(e && e[0] == '0');
+        return e && e[0] == '0' ? 0 : (e && e[0] == '2' ? 2 : 1);
     }();
-    return on;
+    return mode;
 }
+bool exact_gemm_enabled() { return exact_gemm_mode() != 0; }
 constexpr int kExactGemmMin = 9;  // from this M on, one launch per 64 rows
-// ... for matrices up to this many rows: each 32-row CTA of that kernel reads
-// all activation rows, which outweighs the single weight stream for a
-// vocabulary head (lm_head [151936, 2560] at M = 64: 2.35 ms vs 2.11 ms as
-// launches of 8 rows; [2560, 9728]: 0.27 vs 1.29 ms).
+// ... for matrices up to this many rows: every pass of that kernel restages
+// all activation rows of its chunks, which outweighs the single weight stream
+// for a vocabulary head. Measured with QLM_GEMM_EXACT=2 against launches of 8
+// rows: lm_head [151936, 2560] at M = 16/32/64 0.64/1.24/2.42 ms vs
+// 0.53/1.06/2.11 ms, its half [75968, 2560] 0.34/0.64/1.23 vs 0.29/0.58/1.15
+// ms; [2560, 9728] at M = 64: 0.22 vs 1.29 ms.
 constexpr int kExactGemmMaxRows = 65536;
 
 bool pdl_enabled() {
@@ -618,7 +622,8 @@ int qlm_linear_int8(const float* x, int M, int k, int64_t ldx, const qlm_w8* w, 
         QLM_CUDA(qlm::launch_gemm_tc(*w->maps, w->ew, w->rows, k, dx, dldx, M, st->x16, st->ea, dy, dldy, st->status,
                                      s, pdl_enabled()),
                  "tensor-core GEMM launch");
-    } else if (M >= kExactGemmMin && exact_gemm_enabled() && w->rows <= kExactGemmMaxRows) {
+    } else if (M >= kExactGemmMin && exact_gemm_enabled() &&
+               (w->rows <= kExactGemmMaxRows || exact_gemm_mode() == 2)) {
         {
             std::lock_guard<std::mutex> lk(g_dev_mu);
             if ((rc = ensure_buf(&st->xpair, &st->xpair_cap, qlm::gemm_exact_scratch_bytes(64, k)))) return rc;
