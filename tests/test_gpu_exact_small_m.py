@@ -76,3 +76,31 @@ def test_grouped_small_m_matches_single(q):
             assert bits_equal(y[mm - 1:].cpu().numpy(), q.matmul(x[mm - 1], w, flags=q.SYNC).cpu().numpy())
     for w in ws:
         w.free()
+
+
+def test_forced_kernel_on_tall_matrix_matches_default(qlm_lib, cuda_device, tmp_path):
+    """QLM_GEMM_EXACT=2 sends matrices of more than 65536 rows (the vocabulary
+    head) to the one-launch kernel as well; its rows must carry the same bits
+    as the default path (launches of 8 rows) there. The switch is read once
+    per process, so the forced run is a child process."""
+    import os
+    import subprocess
+    import sys
+    from tests.conftest import ROOT
+    code = (
+        "import numpy as np, sys\n"
+        "import quicklm_b200 as q\n"
+        "rng = np.random.default_rng(5)\n"
+        "w = q.Int8Weight.quantize((rng.standard_normal((70001, 160)) * 0.02).astype(np.float32))\n"
+        "x = rng.standard_normal((24, 160)).astype(np.float32)\n"
+        "np.save(sys.argv[1], q.matmul(x, w))\n"
+    )
+    outs = []
+    for mode in ("1", "2"):
+        path = str(tmp_path / f"tall_{mode}.npy")
+        env = {**os.environ, "QLM_GEMM_EXACT": mode}
+        r = subprocess.run([sys.executable, "-c", code, path], cwd=ROOT, env=env, capture_output=True, text=True,
+                           timeout=600)
+        assert r.returncode == 0, r.stderr[-2000:]
+        outs.append(np.load(path))
+    assert bits_equal(outs[0], outs[1])
